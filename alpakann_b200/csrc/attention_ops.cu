@@ -1,0 +1,223 @@
+// attention_ops.cu -- attentionScores / attentionApply as separate drop-in ops
+// (reference: onHost/nn/attention.hpp:54-110, onAcc/internal/nn/attention.hpp:15-69).
+//
+// Both are batched contractions per (batch, query head):
+//   scores: S[i,j] = sum_d Q[i,d] K[j,d]      (M=Tq, N=Tk, K=D)
+//   apply:  O[i,d] = sum_j P[i,j] V[j,d]      (M=Tq, N=D,  K=Tk)
+// with the KV head hq / queriesPerKvGroup (GQA) and K/V in BTHD or BHTD. One
+// strided tiled kernel serves both: 64x64 output tiles, 16-deep K slices
+// staged in shared memory with the global loads walking the unit-stride axis,
+// 4x4 register blocking, FMA accumulation in ascending k per output -- the
+// reference's summation order. These ops materialise the full score matrix
+// like the reference does; the fused decode kernel is the fast path.
+#include "common.cuh"
+
+namespace ann {
+namespace {
+
+struct BgemmArgs {
+    const void* A;
+    const void* B;
+    void* C;
+    int64_t M, N, K;
+    int64_t am, ak, bk, bn, cm, cn;        // element strides inside one batch
+    int64_t a_b, a_h, b_b, b_h, c_b, c_h;  // batch / head strides; B uses head hq / g
+    int64_t heads;
+    uint32_t g;
+    int a_k_unit, b_k_unit;  // load mapping: walk k (1) or m/n (0) across threads
+};
+
+constexpr int BM = 64, BN = 64, BK = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) bgemm_kernel(BgemmArgs a) {
+    __shared__ T As[BK][BM + 1];
+    __shared__ T Bs[BK][BN + 1];
+    int const tid = threadIdx.x;
+    int const tx = tid % 16, ty = tid / 16;
+    int64_t const z = blockIdx.z;
+    int64_t const b = z / a.heads, hq = z % a.heads;
+    int64_t const kvh = hq / a.g;
+    T const* A = static_cast<T const*>(a.A) + b * a.a_b + hq * a.a_h;
+    T const* B = static_cast<T const*>(a.B) + b * a.b_b + kvh * a.b_h;
+    T* C = static_cast<T*>(a.C) + b * a.c_b + hq * a.c_h;
+    int64_t const m0 = static_cast<int64_t>(blockIdx.y) * BM, n0 = static_cast<int64_t>(blockIdx.x) * BN;
+    T acc[4][4] = {};
+    for (int64_t k0 = 0; k0 < a.K; k0 += BK) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int const lin = tid + e * 256;
+            int const m = a.a_k_unit ? lin / BK : lin % BM;
+            int const k = a.a_k_unit ? lin % BK : lin / BM;
+            int64_t const gm = m0 + m, gk = k0 + k;
+            As[k][m] = (gm < a.M && gk < a.K) ? A[gm * a.am + gk * a.ak] : T{};
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int const lin = tid + e * 256;
+            int const n = a.b_k_unit ? lin / BK : lin % BN;
+            int const k = a.b_k_unit ? lin % BK : lin / BN;
+            int64_t const gn = n0 + n, gk = k0 + k;
+            Bs[k][n] = (gn < a.N && gk < a.K) ? B[gk * a.bk + gn * a.bn] : T{};
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            T av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) av[i] = As[k][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[j] = Bs[k][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int64_t const gm = m0 + ty * 4 + i;
+        if (gm >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int64_t const gn = n0 + tx * 4 + j;
+            if (gn < a.N) C[gm * a.cm + gn * a.cn] = acc[i][j];
+        }
+    }
+}
+
+template <typename T>
+int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* what) {
+    a.a_k_unit = a.ak == 1 ? 1 : 0;
+    a.b_k_unit = a.bk == 1 ? 1 : 0;
+    int64_t const gx = ceil_div(a.N, BN), gy = ceil_div(a.M, BM);
+    if (gy > 65535 || batches > 65535) return fail(ANN_ENOTSUP, "%s: grid too large for this build.", what);
+    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batches));
+    bgemm_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(a);
+    return check_launch(what);
+}
+
+int check_layout(int layout, const char* what) {
+    if (layout != ANN_LAYOUT_BTHD && layout != ANN_LAYOUT_BHTD) return fail(ANN_EINVAL, "%s: invalid kv layout.", what);
+    return ANN_OK;
+}
+
+template <typename T>
+int attention_scores(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const ann_view* s_v, uint32_t g,
+                     int layout) {
+    // attention.hpp:64-65
+    if (g == 0u) return fail(ANN_EINVAL, "attentionScores requires queriesPerKvGroup > 0.");
+    ANN_TRY(check_layout(layout, "attentionScores"));
+    Dims q, k, s;
+    ANN_TRY(to_dims(q_v, sizeof(T), "attentionScores Q", q));
+    ANN_TRY(to_dims(k_v, sizeof(T), "attentionScores K", k));
+    ANN_TRY(to_dims(s_v, sizeof(T), "attentionScores scores", s));
+    if (q.rank != 4 || k.rank != 4 || s.rank != 4)
+        return fail(ANN_EINVAL, "attentionScores expects rank-4 Q, K and scores.");
+    int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
+    int64_t const B = s.ext[0], Hq = s.ext[1], Tq = s.ext[2], Tk = s.ext[3], D = q.ext[3];
+    if (s.numel() == 0) return ANN_OK;
+    // Reads the reference kernel would make out of bounds are rejected.
+    if (q.ext[0] < B || q.ext[1] < Tq || q.ext[2] < Hq || k.ext[0] < B || k.ext[tok] < Tk ||
+        k.ext[head] <= (Hq - 1) / static_cast<int64_t>(g) || k.ext[3] < D)
+        return fail(ANN_EINVAL, "attentionScores: Q %s / K %s do not cover scores %s.", extents_str(q).c_str(),
+                    extents_str(k).c_str(), extents_str(s).c_str());
+    BgemmArgs a{};
+    a.A = q.data;
+    a.B = k.data;
+    a.C = s.data;
+    a.M = Tq;
+    a.N = Tk;
+    a.K = D;
+    a.am = q.str[1];
+    a.ak = q.str[3];
+    a.bk = k.str[3];
+    a.bn = k.str[tok];
+    a.cm = s.str[2];
+    a.cn = s.str[3];
+    a.a_b = q.str[0];
+    a.a_h = q.str[2];
+    a.b_b = k.str[0];
+    a.b_h = k.str[head];
+    a.c_b = s.str[0];
+    a.c_h = s.str[1];
+    a.heads = Hq;
+    a.g = g;
+    return launch_bgemm<T>(stream, a, B * Hq, "attentionScores");
+}
+
+template <typename T>
+int attention_apply(ann_stream stream, const ann_view* p_v, const ann_view* v_v, const ann_view* o_v, uint32_t g,
+                    int layout) {
+    // attention.hpp:93-94
+    if (g == 0u) return fail(ANN_EINVAL, "attentionApply requires queriesPerKvGroup > 0.");
+    ANN_TRY(check_layout(layout, "attentionApply"));
+    Dims p, v, o;
+    ANN_TRY(to_dims(p_v, sizeof(T), "attentionApply probs", p));
+    ANN_TRY(to_dims(v_v, sizeof(T), "attentionApply values", v));
+    ANN_TRY(to_dims(o_v, sizeof(T), "attentionApply out", o));
+    if (p.rank != 4 || v.rank != 4 || o.rank != 4)
+        return fail(ANN_EINVAL, "attentionApply expects rank-4 probs, values and out.");
+    int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
+    int64_t const B = o.ext[0], Tq = o.ext[1], Hq = o.ext[2], D = o.ext[3], Tk = p.ext[3];
+    if (o.numel() == 0) return ANN_OK;
+    if (p.ext[0] < B || p.ext[1] < Hq || p.ext[2] < Tq || v.ext[0] < B || v.ext[tok] < Tk ||
+        v.ext[head] <= (Hq - 1) / static_cast<int64_t>(g) || v.ext[3] < D)
+        return fail(ANN_EINVAL, "attentionApply: probs %s / values %s do not cover out %s.", extents_str(p).c_str(),
+                    extents_str(v).c_str(), extents_str(o).c_str());
+    BgemmArgs a{};
+    a.A = p.data;
+    a.B = v.data;
+    a.C = o.data;
+    a.M = Tq;
+    a.N = D;
+    a.K = Tk;
+    a.am = p.str[2];
+    a.ak = p.str[3];
+    a.bk = v.str[tok];
+    a.bn = v.str[3];
+    a.cm = o.str[1];
+    a.cn = o.str[3];
+    a.a_b = p.str[0];
+    a.a_h = p.str[1];
+    a.b_b = v.str[0];
+    a.b_h = v.str[head];
+    a.c_b = o.str[0];
+    a.c_h = o.str[2];
+    a.heads = Hq;
+    a.g = g;
+    return launch_bgemm<T>(stream, a, B * Hq, "attentionApply");
+}
+
+}  // namespace
+}  // namespace ann
+
+extern "C" {
+
+int ann_attention_scores_f32(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* sc, uint32_t g,
+                             int32_t layout) {
+    ANN_API_BEGIN
+    return ann::attention_scores<float>(s, q, k, sc, g, layout);
+    ANN_API_END
+}
+int ann_attention_scores_f64(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* sc, uint32_t g,
+                             int32_t layout) {
+    ANN_API_BEGIN
+    return ann::attention_scores<double>(s, q, k, sc, g, layout);
+    ANN_API_END
+}
+int ann_attention_apply_f32(ann_stream s, const ann_view* p, const ann_view* v, const ann_view* o, uint32_t g,
+                            int32_t layout) {
+    ANN_API_BEGIN
+    return ann::attention_apply<float>(s, p, v, o, g, layout);
+    ANN_API_END
+}
+int ann_attention_apply_f64(ann_stream s, const ann_view* p, const ann_view* v, const ann_view* o, uint32_t g,
+                            int32_t layout) {
+    ANN_API_BEGIN
+    return ann::attention_apply<double>(s, p, v, o, g, layout);
+    ANN_API_END
+}
+
+}  // extern "C"

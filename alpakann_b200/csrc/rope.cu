@@ -1,0 +1,236 @@
+// rope.cu -- rope / ropeInPlace (reference: onHost/nn/rope.hpp:21-135,
+// onAcc/internal/nn/rope.hpp:15-49).
+//
+// Interleaved-pair rotation: for pair p of a head vector,
+//   x'[2p]   = x[2p] * cos - x[2p+1] * sin
+//   x'[2p+1] = x[2p] * sin + x[2p+1] * cos
+// with cos/sin = table[positionOffset + token][p].
+//
+// The reference's ropeInPlace allocates a temporary, launches one kernel per
+// element into it and copies back, per tensor (rope.hpp:96-135). Here one
+// launch rotates Q and K together, truly in place: each thread owns whole
+// pairs (two pairs = one 16-byte vector in fp32, one pair in fp64), reads them
+// and writes them back. Products and sums are left uncontracted (no FMA), so
+// the result is bit-identical to the reference expression evaluated in order.
+#include "common.cuh"
+#include "reduce.cuh"
+
+namespace ann {
+namespace {
+
+struct RopeJob {
+    const void* in;
+    void* out;
+    int64_t e0, e1, e2;    // leading extents
+    int64_t npv;           // pair-vectors per head vector
+    int64_t si[4], so[4];  // element strides
+    int64_t items;         // e0 * e1 * e2 * npv
+};
+
+struct RopeArgs {
+    RopeJob job[2];
+    int njobs;
+    const void* cos;
+    const void* sin;
+    int64_t cs0, cs1, ss0, ss1;
+    int layout;
+    int64_t pos_off;
+};
+
+template <typename T, int PV, bool VEC>  // PV pairs per work item; 2*PV contiguous elements when VEC
+__device__ __forceinline__ void rope_item(RopeArgs const& a, RopeJob const& j, int64_t flat) {
+    T const* cosT = static_cast<T const*>(a.cos);
+    T const* sinT = static_cast<T const*>(a.sin);
+    int64_t const pv = flat % j.npv;
+    int64_t r = flat / j.npv;
+    int64_t const a2 = r % j.e2;
+    r /= j.e2;
+    int64_t const a1 = r % j.e1;
+    int64_t const a0 = r / j.e1;
+    int64_t const tok = a.layout == ANN_LAYOUT_BTHD ? a1 : a2;
+    int64_t const pos = a.pos_off + tok;
+    T const* in = static_cast<T const*>(j.in) + a0 * j.si[0] + a1 * j.si[1] + a2 * j.si[2];
+    T* out = static_cast<T*>(j.out) + a0 * j.so[0] + a1 * j.so[1] + a2 * j.so[2];
+    T x[2 * PV];
+    if constexpr (VEC) {
+        using V = typename Vec16<T>::type;
+        V const v = *reinterpret_cast<V const*>(in + 2 * PV * pv);
+        if constexpr (Vec16<T>::n == 4) {
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else {
+            x[0] = v.x; x[1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 2 * PV; ++e) x[e] = in[(2 * PV * pv + e) * j.si[3]];
+    }
+    T y[2 * PV];
+#pragma unroll
+    for (int k = 0; k < PV; ++k) {
+        int64_t const p = pv * PV + k;
+        T const c = cosT[pos * a.cs0 + p * a.cs1];
+        T const s = sinT[pos * a.ss0 + p * a.ss1];
+        T const even = x[2 * k], odd = x[2 * k + 1];
+        y[2 * k] = sub_rn(mul_rn(even, c), mul_rn(odd, s));
+        y[2 * k + 1] = add_rn(mul_rn(even, s), mul_rn(odd, c));
+    }
+    if constexpr (VEC) {
+        using V = typename Vec16<T>::type;
+        V v;
+        if constexpr (Vec16<T>::n == 4) {
+            v.x = y[0]; v.y = y[1]; v.z = y[2]; v.w = y[3];
+        } else {
+            v.x = y[0]; v.y = y[1];
+        }
+        *reinterpret_cast<V*>(out + 2 * PV * pv) = v;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 2 * PV; ++e) out[(2 * PV * pv + e) * j.so[3]] = y[e];
+    }
+}
+
+template <typename T, int PV, bool VEC>
+__global__ void __launch_bounds__(256) rope_kernel(RopeArgs a) {
+    int64_t const total = a.job[0].items + (a.njobs > 1 ? a.job[1].items : 0);
+    int64_t const step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += step) {
+        if (i < a.job[0].items)
+            rope_item<T, PV, VEC>(a, a.job[0], i);
+        else
+            rope_item<T, PV, VEC>(a, a.job[1], i - a.job[0].items);
+    }
+}
+
+// validateRopeShape (rope.hpp:21-46), with the coverage check on the layout's
+// real token axis (the reference tests axis 1 for every rank-4 tensor).
+template <typename T>
+int validate(const Dims& in, const Dims& out, const Dims& c, const Dims& s, int layout, uint32_t off) {
+    if (!same_extents(in, out)) return fail(ANN_EINVAL, "rope shape mismatch.");
+    if (in.rank != 4) return fail(ANN_EINVAL, "rope expects a rank-4 BTHD or BHTD tensor.");
+    if (layout != ANN_LAYOUT_BTHD && layout != ANN_LAYOUT_BHTD) return fail(ANN_EINVAL, "rope layout is invalid.");
+    int64_t const headDim = in.ext[3];
+    if (headDim % 2 != 0) return fail(ANN_EINVAL, "rope requires an even head dimension.");
+    if (!same_extents(c, s)) return fail(ANN_EINVAL, "rope cosine/sine table shape mismatch.");
+    if (c.rank != 2) return fail(ANN_EINVAL, "rope tables must be rank 2 [positions, headDim/2].");
+    if (c.ext[1] != headDim / 2) return fail(ANN_EINVAL, "rope table pair count mismatch.");
+    int64_t const tokens = layout == ANN_LAYOUT_BTHD ? in.ext[1] : in.ext[2];
+    if (static_cast<int64_t>(off) + tokens > c.ext[0])
+        return fail(ANN_EINVAL, "rope table does not cover requested positions.");
+    return ANN_OK;
+}
+
+template <typename T>
+void make_job(RopeJob& j, const Dims& in, const Dims& out, int pv) {
+    j.in = in.data;
+    j.out = out.data;
+    j.e0 = in.ext[0];
+    j.e1 = in.ext[1];
+    j.e2 = in.ext[2];
+    j.npv = in.ext[3] / 2 / pv;
+    for (int i = 0; i < 4; ++i) {
+        j.si[i] = in.str[i];
+        j.so[i] = out.str[i];
+    }
+    j.items = j.e0 * j.e1 * j.e2 * j.npv;
+}
+
+template <typename T>
+bool vec_ok(const Dims& in, const Dims& out) {
+    constexpr int NV = Vec16<T>::n;
+    if (in.str[3] != 1 || out.str[3] != 1 || in.ext[3] % NV != 0) return false;
+    if (!aligned(in.data, 16) || !aligned(out.data, 16)) return false;
+    for (int i = 0; i < 3; ++i)
+        if ((in.str[i] * sizeof(T)) % 16 != 0 || (out.str[i] * sizeof(T)) % 16 != 0) return false;
+    return true;
+}
+
+template <typename T>
+int launch(ann_stream stream, const Dims* ins, const Dims* outs, int njobs, const Dims& c, const Dims& s, int layout,
+           uint32_t off) {
+    constexpr int PVV = Vec16<T>::n / 2;  // pairs per 16-byte vector
+    bool vec = true;
+    for (int k = 0; k < njobs; ++k) vec = vec && vec_ok<T>(ins[k], outs[k]);
+    int const pv = vec ? PVV : 1;
+    RopeArgs a{};
+    a.njobs = 0;
+    for (int k = 0; k < njobs; ++k) {
+        if (ins[k].numel() == 0) continue;
+        make_job<T>(a.job[a.njobs++], ins[k], outs[k], pv);
+    }
+    if (a.njobs == 0) return ANN_OK;
+    a.cos = c.data;
+    a.sin = s.data;
+    a.cs0 = c.str[0];
+    a.cs1 = c.str[1];
+    a.ss0 = s.str[0];
+    a.ss1 = s.str[1];
+    a.layout = layout;
+    a.pos_off = off;
+    int64_t const total = a.job[0].items + (a.njobs > 1 ? a.job[1].items : 0);
+    int const grid = grid_for(total, 256);
+    if (vec)
+        rope_kernel<T, PVV, true><<<grid, 256, 0, as_stream(stream)>>>(a);
+    else
+        rope_kernel<T, 1, false><<<grid, 256, 0, as_stream(stream)>>>(a);
+    return check_launch("rope");
+}
+
+template <typename T>
+int rope(ann_stream stream, const ann_view* in_v, const ann_view* c_v, const ann_view* s_v, const ann_view* out_v,
+         int layout, uint32_t off) {
+    Dims in, out, c, s;
+    ANN_TRY(to_dims(in_v, sizeof(T), "rope input", in));
+    ANN_TRY(to_dims(out_v, sizeof(T), "rope output", out));
+    ANN_TRY(to_dims(c_v, sizeof(T), "rope cosine table", c));
+    ANN_TRY(to_dims(s_v, sizeof(T), "rope sine table", s));
+    ANN_TRY(validate<T>(in, out, c, s, layout, off));
+    return launch<T>(stream, &in, &out, 1, c, s, layout, off);
+}
+
+template <typename T>
+int rope_inplace(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const ann_view* c_v,
+                 const ann_view* s_v, int layout, uint32_t off) {
+    Dims t[2], c, s;
+    ANN_TRY(to_dims(q_v, sizeof(T), "ropeInPlace q", t[0]));
+    int n = 1;
+    if (k_v != nullptr) {
+        ANN_TRY(to_dims(k_v, sizeof(T), "ropeInPlace k", t[1]));
+        n = 2;
+    }
+    ANN_TRY(to_dims(c_v, sizeof(T), "rope cosine table", c));
+    ANN_TRY(to_dims(s_v, sizeof(T), "rope sine table", s));
+    for (int k = 0; k < n; ++k) ANN_TRY(validate<T>(t[k], t[k], c, s, layout, off));
+    return launch<T>(stream, t, t, n, c, s, layout, off);
+}
+
+}  // namespace
+}  // namespace ann
+
+extern "C" {
+
+int ann_rope_f32(ann_stream st, const ann_view* in, const ann_view* c, const ann_view* s, const ann_view* out,
+                 int32_t layout, uint32_t off) {
+    ANN_API_BEGIN
+    return ann::rope<float>(st, in, c, s, out, layout, off);
+    ANN_API_END
+}
+int ann_rope_f64(ann_stream st, const ann_view* in, const ann_view* c, const ann_view* s, const ann_view* out,
+                 int32_t layout, uint32_t off) {
+    ANN_API_BEGIN
+    return ann::rope<double>(st, in, c, s, out, layout, off);
+    ANN_API_END
+}
+int ann_rope_inplace_f32(ann_stream st, const ann_view* q, const ann_view* k, const ann_view* c, const ann_view* s,
+                         int32_t layout, uint32_t off) {
+    ANN_API_BEGIN
+    return ann::rope_inplace<float>(st, q, k, c, s, layout, off);
+    ANN_API_END
+}
+int ann_rope_inplace_f64(ann_stream st, const ann_view* q, const ann_view* k, const ann_view* c, const ann_view* s,
+                         int32_t layout, uint32_t off) {
+    ANN_API_BEGIN
+    return ann::rope_inplace<double>(st, q, k, c, s, layout, off);
+    ANN_API_END
+}
+
+}  // extern "C"

@@ -1,0 +1,220 @@
+// softmax.cu -- softmax / causalSoftmax (reference: onHost/nn/softmax.hpp:14-80,
+// onAcc/internal/nn/softmax.hpp:15-75) and ops::scale
+// (onHost/ops/elementwise.hpp:64-73, 330-334).
+//
+// Softmax rows run along an arbitrary axis of a tensor of any rank. A row is
+// owned by one warp (rows up to 1024 elements) or by a whole 256-thread CTA
+// (longer rows): max over the unmasked entries from lowest(), sum of
+// exp(x - max), then out = exp(x - max) / sum with masked entries written as 0
+// -- the reference's three passes, with the passes' reductions done by warp
+// shuffles instead of one thread per row. Re-reads of a row come from L1/L2.
+#include "common.cuh"
+#include "reduce.cuh"
+
+namespace ann {
+namespace {
+
+struct SoftmaxArgs {
+    const void* in;
+    void* out;
+    int64_t rows, len, s_in, s_out;  // row count, axis extent, axis strides
+    Outer2 outer;                    // all axes, the softmax axis with extent 1
+    int causal;
+    int q_is_axis, k_is_axis;        // query / key axis coincides with the softmax axis
+    int64_t q_div, q_mod, k_div, k_mod;  // component of the row index on the query / key axis
+};
+
+template <typename T, int GROUP>
+__global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
+    constexpr int RPB = 256 / GROUP;
+    __shared__ T scratch[8];
+    int const gl = threadIdx.x % GROUP;
+    T const* in = static_cast<T const*>(a.in);
+    T* out = static_cast<T*>(a.out);
+    int64_t const iters = ceil_div(a.rows, static_cast<int64_t>(gridDim.x) * RPB);
+    for (int64_t it = 0; it < iters; ++it) {
+        int64_t const row = (it * gridDim.x + blockIdx.x) * RPB + threadIdx.x / GROUP;
+        bool const live = row < a.rows;
+        int64_t oi = 0, oo = 0, qf = 0, kf = 0;
+        if (live) {
+            a.outer.offsets(row, oi, oo);
+            qf = (row / a.q_div) % a.q_mod;
+            kf = (row / a.k_div) % a.k_mod;
+        }
+        // masked(i) <=> probe[queryAxis] < probe[keyAxis] with probe[axis] = i
+        auto masked = [&](int64_t i) {
+            if (!a.causal) return false;
+            int64_t const qv = a.q_is_axis ? i : qf;
+            int64_t const kv = a.k_is_axis ? i : kf;
+            return qv < kv;
+        };
+        T m = Lowest<T>::value;
+        if (live)
+            for (int64_t i = gl; i < a.len; i += GROUP)
+                if (!masked(i)) m = fmax(m, in[oi + i * a.s_in]);
+        if constexpr (GROUP == 32) m = warp_max(m);
+        else m = block_max<8>(m, scratch);
+        T sum{};
+        if (live)
+            for (int64_t i = gl; i < a.len; i += GROUP)
+                if (!masked(i)) sum += exp_t(in[oi + i * a.s_in] - m);
+        if constexpr (GROUP == 32) sum = warp_sum(sum);
+        else sum = block_sum<8>(sum, scratch);
+        if (!live) continue;
+        for (int64_t i = gl; i < a.len; i += GROUP) {
+            T const v = masked(i) ? T{} : exp_t(in[oi + i * a.s_in] - m) / sum;
+            out[oo + i * a.s_out] = v;
+        }
+    }
+}
+
+template <typename T>
+int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint32_t axis, bool causal,
+            uint32_t qaxis, uint32_t kaxis) {
+    Dims in, out;
+    ANN_TRY(to_dims(in_v, sizeof(T), "softmax input", in));
+    ANN_TRY(to_dims(out_v, sizeof(T), "softmax output", out));
+    if (!same_extents(in, out)) return fail(ANN_EINVAL, "softmax shape mismatch.");  // softmax.hpp:29-30
+    if (axis >= static_cast<uint32_t>(in.rank)) return fail(ANN_EINVAL, "softmax axis out of range.");
+    if (causal && (qaxis >= static_cast<uint32_t>(in.rank) || kaxis >= static_cast<uint32_t>(in.rank)))
+        return fail(ANN_EINVAL, "causalSoftmax query/key axis out of range.");
+    if (in.numel() == 0) return ANN_OK;
+
+    SoftmaxArgs a{};
+    a.in = in.data;
+    a.out = out.data;
+    a.len = in.ext[axis];
+    a.rows = in.numel() / a.len;
+    a.s_in = in.str[axis];
+    a.s_out = out.str[axis];
+    a.outer.n = in.rank;
+    for (int i = 0; i < in.rank; ++i) {
+        a.outer.ext[i] = (i == static_cast<int>(axis)) ? 1 : in.ext[i];
+        a.outer.sa[i] = in.str[i];
+        a.outer.sb[i] = out.str[i];
+    }
+    a.causal = causal ? 1 : 0;
+    a.q_is_axis = qaxis == axis;
+    a.k_is_axis = kaxis == axis;
+    auto component = [&](uint32_t ax, int64_t& div, int64_t& mod) {
+        div = 1;
+        for (int i = in.rank - 1; i > static_cast<int>(ax); --i) div *= a.outer.ext[i];
+        mod = a.outer.ext[ax];
+    };
+    component(causal ? qaxis : 0, a.q_div, a.q_mod);
+    component(causal ? kaxis : 0, a.k_div, a.k_mod);
+    cudaStream_t s = as_stream(stream);
+    if (a.len <= 1024) {
+        softmax_kernel<T, 32><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+    } else {
+        softmax_kernel<T, 256><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
+    }
+    return check_launch(causal ? "causalSoftmax" : "softmax");
+}
+
+// ---- ops::scale ----------------------------------------------------------
+struct ScaleArgs {
+    const void* in;
+    void* out;
+    int64_t n;
+    Outer2 idx;  // all axes (generic path)
+};
+
+template <typename T, bool DENSE>
+__global__ void __launch_bounds__(256) scale_kernel(ScaleArgs a, T scalar) {
+    T const* in = static_cast<T const*>(a.in);
+    T* out = static_cast<T*>(a.out);
+    int64_t const step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t const i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if constexpr (DENSE) {
+        using V = typename Vec16<T>::type;
+        constexpr int NV = Vec16<T>::n;
+        int64_t const nv = a.n / NV;
+        V const* iv = reinterpret_cast<V const*>(in);
+        V* ov = reinterpret_cast<V*>(out);
+        for (int64_t i = i0; i < nv; i += step) {
+            V v = iv[i];
+            if constexpr (NV == 4) {
+                v.x = v.x * scalar; v.y = v.y * scalar; v.z = v.z * scalar; v.w = v.w * scalar;
+            } else {
+                v.x = v.x * scalar; v.y = v.y * scalar;
+            }
+            ov[i] = v;
+        }
+        for (int64_t i = nv * NV + i0; i < a.n; i += step) out[i] = in[i] * scalar;
+    } else {
+        for (int64_t i = i0; i < a.n; i += step) {
+            int64_t oi, oo;
+            a.idx.offsets(i, oi, oo);
+            out[oo] = in[oi] * scalar;
+        }
+    }
+}
+
+template <typename T>
+int scale(ann_stream stream, const ann_view* in_v, T scalar, const ann_view* out_v) {
+    Dims in, out;
+    ANN_TRY(to_dims(in_v, sizeof(T), "scale input", in));
+    ANN_TRY(to_dims(out_v, sizeof(T), "scale output", out));
+    if (!same_extents(in, out)) return fail(ANN_EINVAL, "scale shape mismatch.");
+    if (in.numel() == 0) return ANN_OK;
+    ScaleArgs a{};
+    a.in = in.data;
+    a.out = out.data;
+    a.n = in.numel();
+    a.idx.n = in.rank;
+    bool same = true;
+    for (int i = 0; i < in.rank; ++i) {
+        a.idx.ext[i] = in.ext[i];
+        a.idx.sa[i] = in.str[i];
+        a.idx.sb[i] = out.str[i];
+        same = same && (in.ext[i] == 1 || in.str[i] == out.str[i]);
+    }
+    bool const dense = same && in.dense() && aligned(in.data, 16) && aligned(out.data, 16);
+    int const grid = grid_for(a.n, 256 * 4);
+    if (dense)
+        scale_kernel<T, true><<<grid, 256, 0, as_stream(stream)>>>(a, scalar);
+    else
+        scale_kernel<T, false><<<grid, 256, 0, as_stream(stream)>>>(a, scalar);
+    return check_launch("scale");
+}
+
+}  // namespace
+}  // namespace ann
+
+extern "C" {
+
+int ann_softmax_f32(ann_stream s, const ann_view* in, const ann_view* out, uint32_t axis) {
+    ANN_API_BEGIN
+    return ann::softmax<float>(s, in, out, axis, false, 0, 0);
+    ANN_API_END
+}
+int ann_softmax_f64(ann_stream s, const ann_view* in, const ann_view* out, uint32_t axis) {
+    ANN_API_BEGIN
+    return ann::softmax<double>(s, in, out, axis, false, 0, 0);
+    ANN_API_END
+}
+int ann_causal_softmax_f32(ann_stream s, const ann_view* in, const ann_view* out, uint32_t axis, uint32_t qa,
+                           uint32_t ka) {
+    ANN_API_BEGIN
+    return ann::softmax<float>(s, in, out, axis, true, qa, ka);
+    ANN_API_END
+}
+int ann_causal_softmax_f64(ann_stream s, const ann_view* in, const ann_view* out, uint32_t axis, uint32_t qa,
+                           uint32_t ka) {
+    ANN_API_BEGIN
+    return ann::softmax<double>(s, in, out, axis, true, qa, ka);
+    ANN_API_END
+}
+int ann_scale_f32(ann_stream s, const ann_view* in, float scalar, const ann_view* out) {
+    ANN_API_BEGIN
+    return ann::scale<float>(s, in, scalar, out);
+    ANN_API_END
+}
+int ann_scale_f64(ann_stream s, const ann_view* in, double scalar, const ann_view* out) {
+    ANN_API_BEGIN
+    return ann::scale<double>(s, in, scalar, out);
+    ANN_API_END
+}
+
+}  // extern "C"

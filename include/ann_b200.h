@@ -1,0 +1,190 @@
+/*
+ * ann_b200.h -- C ABI of the B200-native alpakaNN attention path.
+ *
+ * Every entry point replaces one call of the reference's header-only host API
+ * (namespace alpaka::nn::onHost::nn, files include/alpaka/nn/onHost/...) and
+ * keeps its argument meaning: same tensors, same extents, same scalar
+ * parameters, same default semantics. Views are passed as plain descriptors
+ * (pointer, extents, byte pitches), the in-order alpaka queue becomes a CUDA
+ * stream handle, and the alpaka executor argument disappears (it only chose
+ * alpaka's thread mapping).
+ *
+ * Conventions
+ *  - All data pointers are device pointers (or pointers the device can read,
+ *    such as managed memory) unless a function says otherwise.
+ *  - ann_view.pitches are BYTE strides per axis, the convention of alpaka's
+ *    getPitches(); the innermost pitch of a dense view is sizeof(element).
+ *  - Work is enqueued asynchronously on `stream` (NULL = legacy default
+ *    stream). Inputs and outputs must stay alive until the stream reaches the
+ *    enqueued work, as in the reference (onHost/nn/rope.hpp:88-95).
+ *  - Return value: ANN_OK, or an error code. ANN_EINVAL is raised on the host
+ *    before anything is enqueued, for exactly the shape conditions on which
+ *    the reference throws std::invalid_argument, plus the conditions under
+ *    which the reference would read out of bounds (documented per function).
+ *    ann_last_error() returns the message of the calling thread's last error.
+ *  - The library never falls back to a CPU implementation. Without a usable
+ *    CUDA device every compute entry point returns ANN_ECUDA.
+ */
+#ifndef ANN_B200_H
+#define ANN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ANN_B200_VERSION 100 /* 0.1.0 */
+
+#define ANN_OK 0
+#define ANN_EINVAL 1  /* shape / argument error (std::invalid_argument in the reference) */
+#define ANN_ECUDA 2   /* CUDA runtime error (launch, memcpy, no device)            */
+#define ANN_ENOTSUP 3 /* valid request this build does not implement               */
+#define ANN_EDEVICE 4 /* a kernel reported an error through the device error word  */
+
+#define ANN_MAX_RANK 8
+
+/* alpaka::nn::AttentionKvLayout (nn/attention.hpp:10-14) and
+ * alpaka::nn::RopeLayout (nn/rope.hpp:10-14) share these values. */
+#define ANN_LAYOUT_BTHD 0
+#define ANN_LAYOUT_BHTD 1
+
+/* Device error word bits (ann_take_device_error). */
+#define ANN_DEVERR_TOKEN_ID 0x1u     /* embeddingLookup saw an id >= vocabulary rows      */
+#define ANN_DEVERR_WAIT_TIMEOUT 0x2u /* a kernel gave up waiting for its own copies (1 s) */
+
+typedef void* ann_stream; /* cudaStream_t */
+
+/* Strided view of a tensor: the B200 counterpart of an alpaka IMdSpan
+ * (extents from getExtents(), byte pitches from getPitches(), data()). */
+typedef struct ann_view {
+    void* data;
+    int32_t rank;
+    int32_t reserved;
+    int64_t extents[ANN_MAX_RANK];
+    int64_t pitches[ANN_MAX_RANK];
+} ann_view;
+
+/* ---- library ---------------------------------------------------------- */
+
+int ann_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+const char* ann_last_error(void);
+/* Reads and clears the device error word of the current device; synchronises
+ * `stream` first. *bits receives the ANN_DEVERR_* bits that were set. */
+int ann_take_device_error(ann_stream stream, uint32_t* bits);
+
+/* ---- embeddingLookup: onHost/nn/embedding.hpp:17-36 --------------------
+ * out[t, h] = embedding[ids[t], h]. ids: rank-1 uint32; embedding, output:
+ * rank 2. Throws (ANN_EINVAL) unless output = [len(ids), embedding.H]
+ * (embedding.hpp:23-27). The reference does not range-check ids; here an id
+ * >= embedding rows writes zeros to its output row and sets
+ * ANN_DEVERR_TOKEN_ID instead of reading out of bounds. Bit-exact copy. */
+int ann_embedding_lookup_f32(ann_stream stream, const ann_view* token_ids, const ann_view* embedding,
+                             const ann_view* output);
+int ann_embedding_lookup_f64(ann_stream stream, const ann_view* token_ids, const ann_view* embedding,
+                             const ann_view* output);
+
+/* ---- rmsNorm: onHost/nn/rms_norm.hpp:17-35 ----------------------------
+ * y = x * rsqrt(sum(x^2)/H + eps) * w[h] along the last axis of any rank.
+ * Throws on in/out extent mismatch or weight not rank-1 [H]. */
+int ann_rms_norm_f32(ann_stream stream, const ann_view* input, const ann_view* weight, const ann_view* output,
+                     float epsilon);
+int ann_rms_norm_f64(ann_stream stream, const ann_view* input, const ann_view* weight, const ann_view* output,
+                     double epsilon);
+
+/* ---- rope (out of place): onHost/nn/rope.hpp:49-62 ---------------------
+ * Interleaved-pair rotation with caller tables cos/sin[position][D/2],
+ * position = position_offset + token index (axis 1 for BTHD, axis 2 for
+ * BHTD). Validation follows validateRopeShape (rope.hpp:21-46) with the
+ * coverage check taken on the layout's real token axis. */
+int ann_rope_f32(ann_stream stream, const ann_view* in, const ann_view* cos_table, const ann_view* sin_table,
+                 const ann_view* out, int32_t layout, uint32_t position_offset);
+int ann_rope_f64(ann_stream stream, const ann_view* in, const ann_view* cos_table, const ann_view* sin_table,
+                 const ann_view* out, int32_t layout, uint32_t position_offset);
+
+/* ---- ropeInPlace: onHost/nn/rope.hpp:96-135 ---------------------------
+ * Rotates q and (if k != NULL) k in place, in ONE launch and without the
+ * reference's temporary buffer + copy. k may have a different head count. */
+int ann_rope_inplace_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* cos_table,
+                         const ann_view* sin_table, int32_t layout, uint32_t position_offset);
+int ann_rope_inplace_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* cos_table,
+                         const ann_view* sin_table, int32_t layout, uint32_t position_offset);
+
+/* ---- attentionScores: onHost/nn/attention.hpp:54-81 --------------------
+ * scores[b,hq,i,j] = sum_d Q[b,i,hq,d] * K(b,j,hq/g,d), unscaled. Q BTHD;
+ * K BTHD [B,Tk,Hkv,D] or BHTD [B,Hkv,Tk,D]. Throws if g == 0 (as the
+ * reference) and, unlike the reference, if Q/K extents do not cover the
+ * scores grid (the reference reads out of bounds there). */
+int ann_attention_scores_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* scores,
+                             uint32_t queries_per_kv_group, int32_t kv_layout);
+int ann_attention_scores_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* scores,
+                             uint32_t queries_per_kv_group, int32_t kv_layout);
+
+/* ---- ops::scale: onHost/ops/elementwise.hpp:330-334 --------------------
+ * out = in * scalar (in == out allowed). Throws on extent mismatch. */
+int ann_scale_f32(ann_stream stream, const ann_view* in, float scalar, const ann_view* out);
+int ann_scale_f64(ann_stream stream, const ann_view* in, double scalar, const ann_view* out);
+
+/* ---- softmax: onHost/nn/softmax.hpp:26-40 ------------------------------
+ * Row softmax along `axis` (max-subtracted, exp, divide by the sum). */
+int ann_softmax_f32(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis);
+int ann_softmax_f64(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis);
+
+/* ---- causalSoftmax: onHost/nn/softmax.hpp:59-80 ------------------------
+ * As softmax, with element i of a row masked (output 0, excluded from max
+ * and sum) iff idx[query_axis] < idx[key_axis] for idx with idx[axis] = i
+ * (top-left aligned, onAcc/internal/nn/softmax.hpp:23-30). */
+int ann_causal_softmax_f32(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis,
+                           uint32_t query_axis, uint32_t key_axis);
+int ann_causal_softmax_f64(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis,
+                           uint32_t query_axis, uint32_t key_axis);
+
+/* ---- attentionApply: onHost/nn/attention.hpp:83-110 -------------------
+ * out[b,i,hq,d] = sum_j probs[b,hq,i,j] * V(b,j,hq/g,d) over all Tk keys. */
+int ann_attention_apply_f32(ann_stream stream, const ann_view* probs, const ann_view* values, const ann_view* out,
+                            uint32_t queries_per_kv_group, int32_t kv_layout);
+int ann_attention_apply_f64(ann_stream stream, const ann_view* probs, const ann_view* values, const ann_view* out,
+                            uint32_t queries_per_kv_group, int32_t kv_layout);
+
+/* ---- gemm: onHost/matrix/gemm.hpp:28-33 (qkvProjection's building block)
+ * C = A * B, row-major rank-2 views with unit column stride. Runs on cuBLAS,
+ * loaded at first use; ANN_ENOTSUP if cuBLAS cannot be loaded. */
+int ann_gemm_f32(ann_stream stream, const ann_view* a, const ann_view* b, const ann_view* c);
+int ann_gemm_f64(ann_stream stream, const ann_view* a, const ann_view* b, const ann_view* c);
+
+/* ---- qkvProjection: onHost/nn/attention.hpp:38-52 ---------------------- */
+int ann_qkv_projection_f32(ann_stream stream, const ann_view* input, const ann_view* wq, const ann_view* wk,
+                           const ann_view* wv, const ann_view* q, const ann_view* k, const ann_view* v);
+int ann_qkv_projection_f64(ann_stream stream, const ann_view* input, const ann_view* wq, const ann_view* wk,
+                           const ann_view* wv, const ann_view* q, const ann_view* k, const ann_view* v);
+
+/* ---- fused decode attention (split-K over the KV cache) -----------------
+ * One launch computing the reference's decode pipeline
+ *   attentionScores(q, k) -> ops::scale(scale) -> softmax(axis 3)
+ *   -> attentionApply(probs, v)
+ * (test/unit/nn/attention.cpp:675-734) without materialising scores/probs.
+ * q, out: BTHD [B,Tq,Hq,D]; k, v: `kv_layout` with Tk keys and Hkv = Hq/g
+ * heads; softmax over all Tk keys (non-causal, as decode uses it).
+ * Requires unit innermost stride, 16-byte aligned K/V rows, D*sizeof(T) a
+ * multiple of 16 and D <= 256.
+ * The kernel keeps per-split partial results in a caller-provided device
+ * workspace of ann_attention_decode_workspace_size() bytes, 256-byte aligned.
+ * Its last 4*B*Tq*Hq bytes are completion counters that must be zero before
+ * the first call; every call leaves them zero again. Calls that share a
+ * workspace must be ordered on one stream. */
+size_t ann_attention_decode_workspace_size(int64_t batch, int64_t query_tokens, int64_t query_heads,
+                                           int64_t head_dim, int64_t kv_tokens, int32_t elem_bytes);
+int ann_attention_decode_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                             const ann_view* out, float scale, uint32_t queries_per_kv_group, int32_t kv_layout,
+                             void* workspace, size_t workspace_bytes);
+int ann_attention_decode_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                             const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout,
+                             void* workspace, size_t workspace_bytes);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* ANN_B200_H */
