@@ -28,7 +28,7 @@ lib = ctypes.CDLL(LIB_PATH)
 
 _P = ctypes.POINTER(AnnView)
 _S = ctypes.c_void_p
-_u32, _i32, _i64 = ctypes.c_uint32, ctypes.c_int32, ctypes.c_int64
+_u32, _i32 = ctypes.c_uint32, ctypes.c_int32
 _f = {"f32": ctypes.c_float, "f64": ctypes.c_double}
 
 # Every exported entry point and its argument types. The symbol test checks
@@ -37,7 +37,6 @@ SIGNATURES = {
     "ann_version": ([], ctypes.c_int),
     "ann_last_error": ([], ctypes.c_char_p),
     "ann_take_device_error": ([_S, ctypes.POINTER(_u32)], ctypes.c_int),
-    "ann_attention_decode_workspace_size": ([_i64, _i64, _i64, _i64, _i64, _i32], ctypes.c_size_t),
 }
 for _sfx, _ft in _f.items():
     SIGNATURES.update({
@@ -52,8 +51,7 @@ for _sfx, _ft in _f.items():
         f"ann_attention_apply_{_sfx}": ([_S, _P, _P, _P, _u32, _i32], ctypes.c_int),
         f"ann_gemm_{_sfx}": ([_S, _P, _P, _P], ctypes.c_int),
         f"ann_qkv_projection_{_sfx}": ([_S, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
-        f"ann_attention_decode_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32, ctypes.c_void_p, ctypes.c_size_t],
-                                         ctypes.c_int),
+        f"ann_attention_decode_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32], ctypes.c_int),
     })
 
 for _name, (_args, _res) in SIGNATURES.items():

@@ -1,4 +1,4 @@
-// decode.cu -- fused decode attention over a KV cache, split-K.
+// decode.cu -- fused decode attention over a KV cache (split-K, cluster merge).
 //
 // Computes in ONE launch what the reference's decode pipeline computes in four
 // (test/unit/nn/attention.cpp:675-734):
@@ -8,29 +8,37 @@
 //   -> attentionApply (onAcc/internal/nn/attention.hpp:49-67)
 // without writing the [B,Hq,Tq,Tk] score and probability tensors to memory.
 //
-// The work is memory-bound (each K/V byte is used for one FMA), so the design
-// is about streaming the cache at HBM rate:
-//  * grid = query rows x key splits; each CTA owns a contiguous key range of
-//    one (batch, query token, query head) row and its KV head (GQA: hq / g);
-//  * K and V rows of the range are streamed through a 4-stage ring of 16 KB
-//    shared-memory tiles by 1-D bulk copies (TMA, cp.async.bulk) completing on
-//    mbarriers: K tiles first (scores), then V tiles (weighted sum), so the V
-//    loads are already in flight while the split's softmax is computed;
-//  * scores: 8 lanes per key, each lane a 16-byte slice, reduced with three
-//    shuffles (conflict-free 128-byte shared-memory phases);
-//  * the split's scores stay in shared memory: max, exp and sum are exact
-//    over the split, no online rescaling;
-//  * splits are merged by the last CTA of a row to finish (completion counter
-//    in the workspace) with the log-sum-exp rule
-//      out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s.
+// The work is memory-bound (each K/V byte feeds one FMA), so the design is
+// about streaming the cache at HBM rate with no extra traffic:
+//  * one thread-block CLUSTER of S CTAs per query row (batch, query token,
+//    query head); CTA s of the cluster owns a contiguous key range of the
+//    row's KV head (GQA: hq / g);
+//  * K and V rows are streamed through a 4-stage ring of 16 KB shared-memory
+//    tiles by 1-D bulk copies (TMA, cp.async.bulk, never multicast)
+//    completing on mbarriers;
+//  * keys are taken in sub-chunks of up to 2048: the sub-chunk's K tiles give
+//    its scores (8 lanes per key, 16-byte slices, 3-shuffle reduction, kept
+//    in shared memory), then its exact max / exp / sum, then its V tiles
+//    accumulate sum(p * v). Sub-chunks merge into a running (max, sum, acc)
+//    with the online-softmax rescale, so any cache length is handled;
+//  * the S partial results of a row meet in distributed shared memory: each
+//    CTA merges one slice of the head dimension from all S peers with the
+//    log-sum-exp rule  out = sum_s e^(m_s-M) acc_s / sum_s e^(m_s-M) l_s.
+//    No global scratch memory, no atomics, no second launch.
 // Summation order differs from the reference's sequential loops (tree
 // reductions, split merge); results agree within the fp32/fp64 tolerances.
+#include <cooperative_groups.h>
+
+#include <array>
 #include <cstdlib>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
 #include "reduce.cuh"
 #include "tma.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace ann {
 namespace {
@@ -41,24 +49,21 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kStages = 4;
 constexpr int kStageBytes = 16384;
-constexpr int kMaxSplits = 64;
-constexpr int kMaxChunk = 2048;  // keys per split (scores kept in shared memory)
+constexpr int kSub = 2048;       // keys per sub-chunk (scores kept in shared memory)
+constexpr int kMaxCluster = 16;  // splits per row (non-portable cluster size)
 
 struct DecodeArgs {
     const void* q;
     const void* k;
     const void* v;
     void* out;
-    int64_t q_b, q_t, q_h;        // element strides of Q (unit stride along d)
-    int64_t o_b, o_t, o_h, o_d;   // element strides of out
-    int64_t k_b, k_h, k_t;        // element strides of K by batch, kv head, token
+    int64_t q_b, q_t, q_h;       // element strides of Q (unit stride along d)
+    int64_t o_b, o_t, o_h, o_d;  // element strides of out
+    int64_t k_b, k_h, k_t;       // element strides of K by batch, kv head, token
     int64_t v_b, v_h, v_t;
     int64_t Tq, Hq, Tk, chunk, rows;
     uint32_t g;
     int splits;
-    void* part_acc;       // [rows][splits][D]
-    void* part_ml;        // [rows][splits][2]
-    unsigned int* count;  // [rows]
 };
 
 template <typename T, int D>
@@ -68,13 +73,18 @@ struct Cfg {
     static constexpr int ROWB = D * static_cast<int>(sizeof(T));  // bytes per key row
     static constexpr int VPR = ROWB / 16;                         // 16-byte vectors per row
     static constexpr int TILE = kStageBytes / ROWB;               // keys per stage
+    static constexpr int TPS = kSub / TILE;                       // tiles per full sub-chunk
     static constexpr int LPK = 8;                                 // score phase: lanes per key
     static constexpr int KPW = 32 / LPK;                          // keys per warp step
     static constexpr int VPL = VPR / LPK;                         // vectors per lane per key
     static constexpr int KPS = VPR >= 32 ? 1 : 32 / VPR;          // PV phase: keys per warp step
     static constexpr int VPLN = VPR >= 32 ? VPR / 32 : 1;         // PV phase: vectors per lane
-    static constexpr size_t SMEM = kStages * kStageBytes + kMaxChunk * sizeof(T) + kStages * sizeof(uint64_t);
+    static constexpr size_t OFF_SC = kStages * kStageBytes;
+    static constexpr size_t OFF_BAR = OFF_SC + kSub * sizeof(T);
+    static constexpr size_t OFF_XCH = OFF_BAR + kStages * sizeof(uint64_t);
+    static constexpr size_t SMEM = OFF_XCH + (D + 2) * sizeof(T);
     static_assert(ROWB % 128 == 0, "row must be a multiple of 128 bytes");
+    static_assert(kSub % TILE == 0, "sub-chunk must be whole tiles");
     static_assert(kWarps * D * sizeof(T) <= kStages * kStageBytes, "reduction buffer aliases the stages");
 };
 
@@ -108,51 +118,93 @@ __device__ __forceinline__ void axpy16<double>(double2& acc, double p, double2 v
     acc.y = fma(p, v.y, acc.y);
 }
 
+template <typename T>
+__device__ __forceinline__ void scale16(typename Vec16<T>::type& acc, T f);
+template <>
+__device__ __forceinline__ void scale16<float>(float4& acc, float f) {
+    acc.x *= f;
+    acc.y *= f;
+    acc.z *= f;
+    acc.w *= f;
+}
+template <>
+__device__ __forceinline__ void scale16<double>(double2& acc, double f) {
+    acc.x *= f;
+    acc.y *= f;
+}
+
+template <typename T>
+__device__ __forceinline__ void shfl_add16(typename Vec16<T>::type& acc, int o) {
+    if constexpr (Vec16<T>::n == 4) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+    } else {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale) {
     using C = Cfg<T, D>;
     using V = typename C::V;
     extern __shared__ __align__(128) unsigned char smem[];
-    T* sc = reinterpret_cast<T*>(smem + kStages * kStageBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kMaxChunk * sizeof(T));
+    T* sc = reinterpret_cast<T*>(smem + C::OFF_SC);
+    T* xch = reinterpret_cast<T*>(smem + C::OFF_XCH);  // this CTA's [acc(D), m, l] for the cluster merge
     __shared__ T red_s[kWarps];
-    __shared__ int s_last;
 
     int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int64_t const bid = blockIdx.x;
-    int const split = static_cast<int>(bid % a.splits);
-    int64_t const row = bid / a.splits;
+    int const split = static_cast<int>(blockIdx.x % a.splits);  // == rank in the cluster
+    int64_t const row = blockIdx.x / a.splits;
     int64_t const hq = row % a.Hq;
     int64_t const tq = (row / a.Hq) % a.Tq;
     int64_t const b = row / (a.Hq * a.Tq);
     int64_t const kvh = hq / a.g;
     int64_t const key0 = static_cast<int64_t>(split) * a.chunk;
     int64_t const left = a.Tk - key0;
-    int const nkeys = static_cast<int>(left <= 0 ? 0 : (left < a.chunk ? left : a.chunk));
-    int const ntile = (nkeys + C::TILE - 1) / C::TILE;
-    int const total = 2 * ntile;
+    int const n = static_cast<int>(left <= 0 ? 0 : (left < a.chunk ? left : a.chunk));
+    int const total = 2 * ((n + C::TILE - 1) / C::TILE);
 
     T const* kbase = static_cast<T const*>(a.k) + b * a.k_b + kvh * a.k_h + key0 * a.k_t;
     T const* vbase = static_cast<T const*>(a.v) + b * a.v_b + kvh * a.v_h + key0 * a.v_t;
     uint32_t const stage0 = smem_u32(smem);
-    uint32_t const bar0 = smem_u32(bars);
+    uint32_t const bar0 = smem_u32(smem + C::OFF_BAR);
 
-    // Warp 0 issues the bulk copies of tile t (K tiles 0..ntile-1, then V tiles).
+    // Tile t of the stream K(sub 0), V(sub 0), K(sub 1), V(sub 1), ...
+    struct TileInfo {
+        int sub, nc, lt, rows;
+        bool is_v;
+    };
+    auto tile_info = [&](int t) {
+        TileInfo ti;
+        ti.sub = t / (2 * C::TPS);
+        int const within = t - ti.sub * 2 * C::TPS;
+        ti.nc = min(kSub, n - ti.sub * kSub);
+        int const ntc = (ti.nc + C::TILE - 1) / C::TILE;
+        ti.is_v = within >= ntc;
+        ti.lt = ti.is_v ? within - ntc : within;
+        ti.rows = min(C::TILE, ti.nc - ti.lt * C::TILE);
+        return ti;
+    };
+
+    // Warp 0 issues the bulk copies of tile t into stage t % kStages.
     auto issue = [&](int t) {
-        bool const is_v = t >= ntile;
-        int const lt = is_v ? t - ntile : t;
-        int const rows = min(C::TILE, nkeys - lt * C::TILE);
-        int64_t const stride = is_v ? a.v_t : a.k_t;
-        T const* src = (is_v ? vbase : kbase) + static_cast<int64_t>(lt) * C::TILE * stride;
+        TileInfo const ti = tile_info(t);
+        int64_t const stride = ti.is_v ? a.v_t : a.k_t;
+        int64_t const key = static_cast<int64_t>(ti.sub) * kSub + static_cast<int64_t>(ti.lt) * C::TILE;
+        T const* src = (ti.is_v ? vbase : kbase) + key * stride;
         int const s = t % kStages;
         uint32_t const bar = bar0 + s * 8;
         uint32_t const dst = stage0 + s * kStageBytes;
-        if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rows * C::ROWB));
+        if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(ti.rows * C::ROWB));
         __syncwarp();
         if (stride == D) {
-            if (lane == 0) bulk_copy_g2s(dst, src, static_cast<uint32_t>(rows * C::ROWB), bar);
+            if (lane == 0) bulk_copy_g2s(dst, src, static_cast<uint32_t>(ti.rows * C::ROWB), bar);
         } else {
-            for (int r = lane; r < rows; r += 32) bulk_copy_g2s(dst + r * C::ROWB, src + r * stride, C::ROWB, bar);
+            for (int r = lane; r < ti.rows; r += 32)
+                bulk_copy_g2s(dst + r * C::ROWB, src + r * stride, C::ROWB, bar);
         }
     };
 
@@ -173,8 +225,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
         for (int m = 0; m < C::VPL; ++m) qr[m] = *reinterpret_cast<V const*>(qrow + (sub + C::LPK * m) * C::NV);
     }
 
-    T mx = Lowest<T>::value;  // running max of this thread's scores
-    T mrow = Lowest<T>::value, lrow = T{};
+    T mx = Lowest<T>::value;  // max of this thread's scores in the current sub-chunk
+    T m_run = Lowest<T>::value, l_run = T{};
     V acc[C::VPLN];
 #pragma unroll
     for (int m = 0; m < C::VPLN; ++m) acc[m] = V{};
@@ -184,54 +236,57 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
     for (int t = 0; t < total; ++t) {
         int const s = t % kStages;
         bool const ok = mbar_wait_bounded(bar0 + s * 8, (t / kStages) & 1);
-        // All threads agree on abort; the barrier also retires reads of tile t-1.
+        // All threads agree on abort; the barrier also retires the reads of tile t-1.
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicOr(&g_decode_error, ANN_DEVERR_WAIT_TIMEOUT);
-                // Drain the copies still in flight (bounded) before leaving.
-                for (int u = t + 1; u < min(total, t - 1 + kStages); ++u)
+                for (int u = t + 1; u < min(total, t - 1 + kStages); ++u)  // drain copies in flight (bounded)
                     mbar_wait_bounded(bar0 + (u % kStages) * 8, (u / kStages) & 1);
             }
-            return;
+            break;  // still joins the cluster barriers below
         }
         if (t >= 1 && warp == 0 && t - 1 + kStages < total) issue(t - 1 + kStages);
 
+        TileInfo const ti = tile_info(t);
         V const* tile = reinterpret_cast<V const*>(smem + s * kStageBytes);
-        if (t < ntile) {
-            int const kb = t * C::TILE;
-            int const rows = min(C::TILE, nkeys - kb);
-            for (int base = warp * C::KPW; base < rows; base += kWarps * C::KPW) {
+        int const kb = ti.lt * C::TILE;
+        if (!ti.is_v) {
+            for (int base = warp * C::KPW; base < ti.rows; base += kWarps * C::KPW) {
                 int const kk = base + grp;
                 T part{};
-                if (kk < rows) {
+                if (kk < ti.rows) {
 #pragma unroll
                     for (int m = 0; m < C::VPL; ++m) part = dot16<T>(qr[m], tile[kk * C::VPR + sub + C::LPK * m], part);
                 }
 #pragma unroll
                 for (int o = C::LPK / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-                if (kk < rows && sub == 0) {
+                if (kk < ti.rows && sub == 0) {
                     T const sv = part * scale;  // attentionScores, then ops::scale
                     sc[kb + kk] = sv;
                     mx = fmax(mx, sv);
                 }
             }
         } else {
-            if (t == ntile) {
-                // softmax over this split's keys (all scores are in `sc`)
-                mrow = block_max<kWarps>(mx, red_s);
+            if (ti.lt == 0) {
+                // softmax statistics of this sub-chunk, merged into the running ones
+                T const m_c = block_max<kWarps>(mx, red_s);
+                T const m_new = fmax(m_run, m_c);
+                T const alpha = exp_t(m_run - m_new);
+#pragma unroll
+                for (int m = 0; m < C::VPLN; ++m) scale16<T>(acc[m], alpha);
                 T ls{};
-                for (int i = tid; i < nkeys; i += kThreads) {
-                    T const p = exp_t(sc[i] - mrow);
+                for (int i = tid; i < ti.nc; i += kThreads) {
+                    T const p = exp_t(sc[i] - m_new);
                     sc[i] = p;
                     ls += p;
                 }
-                lrow = block_sum<kWarps>(ls, red_s);
+                l_run = l_run * alpha + block_sum<kWarps>(ls, red_s);
+                m_run = m_new;
+                mx = Lowest<T>::value;
             }
-            int const kb = (t - ntile) * C::TILE;
-            int const rows = min(C::TILE, nkeys - kb);
-            for (int base = warp * C::KPS; base < rows; base += kWarps * C::KPS) {
+            for (int base = warp * C::KPS; base < ti.rows; base += kWarps * C::KPS) {
                 int const kk = base + pv_key;
-                if (kk < rows) {
+                if (kk < ti.rows) {
                     T const p = sc[kb + kk];
 #pragma unroll
                     for (int m = 0; m < C::VPLN; ++m) axpy16<T>(acc[m], p, tile[kk * C::VPR + pv_vec + 32 * m]);
@@ -240,24 +295,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
         }
     }
 
-    // Reduce the per-warp partial sums: lanes holding the same vector first,
-    // then the warps through shared memory (aliasing the drained stages).
+    // Per-CTA result: lanes holding the same vector first, then the warps
+    // through shared memory (aliasing the drained stages).
     if constexpr (C::KPS > 1) {
 #pragma unroll
-        for (int m = 0; m < C::VPLN; ++m) {
+        for (int m = 0; m < C::VPLN; ++m)
 #pragma unroll
-            for (int o = C::VPR; o < 32; o <<= 1) {
-                if constexpr (C::NV == 4) {
-                    acc[m].x += __shfl_xor_sync(0xffffffffu, acc[m].x, o);
-                    acc[m].y += __shfl_xor_sync(0xffffffffu, acc[m].y, o);
-                    acc[m].z += __shfl_xor_sync(0xffffffffu, acc[m].z, o);
-                    acc[m].w += __shfl_xor_sync(0xffffffffu, acc[m].w, o);
-                } else {
-                    acc[m].x += __shfl_xor_sync(0xffffffffu, acc[m].x, o);
-                    acc[m].y += __shfl_xor_sync(0xffffffffu, acc[m].y, o);
-                }
-            }
-        }
+            for (int o = C::VPR; o < 32; o <<= 1) shfl_add16<T>(acc[m], o);
     }
     __syncthreads();
     T* red = reinterpret_cast<T*>(smem);
@@ -267,136 +311,151 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
             *reinterpret_cast<V*>(red + warp * D + (pv_vec + 32 * m) * C::NV) = acc[m];
     }
     __syncthreads();
-
     T* out = static_cast<T*>(a.out) + b * a.o_b + tq * a.o_t + hq * a.o_h;
     if (a.splits == 1) {
         for (int d = tid; d < D; d += kThreads) {
             T s{};
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) s += red[w * D + d];
-            out[d * a.o_d] = lrow > T{} ? s / lrow : T{};
+            out[d * a.o_d] = l_run > T{} ? s / l_run : T{};
         }
         return;
     }
-
-    T* pacc = static_cast<T*>(a.part_acc) + (row * a.splits) * D;
-    T* pml = static_cast<T*>(a.part_ml) + (row * a.splits) * 2;
     for (int d = tid; d < D; d += kThreads) {
         T s{};
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) s += red[w * D + d];
-        pacc[split * D + d] = s;
+        xch[d] = s;
     }
     if (tid == 0) {
-        pml[2 * split] = mrow;
-        pml[2 * split + 1] = lrow;
+        xch[D] = m_run;
+        xch[D + 1] = l_run;
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.count + row, 1u) == static_cast<unsigned>(a.splits - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    T M = Lowest<T>::value;
-    for (int s2 = 0; s2 < a.splits; ++s2) M = fmax(M, __ldcg(pml + 2 * s2));
-    T L{};
-    for (int s2 = 0; s2 < a.splits; ++s2) L += exp_t(__ldcg(pml + 2 * s2) - M) * __ldcg(pml + 2 * s2 + 1);
-    for (int d = tid; d < D; d += kThreads) {
-        T o{};
-        for (int s2 = 0; s2 < a.splits; ++s2) o += exp_t(__ldcg(pml + 2 * s2) - M) * __ldcg(pacc + s2 * D + d);
-        out[d * a.o_d] = L > T{} ? o / L : T{};
+
+    // Merge the cluster's partial results through distributed shared memory:
+    // CTA `split` produces the output dims [lo, hi).
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    int const per = (D + a.splits - 1) / a.splits;
+    int const lo = split * per, hi = min(D, lo + per);
+    if (tid < hi - lo) {
+        T M = Lowest<T>::value;
+        for (int r = 0; r < a.splits; ++r) M = fmax(M, cluster.map_shared_rank(xch, r)[D]);
+        T L{}, o{};
+        for (int r = 0; r < a.splits; ++r) {
+            T const* px = cluster.map_shared_rank(xch, r);
+            T const w = exp_t(px[D] - M);
+            L += w * px[D + 1];
+            o += w * px[lo + tid];
+        }
+        out[(lo + tid) * a.o_d] = L > T{} ? o / L : T{};
     }
-    if (tid == 0) a.count[row] = 0u;  // leave the workspace ready for the next call
+    cluster.sync();  // peers' shared memory must outlive the reads above
 }
 
-size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
-
-struct WsLayout {
-    size_t acc, ml, count, total;
-};
-
-WsLayout ws_layout(int64_t rows, int64_t D, size_t eb) {
-    WsLayout w{};
-    w.acc = 0;
-    w.ml = align256(static_cast<size_t>(rows) * kMaxSplits * D * eb);
-    w.count = w.ml + align256(static_cast<size_t>(rows) * kMaxSplits * 2 * eb);
-    w.total = w.count + static_cast<size_t>(rows) * sizeof(unsigned int);
-    return w;
-}
-
-// Splits per row: enough CTAs to fill every resident slot, chosen to keep the
-// last wave full; keys per split a multiple of the tile, at most kMaxChunk.
-int choose_splits(int64_t rows, int64_t Tk, int tile, int slots, int64_t& chunk) {
+// Splits per row = cluster size: enough CTAs to fill the resident slots with
+// a full last wave, at least 4 tiles of keys per CTA.
+template <typename T, int D>
+int choose_splits(int64_t rows, int64_t Tk, int64_t& chunk, const int* slots_for) {
+    using C = Cfg<T, D>;
     if (Tk <= 0) {
         chunk = 1;
         return 1;
     }
-    int64_t const max_s = std::min<int64_t>(kMaxSplits, ceil_div(Tk, tile));
-    int64_t const min_s = ceil_div(Tk, kMaxChunk);
     if (const char* env = std::getenv("ANN_DECODE_SPLITS")) {
-        int64_t s = std::atoll(env);
-        if (s >= min_s && s <= max_s) {
-            chunk = ceil_div(ceil_div(Tk, s), tile) * tile;
+        int s = std::atoi(env);
+        if (s >= 1 && s <= kMaxCluster && slots_for[s] > 0 && Tk > 0) {
+            chunk = ceil_div(ceil_div(Tk, s), C::TILE) * C::TILE;
             return static_cast<int>(ceil_div(Tk, chunk));
         }
     }
+    int64_t const max_s = std::max<int64_t>(1, std::min<int64_t>(kMaxCluster, Tk / (4 * C::TILE)));
     double best = -1.0;
-    int best_s = static_cast<int>(min_s);
-    int64_t best_chunk = ceil_div(ceil_div(Tk, min_s), tile) * tile;
-    for (int64_t s = min_s; s <= max_s; ++s) {
-        int64_t const c = ceil_div(ceil_div(Tk, s), tile) * tile;
-        int64_t const real_s = ceil_div(Tk, c);
-        if (real_s != s) continue;
-        int64_t const ctas = rows * real_s;
-        int64_t const waves = ceil_div(ctas, slots);
-        double const eff = static_cast<double>(ctas) / static_cast<double>(waves * slots);
+    int best_s = 1;
+    chunk = std::max<int64_t>(1, Tk);
+    for (int s = 1; s <= max_s; ++s) {
+        if (slots_for[s] <= 0) continue;
+        int64_t const c = ceil_div(ceil_div(Tk, s), C::TILE) * C::TILE;
+        if (ceil_div(Tk, c) != s) continue;
+        int64_t const ctas = rows * s;
+        int64_t const waves = ceil_div(ctas, slots_for[s]);
+        double const eff = static_cast<double>(ctas) / static_cast<double>(waves * slots_for[s]);
         if (eff > best + 0.02) {
             best = eff;
-            best_s = static_cast<int>(real_s);
-            best_chunk = c;
+            best_s = s;
+            chunk = c;
         }
     }
-    chunk = best_chunk;
     return best_s;
 }
 
 template <typename T, int D>
-int launch(ann_stream stream, DecodeArgs& a, T scale, void* ws, size_t ws_bytes) {
+int launch(ann_stream stream, DecodeArgs& a, T scale) {
     using C = Cfg<T, D>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    static int occ = 0;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(C::SMEM));
-        if (attr_err == cudaSuccess)
-            attr_err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D>, kThreads, C::SMEM);
-    });
-    if (attr_err != cudaSuccess) return fail(ANN_ECUDA, "attention decode setup: %s", cudaGetErrorString(attr_err));
-    int const slots = std::max(1, occ) * sm_count();
-    int64_t chunk = 0;
-    a.splits = choose_splits(a.rows, a.Tk, C::TILE, slots, chunk);
-    a.chunk = chunk;
-    if (a.splits > kMaxSplits)
-        return fail(ANN_ENOTSUP, "attention decode: more than %d keys per row not supported.", kMaxSplits * kMaxChunk);
-    if (a.splits > 1) {
-        WsLayout const w = ws_layout(a.rows, D, sizeof(T));
-        if (ws == nullptr || ws_bytes < w.total || !aligned(ws, 256))
-            return fail(ANN_EINVAL, "attention decode: workspace of %zu bytes (256-byte aligned) required.", w.total);
-        char* base = static_cast<char*>(ws);
-        a.part_acc = base + w.acc;
-        a.part_ml = base + w.ml;
-        a.count = reinterpret_cast<unsigned int*>(base + w.count);
+    static std::mutex mu;
+    static std::map<int, std::array<int, kMaxCluster + 1>> slots_by_dev;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(ANN_ECUDA, "attention decode: no CUDA device.");
+    std::array<int, kMaxCluster + 1> slots{};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = slots_by_dev.find(dev);
+        if (it == slots_by_dev.end()) {
+            cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(C::SMEM));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(decode_kernel<T, D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return fail(ANN_ECUDA, "attention decode setup: %s", cudaGetErrorString(e));
+            for (int s = 1; s <= kMaxCluster; ++s) {
+                cudaLaunchConfig_t cfg{};
+                cudaLaunchAttribute attr{};
+                attr.id = cudaLaunchAttributeClusterDimension;
+                attr.val.clusterDim.x = s;
+                attr.val.clusterDim.y = 1;
+                attr.val.clusterDim.z = 1;
+                cfg.gridDim = dim3(s * 1024);
+                cfg.blockDim = dim3(kThreads);
+                cfg.dynamicSmemBytes = C::SMEM;
+                cfg.attrs = &attr;
+                cfg.numAttrs = 1;
+                int clusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&clusters, decode_kernel<T, D>, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    clusters = 0;
+                }
+                slots[s] = clusters * s;
+            }
+            if (slots[1] <= 0) return fail(ANN_ECUDA, "attention decode: kernel does not fit on this device.");
+            slots_by_dev[dev] = slots;
+        } else {
+            slots = it->second;
+        }
     }
+    int64_t chunk = 0;
+    a.splits = choose_splits<T, D>(a.rows, a.Tk, chunk, slots.data());
+    a.chunk = chunk;
     int64_t const grid = a.rows * a.splits;
     if (grid > INT32_MAX) return fail(ANN_ENOTSUP, "attention decode: grid too large.");
-    decode_kernel<T, D><<<static_cast<unsigned>(grid), kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(a.splits);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = as_stream(stream);
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, decode_kernel<T, D>, a, scale);
+    if (e != cudaSuccess) return fail(ANN_ECUDA, "attention decode: %s", cudaGetErrorString(e));
     return check_launch("attention decode");
 }
 
 template <typename T>
 int decode(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const ann_view* v_v, const ann_view* o_v,
-           T scale, uint32_t g, int layout, void* ws, size_t ws_bytes) {
+           T scale, uint32_t g, int layout) {
     if (g == 0u) return fail(ANN_EINVAL, "attention decode requires queriesPerKvGroup > 0.");
     if (layout != ANN_LAYOUT_BTHD && layout != ANN_LAYOUT_BHTD)
         return fail(ANN_EINVAL, "attention decode: invalid kv layout.");
@@ -450,13 +509,14 @@ int decode(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const an
     a.Tk = k.ext[tok];
     a.rows = B * Tq * Hq;
     a.g = g;
-    if (sizeof(T) == 4) {
-        if (D == 64) return launch<T, 64>(stream, a, scale, ws, ws_bytes);
-        if (D == 128) return launch<T, 128>(stream, a, scale, ws, ws_bytes);
-        return launch<T, (sizeof(T) == 4 ? 256 : 128)>(stream, a, scale, ws, ws_bytes);
+    if constexpr (sizeof(T) == 4) {
+        if (D == 64) return launch<T, 64>(stream, a, scale);
+        if (D == 128) return launch<T, 128>(stream, a, scale);
+        return launch<T, 256>(stream, a, scale);
+    } else {
+        if (D == 64) return launch<T, 64>(stream, a, scale);
+        return launch<T, 128>(stream, a, scale);
     }
-    if (D == 64) return launch<T, 64>(stream, a, scale, ws, ws_bytes);
-    return launch<T, 128>(stream, a, scale, ws, ws_bytes);
 }
 
 }  // namespace
@@ -475,27 +535,17 @@ int take_decode_error(cudaStream_t s, uint32_t* bits) {
 
 extern "C" {
 
-size_t ann_attention_decode_workspace_size(int64_t batch, int64_t query_tokens, int64_t query_heads,
-                                           int64_t head_dim, int64_t kv_tokens, int32_t elem_bytes) {
-    (void)kv_tokens;
-    if (batch < 0 || query_tokens < 0 || query_heads < 0 || head_dim < 0 || (elem_bytes != 4 && elem_bytes != 8))
-        return 0;
-    return ann::ws_layout(batch * query_tokens * query_heads, head_dim, static_cast<size_t>(elem_bytes)).total;
-}
-
 int ann_attention_decode_f32(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
-                             const ann_view* out, float scale, uint32_t g, int32_t layout, void* ws,
-                             size_t ws_bytes) {
+                             const ann_view* out, float scale, uint32_t g, int32_t layout) {
     ANN_API_BEGIN
-    return ann::decode<float>(s, q, k, v, out, scale, g, layout, ws, ws_bytes);
+    return ann::decode<float>(s, q, k, v, out, scale, g, layout);
     ANN_API_END
 }
 
 int ann_attention_decode_f64(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
-                             const ann_view* out, double scale, uint32_t g, int32_t layout, void* ws,
-                             size_t ws_bytes) {
+                             const ann_view* out, double scale, uint32_t g, int32_t layout) {
     ANN_API_BEGIN
-    return ann::decode<double>(s, q, k, v, out, scale, g, layout, ws, ws_bytes);
+    return ann::decode<double>(s, q, k, v, out, scale, g, layout);
     ANN_API_END
 }
 

@@ -63,18 +63,4 @@ def gemm(queue, A, B, C):
     check(fn("gemm", sfx)(handle(queue), ref(A), ref(B), ref(C)))
 
 
-_workspaces = {}
-
-
-def decode_workspace(device, nbytes: int):
-    """Zero-initialised decode workspace, cached per device and grown on
-    demand; the kernel leaves its completion counters at zero."""
-    key = torch.device(device).index
-    ws = _workspaces.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=device)
-        _workspaces[key] = ws
-    return ws
-
-
-__all__ = ["suffix", "fn", "handle", "trace", "ext", "gemm", "decode_workspace", "_capi"]
+__all__ = ["suffix", "fn", "handle", "trace", "ext", "gemm", "_capi"]

@@ -5,13 +5,12 @@ Same function names, argument order, defaults and error conditions as the
 reference; shape errors raise AnnShapeError (a ValueError), the analogue of
 std::invalid_argument. `exec` is accepted and ignored.
 """
-import ctypes
 import math
 
 import torch
 
 from .._capi import check, lib, ref
-from ._common import decode_workspace, ext, fn, gemm, handle, suffix, trace
+from ._common import ext, fn, gemm, handle, suffix, trace
 
 BTHD, BHTD = 0, 1
 
@@ -117,25 +116,15 @@ def causalSoftmax(queue, exec, input, output, axis, queryAxis, keyAxis):
                                                      int(queryAxis), int(keyAxis)))
 
 
-def attentionDecode(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1, kvLayout=BHTD, workspace=None):
+def attentionDecode(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1, kvLayout=BHTD):
     """Fused decode pipeline attentionScores -> ops::scale -> softmax(axis 3)
     -> attentionApply in one kernel (test/unit/nn/attention.cpp:675-734 is
     the reference composition). scale defaults to 1/sqrt(D)."""
     sfx = suffix(Q, K, V, out)
     if scale is None:
         scale = 1.0 / math.sqrt(Q.shape[3])
-    B, Tq, Hq, D = Q.shape
-    Tk = K.shape[1] if int(kvLayout) == BTHD else K.shape[2]
-    need = lib.ann_attention_decode_workspace_size(B, Tq, Hq, D, Tk, Q.element_size())
-    if workspace is None:
-        workspace = decode_workspace(Q.device, need)
     check(fn("attention_decode", sfx)(handle(queue), ref(Q), ref(K), ref(V), ref(out), float(scale),
-                                      int(queriesPerKvGroup), int(kvLayout), ctypes.c_void_p(workspace.data_ptr()),
-                                      workspace.numel() * workspace.element_size()))
-
-
-def decodeWorkspaceBytes(B, Tq, Hq, D, Tk, elem_bytes):
-    return lib.ann_attention_decode_workspace_size(B, Tq, Hq, D, Tk, elem_bytes)
+                                      int(queriesPerKvGroup), int(kvLayout)))
 
 
 def raise_shape(msg):

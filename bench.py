@@ -239,8 +239,6 @@ def main():
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     lib = _capi.lib
-    ws_bytes = lib.ann_attention_decode_workspace_size(B, 1, Hl, D, Tk, 4)
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
 
     # Descriptors built once: the timed loop only issues C-ABI calls.
     V = _capi.view
@@ -257,8 +255,7 @@ def main():
         vk, vv = vkv[i % copies]
         if ev is not None:
             ev[0].record(stream)
-        _capi.check(lib.ann_attention_decode_f32(sh, R(vq), R(vk), R(vv), R(vout), scale, 1, 1,
-                                                 ctypes.c_void_p(ws.data_ptr()), ws_bytes))
+        _capi.check(lib.ann_attention_decode_f32(sh, R(vq), R(vk), R(vv), R(vout), scale, 1, 1))
         if ev is not None:
             ev[1].record(stream)
         if world > 1:
@@ -308,7 +305,7 @@ def main():
         knew.copy_(hk, non_blocking=True)
         nn.ropeInPlace(queue, None, q, knew, cos, sin, ann.RopeLayout.BTHD, Tk)
         k, v = caches[i % copies]
-        nn.attentionDecode(queue, None, q, k, v, out, scale, 1, ann.AttentionKvLayout.BHTD, ws)
+        nn.attentionDecode(queue, None, q, k, v, out, scale, 1, ann.AttentionKvLayout.BHTD)
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
             ann.onHost.ops.scale(queue, None, gathered.permute(1, 2, 0, 3, 4), 1.0, full.view(B, 1, world, Hl, D))

@@ -160,28 +160,24 @@ int ann_qkv_projection_f32(ann_stream stream, const ann_view* input, const ann_v
 int ann_qkv_projection_f64(ann_stream stream, const ann_view* input, const ann_view* wq, const ann_view* wk,
                            const ann_view* wv, const ann_view* q, const ann_view* k, const ann_view* v);
 
-/* ---- fused decode attention (split-K over the KV cache) -----------------
+/* ---- fused decode attention ----------------------------------------------
  * One launch computing the reference's decode pipeline
  *   attentionScores(q, k) -> ops::scale(scale) -> softmax(axis 3)
  *   -> attentionApply(probs, v)
  * (test/unit/nn/attention.cpp:675-734) without materialising scores/probs.
- * q, out: BTHD [B,Tq,Hq,D]; k, v: `kv_layout` with Tk keys and Hkv = Hq/g
- * heads; softmax over all Tk keys (non-causal, as decode uses it).
- * Requires unit innermost stride, 16-byte aligned K/V rows, D*sizeof(T) a
- * multiple of 16 and D <= 256.
- * The kernel keeps per-split partial results in a caller-provided device
- * workspace of ann_attention_decode_workspace_size() bytes, 256-byte aligned.
- * Its last 4*B*Tq*Hq bytes are completion counters that must be zero before
- * the first call; every call leaves them zero again. Calls that share a
- * workspace must be ordered on one stream. */
-size_t ann_attention_decode_workspace_size(int64_t batch, int64_t query_tokens, int64_t query_heads,
-                                           int64_t head_dim, int64_t kv_tokens, int32_t elem_bytes);
+ * q, out: BTHD [B,Tq,Hq,D] (every query row attends to all Tk keys, the
+ * non-causal softmax the reference uses for decode); k, v: `kv_layout` with
+ * Tk keys and Hkv heads, query head hq reads kv head hq / g.
+ * Requires unit innermost stride, 16-byte aligned K/V rows and Q rows, and
+ * D in {64, 128, 256} (fp32) or {64, 128} (fp64); other shapes return
+ * ANN_ENOTSUP (the per-op entry points above take any shape).
+ * The key range of each row is split over the CTAs of one thread-block
+ * cluster, merged in distributed shared memory: no workspace, no global
+ * scratch memory. */
 int ann_attention_decode_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
-                             const ann_view* out, float scale, uint32_t queries_per_kv_group, int32_t kv_layout,
-                             void* workspace, size_t workspace_bytes);
+                             const ann_view* out, float scale, uint32_t queries_per_kv_group, int32_t kv_layout);
 int ann_attention_decode_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
-                             const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout,
-                             void* workspace, size_t workspace_bytes);
+                             const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -165,7 +165,7 @@ def test_decode_c2_per_op_and_fused(ann):
     of = empty((B, 1, H, D), T)
     nn.attentionDecode(queue, None, dq, dk, dv, of, scale, 1, ann.AttentionKvLayout.BHTD)
     assert_close(host(of), ro, T, "fused decode out")
-    # repeated calls reuse the workspace (counters self-reset) and are deterministic
+    # repeated calls are deterministic
     of2 = empty((B, 1, H, D), T)
     nn.attentionDecode(queue, None, dq, dk, dv, of2, scale, 1, ann.AttentionKvLayout.BHTD)
     assert np.array_equal(host(of), host(of2))
@@ -338,3 +338,23 @@ def test_scores_apply_gqa_bthd_ragged(ann, T):
         o = empty(ro.shape, T)
         ann.onHost.nn.attentionApply(ann.Queue(), None, dev(p), dev(v), o, 3, layout)
         assert_close(host(o), ro, T, "apply")
+
+
+@pytest.mark.parametrize("T,D", [(np.float32, 128), (np.float64, 64)])
+@pytest.mark.parametrize("splits", [1, 2, 5, 8, 16])
+def test_decode_forced_cluster_sizes(ann, monkeypatch, T, D, splits):
+    """Every cluster size up to the non-portable 16, and one CTA walking many
+    2048-key sub-chunks (online rescale), on scores with a wide dynamic range."""
+    B, H, Tk = 1, 3, 9000
+    g = rng(splits * 7 + D)
+    q = normal(g, (B, 1, H, D), T) * T(3)
+    k, v = normal(g, (B, H, Tk, D), T), normal(g, (B, H, Tk, D), T)
+    scale = T(1.0 / math.sqrt(D))
+    rows = np.array([[0, 0, h] for h in range(H)], np.int64)
+    ref = oracle.attention_rows(q, k, v, rows, scale, 1, 1, False).reshape(B, 1, H, D)
+    monkeypatch.setenv("ANN_DECODE_SPLITS", str(splits))
+    o = empty((B, 1, H, D), T)
+    queue = ann.Queue()
+    ann.onHost.nn.attentionDecode(queue, None, dev(q), dev(k), dev(v), o, scale, 1, ann.AttentionKvLayout.BHTD)
+    assert_close(host(o), ref, T, f"decode splits={splits}")
+    assert queue.take_device_error() == 0
