@@ -353,8 +353,18 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
     cluster.sync();  // peers' shared memory must outlive the reads above
 }
 
-// Splits per row = cluster size: enough CTAs to fill the resident slots with
-// a full last wave, at least 4 tiles of keys per CTA.
+// Splits per row = cluster size. The kernel is HBM-bound, so what matters is
+// (a) enough CTAs streaming at once and (b) no small last wave, during which
+// too few CTAs are left to keep HBM busy (each CTA keeps 64 KB in flight).
+// Measured on B200 (148 SMs, 3 resident CTAs each): a single wave of about
+// 256 CTAs streams near the read roof, while 512 CTAs over 444 resident slots
+// lose a quarter to the 68-CTA tail; among single-wave choices the smallest
+// power-of-two cluster reaching ~1.7 CTAs per SM was best at every row count
+// tried (32..256 rows of 2048 keys, 128 rows of 32768 keys).
+//  * rows fit in one wave: that cluster size, keeping >= 4 tiles of keys per
+//    CTA;
+//  * rows need several waves anyway: split only to bound the bytes of one CTA
+//    (at most 16384 keys), so the tail stays short.
 template <typename T, int D>
 int choose_splits(int64_t rows, int64_t Tk, int64_t& chunk, const int* slots_for) {
     using C = Cfg<T, D>;
@@ -362,31 +372,22 @@ int choose_splits(int64_t rows, int64_t Tk, int64_t& chunk, const int* slots_for
         chunk = 1;
         return 1;
     }
+    auto realize = [&](int64_t s) {
+        chunk = ceil_div(ceil_div(Tk, s), C::TILE) * C::TILE;
+        return static_cast<int>(ceil_div(Tk, chunk));
+    };
     if (const char* env = std::getenv("ANN_DECODE_SPLITS")) {
         int s = std::atoi(env);
-        if (s >= 1 && s <= kMaxCluster && slots_for[s] > 0 && Tk > 0) {
-            chunk = ceil_div(ceil_div(Tk, s), C::TILE) * C::TILE;
-            return static_cast<int>(ceil_div(Tk, chunk));
-        }
+        if (s >= 1 && s <= kMaxCluster && slots_for[s] > 0) return realize(s);
     }
     int64_t const max_s = std::max<int64_t>(1, std::min<int64_t>(kMaxCluster, Tk / (4 * C::TILE)));
-    double best = -1.0;
-    int best_s = 1;
-    chunk = std::max<int64_t>(1, Tk);
-    for (int s = 1; s <= max_s; ++s) {
-        if (slots_for[s] <= 0) continue;
-        int64_t const c = ceil_div(ceil_div(Tk, s), C::TILE) * C::TILE;
-        if (ceil_div(Tk, c) != s) continue;
-        int64_t const ctas = rows * s;
-        int64_t const waves = ceil_div(ctas, slots_for[s]);
-        double const eff = static_cast<double>(ctas) / static_cast<double>(waves * slots_for[s]);
-        if (eff > best + 0.02) {
-            best = eff;
-            best_s = s;
-            chunk = c;
-        }
+    if (rows < slots_for[1]) {
+        int64_t const target = (17 * static_cast<int64_t>(sm_count()) + 9) / 10;
+        int64_t s = 1;
+        while (rows * s < target && 2 * s <= max_s && slots_for[2 * s] > 0) s *= 2;
+        return realize(s);
     }
-    return best_s;
+    return realize(std::min<int64_t>(max_s, std::max<int64_t>(1, ceil_div(Tk, 16384))));
 }
 
 template <typename T, int D>
