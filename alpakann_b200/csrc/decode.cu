@@ -354,17 +354,18 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
 }
 
 // Splits per row = cluster size. The kernel is HBM-bound, so what matters is
-// (a) enough CTAs streaming at once and (b) no small last wave, during which
-// too few CTAs are left to keep HBM busy (each CTA keeps 64 KB in flight).
-// Measured on B200 (148 SMs, 3 resident CTAs each): a single wave of about
-// 256 CTAs streams near the read roof, while 512 CTAs over 444 resident slots
-// lose a quarter to the 68-CTA tail; among single-wave choices the smallest
-// power-of-two cluster reaching ~1.7 CTAs per SM was best at every row count
-// tried (32..256 rows of 2048 keys, 128 rows of 32768 keys).
-//  * rows fit in one wave: that cluster size, keeping >= 4 tiles of keys per
-//    CTA;
-//  * rows need several waves anyway: split only to bound the bytes of one CTA
-//    (at most 16384 keys), so the tail stays short.
+// (a) enough CTAs streaming at once (each keeps 64 KB in flight) and (b) no
+// short last wave of long CTAs, during which HBM idles. Rule: the smallest
+// split count s with
+//   * rows*s >= ~1.7 CTAs per SM,
+//   * at most 16384 keys per CTA, and
+//   * a single wave (rows*s <= resident slots) or a last wave that is full or
+//     holds >= ~1.7 CTAs per SM;
+// else the smallest s meeting the first two. Measured on B200 (148 SMs, 3
+// resident CTAs each) this picks the fastest or within 3 % of the fastest
+// split at every row count tried: 32..256 rows of 2048 keys, 128..1024 rows
+// of 32768 keys (e.g. 256 rows of 32768 keys: 1 split 6.6 TB/s, 2 splits
+// 5.5 TB/s with a 68-CTA last wave, 3 splits 7.1 TB/s).
 template <typename T, int D>
 int choose_splits(int64_t rows, int64_t Tk, int64_t& chunk, const int* slots_for) {
     using C = Cfg<T, D>;
@@ -381,13 +382,19 @@ int choose_splits(int64_t rows, int64_t Tk, int64_t& chunk, const int* slots_for
         if (s >= 1 && s <= kMaxCluster && slots_for[s] > 0) return realize(s);
     }
     int64_t const max_s = std::max<int64_t>(1, std::min<int64_t>(kMaxCluster, Tk / (4 * C::TILE)));
-    if (rows < slots_for[1]) {
-        int64_t const target = (17 * static_cast<int64_t>(sm_count()) + 9) / 10;
-        int64_t s = 1;
-        while (rows * s < target && 2 * s <= max_s && slots_for[2 * s] > 0) s *= 2;
-        return realize(s);
+    int64_t const target = (17 * static_cast<int64_t>(sm_count()) + 9) / 10;
+    int64_t fallback = 0;
+    for (int64_t s = 1; s <= max_s; ++s) {
+        if (slots_for[s] <= 0) continue;
+        int64_t const ctas = rows * s;
+        bool const enough = ctas >= target || s == max_s;
+        bool const short_ctas = ceil_div(Tk, s) <= 16384 || s == max_s;
+        if (!enough || !short_ctas) continue;
+        if (fallback == 0) fallback = s;
+        int64_t const tail = ctas % slots_for[s];
+        if (ctas <= slots_for[s] || tail == 0 || tail >= target) return realize(s);
     }
-    return realize(std::min<int64_t>(max_s, std::max<int64_t>(1, ceil_div(Tk, 16384))));
+    return realize(fallback > 0 ? fallback : 1);
 }
 
 template <typename T, int D>

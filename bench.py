@@ -1,14 +1,17 @@
 """Benchmark of the attention decode step (one JSON line on rank 0).
 
-Workload (default): batch 8, one query token per sequence, KV cache of 2048
-tokens, 32 heads x head_dim 128, fp32, BHTD cache; each step rotates Q and the
-new K row with RoPE (theta 1e4) at position 2048 and runs fused decode
-attention (scores -> scale 1/sqrt(128) -> softmax -> apply) over the cache.
-With N GPUs the heads are sharded (32/N per GPU) and the per-head outputs are
-all-gathered and re-assembled into [B,1,H,D] on every rank.
+Headline workload (c5): batch 16, one query token per sequence, KV cache of
+32768 tokens, 64 heads x head_dim 128, fp32, BHTD cache (32 GiB of K+V). Each
+step rotates Q and the new K row with RoPE (theta 5e5) at position 32768 and
+runs fused decode attention (scores -> scale 1/sqrt(128) -> softmax -> apply)
+over the cache. With N GPUs the heads are sharded (64/N per GPU, each GPU
+holds only its heads' cache) and the per-head outputs are all-gathered (NCCL)
+and re-assembled into [B,1,H,D] on every rank: total work is fixed, so the
+scaling is strong. The same line carries, under "extra", the smaller decode
+workload c2 (batch 8, cache 2048, 32 heads x 128) measured the same way.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c2|c5]
+                  [--workload c5|c2] [--no-extra]
 
 --impl reference times the CPU oracle (the reference's per-element host
 algorithm restated in C++/OpenMP; the reference itself cannot be built
@@ -32,8 +35,8 @@ WORKLOADS = {
     "c2": dict(B=8, Tk=2048, H=32, D=128, theta=1e4,
                desc="decode: batch 8, 1 query token, KV cache 2048, 32 heads x 128, fp32, BHTD, RoPE 1e4 at pos 2048"),
     "c5": dict(B=16, Tk=32768, H=64, D=128, theta=5e5,
-               desc="decode: batch 16, 1 query token, KV cache 32768, 64 heads x 128, fp32, BHTD, RoPE 5e5 at "
-                    "pos 32768"),
+               desc="decode: batch 16, 1 query token, KV cache 32768, 64 heads x 128 (d_model 8192), fp32, BHTD, "
+                    "RoPE 5e5 at pos 32768"),
 }
 L2_BYTES = 126 * 1024 * 1024
 
@@ -41,10 +44,11 @@ L2_BYTES = 126 * 1024 * 1024
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
-    p.add_argument("--steps", type=int, default=5000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=3000)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
+    p.add_argument("--no-extra", action="store_true", help="skip the secondary c2 measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
     return p.parse_args()
 
@@ -60,7 +64,7 @@ def peaks():
 
 
 def ncu_traffic(workload):
-    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    """DRAM bytes per decode launch (1 GPU) from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", f"decode_{workload}_ncu.md")
     try:
         for line in open(path):
@@ -79,7 +83,6 @@ class Clocks:
 
     def __init__(self):
         self.samples = []
-        self.window = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -93,10 +96,7 @@ class Clocks:
         for line in self.proc.stdout:
             self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
 
-    def mark(self, t0, t1):
-        self.window = (t0, t1)
-
-    def stop(self):
+    def stop(self, t0, t1):
         if self.proc is None:
             return None
         time.sleep(0.3)
@@ -105,7 +105,6 @@ class Clocks:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        t0, t1 = self.window
         inside = [s for ts, s in self.samples if t0 - 0.2 <= ts <= t1 + 0.2]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -120,13 +119,6 @@ class Clocks:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
-
-
-def rope_tables(positions, D, theta, torch, dtype):
-    import numpy as np
-    pos = np.arange(positions, dtype=np.float64)[:, None]
-    ang = pos * np.power(theta, -2.0 * np.arange(D // 2, dtype=np.float64) / D)[None, :]
-    return (torch.from_numpy(np.cos(ang)).to(dtype).cuda(), torch.from_numpy(np.sin(ang)).to(dtype).cuda())
 
 
 # ------------------------------------------------------------------ CPU ---
@@ -176,14 +168,18 @@ class CpuSample:
         return (time.perf_counter() - t0) / reps / self.frac, reps
 
 
+def cpu_sample_for(w):
+    # c2: one sequence x all heads (1/8 of a step); c5: one sequence x one head (1/1024)
+    return CpuSample(w, 1, w["H"]) if w["Tk"] <= 4096 else CpuSample(w, 1, 1)
+
+
 def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import oracle
     oracle.set_threads(os.cpu_count() or 1)
-    # one sequence x all heads per step (1/B of the work) keeps --steps K bounded
-    smp = CpuSample(w, 1, w["H"])
+    smp = cpu_sample_for(w)
     for _ in range(args.warmup):
         smp.step()
     step, _ = smp.time_full_steps(steps=args.steps)
@@ -200,6 +196,134 @@ def run_reference(args, w):
 
 
 # ------------------------------------------------------------------ GPU ---
+class DecodeBench:
+    """Inputs and the two step flavours (device-resident and end-to-end) of
+    the head-sharded decode workload on this rank."""
+
+    def __init__(self, w, rank, world, group):
+        import numpy as np
+        import torch
+
+        import alpakann_b200 as ann
+        from alpakann_b200 import _capi
+        from alpakann_b200.sharded import HeadShard, HeadShardedDecode
+        self.torch, self.capi, self.w = torch, _capi, w
+        self.world = world
+        B, Tk, H, D = w["B"], w["Tk"], w["H"], w["D"]
+        self.shard = HeadShard(rank, world, H, H)
+        Hl = self.shard.local_heads
+        f32 = torch.float32
+        gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+        self.kv_bytes = 2 * B * Hl * Tk * D * 4
+        self.copies = max(1, math.ceil(3 * L2_BYTES / self.kv_bytes))  # rotate caches: every step reads cold HBM
+        self.caches = [(torch.randn((B, Hl, Tk, D), generator=gen, dtype=f32, device="cuda"),
+                        torch.randn((B, Hl, Tk, D), generator=gen, dtype=f32, device="cuda"))
+                       for _ in range(self.copies)]
+        self.q = torch.randn((B, 1, Hl, D), generator=gen, dtype=f32, device="cuda")
+        self.knew = torch.randn((B, 1, Hl, D), generator=gen, dtype=f32, device="cuda")
+        ang = np.arange(Tk + 1, dtype=np.float64)[:, None] * np.power(w["theta"], -2.0 * np.arange(D // 2) / D)[None]
+        self.cos = torch.from_numpy(np.cos(ang)).to(f32).cuda()
+        self.sin = torch.from_numpy(np.sin(ang)).to(f32).cuda()
+        self.scale = 1.0 / math.sqrt(D)
+        self.sharded = HeadShardedDecode(self.shard, B, D, f32, "cuda", group)
+        self.stream = torch.cuda.current_stream()
+        self.queue = ann.Queue(self.stream)
+        # descriptors built once: the device-timed loop only issues C-ABI calls
+        V = _capi.view
+        self.vq, self.vkn, self.vcos, self.vsin = V(self.q), V(self.knew), V(self.cos), V(self.sin)
+        self.vout = V(self.sharded.out if world == 1 else self.sharded.out_local)
+        self.vkv = [(V(k), V(v)) for k, v in self.caches]
+        if world > 1:
+            self.vsrc, self.vdst = V(self.sharded._src), V(self.sharded._dst)
+        self.launches_per_step = 2 if world == 1 else 3
+        # pinned host buffers of the end-to-end step
+        self.hq = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
+        self.hk = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
+        self.hout = torch.empty((B, 1, H, D), dtype=f32).pin_memory()
+
+    def step(self, i, ev=None):
+        lib, R, sh, chk = self.capi.lib, ctypes.byref, self.stream.cuda_stream, self.capi.check
+        chk(lib.ann_rope_inplace_f32(sh, R(self.vq), R(self.vkn), R(self.vcos), R(self.vsin), 0, self.w["Tk"]))
+        vk, vv = self.vkv[i % self.copies]
+        if ev is not None:
+            ev[0].record(self.stream)
+        chk(lib.ann_attention_decode_f32(sh, R(self.vq), R(vk), R(vv), R(self.vout), self.scale, 1, 1))
+        if ev is not None:
+            ev[1].record(self.stream)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(self.sharded.gathered, self.sharded.out_local, group=self.sharded.group)
+            chk(lib.ann_scale_f32(sh, R(self.vsrc), 1.0, R(self.vdst)))
+
+    def e2e_step(self, i):
+        """Through the public Python API, with the step's inputs copied from
+        pinned host memory and the full output read back."""
+        self.q.copy_(self.hq, non_blocking=True)
+        self.knew.copy_(self.hk, non_blocking=True)
+        k, v = self.caches[i % self.copies]
+        out = self.sharded.step(self.queue, self.q, self.knew, k, v, self.cos, self.sin, self.w["Tk"], self.scale)
+        self.hout.copy_(out, non_blocking=True)
+
+    def release(self):
+        self.caches.clear()
+        self.vkv.clear()
+        self.torch.cuda.empty_cache()
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(values, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def measure(bench, steps, warmup, world, rank, with_clocks):
+    import torch
+    for i in range(warmup):
+        bench.step(i)
+    barrier(world)
+    clocks = Clocks() if (with_clocks and rank == 0) else None
+    if clocks:
+        time.sleep(0.5)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    t_wall0 = time.time()
+    start.record(bench.stream)
+    for i in range(steps):
+        bench.step(i, kev[i])
+    end.record(bench.stream)
+    barrier(world)
+    t_wall1 = time.time()
+    elapsed = start.elapsed_time(end) / 1e3
+    kernel_s = sum(a.elapsed_time(b) for a, b in kev) / 1e3 / steps
+    clk = clocks.stop(t_wall0, t_wall1) if clocks else None
+
+    e2e_steps = max(1, min(steps, 1000))
+    for i in range(min(warmup, 5)):
+        bench.e2e_step(i)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(bench.stream)
+    for i in range(e2e_steps):
+        bench.e2e_step(i)
+    e1.record(bench.stream)
+    barrier(world)
+    e2e_s = e0.elapsed_time(e1) / 1e3 / e2e_steps
+    elapsed, kernel_s, e2e_s = max_over_ranks([elapsed, kernel_s, e2e_s], world)
+    return elapsed, kernel_s, e2e_s, e2e_steps, clk
+
+
 def main():
     args = parse()
     w = WORKLOADS[args.workload]
@@ -209,155 +333,70 @@ def main():
     import torch
     import torch.distributed as dist
 
-    import alpakann_b200 as ann
-    from alpakann_b200 import _capi
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    group = None
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=120))
-    B, Tk, H, D = w["B"], w["Tk"], w["H"], w["D"]
-    if H % world:
-        raise SystemExit(f"{H} heads do not shard over {world} GPUs")
-    Hl = H // world
-    f32 = torch.float32
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    kv_bytes = 2 * B * Hl * Tk * D * 4
-    copies = max(1, math.ceil(3 * L2_BYTES / kv_bytes))  # rotate caches so each step reads cold HBM
-    caches = [(torch.randn((B, Hl, Tk, D), generator=gen, dtype=f32, device="cuda"),
-               torch.randn((B, Hl, Tk, D), generator=gen, dtype=f32, device="cuda")) for _ in range(copies)]
-    q = torch.randn((B, 1, Hl, D), generator=gen, dtype=f32, device="cuda")
-    knew = torch.randn((B, 1, Hl, D), generator=gen, dtype=f32, device="cuda")
-    out = torch.empty((B, 1, Hl, D), dtype=f32, device="cuda")
-    cos, sin = rope_tables(Tk + 1, D, w["theta"], torch, f32)
-    full = torch.empty((B, 1, H, D), dtype=f32, device="cuda")
-    gathered = torch.empty((world, B, 1, Hl, D), dtype=f32, device="cuda") if world > 1 else None
-    scale = 1.0 / math.sqrt(D)
-    stream = torch.cuda.current_stream()
-    sh = stream.cuda_stream
-    lib = _capi.lib
+    peak, peak_kind = peaks()
 
-    # Descriptors built once: the timed loop only issues C-ABI calls.
-    V = _capi.view
-    vq, vkn, vout, vcos, vsin = V(q), V(knew), V(out), V(cos), V(sin)
-    vkv = [(V(k), V(v)) for k, v in caches]
-    if world > 1:
-        # re-assembly: gathered[r, b, 0, h, d] -> full[b, 0, r*Hl + h, d] (a strided copy = scale by 1)
-        vsrc = V(gathered.permute(1, 2, 0, 3, 4))
-        vdst = V(full.view(B, 1, world, Hl, D))
-    R = ctypes.byref
+    def run(wl, steps, warmup, with_clocks):
+        bench = DecodeBench(WORKLOADS[wl], rank, world, group)
+        elapsed, kernel_s, e2e_s, e2e_steps, clk = measure(bench, steps, warmup, world, rank, with_clocks)
+        ww = WORKLOADS[wl]
+        B, Tk, H, D = ww["B"], ww["Tk"], ww["H"], ww["D"]
+        Hl = H // world
+        alg = 2 * B * Hl * Tk * D * 4 + 2 * B * Hl * D * 4  # per launch per GPU: K+V read, Q read, O write
+        res = dict(value=B * steps / elapsed, ms_per_step=elapsed / steps * 1e3, kernel_us=kernel_s * 1e6,
+                   achieved=alg / kernel_s / 1e9, e2e=B / e2e_s, e2e_steps=e2e_steps, clk=clk,
+                   copies=bench.copies, kv_mib=bench.kv_bytes / 2**20, launches=bench.launches_per_step * steps,
+                   h2d=2 * B * Hl * D * 4 * world, d2h=B * H * D * 4 * world, alg=alg)
+        bench.release()
+        return res
 
-    def step(i, ev=None):
-        _capi.check(lib.ann_rope_inplace_f32(sh, R(vq), R(vkn), R(vcos), R(vsin), 0, Tk))
-        vk, vv = vkv[i % copies]
-        if ev is not None:
-            ev[0].record(stream)
-        _capi.check(lib.ann_attention_decode_f32(sh, R(vq), R(vk), R(vv), R(vout), scale, 1, 1))
-        if ev is not None:
-            ev[1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            _capi.check(lib.ann_scale_f32(sh, R(vsrc), 1.0, R(vdst)))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for i in range(args.warmup):
-        step(i)
-    barrier()
-    clocks = Clocks() if rank == 0 else None
-    time.sleep(0.5 if clocks else 0)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    t_wall0 = time.time()
-    start.record(stream)
-    for i in range(args.steps):
-        step(i, kev[i])
-    end.record(stream)
-    barrier()
-    t_wall1 = time.time()
-    if clocks:
-        clocks.mark(t_wall0, t_wall1)
-    elapsed = start.elapsed_time(end) / 1e3
-    kernel_s = sum(a.elapsed_time(b) for a, b in kev) / 1e3 / args.steps
-    t = torch.tensor([elapsed, kernel_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed, kernel_s = float(t[0]), float(t[1])
-    clk = clocks.stop() if clocks else None
-
-    # ---- end to end through the public API with host buffers ----
-    hq = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
-    hk = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
-    hout = torch.empty((B, 1, H, D), dtype=f32).pin_memory()
-    nn = ann.onHost.nn
-    queue = ann.Queue(stream)
-    e2e_steps = min(args.steps, 2000)
-
-    def e2e_step(i):
-        q.copy_(hq, non_blocking=True)
-        knew.copy_(hk, non_blocking=True)
-        nn.ropeInPlace(queue, None, q, knew, cos, sin, ann.RopeLayout.BTHD, Tk)
-        k, v = caches[i % copies]
-        nn.attentionDecode(queue, None, q, k, v, out, scale, 1, ann.AttentionKvLayout.BHTD)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            ann.onHost.ops.scale(queue, None, gathered.permute(1, 2, 0, 3, 4), 1.0, full.view(B, 1, world, Hl, D))
-            hout.copy_(full, non_blocking=True)
-        else:
-            hout.copy_(out, non_blocking=True)
-
-    for i in range(min(args.warmup, 10)):
-        e2e_step(i)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    e1.record(stream)
-    barrier()
-    te = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te[0]) / e2e_steps
+    main_res = run(args.workload, args.steps, args.warmup, True)
+    extra = {}
+    if not args.no_extra:
+        other = "c2" if args.workload == "c5" else "c5"
+        o = run(other, max(10, args.steps if other == "c2" else args.steps // 16), args.warmup, False)
+        extra[other] = {"workload": WORKLOADS[other]["desc"], "value": o["value"], "unit": "tokens/s",
+                        "ms_per_step": o["ms_per_step"], "kernel_us": o["kernel_us"],
+                        "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"]}
 
     if rank == 0:
-        peak, peak_kind = peaks()
-        alg_bytes = 2 * B * Hl * Tk * D * 4 + 2 * B * Hl * D * 4  # K+V + Q read + O write, per launch per GPU
-        achieved = alg_bytes / kernel_s / 1e9
-        traffic = ncu_traffic(args.workload) if world == 1 else None
+        r = main_res
         cpu = None
         if world == 1:
             import oracle
-            smp = CpuSample(w, 1, w["H"])
+            smp = cpu_sample_for(w)
             smp.step()
             cpu_step, reps = smp.time_full_steps(seconds=args.cpu_seconds)
-            cpu = {"value": B / cpu_step, "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
+            cpu = {"value": w["B"] / cpu_step, "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
                    "sample": f"{smp.desc}; {reps} reps"}
         line = {
-            "metric": "decode attn tokens/s", "value": B * args.steps / elapsed, "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+            "metric": "decode attn tokens/s", "value": r["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w["desc"], "batch": B, "kv_len": Tk, "heads": H, "head_dim": D,
+            "config": {"workload": w["desc"], "batch": w["B"], "kv_len": w["Tk"], "heads": w["H"],
+                       "head_dim": w["D"],
                        "parallelism": f"head-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-                       "l2": f"inputs larger than L2: {copies} KV cache copies of {kv_bytes / 2**20:.0f} MiB per GPU "
-                             f"rotated per step"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "decode_kernel<float,128>", "kernel_us": kernel_s * 1e6,
-                         "frac_of_8TBs_nominal": achieved / 8000.0},
+                       "l2": f"inputs larger than L2: {r['copies']} KV cache cop{'y' if r['copies'] == 1 else 'ies'} "
+                             f"of {r['kv_mib']:.0f} MiB per GPU, rotated per step"},
+            "roofline": {"bound": "hbm", "achieved": r["achieved"], "peak": peak, "unit": "GB/s",
+                         "frac": r["achieved"] / peak,
+                         "traffic": ncu_traffic(args.workload) if world == 1 else None,
+                         "peak_kind": peak_kind, "kernel": "decode_kernel<float,128>",
+                         "kernel_us": r["kernel_us"], "alg_bytes_per_launch": r["alg"],
+                         "frac_of_8TBs_nominal": r["achieved"] / 8000.0},
             "cpu_baseline": cpu,
-            "e2e": {"value": B / e2e_s, "unit": "tokens/s",
-                    "h2d_bytes_per_step": 2 * B * Hl * D * 4 * world, "d2h_bytes_per_step": B * H * D * 4 * world,
-                    "steps": e2e_steps},
-            "gpu_launches": args.steps * (2 if world == 1 else 3),
-            "clocks": clk,
+            "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"], "steps": r["e2e_steps"]},
+            "gpu_launches": r["launches"],
+            "clocks": r["clk"],
+            "extra": extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
