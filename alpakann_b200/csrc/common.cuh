@@ -28,6 +28,7 @@ int sm_count();
 // errors: each reads its word on `s`, ORs it into *bits and clears it.
 int take_embedding_error(cudaStream_t s, uint32_t* bits);
 int take_decode_error(cudaStream_t s, uint32_t* bits);
+int take_prefill_error(cudaStream_t s, uint32_t* bits);
 
 // ---------------------------------------------------------------------------
 // Views: ann_view with byte pitches -> element strides, validated.

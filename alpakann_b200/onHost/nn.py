@@ -127,6 +127,18 @@ def attentionDecode(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1, 
                                       int(queriesPerKvGroup), int(kvLayout)))
 
 
+def attentionPrefill(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1, kvLayout=BTHD, causal=True):
+    """Fused prefill pipeline attentionScores -> ops::scale -> causalSoftmax
+    (top-left mask) or softmax -> attentionApply in one kernel
+    (test/unit/nn/attention.cpp:591-651 is the reference composition).
+    scale defaults to 1/sqrt(D)."""
+    sfx = suffix(Q, K, V, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.shape[3])
+    check(fn("attention_prefill", sfx)(handle(queue), ref(Q), ref(K), ref(V), ref(out), float(scale),
+                                       int(queriesPerKvGroup), int(kvLayout), 1 if causal else 0))
+
+
 def raise_shape(msg):
     from .._capi import ANN_EINVAL, AnnShapeError
     raise AnnShapeError(ANN_EINVAL, msg)

@@ -179,6 +179,24 @@ int ann_attention_decode_f32(ann_stream stream, const ann_view* q, const ann_vie
 int ann_attention_decode_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
                              const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout);
 
+/* ---- fused prefill attention ---------------------------------------------
+ * One launch computing the reference's prefill pipeline
+ *   attentionScores(q, k) -> ops::scale(scale)
+ *   -> causalSoftmax(axis 3, query axis 2, key axis 3)   (causal != 0)
+ *      or softmax(axis 3)                               (causal == 0)
+ *   -> attentionApply(probs, v)
+ * (test/unit/nn/attention.cpp:591-651) without materialising scores/probs.
+ * The causal mask is the reference's top-left one: key j is hidden from
+ * query i iff i < j (onAcc/internal/nn/softmax.hpp:23-30), also when
+ * Tq != Tk. q, out: BTHD [B,Tq,Hq,D]; k, v: `kv_layout` with Tk keys.
+ * Requires unit innermost stride, 16-byte aligned rows, D in {64, 128}. */
+int ann_attention_prefill_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                              const ann_view* out, float scale, uint32_t queries_per_kv_group, int32_t kv_layout,
+                              int32_t causal);
+int ann_attention_prefill_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                              const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout,
+                              int32_t causal);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -163,3 +163,16 @@ def test_view_descriptor_rejects_bad_pitch(capi):
     rc = capi.lib.ann_scale_f32(None, ctypes.byref(v), 1.0, capi.ref(w))
     assert rc == capi.ANN_EINVAL
     assert b"pitch" in capi.lib.ann_last_error()
+
+
+@pytest.mark.parametrize("sfx,T", [("f32", np.float32), ("f64", np.float64)])
+def test_prefill_validation(capi, sfx, T):
+    r = capi.ref
+    fp = getattr(capi.lib, f"ann_attention_prefill_{sfx}")
+    q = np.ones((1, 8, 4, 64), T)
+    kv = np.ones((1, 8, 4, 64), T)
+    assert "queriesPerKvGroup > 0" in _call_einval(capi, fp, r(q), r(kv), r(kv), r(q), 0.1, 0, 0, 1)
+    assert "invalid kv layout" in _call_einval(capi, fp, r(q), r(kv), r(kv), r(q), 0.1, 1, 2, 1)
+    assert "extents of Q" in _call_einval(capi, fp, r(q), r(kv), r(kv), r(np.ones((1, 8, 4, 32), T)), 0.1, 1, 0, 1)
+    assert "does not match" in _call_einval(capi, fp, r(q), r(np.ones((1, 8, 4, 32), T)),
+                                            r(np.ones((1, 8, 4, 32), T)), r(q), 0.1, 1, 0, 1)

@@ -1,0 +1,131 @@
+"""Fused prefill attention against the oracle's per-op pipeline
+(scores -> scale -> causalSoftmax / softmax -> apply): full comparison where
+the oracle finishes in seconds, sampled rows at the full configuration
+sizes. Tolerances as in tests/helpers.py TOL (fp32 1e-4 rel + 1e-5 abs,
+fp64 1e-11 rel + 1e-12 abs)."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.helpers import assert_close, normal, rng
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ann():
+    import alpakann_b200
+    return alpakann_b200
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+def empty(shape, T):
+    import torch
+    return torch.full(shape, float("nan"), dtype=torch.float32 if T == np.float32 else torch.float64, device="cuda")
+
+
+def oracle_pipeline(q, k, v, scale, g, layout, causal):
+    T = q.dtype.type
+    B, Tq, Hq, D = q.shape
+    Tk = k.shape[1] if layout == 0 else k.shape[2]
+    s = np.empty((B, Hq, Tq, Tk), q.dtype)
+    oracle.attention_scores(q, k, s, g, layout)
+    oracle.scale(s, T(scale), s)
+    p = np.empty_like(s)
+    if causal:
+        oracle.causal_softmax(s, p, 3, 2, 3)
+    else:
+        oracle.softmax(s, p, 3)
+    o = np.empty_like(q)
+    oracle.attention_apply(p, v, o, g, layout)
+    return o
+
+
+def run(ann, q, k, v, scale, g, layout, causal):
+    o = empty(q.shape, q.dtype.type)
+    queue = ann.Queue()
+    ann.onHost.nn.attentionPrefill(queue, None, dev(q), dev(k), dev(v), o, scale, g, layout, causal)
+    got = host(o)
+    assert queue.take_device_error() == 0
+    return got
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+def test_prefill_c1_full(ann, T):
+    """c1 shape (batch 1, seq 128, 4 heads x 64), causal, scale 1/8."""
+    g = rng(0x5EED + 11)
+    q, k, v = (normal(g, (1, 128, 4, 64), T) for _ in range(3))
+    ref = oracle_pipeline(q, k, v, 0.125, 1, 0, True)
+    assert_close(run(ann, q, k, v, 0.125, 1, 0, True), ref, T, "prefill c1")
+
+
+@pytest.mark.parametrize("T,D", [(np.float32, 64), (np.float32, 128), (np.float64, 64), (np.float64, 128)])
+@pytest.mark.parametrize("Tq,Tk,causal", [(1, 1, True), (100, 100, True), (130, 130, True), (50, 130, True),
+                                          (130, 50, True), (77, 200, False), (64, 64, True)])
+def test_prefill_shapes(ann, T, D, Tq, Tk, causal):
+    """Ragged tiles, Tq != Tk with the reference's top-left mask, non-causal."""
+    g = rng(Tq * 1000 + Tk + D)
+    q = normal(g, (2, Tq, 3, D), T)
+    k, v = normal(g, (2, Tk, 3, D), T), normal(g, (2, Tk, 3, D), T)
+    sc = 1.0 / math.sqrt(D)
+    ref = oracle_pipeline(q, k, v, sc, 1, 0, causal)
+    assert_close(run(ann, q, k, v, sc, 1, 0, causal), ref, T, f"prefill Tq={Tq} Tk={Tk} causal={causal}")
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("layout", [0, 1])
+def test_prefill_gqa_layouts(ann, T, layout):
+    g = rng(40 + layout)
+    B, Tt, Hq, Hkv, D = 2, 150, 8, 2, 64
+    q = normal(g, (B, Tt, Hq, D), T)
+    shape = (B, Tt, Hkv, D) if layout == 0 else (B, Hkv, Tt, D)
+    k, v = normal(g, shape, T), normal(g, shape, T)
+    ref = oracle_pipeline(q, k, v, 0.125, 4, layout, True)
+    assert_close(run(ann, q, k, v, 0.125, 4, layout, True), ref, T, "prefill gqa")
+
+
+def _sampled(ann, T, B, Tt, H, D, seed, nrows=24):
+    import torch
+    dt = torch.float32 if T == np.float32 else torch.float64
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn((B, Tt, H, D), generator=gen, dtype=dt, device="cuda")
+    k = torch.randn((B, Tt, H, D), generator=gen, dtype=dt, device="cuda")
+    v = torch.randn((B, Tt, H, D), generator=gen, dtype=dt, device="cuda")
+    o = torch.full_like(q, float("nan"))
+    sc = 1.0 / math.sqrt(D)
+    queue = ann.Queue()
+    ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(o).all())
+    g = np.random.default_rng(seed)
+    rows = [(0, 0, 0), (B - 1, Tt - 1, H - 1), (0, 63, 1), (0, 64, 1)]
+    rows += [(int(g.integers(B)), int(g.integers(Tt)), int(g.integers(H))) for _ in range(nrows - len(rows))]
+    for b, i, h in rows:
+        qh = q[b:b + 1, i:i + 1, h:h + 1].cpu().numpy()
+        kh = k[b:b + 1, :i + 1, h:h + 1].cpu().numpy()  # causal: keys 0..i
+        vh = v[b:b + 1, :i + 1, h:h + 1].cpu().numpy()
+        ref = oracle.attention_rows(qh, kh, vh, np.array([[0, 0, 0]], np.int64), T(sc), 1, 0, False)[0]
+        assert_close(o[b, i, h].cpu().numpy(), ref, T, f"row {(b, i, h)}")
+    assert queue.take_device_error() == 0
+
+
+def test_prefill_c4_fp64_sampled(ann):
+    """c4: batch 2, seq 1024, 16 heads x 64, fp64, causal."""
+    _sampled(ann, np.float64, 2, 1024, 16, 64, 4)
+
+
+def test_prefill_c3_fp32_sampled(ann):
+    """c3: batch 4, seq 4096, 32 heads x 128, fp32, causal."""
+    _sampled(ann, np.float32, 4, 4096, 32, 128, 3)
