@@ -324,6 +324,47 @@ def measure(bench, steps, warmup, world, rank, with_clocks):
     return elapsed, kernel_s, e2e_s, e2e_steps, clk
 
 
+PREFILL = {
+    "c3": dict(B=4, T=4096, H=32, D=128, dtype="f32",
+               desc="prefill: batch 4, seq 4096, 32 heads x 128, fp32, causal, scale 1/sqrt(128)"),
+    "c4": dict(B=2, T=1024, H=16, D=64, dtype="f64",
+               desc="prefill: batch 2, seq 1024, 16 heads x 64, fp64, causal, scale 1/8"),
+}
+
+
+def measure_prefill(name, world, rank, reps=10):
+    """Fused causal prefill of this rank's heads (heads sharded over ranks),
+    timed with CUDA events; TFLOP/s counts QK^T + PV over the causal half
+    including the diagonal, 4*B*H*D*T(T+1)/2, for the whole job."""
+    import torch
+
+    import alpakann_b200 as ann
+    p = PREFILL[name]
+    B, T, H, D = p["B"], p["T"], p["H"], p["D"]
+    dt = torch.float32 if p["dtype"] == "f32" else torch.float64
+    Hl = H // world
+    gen = torch.Generator(device="cuda").manual_seed(77 + rank)
+    q, k, v = (torch.randn((B, T, Hl, D), generator=gen, dtype=dt, device="cuda") for _ in range(3))
+    o = torch.empty_like(q)
+    queue = ann.Queue()
+    sc = 1.0 / math.sqrt(D)
+    for _ in range(2):
+        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+    e1.record()
+    barrier(world)
+    t = max_over_ranks([e0.elapsed_time(e1) / 1e3 / reps], world)[0]
+    flops = 4 * B * H * D * T * (T + 1) / 2
+    del q, k, v, o
+    torch.cuda.empty_cache()
+    return {"workload": p["desc"], "ms": t * 1e3, "tflops": flops / t / 1e12, "tokens_per_s": B * T / t,
+            "dtype": p["dtype"], "kernel": "prefill_kernel (FMA/DFMA flash)"}
+
+
 def main():
     args = parse()
     w = WORKLOADS[args.workload]
@@ -365,6 +406,8 @@ def main():
         extra[other] = {"workload": WORKLOADS[other]["desc"], "value": o["value"], "unit": "tokens/s",
                         "ms_per_step": o["ms_per_step"], "kernel_us": o["kernel_us"],
                         "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"]}
+        for name in ("c3", "c4"):
+            extra[f"{name}_prefill"] = measure_prefill(name, world, rank)
 
     if rank == 0:
         r = main_res

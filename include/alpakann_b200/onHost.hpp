@@ -1,0 +1,391 @@
+/*
+ * alpakann_b200/onHost.hpp -- C++20 drop-in for alpakaNN's attention path.
+ *
+ * Same namespaces, function names, template parameter (T_Type), argument
+ * order, defaults and exceptions as the reference's header-only host API
+ * (include/alpaka/nn/onHost/nn/{embedding,rms_norm,attention,rope,softmax}.hpp,
+ * include/alpaka/nn/onHost/ops/elementwise.hpp, include/alpaka/nn/onHost/matrix/gemm.hpp),
+ * implemented on the sm_100a kernels behind include/ann_b200.h.
+ *
+ *  - queue: anything nativeStream() understands -- alpaka::nn::b200::Queue
+ *    (one CUDA stream), a cudaStream_t, or a type with getNativeHandle().
+ *  - exec: accepted and ignored (it selected alpaka's thread mapping).
+ *  - views: any type with data(), getExtents() and getPitches() (BYTE
+ *    pitches, alpaka's convention), e.g. alpaka::nn::b200::View.
+ *  - ANN_EINVAL becomes std::invalid_argument with the reference's message,
+ *    every other failure std::runtime_error.
+ */
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <array>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+
+#include "../ann_b200.h"
+
+namespace alpaka::nn {
+// nn/attention.hpp:10-14 and nn/rope.hpp:10-14
+enum class AttentionKvLayout { BTHD = ANN_LAYOUT_BTHD, BHTD = ANN_LAYOUT_BHTD };
+enum class RopeLayout { BTHD = ANN_LAYOUT_BTHD, BHTD = ANN_LAYOUT_BHTD };
+}  // namespace alpaka::nn
+
+namespace alpaka::nn::b200 {
+
+// In-order queue = one CUDA stream on one device.
+struct Queue {
+    cudaStream_t stream = nullptr;
+    int device = 0;
+    bool owned = false;
+
+    Queue() = default;
+    explicit Queue(int dev) : device(dev), owned(true) {
+        cudaSetDevice(dev);
+        if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess)
+            throw std::runtime_error("alpakann_b200: cudaStreamCreate failed");
+    }
+    Queue(cudaStream_t s, int dev) : stream(s), device(dev) {}
+    Queue(Queue const&) = delete;
+    Queue& operator=(Queue const&) = delete;
+    ~Queue() {
+        if (owned && stream) cudaStreamDestroy(stream);
+    }
+    void wait() const {
+        if (cudaStreamSynchronize(stream) != cudaSuccess) throw std::runtime_error("alpakann_b200: stream error");
+    }
+    cudaStream_t getNativeHandle() const { return stream; }
+};
+
+// Strided view over device (or host) memory: extents and BYTE pitches.
+template <typename T, std::size_t R>
+struct View {
+    using value_type = T;
+    T* ptr = nullptr;
+    std::array<int64_t, R> extents{};
+    std::array<int64_t, R> pitches{};
+    T* data() const { return ptr; }
+    std::array<int64_t, R> const& getExtents() const { return extents; }
+    std::array<int64_t, R> const& getPitches() const { return pitches; }
+};
+
+// Dense row-major view (alpaka::makeView analogue).
+template <typename T, std::size_t R>
+View<T, R> makeView(T* ptr, std::array<int64_t, R> const& ext) {
+    View<T, R> v;
+    v.ptr = ptr;
+    v.extents = ext;
+    int64_t p = sizeof(T);
+    for (std::size_t i = R; i-- > 0;) {
+        v.pitches[i] = p;
+        p *= ext[i];
+    }
+    return v;
+}
+
+// Sub-view at an element offset (getSubView analogue, same pitches).
+template <typename T, std::size_t R>
+View<T, R> subView(View<T, R> const& src, std::array<int64_t, R> const& offset, std::array<int64_t, R> const& ext) {
+    View<T, R> v = src;
+    char* p = reinterpret_cast<char*>(src.ptr);
+    for (std::size_t i = 0; i < R; ++i) p += offset[i] * src.pitches[i];
+    v.ptr = reinterpret_cast<T*>(p);
+    v.extents = ext;
+    return v;
+}
+
+namespace detail {
+template <typename E>
+constexpr std::size_t rank_of(E const& e) {
+    if constexpr (requires { e.size(); })
+        return static_cast<std::size_t>(e.size());
+    else
+        return static_cast<std::size_t>(std::remove_cvref_t<E>::dim());
+}
+
+template <typename V>
+ann_view to_ann(V const& v) {
+    ann_view a{};
+    auto const& ext = v.getExtents();
+    auto const& pit = v.getPitches();
+    std::size_t const r = rank_of(ext);
+    if (r > ANN_MAX_RANK) throw std::invalid_argument("alpakann_b200: view rank exceeds 8.");
+    a.data = const_cast<void*>(static_cast<void const*>(v.data()));
+    a.rank = static_cast<int32_t>(r);
+    for (std::size_t i = 0; i < r; ++i) {
+        a.extents[i] = static_cast<int64_t>(ext[i]);
+        a.pitches[i] = static_cast<int64_t>(pit[i]);
+    }
+    return a;
+}
+
+template <typename Q>
+ann_stream stream_of(Q& q) {
+    if constexpr (std::is_same_v<std::remove_cvref_t<Q>, cudaStream_t>)
+        return reinterpret_cast<ann_stream>(q);
+    else
+        return reinterpret_cast<ann_stream>(q.getNativeHandle());
+}
+
+inline void check(int rc) {
+    if (rc == ANN_OK) return;
+    std::string msg = ann_last_error();
+    if (rc == ANN_EINVAL) throw std::invalid_argument(msg);
+    throw std::runtime_error("alpakann_b200: " + msg);
+}
+
+template <typename T>
+constexpr bool is_f32 = std::is_same_v<T, float>;
+template <typename T>
+constexpr bool is_f64 = std::is_same_v<T, double>;
+template <typename T>
+constexpr void require_float() {
+    static_assert(is_f32<T> || is_f64<T>, "alpakann_b200 supports float and double");
+}
+
+// ALPAKANN_DEBUG_ATTENTION_TRACE (onHost/nn/attention.hpp:24-34)
+inline bool attention_trace_enabled() {
+    auto const* env = std::getenv("ALPAKANN_DEBUG_ATTENTION_TRACE");
+    return env != nullptr && env[0] != '\0' && env[0] != '0';
+}
+inline std::string ext_str(ann_view const& v) {
+    std::ostringstream os;
+    os << "{";
+    for (int i = 0; i < v.rank; ++i) os << (i ? ", " : "") << v.extents[i];
+    os << "}";
+    return os.str();
+}
+}  // namespace detail
+}  // namespace alpaka::nn::b200
+
+namespace alpaka::nn::onHost {
+
+// onHost/matrix/gemm.hpp:28-33 -- C = A * B on cuBLAS
+template <typename T_Type = float>
+void gemm(auto& queue, auto const& A, auto const& B, auto& C) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto a = d::to_ann(A), b = d::to_ann(B), c = d::to_ann(C);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_gemm_f32(d::stream_of(queue), &a, &b, &c));
+    else
+        d::check(ann_gemm_f64(d::stream_of(queue), &a, &b, &c));
+}
+
+}  // namespace alpaka::nn::onHost
+
+namespace alpaka::nn::onHost::ops {
+
+// onHost/ops/elementwise.hpp:330-334
+template <typename T_Type>
+void scale(auto& queue, auto /*exec*/, auto const& in, T_Type scalar, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(in), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_scale_f32(d::stream_of(queue), &i, scalar, &o));
+    else
+        d::check(ann_scale_f64(d::stream_of(queue), &i, scalar, &o));
+}
+
+}  // namespace alpaka::nn::onHost::ops
+
+namespace alpaka::nn::onHost::nn {
+
+// onHost/nn/embedding.hpp:17-36
+template <typename T_Type>
+void embeddingLookup(auto& queue, auto /*exec*/, auto const& tokenIds, auto const& embedding, auto& output) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto ids = d::to_ann(tokenIds), e = d::to_ann(embedding), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_embedding_lookup_f32(d::stream_of(queue), &ids, &e, &o));
+    else
+        d::check(ann_embedding_lookup_f64(d::stream_of(queue), &ids, &e, &o));
+}
+
+// onHost/nn/rms_norm.hpp:17-35
+template <typename T_Type>
+void rmsNorm(auto& queue, auto /*exec*/, auto const& input, auto const& weight, auto& output, T_Type epsilon) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), w = d::to_ann(weight), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_rms_norm_f32(d::stream_of(queue), &i, &w, &o, epsilon));
+    else
+        d::check(ann_rms_norm_f64(d::stream_of(queue), &i, &w, &o, epsilon));
+}
+
+// onHost/nn/attention.hpp:38-52
+template <typename T_Type>
+void qkvProjection(auto& queue, auto const& input, auto const& Wq, auto const& Wk, auto const& Wv, auto& Q, auto& K,
+                   auto& V) {
+    alpaka::nn::onHost::gemm<T_Type>(queue, input, Wq, Q);
+    alpaka::nn::onHost::gemm<T_Type>(queue, input, Wk, K);
+    alpaka::nn::onHost::gemm<T_Type>(queue, input, Wv, V);
+}
+
+// onHost/nn/attention.hpp:112-116
+template <typename T_Type>
+void outputProjection(auto& queue, auto const& input, auto const& Wo, auto& output) {
+    alpaka::nn::onHost::gemm<T_Type>(queue, input, Wo, output);
+}
+
+// onHost/nn/attention.hpp:54-81
+template <typename T_Type>
+void attentionScores(auto& queue, auto /*exec*/, auto const& Q, auto const& K, auto& scores,
+                     uint32_t queriesPerKvGroup = 1u,
+                     alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BTHD) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    if (queriesPerKvGroup == 0u) throw std::invalid_argument{"attentionScores requires queriesPerKvGroup > 0."};
+    auto q = d::to_ann(Q), k = d::to_ann(K), s = d::to_ann(scores);
+    if (d::attention_trace_enabled())
+        std::fprintf(stderr, "attentionScores q=%s k=%s scores=%s queriesPerKvGroup=%u layout=%s\n",
+                     d::ext_str(q).c_str(), d::ext_str(k).c_str(), d::ext_str(s).c_str(), queriesPerKvGroup,
+                     kvLayout == alpaka::nn::AttentionKvLayout::BTHD ? "BTHD" : "BHTD");
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_scores_f32(d::stream_of(queue), &q, &k, &s, queriesPerKvGroup,
+                                          static_cast<int32_t>(kvLayout)));
+    else
+        d::check(ann_attention_scores_f64(d::stream_of(queue), &q, &k, &s, queriesPerKvGroup,
+                                          static_cast<int32_t>(kvLayout)));
+}
+
+// onHost/nn/attention.hpp:83-110
+template <typename T_Type>
+void attentionApply(auto& queue, auto /*exec*/, auto const& probs, auto const& values, auto& out,
+                    uint32_t queriesPerKvGroup = 1u,
+                    alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BTHD) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    if (queriesPerKvGroup == 0u) throw std::invalid_argument{"attentionApply requires queriesPerKvGroup > 0."};
+    auto p = d::to_ann(probs), v = d::to_ann(values), o = d::to_ann(out);
+    if (d::attention_trace_enabled())
+        std::fprintf(stderr, "attentionApply probs=%s values=%s out=%s queriesPerKvGroup=%u layout=%s\n",
+                     d::ext_str(p).c_str(), d::ext_str(v).c_str(), d::ext_str(o).c_str(), queriesPerKvGroup,
+                     kvLayout == alpaka::nn::AttentionKvLayout::BTHD ? "BTHD" : "BHTD");
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_apply_f32(d::stream_of(queue), &p, &v, &o, queriesPerKvGroup,
+                                         static_cast<int32_t>(kvLayout)));
+    else
+        d::check(ann_attention_apply_f64(d::stream_of(queue), &p, &v, &o, queriesPerKvGroup,
+                                         static_cast<int32_t>(kvLayout)));
+}
+
+// onHost/nn/softmax.hpp:26-40
+template <typename T_Type>
+void softmax(auto& queue, auto /*exec*/, auto const& input, auto& output, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_softmax_f32(d::stream_of(queue), &i, &o, axis));
+    else
+        d::check(ann_softmax_f64(d::stream_of(queue), &i, &o, axis));
+}
+
+// onHost/nn/softmax.hpp:59-80
+template <typename T_Type>
+void causalSoftmax(auto& queue, auto /*exec*/, auto const& input, auto& output, uint32_t axis, uint32_t queryAxis,
+                   uint32_t keyAxis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_causal_softmax_f32(d::stream_of(queue), &i, &o, axis, queryAxis, keyAxis));
+    else
+        d::check(ann_causal_softmax_f64(d::stream_of(queue), &i, &o, axis, queryAxis, keyAxis));
+}
+
+// onHost/nn/rope.hpp:49-62
+template <typename T_Type>
+void rope(auto& queue, auto /*exec*/, auto const& in, auto const& cosTable, auto const& sinTable, auto& out,
+          alpaka::nn::RopeLayout layout = alpaka::nn::RopeLayout::BTHD, uint32_t positionOffset = 0u) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(in), c = d::to_ann(cosTable), s = d::to_ann(sinTable), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_rope_f32(d::stream_of(queue), &i, &c, &s, &o, static_cast<int32_t>(layout), positionOffset));
+    else
+        d::check(ann_rope_f64(d::stream_of(queue), &i, &c, &s, &o, static_cast<int32_t>(layout), positionOffset));
+}
+
+// onHost/nn/rope.hpp:64-86 (query/key overload)
+template <typename T_Type>
+void rope(auto& queue, auto exec, auto const& q, auto const& k, auto const& cosTable, auto const& sinTable, auto& outQ,
+          auto& outK, alpaka::nn::RopeLayout layout = alpaka::nn::RopeLayout::BTHD, uint32_t positionOffset = 0u) {
+    rope<T_Type>(queue, exec, q, cosTable, sinTable, outQ, layout, positionOffset);
+    rope<T_Type>(queue, exec, k, cosTable, sinTable, outK, layout, positionOffset);
+}
+
+// onHost/nn/rope.hpp:96-113 -- truly in place, no temporary
+template <typename T_Type>
+void ropeInPlace(auto& queue, auto /*exec*/, auto& tensor, auto const& cosTable, auto const& sinTable,
+                 alpaka::nn::RopeLayout layout = alpaka::nn::RopeLayout::BTHD, uint32_t positionOffset = 0u) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto t = d::to_ann(tensor), c = d::to_ann(cosTable), s = d::to_ann(sinTable);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_rope_inplace_f32(d::stream_of(queue), &t, nullptr, &c, &s, static_cast<int32_t>(layout),
+                                      positionOffset));
+    else
+        d::check(ann_rope_inplace_f64(d::stream_of(queue), &t, nullptr, &c, &s, static_cast<int32_t>(layout),
+                                      positionOffset));
+}
+
+// onHost/nn/rope.hpp:122-135 -- q and k rotated in one launch
+template <typename T_Type>
+void ropeInPlace(auto& queue, auto /*exec*/, auto& q, auto& k, auto const& cosTable, auto const& sinTable,
+                 alpaka::nn::RopeLayout layout = alpaka::nn::RopeLayout::BTHD, uint32_t positionOffset = 0u) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto qa = d::to_ann(q), ka = d::to_ann(k), c = d::to_ann(cosTable), s = d::to_ann(sinTable);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_rope_inplace_f32(d::stream_of(queue), &qa, &ka, &c, &s, static_cast<int32_t>(layout),
+                                      positionOffset));
+    else
+        d::check(ann_rope_inplace_f64(d::stream_of(queue), &qa, &ka, &c, &s, static_cast<int32_t>(layout),
+                                      positionOffset));
+}
+
+// Fused decode: attentionScores -> ops::scale -> softmax -> attentionApply in one kernel.
+template <typename T_Type>
+void attentionDecode(auto& queue, auto /*exec*/, auto const& Q, auto const& K, auto const& V, auto& out,
+                     T_Type scale, uint32_t queriesPerKvGroup = 1u,
+                     alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BHTD) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto q = d::to_ann(Q), k = d::to_ann(K), v = d::to_ann(V), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_decode_f32(d::stream_of(queue), &q, &k, &v, &o, scale, queriesPerKvGroup,
+                                          static_cast<int32_t>(kvLayout)));
+    else
+        d::check(ann_attention_decode_f64(d::stream_of(queue), &q, &k, &v, &o, scale, queriesPerKvGroup,
+                                          static_cast<int32_t>(kvLayout)));
+}
+
+// Fused prefill: attentionScores -> ops::scale -> causalSoftmax / softmax -> attentionApply in one kernel.
+template <typename T_Type>
+void attentionPrefill(auto& queue, auto /*exec*/, auto const& Q, auto const& K, auto const& V, auto& out,
+                      T_Type scale, uint32_t queriesPerKvGroup = 1u,
+                      alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BTHD,
+                      bool causal = true) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto q = d::to_ann(Q), k = d::to_ann(K), v = d::to_ann(V), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_prefill_f32(d::stream_of(queue), &q, &k, &v, &o, scale, queriesPerKvGroup,
+                                           static_cast<int32_t>(kvLayout), causal ? 1 : 0));
+    else
+        d::check(ann_attention_prefill_f64(d::stream_of(queue), &q, &k, &v, &o, scale, queriesPerKvGroup,
+                                           static_cast<int32_t>(kvLayout), causal ? 1 : 0));
+}
+
+}  // namespace alpaka::nn::onHost::nn

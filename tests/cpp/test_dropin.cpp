@@ -1,0 +1,388 @@
+// test_dropin.cpp -- the reference's hot-path test cases (test/unit/nn/*.cpp of
+// alpakaNN), written against the C++20 drop-in header alpakann_b200/onHost.hpp
+// exactly as a reference user would call it: same namespaces, function names,
+// template parameter and argument order. Host reference loops and known
+// answers follow the reference tests; tolerance is Catch::Approx(expected)
+// .epsilon(eps).margin(margin) (testHelper/test.hpp:47-54). Needs a GPU.
+#include <alpakann_b200/onHost.hpp>
+
+#include <cmath>
+#include <cstdio>
+#include <limits>
+#include <vector>
+
+namespace b200 = alpaka::nn::b200;
+namespace nn = alpaka::nn::onHost::nn;
+namespace ops = alpaka::nn::onHost::ops;
+using alpaka::nn::AttentionKvLayout;
+
+static int g_failures = 0, g_checks = 0;
+
+template <typename T>
+static void checkValue(T actual, T expected, double eps, double margin, char const* what) {
+    ++g_checks;
+    double const diff = std::fabs(static_cast<double>(actual) - static_cast<double>(expected));
+    if (!(diff <= margin || diff <= eps * std::fabs(static_cast<double>(expected)))) {
+        if (++g_failures < 20)
+            std::fprintf(stderr, "FAIL %s: %.17g vs %.17g\n", what, static_cast<double>(actual),
+                         static_cast<double>(expected));
+    }
+}
+
+#define REQUIRE(...)                                                              \
+    do {                                                                          \
+        ++g_checks;                                                               \
+        if (!(__VA_ARGS__)) {                                                     \
+            ++g_failures;                                                         \
+            std::fprintf(stderr, "FAIL %s:%d: %s\n", __FILE__, __LINE__, #__VA_ARGS__); \
+        }                                                                         \
+    } while (0)
+
+// Device buffer + dense view, host mirror in a std::vector.
+template <typename T, std::size_t R>
+struct Tensor {
+    std::array<int64_t, R> ext;
+    std::vector<T> host;
+    T* dev = nullptr;
+    explicit Tensor(std::array<int64_t, R> e, T fill = T{}) : ext(e) {
+        int64_t n = 1;
+        for (auto x : e) n *= x;
+        host.assign(static_cast<size_t>(n), fill);
+        cudaMalloc(&dev, sizeof(T) * (n > 0 ? n : 1));
+    }
+    ~Tensor() { cudaFree(dev); }
+    Tensor(Tensor const&) = delete;
+    int64_t flat(std::array<int64_t, R> const& i) const {
+        int64_t f = 0;
+        for (std::size_t a = 0; a < R; ++a) f = f * ext[a] + i[a];
+        return f;
+    }
+    T& operator[](std::array<int64_t, R> const& i) { return host[flat(i)]; }
+    T operator[](std::array<int64_t, R> const& i) const { return host[flat(i)]; }
+    void upload() { cudaMemcpy(dev, host.data(), sizeof(T) * host.size(), cudaMemcpyHostToDevice); }
+    void download() { cudaMemcpy(host.data(), dev, sizeof(T) * host.size(), cudaMemcpyDeviceToHost); }
+    b200::View<T, R> view() { return b200::makeView<T, R>(dev, ext); }
+};
+
+using E4 = std::array<int64_t, 4>;
+
+// attention.cpp:24-28
+template <typename T>
+static void fill4D(Tensor<T, 4>& t, T base) {
+    for (int64_t a = 0; a < t.ext[0]; ++a)
+        for (int64_t b = 0; b < t.ext[1]; ++b)
+            for (int64_t c = 0; c < t.ext[2]; ++c)
+                for (int64_t d = 0; d < t.ext[3]; ++d)
+                    t[{a, b, c, d}] = base + static_cast<T>(a * 101 + b * 17 + c * 7 + d * 3);
+}
+
+// attention.cpp:30-66 (scores, BTHD or BHTD)
+template <typename T>
+static std::vector<T> refScores(Tensor<T, 4> const& q, Tensor<T, 4> const& k, bool bhtd, int64_t Tk) {
+    int64_t const B = q.ext[0], Tq = q.ext[1], H = q.ext[2], D = q.ext[3];
+    std::vector<T> s(static_cast<size_t>(B * H * Tq * Tk));
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t i = 0; i < Tq; ++i)
+                for (int64_t j = 0; j < Tk; ++j) {
+                    T sum{};
+                    for (int64_t d = 0; d < D; ++d) sum += q[{b, i, h, d}] * (bhtd ? k[{b, h, j, d}] : k[{b, j, h, d}]);
+                    s[((b * H + h) * Tq + i) * Tk + j] = sum;
+                }
+    return s;
+}
+
+// attention.cpp:115-174 (causal / plain softmax in place on [B,H,Tq,Tk])
+template <typename T>
+static void refSoftmax(std::vector<T>& s, int64_t rows, int64_t Tq, int64_t Tk, bool causal) {
+    for (int64_t r = 0; r < rows; ++r) {
+        int64_t const q = r % Tq;
+        T* x = s.data() + r * Tk;
+        int64_t const last = causal ? q : Tk - 1;
+        T m = -std::numeric_limits<T>::infinity();
+        for (int64_t j = 0; j <= last; ++j) m = std::max(m, x[j]);
+        T sum{};
+        for (int64_t j = 0; j < Tk; ++j) {
+            if (causal && j > q) {
+                x[j] = T{};
+                continue;
+            }
+            x[j] = std::exp(x[j] - m);
+            sum += x[j];
+        }
+        for (int64_t j = 0; j <= last; ++j) x[j] /= sum;
+    }
+}
+
+// attention.cpp:68-106 (apply, BTHD or BHTD values)
+template <typename T>
+static std::vector<T> refApply(std::vector<T> const& p, Tensor<T, 4> const& v, bool bhtd, int64_t B, int64_t H,
+                               int64_t Tq, int64_t Tk, int64_t D) {
+    std::vector<T> o(static_cast<size_t>(B * Tq * H * D));
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t i = 0; i < Tq; ++i)
+            for (int64_t h = 0; h < H; ++h)
+                for (int64_t d = 0; d < D; ++d) {
+                    T sum{};
+                    for (int64_t j = 0; j < Tk; ++j)
+                        sum += p[((b * H + h) * Tq + i) * Tk + j] * (bhtd ? v[{b, h, j, d}] : v[{b, j, h, d}]);
+                    o[((b * Tq + i) * H + h) * D + d] = sum;
+                }
+    return o;
+}
+
+// attention.cpp:240-309 -- grouped query heads, known answers
+template <typename T>
+static void gqaKnownAnswers(b200::Queue& queue) {
+    Tensor<T, 4> q({1, 1, 4, 2}), k({1, 1, 2, 2}), v({1, 1, 2, 2}), s({1, 4, 1, 1}), p({1, 4, 1, 1}), o({1, 1, 4, 2});
+    for (int64_t h = 0; h < 4; ++h) {
+        q[{0, 0, h, 0}] = static_cast<T>(h + 1);
+        q[{0, 0, h, 1}] = static_cast<T>(h + 2);
+    }
+    k.host = {1, 2, 3, 4};
+    v.host = {10, 20, 30, 40};
+    q.upload(), k.upload(), v.upload();
+    auto qv = q.view(), kv = k.view(), vv = v.view(), sv = s.view(), pv = p.view(), ov = o.view();
+    nn::attentionScores<T>(queue, nullptr, qv, kv, sv, 2u, AttentionKvLayout::BTHD);
+    nn::softmax<T>(queue, nullptr, sv, pv, 3u);
+    nn::attentionApply<T>(queue, nullptr, pv, vv, ov, 2u, AttentionKvLayout::BTHD);
+    queue.wait();
+    s.download(), o.download();
+    T const want[4] = {5, 8, 25, 32};
+    for (int h = 0; h < 4; ++h) checkValue(s.host[h], want[h], 1e-5, 1e-6, "gqa scores");
+    for (int h = 0; h < 4; ++h) {
+        checkValue(o[{0, 0, h, 0}], static_cast<T>(h < 2 ? 10 : 30), 1e-5, 1e-6, "gqa out");
+        checkValue(o[{0, 0, h, 1}], static_cast<T>(h < 2 ? 20 : 40), 1e-5, 1e-6, "gqa out");
+    }
+}
+
+// attention.cpp:591-651 (prefill, causal) and :674-734 (decode, BHTD) pipelines;
+// the fused kernels must give the per-op pipeline's output.
+template <typename T>
+static void pipeline(b200::Queue& queue, bool decode) {
+    int64_t const B = 1, Tq = decode ? 1 : 4, H = 4, D = 4, Tk = decode ? 5 : 4;
+    E4 const qe{B, Tq, H, D}, kvext = decode ? E4{B, H, Tk, D} : E4{B, Tk, H, D};
+    Tensor<T, 4> q(qe), k(kvext), v(kvext), s({B, H, Tq, Tk}), p({B, H, Tq, Tk}), o(qe);
+    fill4D<T>(q, decode ? T(0.375) : T(0.125));
+    fill4D<T>(k, decode ? T(-0.0625) : T(-0.25));
+    fill4D<T>(v, decode ? T(0.875) : T(0.5));
+    q.upload(), k.upload(), v.upload();
+    auto es = refScores<T>(q, k, decode, Tk);
+    for (auto& x : es) x *= static_cast<T>(0.5);
+    auto ep = es;
+    refSoftmax<T>(ep, B * H * Tq, Tq, Tk, !decode);
+    auto eo = refApply<T>(ep, v, decode, B, H, Tq, Tk, D);
+    auto const layout = decode ? AttentionKvLayout::BHTD : AttentionKvLayout::BTHD;
+    auto qv = q.view(), kv = k.view(), vv = v.view(), sv = s.view(), pv = p.view(), ov = o.view();
+    nn::attentionScores<T>(queue, nullptr, qv, kv, sv, 1u, layout);
+    ops::scale<T>(queue, nullptr, sv, static_cast<T>(0.5), sv);
+    if (decode)
+        nn::softmax<T>(queue, nullptr, sv, pv, 3u);
+    else
+        nn::causalSoftmax<T>(queue, nullptr, sv, pv, 3u, 2u, 3u);
+    nn::attentionApply<T>(queue, nullptr, pv, vv, ov, 1u, layout);
+    queue.wait();
+    s.download(), p.download(), o.download();
+    for (size_t i = 0; i < es.size(); ++i) checkValue(s.host[i], es[i], 1e-5, 1e-5, "pipeline scores");
+    for (size_t i = 0; i < ep.size(); ++i) checkValue(p.host[i], ep[i], 1e-5, 1e-5, "pipeline probs");
+    for (size_t i = 0; i < eo.size(); ++i) checkValue(o.host[i], eo[i], 1e-5, 1e-5, "pipeline out");
+    // fused kernels take head dims of 64/128: pad D with zeros (scores and outputs unchanged)
+    int64_t const DP = 64;
+    Tensor<T, 4> q2({B, Tq, H, DP}), k2(decode ? E4{B, H, Tk, DP} : E4{B, Tk, H, DP}), v2(k2.ext), o2({B, Tq, H, DP});
+    for (int64_t a = 0; a < q.ext[0]; ++a)
+        for (int64_t b = 0; b < q.ext[1]; ++b)
+            for (int64_t c = 0; c < q.ext[2]; ++c)
+                for (int64_t d = 0; d < D; ++d) q2[{a, b, c, d}] = q[{a, b, c, d}];
+    for (int64_t a = 0; a < k.ext[0]; ++a)
+        for (int64_t b = 0; b < k.ext[1]; ++b)
+            for (int64_t c = 0; c < k.ext[2]; ++c)
+                for (int64_t d = 0; d < D; ++d) k2[{a, b, c, d}] = k[{a, b, c, d}], v2[{a, b, c, d}] = v[{a, b, c, d}];
+    q2.upload(), k2.upload(), v2.upload();
+    auto q2v = q2.view(), k2v = k2.view(), v2v = v2.view(), o2v = o2.view();
+    if (decode)
+        nn::attentionDecode<T>(queue, nullptr, q2v, k2v, v2v, o2v, static_cast<T>(0.5), 1u, layout);
+    else
+        nn::attentionPrefill<T>(queue, nullptr, q2v, k2v, v2v, o2v, static_cast<T>(0.5), 1u, layout, true);
+    queue.wait();
+    o2.download();
+    for (int64_t i = 0; i < Tq; ++i)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t d = 0; d < D; ++d)
+                checkValue(o2[{0, i, h, d}], eo[(i * H + h) * D + d], 1e-5, 1e-5, "fused out");
+}
+
+// softmax.cpp:88-114 -- large logits, causal zeros, rows sum to 1
+template <typename T>
+static void softmaxStability(b200::Queue& queue) {
+    Tensor<T, 4> in({1, 1, 2, 3}), out({1, 1, 2, 3});
+    in.host = {1000, 1001, 999, -1, 0, 1};
+    in.upload();
+    auto iv = in.view(), ov = out.view();
+    nn::causalSoftmax<T>(queue, nullptr, iv, ov, 3u, 2u, 3u);
+    queue.wait();
+    out.download();
+    REQUIRE(out.host[1] == T{});
+    REQUIRE(out.host[2] == T{});
+    checkValue(out.host[0], T{1}, 1e-5, 1e-6, "row 0 sum");
+    checkValue(out.host[3] + out.host[4] + out.host[5], T{1}, 1e-5, 1e-6, "row 1 sum");
+}
+
+// rope.cpp:20-82 and attention.cpp:852-975 (qkvProjection + ropeInPlace on flat buffers)
+template <typename T>
+static void qkvRope(b200::Queue& queue) {
+    int64_t const tokens = 3, hidden = 4, pairs = 2;
+    Tensor<T, 2> x({tokens, hidden}), wq({hidden, hidden}), wk({hidden, hidden}), wv({hidden, hidden});
+    Tensor<T, 2> cosT({tokens, pairs}), sinT({tokens, pairs});
+    for (int64_t r = 0; r < tokens; ++r)
+        for (int64_t c = 0; c < hidden; ++c)
+            x[{r, c}] = static_cast<T>(-0.25) + static_cast<T>(r * 13 + c * 3) * static_cast<T>(0.05);
+    for (int64_t r = 0; r < hidden; ++r)
+        for (int64_t c = 0; c < hidden; ++c) {
+            T const f = static_cast<T>(r * hidden + c);
+            wq[{r, c}] = static_cast<T>(-0.1) + f * static_cast<T>(0.01);
+            wk[{r, c}] = static_cast<T>(0.2) - f * static_cast<T>(0.007);
+            wv[{r, c}] = static_cast<T>(-0.05) + f * static_cast<T>(0.009);
+        }
+    for (int64_t pos = 0; pos < tokens; ++pos)
+        for (int64_t pr = 0; pr < pairs; ++pr) {
+            T const ang = static_cast<T>(pos + 1) * static_cast<T>(0.25) * static_cast<T>(pr + 1);
+            cosT[{pos, pr}] = std::cos(ang);
+            sinT[{pos, pr}] = std::sin(ang);
+        }
+    auto proj = [&](Tensor<T, 2>& w) {
+        std::vector<T> e(static_cast<size_t>(tokens * hidden));
+        for (int64_t r = 0; r < tokens; ++r)
+            for (int64_t c = 0; c < hidden; ++c) {
+                T sum{};
+                for (int64_t i = 0; i < hidden; ++i) sum += x[{r, i}] * w[{i, c}];
+                e[r * hidden + c] = sum;
+            }
+        return e;
+    };
+    auto rot = [&](std::vector<T> e) {
+        for (int64_t t = 0; t < tokens; ++t)
+            for (int64_t pr = 0; pr < pairs; ++pr) {
+                T const c = cosT[{t, pr}], s = sinT[{t, pr}];
+                T const x0 = e[t * hidden + 2 * pr], x1 = e[t * hidden + 2 * pr + 1];
+                e[t * hidden + 2 * pr] = x0 * c - x1 * s;
+                e[t * hidden + 2 * pr + 1] = x0 * s + x1 * c;
+            }
+        return e;
+    };
+    auto eq = rot(proj(wq)), ek = rot(proj(wk)), ev = proj(wv);
+    for (auto* t : {&x, &wq, &wk, &wv, &cosT, &sinT}) t->upload();
+    Tensor<T, 1> qf({tokens * hidden}), kf({tokens * hidden}), vf({tokens * hidden});
+    auto q2 = b200::makeView<T, 2>(qf.dev, {tokens, hidden}), k2 = b200::makeView<T, 2>(kf.dev, {tokens, hidden}),
+         v2 = b200::makeView<T, 2>(vf.dev, {tokens, hidden});
+    auto xv = x.view(), wqv = wq.view(), wkv = wk.view(), wvv = wv.view();
+    nn::qkvProjection<T>(queue, xv, wqv, wkv, wvv, q2, k2, v2);
+    auto q4 = b200::makeView<T, 4>(qf.dev, {1, tokens, 1, hidden}), k4 = b200::makeView<T, 4>(kf.dev, {1, tokens, 1, hidden});
+    auto cv = cosT.view(), sv = sinT.view();
+    nn::ropeInPlace<T>(queue, nullptr, q4, k4, cv, sv);
+    queue.wait();
+    qf.download(), kf.download(), vf.download();
+    for (size_t i = 0; i < eq.size(); ++i) {
+        checkValue(qf.host[i], eq[i], 1e-5, 1e-5, "q");
+        checkValue(kf.host[i], ek[i], 1e-5, 1e-5, "k");
+        checkValue(vf.host[i], ev[i], 1e-5, 1e-5, "v");
+    }
+}
+
+// rms_norm.cpp:18-48
+template <typename T>
+static void rmsNorm(b200::Queue& queue) {
+    Tensor<T, 2> in({2, 4}), out({2, 4});
+    Tensor<T, 1> w({4});
+    for (int64_t r = 0; r < 2; ++r)
+        for (int64_t c = 0; c < 4; ++c) in[{r, c}] = static_cast<T>(r * 4 + c + 1);
+    for (int64_t i = 0; i < 4; ++i) w[{i}] = static_cast<T>(0.5) + static_cast<T>(i);
+    in.upload(), w.upload();
+    auto iv = in.view(), wv = w.view(), ov = out.view();
+    nn::rmsNorm<T>(queue, nullptr, iv, wv, ov, static_cast<T>(1.0e-5));
+    queue.wait();
+    out.download();
+    for (int64_t r = 0; r < 2; ++r) {
+        T ss{};
+        for (int64_t c = 0; c < 4; ++c) ss += in[{r, c}] * in[{r, c}];
+        T const inv = T{1} / std::sqrt(ss / T{4} + static_cast<T>(1.0e-5));
+        for (int64_t c = 0; c < 4; ++c) checkValue(out[{r, c}], in[{r, c}] * inv * w[{c}], 1e-5, 1e-6, "rmsNorm");
+    }
+}
+
+// embedding.cpp:20-170 -- gather, non-contiguous subview, validation throws
+template <typename T>
+static void embedding(b200::Queue& queue) {
+    Tensor<T, 2> storage({3, 5});
+    for (int64_t r = 0; r < 3; ++r)
+        for (int64_t c = 0; c < 5; ++c) storage[{r, c}] = static_cast<T>(r * 10 + c);
+    storage.upload();
+    Tensor<uint32_t, 1> ids({4});
+    ids.host = {2, 0, 1, 2};
+    ids.upload();
+    Tensor<T, 2> out({4, 2});
+    auto table = b200::subView<T, 2>(storage.view(), {0, 2}, {3, 2});
+    auto idv = ids.view(), ov = out.view();
+    nn::embeddingLookup<T>(queue, nullptr, idv, table, ov);
+    queue.wait();
+    out.download();
+    for (int64_t t = 0; t < 4; ++t)
+        for (int64_t c = 0; c < 2; ++c) REQUIRE(out[{t, c}] == storage[{static_cast<int64_t>(ids.host[t]), 2 + c}]);
+    Tensor<T, 2> wrongRows({3, 2}), wrongCols({4, 3});
+    Tensor<T, 3> wrongRank({4, 2, 1});
+    bool threw = false;
+    try {
+        auto v = wrongRows.view();
+        nn::embeddingLookup<T>(queue, nullptr, idv, table, v);
+    } catch (std::invalid_argument const&) {
+        threw = true;
+    }
+    REQUIRE(threw);
+    threw = false;
+    try {
+        auto v = wrongCols.view();
+        nn::embeddingLookup<T>(queue, nullptr, idv, table, v);
+    } catch (std::invalid_argument const&) {
+        threw = true;
+    }
+    REQUIRE(threw);
+    threw = false;
+    try {
+        auto v = wrongRank.view();
+        nn::embeddingLookup<T>(queue, nullptr, idv, table, v);
+    } catch (std::invalid_argument const&) {
+        threw = true;
+    }
+    REQUIRE(threw);
+    threw = false;
+    try {
+        auto qv = out.view();
+        nn::attentionScores<T>(queue, nullptr, qv, qv, qv, 0u);
+    } catch (std::invalid_argument const&) {
+        threw = true;
+    }
+    REQUIRE(threw);
+}
+
+template <typename T>
+static void all(b200::Queue& queue) {
+    gqaKnownAnswers<T>(queue);
+    pipeline<T>(queue, false);
+    pipeline<T>(queue, true);
+    softmaxStability<T>(queue);
+    qkvRope<T>(queue);
+    rmsNorm<T>(queue);
+    embedding<T>(queue);
+}
+
+int main() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        std::fprintf(stderr, "no CUDA device\n");
+        return 2;
+    }
+    b200::Queue queue(0);
+    all<float>(queue);
+    all<double>(queue);
+    std::printf("%d checks, %d failures\n", g_checks, g_failures);
+    return g_failures == 0 ? 0 : 1;
+}
