@@ -25,6 +25,10 @@
 #include "tma.cuh"
 
 namespace ann {
+
+int prefill_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
+                   uint32_t g, int layout, int causal, bool& handled);
+
 namespace {
 
 __device__ unsigned int g_prefill_error;
@@ -339,6 +343,11 @@ int prefill(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const a
         al = al && (q.str[i] * eb) % 16 == 0 && (k.str[i] * eb) % 16 == 0 && (v.str[i] * eb) % 16 == 0;
     if (!unit || !al)
         return fail(ANN_ENOTSUP, "attention prefill needs unit-stride head vectors and 16-byte aligned rows.");
+    if constexpr (sizeof(T) == 4) {  // fp32: tcgen05 3xTF32 kernel when TMA can describe K and V
+        bool handled = false;
+        int const rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+        if (handled || rc != ANN_OK) return rc;
+    }
     PrefillArgs a{};
     a.q = q.data;
     a.k = k.data;

@@ -20,6 +20,17 @@ def ann():
     return alpakann_b200
 
 
+@pytest.fixture(params=["tensor", "fma"], autouse=True)
+def kernel(request, monkeypatch):
+    """fp32 runs on the tcgen05 3xTF32 kernel by default; ANN_PREFILL_FMA=1
+    selects the FMA kernel (fp64 always runs on DFMA)."""
+    if request.param == "fma":
+        monkeypatch.setenv("ANN_PREFILL_FMA", "1")
+    else:
+        monkeypatch.delenv("ANN_PREFILL_FMA", raising=False)
+    return request.param
+
+
 def dev(a):
     import torch
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
