@@ -7,10 +7,12 @@
 // is stored as hi = tf32(x) and lo = x - hi, and each product uses
 // hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-22 relative).
 //
-// One CTA (4 warps, one query row per thread = one TMEM lane) owns 128 query
-// rows of one (batch, head):
+// One CTA owns 128 query rows of one (batch, head): warps 0..3 hold one query
+// row per thread (= one TMEM lane) and do the hi/lo splits and the softmax;
+// warp 4 issues the TMA copies and the MMAs (warp specialisation, so the MMA
+// issue stream never waits behind the softmax):
 //   TMEM  [Q_hi | Q_lo | S (32) | P_hi (32) | P_lo (32) | O (D)]   <= 480 of 512 columns
-//   smem  raw K/V tiles of 32 keys, two stages, written by 4-D TMA in the
+//   smem  raw K/V tiles of 32 keys, kRaw stages each, written by 4-D TMA in the
 //         layouts the MMA reads (K: 128-byte swizzle, 16-byte chunks, K-major;
 //         V: 128-byte swizzle, 32-byte chunks, MN-major); split once into
 //         K_hi/K_lo/V_hi/V_lo with the same layouts
@@ -44,26 +46,32 @@ namespace {
 
 __device__ unsigned int g_tc_error;
 
-constexpr int kBM = 128, kBN = 32, kThreads = 128;
+constexpr int kBM = 128, kBN = 32;
+constexpr int kRaw = 4;  // raw K / V stages (TMA prefetch depth in key tiles)
+constexpr int kSoftmaxThreads = 128;                 // warps 0..3: one query row (TMEM lane) per thread
+constexpr int kThreads = kSoftmaxThreads + 32;       // warp 4: TMA + MMA producer
 constexpr float kLazy = 8.0f;  // rescale O only when the running max grows by more than this
 
 template <int D>
 struct TcCfg {
     static constexpr int TILE = kBN * D * 4;  // bytes of one K or V tile
-    static constexpr int OFF_RAWK = 0;        // 2 stages
-    static constexpr int OFF_RAWV = 2 * TILE;  // 2 stages
-    static constexpr int OFF_KHI = 4 * TILE;
-    static constexpr int OFF_KLO = 5 * TILE;
-    static constexpr int OFF_VHI = 6 * TILE;
-    static constexpr int OFF_VLO = 7 * TILE;
-    static constexpr int OFF_BAR = 8 * TILE;  // barK[2], barV[2], barS, barPV
-    static constexpr int OFF_SLOT = OFF_BAR + 6 * 8;
-    static constexpr int USED = OFF_SLOT + 16;
-    // + 1 KB for aligning the base to the 1 KB swizzle atom; at least 120 KB so
-    // that a single CTA is resident per SM (it allocates all 512 TMEM columns)
+    static constexpr int OFF_RAWK = 0;               // kRaw stages
+    static constexpr int OFF_RAWV = kRaw * TILE;     // kRaw stages
+    static constexpr int OFF_KHI = 2 * kRaw * TILE;
+    static constexpr int OFF_KLO = OFF_KHI + TILE;
+    static constexpr int OFF_VHI = OFF_KHI + 2 * TILE;
+    static constexpr int OFF_VLO = OFF_KHI + 3 * TILE;
+    static constexpr int OFF_BAR = OFF_KHI + 4 * TILE;
+    // barriers: kfull[kRaw] vfull[kRaw] kready vready sfull[2] sfree[2] pfull pvdone
+    static constexpr int NBAR = 2 * kRaw + 8;
+    static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag, progress counters
+    static constexpr int USED = OFF_SLOT + 32;
+    // + 1 KB to align the base to the 1 KB swizzle atom; >= 120 KB so that a
+    // single CTA is resident per SM (it allocates all 512 TMEM columns)
     static constexpr int SMEM = USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024;
-    static constexpr uint32_t Q_HI = 0, Q_LO = D, S_COL = 2 * D, P_HI = 2 * D + 32, P_LO = 2 * D + 64,
-                              O_COL = 2 * D + 96;
+    // TMEM columns: Q_hi | Q_lo | S[0] | S[1] | P_hi | P_lo | O
+    static constexpr uint32_t Q_HI = 0, Q_LO = D, S_COL = 2 * D, P_HI = 2 * D + 2 * kBN, P_LO = 2 * D + 3 * kBN,
+                              O_COL = 2 * D + 4 * kBN;
     static constexpr uint32_t TMEM_COLS = 512;
     static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
     static constexpr uint32_t IDESC_S = tc::idesc_tf32(kBM, kBN, false);
@@ -82,6 +90,13 @@ struct TcArgs {
     int q_tiles;
 };
 
+// Pipeline per key tile t (tensor pipe order S(0), S(1), PV(0), S(2), PV(1), ...):
+//   producer : wait kready(t) -> TMA K(t+kRaw) -> [sfree(t-2)] -> S(t) = Q K^T -> commit sfull[t%2]
+//              wait pfull(t-1), vready(t-1) -> O += P V (t-1) -> commit pvdone -> TMA V(t-1+kRaw)
+//   softmax  : wait sfull(t) -> split K(t+1) -> kready      (lets S(t+1) start at once)
+//              wait pvdone(t-1), vfull(t) -> split V(t) -> vready
+//              S(t) -> registers -> sfree; scale, mask, online softmax, lazy O rescale
+//              P_hi, P_lo -> TMEM -> pfull
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, TcArgs a,
@@ -92,21 +107,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t const pad = (1024u - (raw_base & 1023u)) & 1023u;
     unsigned char* smem = smem_raw + pad;
     uint32_t const sbase = raw_base + pad;
-    uint32_t const barK0 = sbase + C::OFF_BAR, barV0 = barK0 + 16, barS = barK0 + 32, barPV = barK0 + 40;
+    uint32_t const bar = sbase + C::OFF_BAR;
+    uint32_t const kfull = bar, vfull = bar + 8 * kRaw, kready = bar + 16 * kRaw, vready = kready + 8,
+                   sfull = kready + 16, sfree = kready + 32, pfull = kready + 48, pvdone = kready + 56;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
+    volatile int* prog = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 8);  // [0] K issued [1] V issued
+                                                                                 // [2] K waited [3] V waited
+                                                                                 // [4] last commit: 1 + 2*group
 
     int const tid = threadIdx.x, warp = tid >> 5;
     int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);
     int64_t const bh = blockIdx.y;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
-    int64_t const qi = q0 + tid;  // this thread's query row
     int64_t const k_end = a.causal ? (a.Tk < q0 + kBM ? a.Tk : q0 + kBM) : a.Tk;
     int const n_kt = static_cast<int>((k_end + kBN - 1) / kBN);
 
     if (tid == 0) {
-        for (int i = 0; i < 6; ++i) mbar_init(barK0 + 8 * i, 1);
+        for (int i = 0; i < 2 * kRaw; ++i) mbar_init(bar + 8 * i, 1);  // kfull, vfull
+        mbar_init(kready, kSoftmaxThreads);
+        mbar_init(vready, kSoftmaxThreads);
+        for (int i = 0; i < 2; ++i) mbar_init(sfull + 8 * i, 1);
+        for (int i = 0; i < 2; ++i) mbar_init(sfree + 8 * i, kSoftmaxThreads);
+        mbar_init(pfull, kSoftmaxThreads);
+        mbar_init(pvdone, 1);
         fence_mbar_init();
+        *abort = 0;
+        for (int i = 0; i < 5; ++i) prog[i] = 0;
     }
     if (warp == 0) {
         tc::tmem_alloc(smem_u32(slot), C::TMEM_COLS);
@@ -116,200 +144,239 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     uint32_t const tmem = *slot;
-    uint32_t const lane_off = static_cast<uint32_t>(warp * 32) << 16;
 
-    auto issue_tile = [&](CUtensorMap const* map, uint32_t dst, uint32_t bar, int kt) {
-        mbar_arrive_expect_tx(bar, C::TILE);
-        int const t0 = kt * kBN;
-        for (int blk = 0; blk < D / 32; ++blk) {
-            uint32_t const d = dst + blk * (kBN * 128);
-            if (a.kv_bthd)
-                tc::tma_load_4d(d, map, blk * 32, static_cast<int>(kvh), t0, static_cast<int>(b), bar);
-            else
-                tc::tma_load_4d(d, map, blk * 32, t0, static_cast<int>(kvh), static_cast<int>(b), bar);
-        }
-    };
-    if (tid == 0) {
-        for (int kt = 0; kt < (n_kt < 2 ? n_kt : 2); ++kt) {
-            issue_tile(&kmap, sbase + C::OFF_RAWK + kt * C::TILE, barK0 + 8 * kt, kt);
-            issue_tile(&vmap, sbase + C::OFF_RAWV + kt * C::TILE, barV0 + 8 * kt, kt);
-        }
-    }
-
-    // Q row -> TMEM as hi / lo (A operand of S = Q K^T)
-    {
-        float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h;
-        bool const live = qi < a.Tq;
+    if (warp == 4) {
+        // ================================ producer ================================
+        if ((tid & 31) == 0) {
+            auto issue_tile = [&](CUtensorMap const* map, uint32_t dst, uint32_t b_, int kt) {
+                mbar_arrive_expect_tx(b_, C::TILE);
+                int const t0 = kt * kBN;
+                for (int blk = 0; blk < D / 32; ++blk) {
+                    uint32_t const d = dst + blk * (kBN * 128);
+                    if (a.kv_bthd)
+                        tc::tma_load_4d(d, map, blk * 32, static_cast<int>(kvh), t0, static_cast<int>(b), b_);
+                    else
+                        tc::tma_load_4d(d, map, blk * 32, t0, static_cast<int>(kvh), static_cast<int>(b), b_);
+                }
+            };
+            auto issue_pv = [&](int t) {  // O += P V for tile t
+                tc::fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-            float hi[32], lo[32];
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                float4 const x = live ? *reinterpret_cast<float4 const*>(qrow + 32 * c + j) : make_float4(0, 0, 0, 0);
-                float const xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    hi[j + e] = tc::to_tf32(xs[e]);
-                    lo[j + e] = xs[e] - hi[j + e];
+                for (int kk = 0; kk < kBN / 8; ++kk) {
+                    uint64_t const vhi = tc::smem_desc(sbase + C::OFF_VHI + kk * 1024, kBN * 128, 512,
+                                                       tc::kSwizzle128B_32B);
+                    uint64_t const vlo = tc::smem_desc(sbase + C::OFF_VLO + kk * 1024, kBN * 128, 512,
+                                                       tc::kSwizzle128B_32B);
+                    uint32_t const d = tmem + C::O_COL;
+                    tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vhi, C::IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vlo, C::IDESC_PV, 1);
+                    tc::mma_tf32_ts(d, tmem + C::P_LO + 8 * kk, vhi, C::IDESC_PV, 1);
+                }
+                tc::mma_commit(pvdone);
+                prog[4] = 2 + 2 * t;  // pvdone, phase t & 1
+            };
+            int const pre = n_kt < kRaw ? n_kt : kRaw;
+            for (int kt = 0; kt < pre; ++kt) {
+                issue_tile(&kmap, sbase + C::OFF_RAWK + kt * C::TILE, kfull + 8 * kt, kt);
+                issue_tile(&vmap, sbase + C::OFF_RAWV + kt * C::TILE, vfull + 8 * kt, kt);
+            }
+            prog[0] = pre;
+            prog[1] = pre;
+            bool ok = true;
+            for (int t = 0; t < n_kt && ok; ++t) {
+                ok = mbar_wait_or_abort(kready, t & 1, abort);
+                if (!ok) break;
+                if (t + kRaw < n_kt) {  // split K(t) has consumed raw stage t % kRaw
+                    int const st = t % kRaw;
+                    issue_tile(&kmap, sbase + C::OFF_RAWK + st * C::TILE, kfull + 8 * st, t + kRaw);
+                    prog[0] = t + kRaw + 1;
+                }
+                if (t >= 2) ok = mbar_wait_or_abort(sfree + 8 * (t & 1), ((t - 2) >> 1) & 1, abort);
+                if (!ok) break;
+                tc::fence_after_sync();
+                uint32_t const d = tmem + C::S_COL + (t & 1) * kBN;
+#pragma unroll 1
+                for (int kk = 0; kk < D / 8; ++kk) {
+                    uint32_t const boff = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
+                    uint64_t const khi = tc::smem_desc(sbase + C::OFF_KHI + boff, 16, 1024, tc::kSwizzle128B);
+                    uint64_t const klo = tc::smem_desc(sbase + C::OFF_KLO + boff, 16, 1024, tc::kSwizzle128B);
+                    tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, khi, C::IDESC_S, kk > 0);
+                    tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, klo, C::IDESC_S, 1);
+                    tc::mma_tf32_ts(d, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1);
+                }
+                tc::mma_commit(sfull + 8 * (t & 1));
+                prog[4] = 1 + 2 * t;  // sfull[t & 1], phase (t >> 1) & 1
+                if (t >= 1) {
+                    ok = mbar_wait_or_abort(pfull, (t - 1) & 1, abort) &&
+                         mbar_wait_or_abort(vready, (t - 1) & 1, abort);
+                    if (!ok) break;
+                    issue_pv(t - 1);
+                    if (t - 1 + kRaw < n_kt) {  // split V(t-1) has consumed raw stage (t-1) % kRaw
+                        int const st = (t - 1) % kRaw;
+                        issue_tile(&vmap, sbase + C::OFF_RAWV + st * C::TILE, vfull + 8 * st, t - 1 + kRaw);
+                        prog[1] = t + kRaw;
+                    }
                 }
             }
-            tc::tmem_st32(tmem + lane_off + C::Q_HI + 32 * c, hi);
-            tc::tmem_st32(tmem + lane_off + C::Q_LO + 32 * c, lo);
-        }
-        tc::tmem_st_wait();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-
-    float m_used = Lowest<float>::value, l_sum = 0.f;
-    bool ok = true;
-    int pending_s = 0, pending_pv = 0;  // MMA groups issued and not yet waited (thread 0 tracks)
-    int waited_k = 0, waited_v = 0;     // TMA tiles waited so far
-
-    auto split_tile = [&](int raw_off, int hi_off, int lo_off) {
-        float4 const* raw = reinterpret_cast<float4 const*>(smem + raw_off);
-        float4* hi = reinterpret_cast<float4*>(smem + hi_off);
-        float4* lo = reinterpret_cast<float4*>(smem + lo_off);
-#pragma unroll 4
-        for (int i = tid; i < C::TILE / 16; i += kThreads) {
-            float4 const x = raw[i];
-            float4 h, l;
-            h.x = tc::to_tf32(x.x); h.y = tc::to_tf32(x.y); h.z = tc::to_tf32(x.z); h.w = tc::to_tf32(x.w);
-            l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
-            hi[i] = h;
-            lo[i] = l;
-        }
-        tc::fence_proxy_async_smem();
-    };
-
-    for (int t = 0; t < n_kt; ++t) {
-        int const s = t & 1;
-        uint32_t const par = (t >> 1) & 1;
-        // ---- K tile -> S = Q K^T -------------------------------------------------
-        ok = mbar_wait_bounded(barK0 + 8 * s, par);
-        if (__syncthreads_or(!ok)) break;
-        waited_k = t + 1;
-        split_tile(C::OFF_RAWK + s * C::TILE, C::OFF_KHI, C::OFF_KLO);
-        __syncthreads();
-        if (tid == 0) {
-            if (t + 2 < n_kt) issue_tile(&kmap, sbase + C::OFF_RAWK + s * C::TILE, barK0 + 8 * s, t + 2);
-            tc::fence_after_sync();
-#pragma unroll 1
-            for (int kk = 0; kk < D / 8; ++kk) {
-                uint32_t const boff = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-                uint64_t const khi = tc::smem_desc(sbase + C::OFF_KHI + boff, 16, 1024, tc::kSwizzle128B);
-                uint64_t const klo = tc::smem_desc(sbase + C::OFF_KLO + boff, 16, 1024, tc::kSwizzle128B);
-                uint32_t const d = tmem + C::S_COL;
-                tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, khi, C::IDESC_S, kk > 0);
-                tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, klo, C::IDESC_S, 1);
-                tc::mma_tf32_ts(d, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1);
+            if (ok && n_kt > 0) {
+                ok = mbar_wait_or_abort(pfull, (n_kt - 1) & 1, abort) &&
+                     mbar_wait_or_abort(vready, (n_kt - 1) & 1, abort);
+                if (ok) issue_pv(n_kt - 1);
             }
-            tc::mma_commit(barS);
         }
-        pending_s = 1;
-        // ---- V tile split (overlaps the S MMAs); needs the previous P V done ------
-        ok = mbar_wait_bounded(barV0 + 8 * s, par);
-        if (ok && t > 0) ok = mbar_wait_bounded(barPV, (t - 1) & 1);
-        if (__syncthreads_or(!ok)) break;
-        waited_v = t + 1;
-        pending_pv = 0;
-        tc::fence_after_sync();
-        split_tile(C::OFF_RAWV + s * C::TILE, C::OFF_VHI, C::OFF_VLO);
-        // ---- softmax on S ------------------------------------------------------------
-        ok = mbar_wait_bounded(barS, t & 1);
-        if (__syncthreads_or(!ok)) break;
-        pending_s = 0;
-        tc::fence_after_sync();
-        float sv[32];
-        tc::tmem_ld32(tmem + lane_off + C::S_COL, sv);
-        int64_t const key0 = static_cast<int64_t>(t) * kBN;
-        float tmax = Lowest<float>::value;
-        bool live[32];
+    } else {
+        // ======================= softmax / split warps (0..3) =======================
+        uint32_t const lane_off = static_cast<uint32_t>(warp * 32) << 16;
+        int64_t const qi = q0 + tid;
+        // Q row -> TMEM as hi / lo (A operand of S = Q K^T)
+        {
+            float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h;
+            bool const live = qi < a.Tq;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                float hi[32], lo[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            int64_t const kj = key0 + j;
-            live[j] = kj < a.Tk && !(a.causal && qi < kj);
-            sv[j] = sv[j] * scale;  // attentionScores, then ops::scale
-            if (live[j]) tmax = fmaxf(tmax, sv[j]);
+                for (int j = 0; j < 32; j += 4) {
+                    float4 const x =
+                        live ? *reinterpret_cast<float4 const*>(qrow + 32 * c + j) : make_float4(0, 0, 0, 0);
+                    float const xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        hi[j + e] = tc::to_tf32(xs[e]);
+                        lo[j + e] = xs[e] - hi[j + e];
+                    }
+                }
+                tc::tmem_st32(tmem + lane_off + C::Q_HI + 32 * c, hi);
+                tc::tmem_st32(tmem + lane_off + C::Q_LO + 32 * c, lo);
+            }
+            tc::tmem_st_wait();
+            tc::fence_before_sync();
         }
-        bool const grow = tmax > m_used + kLazy;
-        float alpha = 1.f;
-        if (grow) {
-            alpha = expf(m_used - tmax);
-            m_used = tmax;
-            l_sum *= alpha;
+        auto split = [&](int raw_off, int hi_off, int lo_off) {
+            float4 const* raw = reinterpret_cast<float4 const*>(smem + raw_off);
+            float4* hi = reinterpret_cast<float4*>(smem + hi_off);
+            float4* lo = reinterpret_cast<float4*>(smem + lo_off);
+#pragma unroll 4
+            for (int i = tid; i < C::TILE / 16; i += kSoftmaxThreads) {
+                float4 const x = raw[i];
+                float4 h, l;
+                h.x = tc::to_tf32(x.x); h.y = tc::to_tf32(x.y); h.z = tc::to_tf32(x.z); h.w = tc::to_tf32(x.w);
+                l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+                hi[i] = h;
+                lo[i] = l;
+            }
+            tc::fence_proxy_async_smem();  // make the split visible to the tensor core
+        };
+        // Decisions after a wait are made warp-uniform (__all_sync): the tcgen05.ld/st
+        // that follow are warp-collective, so a warp must never split on an abort.
+        auto split_k = [&](int t) {
+            int const st = t % kRaw;
+            bool const w = __all_sync(0xffffffffu, mbar_wait_or_abort(kfull + 8 * st, (t / kRaw) & 1, abort));
+            if (w) {
+                if (tid == 0) prog[2] = t + 1;
+                split(C::OFF_RAWK + st * C::TILE, C::OFF_KHI, C::OFF_KLO);
+            }
+            mbar_arrive(kready);
+            return w;
+        };
+        float m_used = Lowest<float>::value, l_sum = 0.f;
+        bool ok = n_kt == 0 || split_k(0);
+        for (int t = 0; t < n_kt && ok; ++t) {
+            ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * (t & 1), (t >> 1) & 1, abort));
+            if (!ok) break;  // S(t) done: K_hi/K_lo free
+            tc::fence_after_sync();
+            if (t + 1 < n_kt && !split_k(t + 1)) {
+                ok = false;
+                break;
+            }
+            ok = (t == 0 || mbar_wait_or_abort(pvdone, (t - 1) & 1, abort)) &&
+                 mbar_wait_or_abort(vfull + 8 * (t % kRaw), (t / kRaw) & 1, abort);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc::fence_after_sync();
+            if (tid == 0) prog[3] = t + 1;
+            split(C::OFF_RAWV + (t % kRaw) * C::TILE, C::OFF_VHI, C::OFF_VLO);
+            mbar_arrive(vready);
+
+            float sv[32];
+            tc::tmem_ld32(tmem + lane_off + C::S_COL + (t & 1) * kBN, sv);
+            tc::fence_before_sync();
+            mbar_arrive(sfree + 8 * (t & 1));
+            int64_t const key0 = static_cast<int64_t>(t) * kBN;
+            float tmax = Lowest<float>::value;
+            bool live[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                int64_t const kj = key0 + j;
+                live[j] = kj < a.Tk && !(a.causal && qi < kj);
+                sv[j] = sv[j] * scale;  // attentionScores, then ops::scale
+                if (live[j]) tmax = fmaxf(tmax, sv[j]);
+            }
+            bool const grow = tmax > m_used + kLazy;
+            float alpha = 1.f;
+            if (grow) {
+                alpha = expf(m_used - tmax);
+                m_used = tmax;
+                l_sum *= alpha;
+            }
+            if (t > 0 && __any_sync(0xffffffffu, grow)) {  // warp-uniform: tcgen05.ld/st are warp-collective
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    float ov[32];
+                    tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+                    tc::tmem_st32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                }
+            }
+            float phi[32], plo[32], psum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                float const p = live[j] ? expf(sv[j] - m_used) : 0.f;
+                psum += p;
+                phi[j] = tc::to_tf32(p);
+                plo[j] = p - phi[j];
+            }
+            l_sum += psum;
+            tc::tmem_st32(tmem + lane_off + C::P_HI, phi);
+            tc::tmem_st32(tmem + lane_off + C::P_LO, plo);
+            tc::tmem_st_wait();
+            tc::fence_before_sync();
+            mbar_arrive(pfull);
         }
-        if (t > 0 && __any_sync(0xffffffffu, grow)) {  // warp-uniform: tcgen05.ld/st are warp-collective
+        if (ok && n_kt > 0) ok = mbar_wait_or_abort(pvdone, (n_kt - 1) & 1, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            tc::fence_after_sync();
+            float* orow = static_cast<float*>(a.out) + b * a.o_b + qi * a.o_t + hq * a.o_h;
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
                 float ov[32];
                 tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                if (qi < a.Tq) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-                tc::tmem_st32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                    for (int j = 0; j < 32; ++j) orow[(32 * c + j) * a.o_d] = l_sum > 0.f ? ov[j] / l_sum : 0.f;
+                }
             }
         }
-        float phi[32], plo[32], psum = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float const p = live[j] ? expf(sv[j] - m_used) : 0.f;
-            psum += p;
-            phi[j] = tc::to_tf32(p);
-            plo[j] = p - phi[j];
-        }
-        l_sum += psum;
-        tc::tmem_st32(tmem + lane_off + C::P_HI, phi);
-        tc::tmem_st32(tmem + lane_off + C::P_LO, plo);
-        tc::tmem_st_wait();
-        tc::fence_before_sync();
-        __syncthreads();
-        // ---- O += P V ------------------------------------------------------------------
-        if (tid == 0) {
-            if (t + 2 < n_kt) issue_tile(&vmap, sbase + C::OFF_RAWV + s * C::TILE, barV0 + 8 * s, t + 2);
-            tc::fence_after_sync();
-#pragma unroll 1
-            for (int kk = 0; kk < kBN / 8; ++kk) {
-                uint64_t const vhi = tc::smem_desc(sbase + C::OFF_VHI + kk * 1024, kBN * 128, 512, tc::kSwizzle128B_32B);
-                uint64_t const vlo = tc::smem_desc(sbase + C::OFF_VLO + kk * 1024, kBN * 128, 512, tc::kSwizzle128B_32B);
-                uint32_t const d = tmem + C::O_COL;
-                tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vhi, C::IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-                tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vlo, C::IDESC_PV, 1);
-                tc::mma_tf32_ts(d, tmem + C::P_LO + 8 * kk, vhi, C::IDESC_PV, 1);
-            }
-            tc::mma_commit(barPV);
-        }
-        pending_pv = 1;
     }
 
-    if (ok && n_kt > 0) {
-        ok = mbar_wait_bounded(barPV, (n_kt - 1) & 1);
-        ok = !__syncthreads_or(!ok);
-        if (ok) pending_pv = 0;
-    }
-    if (ok) {
-        tc::fence_after_sync();
-        float* orow = static_cast<float*>(a.out) + b * a.o_b + qi * a.o_t + hq * a.o_h;
-        float const inv_ok = l_sum > 0.f ? 1.f : 0.f;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-            float ov[32];
-            tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
-            if (qi < a.Tq) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) orow[(32 * c + j) * a.o_d] = inv_ok > 0.f ? ov[j] / l_sum : 0.f;
-            }
-        }
-    } else if (tid == 0) {
-        atomicOr(&g_tc_error, ANN_DEVERR_WAIT_TIMEOUT);
-        // drain: copies and MMAs still in flight must land before the CTA leaves
-        for (int t = waited_k; t < (n_kt < waited_k + 2 ? n_kt : waited_k + 2); ++t)
-            mbar_wait_bounded(barK0 + 8 * (t & 1), (t >> 1) & 1);
-        for (int t = waited_v; t < (n_kt < waited_v + 2 ? n_kt : waited_v + 2); ++t)
-            mbar_wait_bounded(barV0 + 8 * (t & 1), (t >> 1) & 1);
-        if (pending_s) mbar_wait_bounded(barS, (waited_k - 1) & 1);
-        if (pending_pv) mbar_wait_bounded(barPV, (waited_v - 1) & 1);
-    }
     tc::fence_before_sync();
+    __syncthreads();
+    if (*abort && tid == kSoftmaxThreads) {
+        // A wait gave up: drain the copies and MMAs still in flight before the TMEM goes.
+        atomicOr(&g_tc_error, ANN_DEVERR_WAIT_TIMEOUT);
+        for (int t = prog[2]; t < prog[0]; ++t) mbar_wait_bounded(kfull + 8 * (t % kRaw), (t / kRaw) & 1);
+        for (int t = prog[3]; t < prog[1]; ++t) mbar_wait_bounded(vfull + 8 * (t % kRaw), (t / kRaw) & 1);
+        int const last = prog[4];
+        if (last > 0) {
+            int const g = (last - 1) >> 1;
+            if ((last & 1) == 1)
+                mbar_wait_bounded(sfull + 8 * (g & 1), (g >> 1) & 1);
+            else
+                mbar_wait_bounded(pvdone, g & 1);
+        }
+    }
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
