@@ -3,32 +3,33 @@
 // Same pipeline and semantics as prefill.cu (attentionScores -> ops::scale ->
 // causalSoftmax with the top-left mask / softmax -> attentionApply, reference
 // test/unit/nn/attention.cpp:591-651), with both contractions on tcgen05.mma
-// kind::tf32 and fp32 accuracy kept by the 3xTF32 split: every fp32 operand x
-// is stored as hi = tf32(x) and lo = x - hi, and each product uses
-// hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-22 relative).
+// kind::tf32 and fp32 accuracy kept by the 3xTF32 split x = hi + lo, each
+// product taken as hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-21
+// relative). A kind::tf32 MMA reads an fp32 operand by dropping its low 13
+// mantissa bits, so the raw fp32 value serves as hi as it stands and only
+// lo = x - trunc13(x) (exact in fp32, stored rounded to tf32) is computed.
 //
-// One CTA owns 128 query rows of one (batch, head): warps 0..3 hold one query
-// row per thread (= one TMEM lane) and do the hi/lo splits and the softmax;
-// warp 4 issues the TMA copies and the MMAs (warp specialisation, so the MMA
-// issue stream never waits behind the softmax):
-//   TMEM  [Q_hi | Q_lo | S (32) | P_hi (32) | P_lo (32) | O (D)]   <= 480 of 512 columns
-//   smem  raw K/V tiles of 32 keys, kRaw stages each, written by 4-D TMA in the
-//         layouts the MMA reads (K: 128-byte swizzle, 16-byte chunks, K-major;
-//         V: 128-byte swizzle, 32-byte chunks, MN-major); split once into
-//         K_hi/K_lo/V_hi/V_lo with the same layouts
-// Per key tile:
-//   K raw -> split -> S = Q K^T      (A = Q from TMEM, B = K K-major, N = 32)
-//   V raw -> split (overlaps the S MMAs)
-//   S -> registers (tcgen05.ld): scale, top-left mask, online softmax with a
-//        lazy rescale (O and l are rescaled only when the running max grows by
-//        more than 8, exact because O and l share the reference max)
-//   P_hi, P_lo -> TMEM (tcgen05.st);  O += P V   (A = P from TMEM, B = V MN-major)
-// MMAs are issued by one thread and complete on mbarriers (tcgen05.commit);
-// every wait is bounded, and on a timeout the CTA drains, frees its TMEM and
-// reports ANN_DEVERR_WAIT_TIMEOUT.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
+// One CTA owns 128 query rows of one (batch, head) and walks its keys in tiles
+// of 64, with three warp roles:
+//   warps 0..3  one query row per thread (= one TMEM lane): Q -> TMEM, then per
+//               tile S -> registers, scale, top-left mask, online softmax with a
+//               lazy rescale (O and l are rescaled only when the running max
+//               grows by more than 8, exact because O and l share the max used),
+//               P_hi -> TMEM, P_lo -> shared memory
+//   warps 4..11 K / V tiles global -> registers (one tile ahead) -> shared memory
+//               as hi (raw) and lo, in the layouts the MMA reads (K: K-major,
+//               128-byte swizzle; V: MN-major, 128-byte swizzle of 32-byte chunks)
+//   warp 12     one thread issues every MMA; completion comes back on mbarriers
+//               (tcgen05.commit)
+//   TMEM  [Q_hi | Q_lo | O | S (64) | P_hi (64)]   = 512 columns for D = 128
+//   smem  K hi/lo x 2 buffers | V hi/lo | P_lo     = 224 KB for D = 128
+// Tensor-pipe order S(0) S(1) PV(0) S(2) PV(1) ...: the softmax of tile t and
+// the V split run while S(t+1) and PV(t-1) execute. Per 64-key tile the MMAs
+// are S: 3 x D/8 of M128 N64 K8 (A = Q from TMEM) and PV: 3 x 8 of M128 N=D K8
+// (A = P_hi from TMEM, P_lo from shared memory).
+// Every wait is bounded; on a timeout the CTA stops, waits for its issued MMAs,
+// frees its TMEM and reports ANN_DEVERR_WAIT_TIMEOUT.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -46,34 +47,33 @@ namespace {
 
 __device__ unsigned int g_tc_error;
 
-constexpr int kBM = 128, kBN = 32;
-constexpr int kRaw = 4;  // raw K / V stages (TMA prefetch depth in key tiles)
-constexpr int kSoftmaxThreads = 128;                 // warps 0..3: one query row (TMEM lane) per thread
-constexpr int kThreads = kSoftmaxThreads + 32;       // warp 4: TMA + MMA producer
+constexpr int kBM = 128, kBN = 64;
+constexpr int kRowThreads = 128;    // warps 0..3
+constexpr int kSplitThreads = 256;  // warps 4..11
+constexpr int kThreads = kRowThreads + kSplitThreads + 32;
 constexpr float kLazy = 8.0f;  // rescale O only when the running max grows by more than this
 
 template <int D>
 struct TcCfg {
-    static constexpr int TILE = kBN * D * 4;  // bytes of one K or V tile
-    static constexpr int OFF_RAWK = 0;               // kRaw stages
-    static constexpr int OFF_RAWV = kRaw * TILE;     // kRaw stages
-    static constexpr int OFF_KHI = 2 * kRaw * TILE;
-    static constexpr int OFF_KLO = OFF_KHI + TILE;
-    static constexpr int OFF_VHI = OFF_KHI + 2 * TILE;
-    static constexpr int OFF_VLO = OFF_KHI + 3 * TILE;
-    static constexpr int OFF_BAR = OFF_KHI + 4 * TILE;
-    // barriers: kfull[kRaw] vfull[kRaw] kready vready sfull[2] sfree[2] pfull pvdone
-    static constexpr int NBAR = 2 * kRaw + 8;
-    static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag, progress counters
-    static constexpr int USED = OFF_SLOT + 32;
+    static constexpr int TILE = kBN * D * 4;  // bytes of one K or V tile (hi or lo)
+    static constexpr int BLK = kBN * 128;     // one 32-float column block of a tile: 64 rows x 128 B
+    static constexpr int OFF_K = 0;           // buffer i: hi at OFF_K + 2*i*TILE, lo at + TILE
+    static constexpr int OFF_V = 4 * TILE;    // hi, lo
+    static constexpr int OFF_PLO = 6 * TILE;  // P_lo: 128 rows x 64 keys as two 32-key blocks
+    static constexpr int PLO_BLK = kBM * 128;
+    static constexpr int OFF_BAR = OFF_PLO + 2 * PLO_BLK;
+    // barriers: qready kready[2] kfree[2] vready sfull sfree pfull pvdone drain
+    static constexpr int NBAR = 11;
+    static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
+    static constexpr int USED = OFF_SLOT + 16;
     // + 1 KB to align the base to the 1 KB swizzle atom; >= 120 KB so that a
     // single CTA is resident per SM (it allocates all 512 TMEM columns)
     static constexpr int SMEM = USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024;
-    // TMEM columns: Q_hi | Q_lo | S[0] | S[1] | P_hi | P_lo | O
-    static constexpr uint32_t Q_HI = 0, Q_LO = D, S_COL = 2 * D, P_HI = 2 * D + 2 * kBN, P_LO = 2 * D + 3 * kBN,
-                              O_COL = 2 * D + 4 * kBN;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    // TMEM columns
+    static constexpr uint32_t Q_HI = 0, Q_LO = D, O_COL = 2 * D, S_COL = 3 * D, P_HI = 3 * D + kBN;
     static constexpr uint32_t TMEM_COLS = 512;
-    static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
+    static_assert(P_HI + kBN <= TMEM_COLS, "TMEM budget");
     static constexpr uint32_t IDESC_S = tc::idesc_tf32(kBM, kBN, false);
     static constexpr uint32_t IDESC_PV = tc::idesc_tf32(kBM, D, true);
 };
@@ -81,26 +81,29 @@ struct TcCfg {
 struct TcArgs {
     void* out;
     const float* q;
+    const float* k;
+    const float* v;
     int64_t q_b, q_t, q_h;
+    int64_t k_b, k_t, k_h;
+    int64_t v_b, v_t, v_h;
     int64_t o_b, o_t, o_h, o_d;
     int64_t Tq, Tk, Hq;
     uint32_t g;
     int causal;
-    int kv_bthd;  // tensor-map coordinate order: 1 = (d, head, token, batch), 0 = (d, token, head, batch)
+    int o_vec;  // out rows are unit-stride and 16-byte aligned
     int q_tiles;
 };
 
-// Pipeline per key tile t (tensor pipe order S(0), S(1), PV(0), S(2), PV(1), ...):
-//   producer : wait kready(t) -> TMA K(t+kRaw) -> [sfree(t-2)] -> S(t) = Q K^T -> commit sfull[t%2]
-//              wait pfull(t-1), vready(t-1) -> O += P V (t-1) -> commit pvdone -> TMA V(t-1+kRaw)
-//   softmax  : wait sfull(t) -> split K(t+1) -> kready      (lets S(t+1) start at once)
-//              wait pvdone(t-1), vfull(t) -> split V(t) -> vready
-//              S(t) -> registers -> sfree; scale, mask, online softmax, lazy O rescale
-//              P_hi, P_lo -> TMEM -> pfull
+// lo part of the 3xTF32 split (hi is x itself, truncated by the tensor core)
+__device__ __forceinline__ float tf32_lo(float x) {
+    return tc::to_tf32(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+}
+__device__ __forceinline__ float4 tf32_lo(float4 x) {
+    return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
+
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, TcArgs a,
-                      float scale) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float scale) {
     using C = TcCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -108,16 +111,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* smem = smem_raw + pad;
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
-    uint32_t const kfull = bar, vfull = bar + 8 * kRaw, kready = bar + 16 * kRaw, vready = kready + 8,
-                   sfull = kready + 16, sfree = kready + 32, pfull = kready + 48, pvdone = kready + 56;
+    uint32_t const qready = bar, kready = bar + 8, kfree = bar + 24, vready = bar + 40, sfull = bar + 48,
+                   sfree = bar + 56, pfull = bar + 64, pvdone = bar + 72, drain = bar + 80;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
-    volatile int* prog = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 8);  // [0] K issued [1] V issued
-                                                                                 // [2] K waited [3] V waited
-                                                                                 // [4] last commit: 1 + 2*group
 
     int const tid = threadIdx.x, warp = tid >> 5;
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);
+    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);  // longest rows first
     int64_t const bh = blockIdx.y;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
@@ -125,16 +125,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     int const n_kt = static_cast<int>((k_end + kBN - 1) / kBN);
 
     if (tid == 0) {
-        for (int i = 0; i < 2 * kRaw; ++i) mbar_init(bar + 8 * i, 1);  // kfull, vfull
-        mbar_init(kready, kSoftmaxThreads);
-        mbar_init(vready, kSoftmaxThreads);
-        for (int i = 0; i < 2; ++i) mbar_init(sfull + 8 * i, 1);
-        for (int i = 0; i < 2; ++i) mbar_init(sfree + 8 * i, kSoftmaxThreads);
-        mbar_init(pfull, kSoftmaxThreads);
+        mbar_init(qready, kRowThreads);
+        for (int i = 0; i < 2; ++i) mbar_init(kready + 8 * i, kSplitThreads);
+        for (int i = 0; i < 2; ++i) mbar_init(kfree + 8 * i, 1);
+        mbar_init(vready, kSplitThreads);
+        mbar_init(sfull, 1);
+        mbar_init(sfree, kRowThreads);
+        mbar_init(pfull, kRowThreads);
         mbar_init(pvdone, 1);
+        mbar_init(drain, 1);
         fence_mbar_init();
         *abort = 0;
-        for (int i = 0; i < 5; ++i) prog[i] = 0;
     }
     if (warp == 0) {
         tc::tmem_alloc(smem_u32(slot), C::TMEM_COLS);
@@ -145,91 +146,141 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after_sync();
     uint32_t const tmem = *slot;
 
-    if (warp == 4) {
-        // ================================ producer ================================
+    if (warp == 12) {
+        // ================================ MMA issue ================================
         if ((tid & 31) == 0) {
-            auto issue_tile = [&](CUtensorMap const* map, uint32_t dst, uint32_t b_, int kt) {
-                mbar_arrive_expect_tx(b_, C::TILE);
-                int const t0 = kt * kBN;
-                for (int blk = 0; blk < D / 32; ++blk) {
-                    uint32_t const d = dst + blk * (kBN * 128);
-                    if (a.kv_bthd)
-                        tc::tma_load_4d(d, map, blk * 32, static_cast<int>(kvh), t0, static_cast<int>(b), b_);
-                    else
-                        tc::tma_load_4d(d, map, blk * 32, t0, static_cast<int>(kvh), static_cast<int>(b), b_);
+            // Descriptors are built once; a tile or k-step offset is added to the
+            // 14-bit start-address field (all of shared memory is < 2^18 bytes,
+            // so the field never carries).
+            uint64_t const k_desc = tc::smem_desc(sbase + C::OFF_K, 16, 1024, tc::kSwizzle128B);
+            uint64_t const v_desc = tc::smem_desc(sbase + C::OFF_V, C::BLK, 512, tc::kSwizzle128B_32B);
+            uint64_t const p_desc = tc::smem_desc(sbase + C::OFF_PLO, 16, 1024, tc::kSwizzle128B);
+            auto at = [](uint64_t desc, uint32_t off) { return desc + static_cast<uint64_t>(off >> 4); };
+            auto issue_s = [&](int t) {  // S = Q K^T (tile t)
+                uint32_t const kb = static_cast<uint32_t>(t & 1) * 2 * C::TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 8; ++kk) {
+                    uint32_t const off = kb + (kk >> 2) * C::BLK + (kk & 3) * 32;
+                    uint64_t const khi = at(k_desc, off), klo = at(k_desc, off + C::TILE);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_HI + 8 * kk, khi, C::IDESC_S, kk > 0 ? 1u : 0u);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_HI + 8 * kk, klo, C::IDESC_S, 1u);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1u);
                 }
+                tc::mma_commit(sfull);
+                tc::mma_commit(kfree + 8 * (t & 1));
             };
-            auto issue_pv = [&](int t) {  // O += P V for tile t
-                tc::fence_after_sync();
-#pragma unroll 1
+            auto issue_pv = [&](int t) {  // O += P V (tile t)
+#pragma unroll
                 for (int kk = 0; kk < kBN / 8; ++kk) {
-                    uint64_t const vhi = tc::smem_desc(sbase + C::OFF_VHI + kk * 1024, kBN * 128, 512,
-                                                       tc::kSwizzle128B_32B);
-                    uint64_t const vlo = tc::smem_desc(sbase + C::OFF_VLO + kk * 1024, kBN * 128, 512,
-                                                       tc::kSwizzle128B_32B);
-                    uint32_t const d = tmem + C::O_COL;
-                    tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vhi, C::IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-                    tc::mma_tf32_ts(d, tmem + C::P_HI + 8 * kk, vlo, C::IDESC_PV, 1);
-                    tc::mma_tf32_ts(d, tmem + C::P_LO + 8 * kk, vhi, C::IDESC_PV, 1);
+                    uint64_t const vhi = at(v_desc, kk * 1024), vlo = at(v_desc, C::TILE + kk * 1024);
+                    uint64_t const plo = at(p_desc, (kk >> 2) * C::PLO_BLK + (kk & 3) * 32);
+                    tc::mma_tf32_ts(tmem + C::O_COL, tmem + C::P_HI + 8 * kk, vhi, C::IDESC_PV,
+                                    (t > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_tf32_ts(tmem + C::O_COL, tmem + C::P_HI + 8 * kk, vlo, C::IDESC_PV, 1u);
+                    tc::mma_tf32_ss(tmem + C::O_COL, plo, vhi, C::IDESC_PV, 1u);
                 }
                 tc::mma_commit(pvdone);
-                prog[4] = 2 + 2 * t;  // pvdone, phase t & 1
             };
-            int const pre = n_kt < kRaw ? n_kt : kRaw;
-            for (int kt = 0; kt < pre; ++kt) {
-                issue_tile(&kmap, sbase + C::OFF_RAWK + kt * C::TILE, kfull + 8 * kt, kt);
-                issue_tile(&vmap, sbase + C::OFF_RAWV + kt * C::TILE, vfull + 8 * kt, kt);
-            }
-            prog[0] = pre;
-            prog[1] = pre;
-            bool ok = true;
+            bool ok = n_kt == 0 || mbar_wait_or_abort(qready, 0, abort);
             for (int t = 0; t < n_kt && ok; ++t) {
-                ok = mbar_wait_or_abort(kready, t & 1, abort);
-                if (!ok) break;
-                if (t + kRaw < n_kt) {  // split K(t) has consumed raw stage t % kRaw
-                    int const st = t % kRaw;
-                    issue_tile(&kmap, sbase + C::OFF_RAWK + st * C::TILE, kfull + 8 * st, t + kRaw);
-                    prog[0] = t + kRaw + 1;
-                }
-                if (t >= 2) ok = mbar_wait_or_abort(sfree + 8 * (t & 1), ((t - 2) >> 1) & 1, abort);
+                ok = mbar_wait_or_abort(kready + 8 * (t & 1), (t >> 1) & 1, abort) &&
+                     (t == 0 || mbar_wait_or_abort(sfree, (t - 1) & 1, abort));
                 if (!ok) break;
                 tc::fence_after_sync();
-                uint32_t const d = tmem + C::S_COL + (t & 1) * kBN;
-#pragma unroll 1
-                for (int kk = 0; kk < D / 8; ++kk) {
-                    uint32_t const boff = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-                    uint64_t const khi = tc::smem_desc(sbase + C::OFF_KHI + boff, 16, 1024, tc::kSwizzle128B);
-                    uint64_t const klo = tc::smem_desc(sbase + C::OFF_KLO + boff, 16, 1024, tc::kSwizzle128B);
-                    tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, khi, C::IDESC_S, kk > 0);
-                    tc::mma_tf32_ts(d, tmem + C::Q_HI + 8 * kk, klo, C::IDESC_S, 1);
-                    tc::mma_tf32_ts(d, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1);
-                }
-                tc::mma_commit(sfull + 8 * (t & 1));
-                prog[4] = 1 + 2 * t;  // sfull[t & 1], phase (t >> 1) & 1
+                issue_s(t);
                 if (t >= 1) {
                     ok = mbar_wait_or_abort(pfull, (t - 1) & 1, abort) &&
                          mbar_wait_or_abort(vready, (t - 1) & 1, abort);
                     if (!ok) break;
+                    tc::fence_after_sync();
                     issue_pv(t - 1);
-                    if (t - 1 + kRaw < n_kt) {  // split V(t-1) has consumed raw stage (t-1) % kRaw
-                        int const st = (t - 1) % kRaw;
-                        issue_tile(&vmap, sbase + C::OFF_RAWV + st * C::TILE, vfull + 8 * st, t - 1 + kRaw);
-                        prog[1] = t + kRaw;
-                    }
                 }
             }
             if (ok && n_kt > 0) {
                 ok = mbar_wait_or_abort(pfull, (n_kt - 1) & 1, abort) &&
                      mbar_wait_or_abort(vready, (n_kt - 1) & 1, abort);
-                if (ok) issue_pv(n_kt - 1);
+                if (ok) {
+                    tc::fence_after_sync();
+                    issue_pv(n_kt - 1);
+                }
             }
+            // every MMA issued above has finished reading TMEM and shared memory
+            // before either is released
+            tc::mma_commit(drain);
+            if (!mbar_wait_bounded(drain, 0)) *abort = 1;
+        }
+    } else if (warp >= 4) {
+        // ======================== K / V loads and splits (4..11) ========================
+        constexpr int NV4 = D / 4;                         // float4 per key row
+        constexpr int PER = kBN * NV4 / kSplitThreads;     // float4 per thread per tile
+        int const st = tid - kRowThreads;
+        float const* kbase = a.k + b * a.k_b + kvh * a.k_h;
+        float const* vbase = a.v + b * a.v_b + kvh * a.v_h;
+        float4 rk[PER], rv[PER];
+        // element e = i * kSplitThreads + st of a tile: key row e / NV4, float4 column e % NV4
+        // (a warp reads whole rows: coalesced)
+        auto load = [&](float4 (&r)[PER], float const* base, int64_t stride_t, int t) {
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int64_t const key = static_cast<int64_t>(t) * kBN + row;
+                r[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(base + key * stride_t) + c4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);  // V rows past Tk must be finite
+            }
+        };
+        auto store_k = [&](float4 const (&r)[PER], int buf) {  // K-major, 16-byte chunks XOR (row % 8)
+            unsigned char* hi = smem + C::OFF_K + buf * 2 * C::TILE;
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int const off = (c4 >> 3) * C::BLK + row * 128 + (((c4 & 7) ^ (row & 7)) << 4);
+                *reinterpret_cast<float4*>(hi + off) = r[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(r[i]);
+            }
+            tc::fence_proxy_async_smem();  // visible to the tensor core
+        };
+        auto store_v = [&](float4 const (&r)[PER]) {  // MN-major, 32-byte chunks XOR (row % 4)
+            unsigned char* hi = smem + C::OFF_V;
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int const off =
+                    (c4 >> 3) * C::BLK + row * 128 + ((((c4 & 7) >> 1) ^ (row & 3)) << 5) + ((c4 & 1) << 4);
+                *reinterpret_cast<float4*>(hi + off) = r[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(r[i]);
+            }
+            tc::fence_proxy_async_smem();
+        };
+        bool ok = true;
+        if (n_kt > 0) {
+            load(rk, kbase, a.k_t, 0);
+            load(rv, vbase, a.v_t, 0);
+            store_k(rk, 0);
+            mbar_arrive(kready);
+            if (n_kt > 1) load(rk, kbase, a.k_t, 1);
+        }
+        // iteration t: K(t+1) (needed by S(t+1), its buffer was read by S(t-1)),
+        // then V(t) (needed by PV(t), its buffer was read by PV(t-1))
+        for (int t = 0; t < n_kt && ok; ++t) {
+            if (t + 1 < n_kt) {
+                int const buf = (t + 1) & 1;
+                if (t >= 1) ok = mbar_wait_or_abort(kfree + 8 * buf, ((t - 1) >> 1) & 1, abort);
+                if (!ok) break;
+                store_k(rk, buf);
+                mbar_arrive(kready + 8 * buf);
+                if (t + 2 < n_kt) load(rk, kbase, a.k_t, t + 2);
+            }
+            if (t >= 1) ok = mbar_wait_or_abort(pvdone, (t - 1) & 1, abort);
+            if (!ok) break;
+            store_v(rv);
+            mbar_arrive(vready);
+            if (t + 1 < n_kt) load(rv, vbase, a.v_t, t + 1);
         }
     } else {
-        // ======================= softmax / split warps (0..3) =======================
+        // ============================ softmax rows (0..3) ============================
         uint32_t const lane_off = static_cast<uint32_t>(warp * 32) << 16;
         int64_t const qi = q0 + tid;
-        // Q row -> TMEM as hi / lo (A operand of S = Q K^T)
-        {
+        {  // Q row -> TMEM: hi (raw) and lo, the A operand of S = Q K^T
             float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h;
             bool const live = qi < a.Tq;
 #pragma unroll 1
@@ -237,80 +288,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float hi[32], lo[32];
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
-                    float4 const x =
-                        live ? *reinterpret_cast<float4 const*>(qrow + 32 * c + j) : make_float4(0, 0, 0, 0);
-                    float const xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        hi[j + e] = tc::to_tf32(xs[e]);
-                        lo[j + e] = xs[e] - hi[j + e];
-                    }
+                    float4 const x = live ? __ldg(reinterpret_cast<float4 const*>(qrow + 32 * c + j))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                    hi[j] = x.x, hi[j + 1] = x.y, hi[j + 2] = x.z, hi[j + 3] = x.w;
+                    lo[j] = tf32_lo(x.x), lo[j + 1] = tf32_lo(x.y), lo[j + 2] = tf32_lo(x.z),
+                    lo[j + 3] = tf32_lo(x.w);
                 }
                 tc::tmem_st32(tmem + lane_off + C::Q_HI + 32 * c, hi);
                 tc::tmem_st32(tmem + lane_off + C::Q_LO + 32 * c, lo);
             }
             tc::tmem_st_wait();
             tc::fence_before_sync();
+            mbar_arrive(qready);
         }
-        auto split = [&](int raw_off, int hi_off, int lo_off) {
-            float4 const* raw = reinterpret_cast<float4 const*>(smem + raw_off);
-            float4* hi = reinterpret_cast<float4*>(smem + hi_off);
-            float4* lo = reinterpret_cast<float4*>(smem + lo_off);
-#pragma unroll 4
-            for (int i = tid; i < C::TILE / 16; i += kSoftmaxThreads) {
-                float4 const x = raw[i];
-                float4 h, l;
-                h.x = tc::to_tf32(x.x); h.y = tc::to_tf32(x.y); h.z = tc::to_tf32(x.z); h.w = tc::to_tf32(x.w);
-                l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
-                hi[i] = h;
-                lo[i] = l;
-            }
-            tc::fence_proxy_async_smem();  // make the split visible to the tensor core
-        };
-        // Decisions after a wait are made warp-uniform (__all_sync): the tcgen05.ld/st
-        // that follow are warp-collective, so a warp must never split on an abort.
-        auto split_k = [&](int t) {
-            int const st = t % kRaw;
-            bool const w = __all_sync(0xffffffffu, mbar_wait_or_abort(kfull + 8 * st, (t / kRaw) & 1, abort));
-            if (w) {
-                if (tid == 0) prog[2] = t + 1;
-                split(C::OFF_RAWK + st * C::TILE, C::OFF_KHI, C::OFF_KLO);
-            }
-            mbar_arrive(kready);
-            return w;
-        };
+        unsigned char* plo_row = smem + C::OFF_PLO + tid * 128;
         float m_used = Lowest<float>::value, l_sum = 0.f;
-        bool ok = n_kt == 0 || split_k(0);
+        bool ok = true;
+        // Decisions after a wait are made warp-uniform (__all_sync): tcgen05.ld/st
+        // are warp-collective, so a warp must never split on an abort.
         for (int t = 0; t < n_kt && ok; ++t) {
-            ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * (t & 1), (t >> 1) & 1, abort));
-            if (!ok) break;  // S(t) done: K_hi/K_lo free
-            tc::fence_after_sync();
-            if (t + 1 < n_kt && !split_k(t + 1)) {
-                ok = false;
-                break;
-            }
-            ok = (t == 0 || mbar_wait_or_abort(pvdone, (t - 1) & 1, abort)) &&
-                 mbar_wait_or_abort(vfull + 8 * (t % kRaw), (t / kRaw) & 1, abort);
-            ok = __all_sync(0xffffffffu, ok);
+            ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull, t & 1, abort));
             if (!ok) break;
             tc::fence_after_sync();
-            if (tid == 0) prog[3] = t + 1;
-            split(C::OFF_RAWV + (t % kRaw) * C::TILE, C::OFF_VHI, C::OFF_VLO);
-            mbar_arrive(vready);
-
-            float sv[32];
-            tc::tmem_ld32(tmem + lane_off + C::S_COL + (t & 1) * kBN, sv);
+            float sv[kBN];
+            tc::tmem_ld64(tmem + lane_off + C::S_COL, sv);
             tc::fence_before_sync();
-            mbar_arrive(sfree + 8 * (t & 1));
+            mbar_arrive(sfree);  // S(t+1) may overwrite the accumulator
             int64_t const key0 = static_cast<int64_t>(t) * kBN;
+            // live keys: kj < Tk and (not causal or kj <= qi), a prefix of the tile
+            int64_t lim = a.Tk - key0;
+            if (a.causal && qi + 1 - key0 < lim) lim = qi + 1 - key0;
+            int const n_live = lim < 0 ? 0 : (lim > kBN ? kBN : static_cast<int>(lim));
             float tmax = Lowest<float>::value;
-            bool live[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                int64_t const kj = key0 + j;
-                live[j] = kj < a.Tk && !(a.causal && qi < kj);
+            for (int j = 0; j < kBN; ++j) {
                 sv[j] = sv[j] * scale;  // attentionScores, then ops::scale
-                if (live[j]) tmax = fmaxf(tmax, sv[j]);
+                if (j < n_live) tmax = fmaxf(tmax, sv[j]);
             }
             bool const grow = tmax > m_used + kLazy;
             float alpha = 1.f;
@@ -319,7 +332,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_used = tmax;
                 l_sum *= alpha;
             }
-            if (t > 0 && __any_sync(0xffffffffu, grow)) {  // warp-uniform: tcgen05.ld/st are warp-collective
+            float psum = 0.f;
+#pragma unroll
+            for (int j = 0; j < kBN; ++j) {
+                sv[j] = j < n_live ? expf(sv[j] - m_used) : 0.f;
+                psum += sv[j];
+            }
+            l_sum += psum;
+            // PV(t-1) has finished with P_hi, P_lo and O
+            ok = t == 0 || mbar_wait_or_abort(pvdone, (t - 1) & 1, abort);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc::fence_after_sync();
+            tc::tmem_st32(tmem + lane_off + C::P_HI, *reinterpret_cast<float const(*)[32]>(sv));
+            tc::tmem_st32(tmem + lane_off + C::P_HI + 32, *reinterpret_cast<float const(*)[32]>(sv + 32));
+            // P_lo: K-major A operand, 16-byte chunk c of row tid at chunk (c % 8) ^ (tid % 8)
+#pragma unroll
+            for (int c = 0; c < kBN / 4; ++c) {
+                float4 const lo = tf32_lo(make_float4(sv[4 * c], sv[4 * c + 1], sv[4 * c + 2], sv[4 * c + 3]));
+                *reinterpret_cast<float4*>(plo_row + (c >> 3) * C::PLO_BLK + (((c & 7) ^ (tid & 7)) << 4)) = lo;
+            }
+            // O rescale after P is out (PV(t) is not issued before pfull)
+            if (t > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     float ov[32];
@@ -329,18 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc::tmem_st32(tmem + lane_off + C::O_COL + 32 * c, ov);
                 }
             }
-            float phi[32], plo[32], psum = 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                float const p = live[j] ? expf(sv[j] - m_used) : 0.f;
-                psum += p;
-                phi[j] = tc::to_tf32(p);
-                plo[j] = p - phi[j];
-            }
-            l_sum += psum;
-            tc::tmem_st32(tmem + lane_off + C::P_HI, phi);
-            tc::tmem_st32(tmem + lane_off + C::P_LO, plo);
             tc::tmem_st_wait();
+            tc::fence_proxy_async_smem();
             tc::fence_before_sync();
             mbar_arrive(pfull);
         }
@@ -348,14 +372,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc::fence_after_sync();
+            float const inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
             float* orow = static_cast<float*>(a.out) + b * a.o_b + qi * a.o_t + hq * a.o_h;
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
                 float ov[32];
                 tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
                 if (qi < a.Tq) {
+                    if (a.o_vec) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) orow[(32 * c + j) * a.o_d] = l_sum > 0.f ? ov[j] / l_sum : 0.f;
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(orow + 32 * c + j) =
+                                make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) orow[(32 * c + j) * a.o_d] = ov[j] * inv;
+                    }
                 }
             }
         }
@@ -363,113 +395,64 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc::fence_before_sync();
     __syncthreads();
-    if (*abort && tid == kSoftmaxThreads) {
-        // A wait gave up: drain the copies and MMAs still in flight before the TMEM goes.
-        atomicOr(&g_tc_error, ANN_DEVERR_WAIT_TIMEOUT);
-        for (int t = prog[2]; t < prog[0]; ++t) mbar_wait_bounded(kfull + 8 * (t % kRaw), (t / kRaw) & 1);
-        for (int t = prog[3]; t < prog[1]; ++t) mbar_wait_bounded(vfull + 8 * (t % kRaw), (t / kRaw) & 1);
-        int const last = prog[4];
-        if (last > 0) {
-            int const g = (last - 1) >> 1;
-            if ((last & 1) == 1)
-                mbar_wait_bounded(sfull + 8 * (g & 1), (g >> 1) & 1);
-            else
-                mbar_wait_bounded(pvdone, g & 1);
-        }
-    }
-    __syncthreads();
+    if (*abort && tid == 0) atomicOr(&g_tc_error, ANN_DEVERR_WAIT_TIMEOUT);
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// 4-D map over K or V with dims ordered by increasing stride:
-// BTHD (d, head, token, batch) or BHTD (d, token, head, batch); box = 32 d x 32 tokens.
-bool make_kv_map(CUtensorMap& map, const Dims& t, int layout, CUtensorMapSwizzle swizzle) {
-    auto enc = encode_fn();
-    if (enc == nullptr) return false;
-    int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
-    int const d1 = layout == ANN_LAYOUT_BTHD ? head : tok, d2 = layout == ANN_LAYOUT_BTHD ? tok : head;
-    cuuint64_t dims[4] = {static_cast<cuuint64_t>(t.ext[3]), static_cast<cuuint64_t>(t.ext[d1]),
-                          static_cast<cuuint64_t>(t.ext[d2]), static_cast<cuuint64_t>(t.ext[0])};
-    cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.str[d1]) * 4, static_cast<cuuint64_t>(t.str[d2]) * 4,
-                             static_cast<cuuint64_t>(t.str[0]) * 4};
-    // strides must grow with the dimension (each one covers the previous dimension)
-    if (strides[0] < dims[0] * 4 || strides[1] < strides[0] * dims[1] || strides[2] < strides[1] * dims[2])
-        return false;
-    for (int i = 0; i < 4; ++i)
-        if (dims[i] == 0) return false;
-    cuuint32_t box[4] = {32, layout == ANN_LAYOUT_BTHD ? 1u : static_cast<cuuint32_t>(kBN),
-                         layout == ANN_LAYOUT_BTHD ? static_cast<cuuint32_t>(kBN) : 1u, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult const r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, t.data, dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 template <int D>
 int launch_tc(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale, uint32_t g,
               int layout, int causal, bool& handled) {
     using C = TcCfg<D>;
-    CUtensorMap kmap, vmap;
-    // K is the K-major B operand of S = Q K^T (16-byte swizzle chunks); V is the
-    // MN-major B operand of O = P V, which for 32-bit elements needs 32-byte chunks.
-    if (!make_kv_map(kmap, k, layout, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_kv_map(vmap, v, layout, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
-        return ANN_OK;  // not handled
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
         attr = cudaFuncSetAttribute(prefill_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     });
-    if (attr != cudaSuccess) return fail(ANN_ECUDA, "attention prefill (tensor cores) setup: %s",
-                                         cudaGetErrorString(attr));
+    if (attr != cudaSuccess)
+        return fail(ANN_ECUDA, "attention prefill (tensor cores) setup: %s", cudaGetErrorString(attr));
+    int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
     TcArgs a{};
     a.out = o.data;
     a.q = static_cast<const float*>(q.data);
+    a.k = static_cast<const float*>(k.data);
+    a.v = static_cast<const float*>(v.data);
     a.q_b = q.str[0];
     a.q_t = q.str[1];
     a.q_h = q.str[2];
+    a.k_b = k.str[0];
+    a.k_t = k.str[tok];
+    a.k_h = k.str[head];
+    a.v_b = v.str[0];
+    a.v_t = v.str[tok];
+    a.v_h = v.str[head];
     a.o_b = o.str[0];
     a.o_t = o.str[1];
     a.o_h = o.str[2];
     a.o_d = o.str[3];
+    a.o_vec = o.str[3] == 1 && reinterpret_cast<uintptr_t>(o.data) % 16 == 0 && o.str[0] % 4 == 0 &&
+              o.str[1] % 4 == 0 && o.str[2] % 4 == 0;
     a.Tq = q.ext[1];
-    a.Tk = layout == ANN_LAYOUT_BTHD ? k.ext[1] : k.ext[2];
+    a.Tk = k.ext[tok];
     a.Hq = q.ext[2];
     a.g = g;
     a.causal = causal;
-    a.kv_bthd = layout == ANN_LAYOUT_BTHD ? 1 : 0;
     int64_t const q_tiles = ceil_div(a.Tq, kBM);
     int64_t const bhs = q.ext[0] * q.ext[2];
     if (q_tiles > INT32_MAX || bhs > 65535) return ANN_OK;  // not handled
     a.q_tiles = static_cast<int>(q_tiles);
     handled = true;
     dim3 grid(static_cast<unsigned>(q_tiles), static_cast<unsigned>(bhs));
-    prefill_tc_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(kmap, vmap, a, scale);
+    prefill_tc_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (tensor cores)");
 }
 
 }  // namespace
 
-// Runs the tensor-core kernel when the shapes allow it (fp32, D 64/128, a TMA
-// map can describe K and V); sets `handled` = false otherwise.
+// Runs the tensor-core kernel for fp32 with D 64 or 128 (the caller has checked
+// unit-stride, 16-byte aligned Q/K/V rows); sets `handled` = false otherwise.
 int prefill_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
                    uint32_t g, int layout, int causal, bool& handled) {
     handled = false;
