@@ -7,19 +7,23 @@
 // product taken as hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-21
 // relative). A kind::tf32 MMA reads an fp32 operand by dropping its low 13
 // mantissa bits, so the raw fp32 value serves as hi as it stands and only
-// lo = x - trunc13(x) (exact in fp32, stored rounded to tf32) is computed.
+// lo = x - trunc13(x) (exact in fp32, truncated again by the MMA) is computed.
 //
 // One CTA owns 128 query rows of one (batch, head) and walks its keys in tiles
-// of 64, with three warp roles:
-//   warps 0..3  one query row per thread (= one TMEM lane): Q -> TMEM, then per
-//               tile S -> registers, scale, top-left mask, online softmax with a
-//               lazy rescale (O and l are rescaled only when the running max
-//               grows by more than 8, exact because O and l share the max used),
-//               P_hi -> TMEM, P_lo -> shared memory
-//   warps 4..11 K / V tiles global -> registers (one tile ahead) -> shared memory
-//               as hi (raw) and lo, in the layouts the MMA reads (K: K-major,
-//               128-byte swizzle; V: MN-major, 128-byte swizzle of 32-byte chunks)
-//   warp 12     one thread issues every MMA; completion comes back on mbarriers
+// of 64, with two warp roles:
+//   warps 0..7  two threads per query row (TMEM lane r = tid % 128, half
+//               h = tid / 128): Q -> TMEM; per tile S(t) -> registers (both
+//               halves load the whole row and take its max, so no exchange is
+//               needed), K(t+1) -> shared memory, online softmax with a lazy
+//               rescale (O and l are rescaled only when the running max grows by
+//               more than 8 in natural-log units, exact because O and l share
+//               the max used) over the half's 32 keys, V(t) -> shared memory,
+//               P_hi -> TMEM, P_lo -> shared memory, O rescale of the half's D/2
+//               columns. K and V go global -> registers one tile ahead ->
+//               shared memory as hi (raw) and lo, in the layouts the MMA reads
+//               (K: K-major, 128-byte swizzle; V: MN-major, 128-byte swizzle of
+//               32-byte chunks).
+//   warp 8      one thread issues every MMA; completion comes back on mbarriers
 //               (tcgen05.commit)
 //   TMEM  [Q_hi | Q_lo | O | S (64) | P_hi (64)]   = 512 columns for D = 128
 //   smem  K hi/lo x 2 buffers | V hi/lo | P_lo     = 224 KB for D = 128
@@ -48,10 +52,10 @@ namespace {
 __device__ unsigned int g_tc_error;
 
 constexpr int kBM = 128, kBN = 64;
-constexpr int kRowThreads = 128;    // warps 0..3
-constexpr int kSplitThreads = 256;  // warps 4..11
-constexpr int kThreads = kRowThreads + kSplitThreads + 32;
-constexpr float kLazy = 8.0f;  // rescale O only when the running max grows by more than this
+constexpr int kRowThreads = 256;  // warps 0..7
+constexpr int kThreads = kRowThreads + 32;
+constexpr float kLog2e = 1.44269504088896341f;
+constexpr float kLazy2 = 8.0f * kLog2e;  // lazy-rescale threshold, log2 units
 
 template <int D>
 struct TcCfg {
@@ -62,8 +66,8 @@ struct TcCfg {
     static constexpr int OFF_PLO = 6 * TILE;  // P_lo: 128 rows x 64 keys as two 32-key blocks
     static constexpr int PLO_BLK = kBM * 128;
     static constexpr int OFF_BAR = OFF_PLO + 2 * PLO_BLK;
-    // barriers: qready kready[2] kfree[2] vready sfull sfree pfull pvdone drain
-    static constexpr int NBAR = 11;
+    // barriers: qready kready[2] vready sfull sfree pfull pvdone drain
+    static constexpr int NBAR = 9;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
     static constexpr int USED = OFF_SLOT + 16;
     // + 1 KB to align the base to the 1 KB swizzle atom; >= 120 KB so that a
@@ -94,12 +98,26 @@ struct TcArgs {
     int q_tiles;
 };
 
-// lo part of the 3xTF32 split (hi is x itself, truncated by the tensor core)
+// lo part of the 3xTF32 split: hi is x itself (a kind::tf32 MMA reads an fp32
+// operand by dropping its low 13 mantissa bits), lo = x - trunc13(x) is exact
+// and is in turn truncated to tf32 by the MMA, so each product keeps a relative
+// error below 2^-19 (hi*lo and lo*hi to 2^-20 each, the dropped lo*lo 2^-20).
 __device__ __forceinline__ float tf32_lo(float x) {
-    return tc::to_tf32(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+    return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 __device__ __forceinline__ float4 tf32_lo(float4 x) {
     return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
+
+// 2^x by the ex2.approx instruction (+0 for x = -inf or below -126)
+__device__ __forceinline__ float exp2_approx(float x) {
+    float p;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(x));
+    return p;
+}
+
+__device__ __forceinline__ void row_sync() {  // the 256 row threads (warps 0..7)
+    asm volatile("bar.sync 1, %0;" ::"n"(kRowThreads) : "memory");
 }
 
 template <int D>
@@ -111,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     unsigned char* smem = smem_raw + pad;
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
-    uint32_t const qready = bar, kready = bar + 8, kfree = bar + 24, vready = bar + 40, sfull = bar + 48,
-                   sfree = bar + 56, pfull = bar + 64, pvdone = bar + 72, drain = bar + 80;
+    uint32_t const qready = bar, kready = bar + 8, vready = bar + 24, sfull = bar + 32, sfree = bar + 40,
+                   pfull = bar + 48, pvdone = bar + 56, drain = bar + 64;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
@@ -126,9 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
 
     if (tid == 0) {
         mbar_init(qready, kRowThreads);
-        for (int i = 0; i < 2; ++i) mbar_init(kready + 8 * i, kSplitThreads);
-        for (int i = 0; i < 2; ++i) mbar_init(kfree + 8 * i, 1);
-        mbar_init(vready, kSplitThreads);
+        for (int i = 0; i < 2; ++i) mbar_init(kready + 8 * i, kRowThreads);
+        mbar_init(vready, kRowThreads);
         mbar_init(sfull, 1);
         mbar_init(sfree, kRowThreads);
         mbar_init(pfull, kRowThreads);
@@ -146,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     tc::fence_after_sync();
     uint32_t const tmem = *slot;
 
-    if (warp == 12) {
+    if (warp == 8) {
         // ================================ MMA issue ================================
         if ((tid & 31) == 0) {
             // Descriptors are built once; a tile or k-step offset is added to the
@@ -167,7 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
                     tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1u);
                 }
                 tc::mma_commit(sfull);
-                tc::mma_commit(kfree + 8 * (t & 1));
             };
             auto issue_pv = [&](int t) {  // O += P V (tile t)
 #pragma unroll
@@ -209,82 +225,60 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             tc::mma_commit(drain);
             if (!mbar_wait_bounded(drain, 0)) *abort = 1;
         }
-    } else if (warp >= 4) {
-        // ======================== K / V loads and splits (4..11) ========================
-        constexpr int NV4 = D / 4;                         // float4 per key row
-        constexpr int PER = kBN * NV4 / kSplitThreads;     // float4 per thread per tile
-        int const st = tid - kRowThreads;
+    } else {
+        // ============================ row warps (0..7) ============================
+        int const r = tid & (kBM - 1), h = tid >> 7;
+        uint32_t const lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        int64_t const qi = q0 + r;
+        constexpr int HD = D / 2;  // O / Q columns per half
+
+        // ---- K / V tiles: element e = i * 256 + tid is key row e / NV4, float4 column e % NV4
+        constexpr int NV4 = D / 4;
+        constexpr int PER = kBN * NV4 / kRowThreads;  // float4 per thread per tile
         float const* kbase = a.k + b * a.k_b + kvh * a.k_h;
         float const* vbase = a.v + b * a.v_b + kvh * a.v_h;
         float4 rk[PER], rv[PER];
-        // element e = i * kSplitThreads + st of a tile: key row e / NV4, float4 column e % NV4
-        // (a warp reads whole rows: coalesced)
-        auto load = [&](float4 (&r)[PER], float const* base, int64_t stride_t, int t) {
+        auto load = [&](float4 (&rg)[PER], float const* base, int64_t stride_t, int t) {
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
-                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
                 int64_t const key = static_cast<int64_t>(t) * kBN + row;
-                r[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(base + key * stride_t) + c4)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);  // V rows past Tk must be finite
+                rg[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(base + key * stride_t) + c4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);  // V rows past Tk must be finite
             }
         };
-        auto store_k = [&](float4 const (&r)[PER], int buf) {  // K-major, 16-byte chunks XOR (row % 8)
+        auto store_k = [&](float4 const (&rg)[PER], int buf) {  // K-major, 16-byte chunks XOR (row % 8)
             unsigned char* hi = smem + C::OFF_K + buf * 2 * C::TILE;
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
-                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
                 int const off = (c4 >> 3) * C::BLK + row * 128 + (((c4 & 7) ^ (row & 7)) << 4);
-                *reinterpret_cast<float4*>(hi + off) = r[i];
-                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(r[i]);
+                *reinterpret_cast<float4*>(hi + off) = rg[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(rg[i]);
             }
             tc::fence_proxy_async_smem();  // visible to the tensor core
         };
-        auto store_v = [&](float4 const (&r)[PER]) {  // MN-major, 32-byte chunks XOR (row % 4)
+        auto store_v = [&](float4 const (&rg)[PER]) {  // MN-major, 32-byte chunks XOR (row % 4)
             unsigned char* hi = smem + C::OFF_V;
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
-                int const e = i * kSplitThreads + st, row = e / NV4, c4 = e % NV4;
+                int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
                 int const off =
                     (c4 >> 3) * C::BLK + row * 128 + ((((c4 & 7) >> 1) ^ (row & 3)) << 5) + ((c4 & 1) << 4);
-                *reinterpret_cast<float4*>(hi + off) = r[i];
-                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(r[i]);
+                *reinterpret_cast<float4*>(hi + off) = rg[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(rg[i]);
             }
             tc::fence_proxy_async_smem();
         };
-        bool ok = true;
         if (n_kt > 0) {
             load(rk, kbase, a.k_t, 0);
             load(rv, vbase, a.v_t, 0);
-            store_k(rk, 0);
-            mbar_arrive(kready);
-            if (n_kt > 1) load(rk, kbase, a.k_t, 1);
         }
-        // iteration t: K(t+1) (needed by S(t+1), its buffer was read by S(t-1)),
-        // then V(t) (needed by PV(t), its buffer was read by PV(t-1))
-        for (int t = 0; t < n_kt && ok; ++t) {
-            if (t + 1 < n_kt) {
-                int const buf = (t + 1) & 1;
-                if (t >= 1) ok = mbar_wait_or_abort(kfree + 8 * buf, ((t - 1) >> 1) & 1, abort);
-                if (!ok) break;
-                store_k(rk, buf);
-                mbar_arrive(kready + 8 * buf);
-                if (t + 2 < n_kt) load(rk, kbase, a.k_t, t + 2);
-            }
-            if (t >= 1) ok = mbar_wait_or_abort(pvdone, (t - 1) & 1, abort);
-            if (!ok) break;
-            store_v(rv);
-            mbar_arrive(vready);
-            if (t + 1 < n_kt) load(rv, vbase, a.v_t, t + 1);
-        }
-    } else {
-        // ============================ softmax rows (0..3) ============================
-        uint32_t const lane_off = static_cast<uint32_t>(warp * 32) << 16;
-        int64_t const qi = q0 + tid;
-        {  // Q row -> TMEM: hi (raw) and lo, the A operand of S = Q K^T
-            float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h;
+        {  // Q row half -> TMEM: hi (raw) and lo, the A operand of S = Q K^T
+            float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h + h * HD;
             bool const live = qi < a.Tq;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < HD / 32; ++c) {
                 float hi[32], lo[32];
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
@@ -294,99 +288,141 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
                     lo[j] = tf32_lo(x.x), lo[j + 1] = tf32_lo(x.y), lo[j + 2] = tf32_lo(x.z),
                     lo[j + 3] = tf32_lo(x.w);
                 }
-                tc::tmem_st32(tmem + lane_off + C::Q_HI + 32 * c, hi);
-                tc::tmem_st32(tmem + lane_off + C::Q_LO + 32 * c, lo);
+                tc::tmem_st32(tmem + lane_off + C::Q_HI + h * HD + 32 * c, hi);
+                tc::tmem_st32(tmem + lane_off + C::Q_LO + h * HD + 32 * c, lo);
             }
             tc::tmem_st_wait();
             tc::fence_before_sync();
             mbar_arrive(qready);
         }
-        unsigned char* plo_row = smem + C::OFF_PLO + tid * 128;
-        float m_used = Lowest<float>::value, l_sum = 0.f;
+        if (n_kt > 0) {
+            store_k(rk, 0);
+            mbar_arrive(kready);
+            if (n_kt > 1) load(rk, kbase, a.k_t, 1);
+        }
+        unsigned char* plo_row = smem + C::OFF_PLO + h * C::PLO_BLK + r * 128;
+        float const c2 = scale * kLog2e;  // scores are taken in log2 units: s * scale * log2(e)
+        float m_used = Lowest<float>::value, l_part = 0.f;
         bool ok = true;
         // Decisions after a wait are made warp-uniform (__all_sync): tcgen05.ld/st
         // are warp-collective, so a warp must never split on an abort.
         for (int t = 0; t < n_kt && ok; ++t) {
             ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull, t & 1, abort));
-            if (!ok) break;
+            if (!ok) break;  // S(t) done, and with it S(t-1): K buffer (t+1) % 2 is free
             tc::fence_after_sync();
-            float sv[kBN];
-            tc::tmem_ld64(tmem + lane_off + C::S_COL, sv);
+            float sv[kBN];  // [0, 32): this half's keys, [32, 64): the other half's
+            tc::tmem_ld32x2(tmem + lane_off + C::S_COL + 32 * h, tmem + lane_off + C::S_COL + 32 * (1 - h), sv);
             tc::fence_before_sync();
             mbar_arrive(sfree);  // S(t+1) may overwrite the accumulator
+            if (t + 1 < n_kt) {
+                store_k(rk, (t + 1) & 1);
+                mbar_arrive(kready + 8 * ((t + 1) & 1));
+                if (t + 2 < n_kt) load(rk, kbase, a.k_t, t + 2);
+            }
+            // live keys: kj < Tk and (not causal or kj <= qi), a prefix of the tile;
+            // masking is by selects, not branches, so that the exps overlap
             int64_t const key0 = static_cast<int64_t>(t) * kBN;
-            // live keys: kj < Tk and (not causal or kj <= qi), a prefix of the tile
             int64_t lim = a.Tk - key0;
             if (a.causal && qi + 1 - key0 < lim) lim = qi + 1 - key0;
             int const n_live = lim < 0 ? 0 : (lim > kBN ? kBN : static_cast<int>(lim));
-            float tmax = Lowest<float>::value;
+            float part[8], pv[32];
+            // interior tiles with scale >= 0 (the usual case): the max of the raw
+            // scores gives the max of the scaled ones, and each exponent is one FMA
+            bool const fast = c2 >= 0.f && __all_sync(0xffffffffu, n_live == kBN);
+            if (fast) {
 #pragma unroll
-            for (int j = 0; j < kBN; ++j) {
-                sv[j] = sv[j] * scale;  // attentionScores, then ops::scale
-                if (j < n_live) tmax = fmaxf(tmax, sv[j]);
+                for (int j = 0; j < kBN; ++j) part[j & 7] = j < 8 ? sv[j] : fmaxf(part[j & 7], sv[j]);
+            } else {
+                int const own = n_live - 32 * h, other = n_live - 32 * (1 - h);  // live counts per half
+#pragma unroll
+                for (int j = 0; j < kBN; ++j) {
+                    sv[j] = sv[j] * c2;  // attentionScores, then ops::scale (times log2 e)
+                    float const live = (j < 32 ? j < own : j - 32 < other) ? sv[j] : -INFINITY;
+                    part[j & 7] = j < 8 ? live : fmaxf(part[j & 7], live);
+                }
             }
-            bool const grow = tmax > m_used + kLazy;
+            float tmax = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
+                               fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7])));
+            if (fast) tmax *= c2;
+            // both halves see the same row and take the same decisions
+            bool const grow = tmax > m_used + kLazy2;
             float alpha = 1.f;
             if (grow) {
-                alpha = expf(m_used - tmax);
+                alpha = exp2_approx(m_used - tmax);
                 m_used = tmax;
-                l_sum *= alpha;
+                l_part *= alpha;
             }
-            float psum = 0.f;
+            if (fast) {
 #pragma unroll
-            for (int j = 0; j < kBN; ++j) {
-                sv[j] = j < n_live ? expf(sv[j] - m_used) : 0.f;
-                psum += sv[j];
+                for (int j = 0; j < 32; ++j) {
+                    pv[j] = exp2_approx(fmaf(sv[j], c2, -m_used));  // <= 2^kLazy2
+                    part[j & 7] = j < 8 ? pv[j] : part[j & 7] + pv[j];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float const e = exp2_approx(sv[j] - m_used);
+                    pv[j] = h * 32 + j < n_live ? e : 0.f;
+                    part[j & 7] = j < 8 ? pv[j] : part[j & 7] + pv[j];
+                }
             }
-            l_sum += psum;
-            // PV(t-1) has finished with P_hi, P_lo and O
+            l_part += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+            // PV(t-1) has finished with V, P_hi, P_lo and O
             ok = t == 0 || mbar_wait_or_abort(pvdone, (t - 1) & 1, abort);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc::fence_after_sync();
-            tc::tmem_st32(tmem + lane_off + C::P_HI, *reinterpret_cast<float const(*)[32]>(sv));
-            tc::tmem_st32(tmem + lane_off + C::P_HI + 32, *reinterpret_cast<float const(*)[32]>(sv + 32));
-            // P_lo: K-major A operand, 16-byte chunk c of row tid at chunk (c % 8) ^ (tid % 8)
+            tc::tmem_st32(tmem + lane_off + C::P_HI + 32 * h, pv);
+            // P_lo: K-major A operand, 16-byte chunk c of row r at chunk c ^ (r % 8)
 #pragma unroll
-            for (int c = 0; c < kBN / 4; ++c) {
-                float4 const lo = tf32_lo(make_float4(sv[4 * c], sv[4 * c + 1], sv[4 * c + 2], sv[4 * c + 3]));
-                *reinterpret_cast<float4*>(plo_row + (c >> 3) * C::PLO_BLK + (((c & 7) ^ (tid & 7)) << 4)) = lo;
+            for (int c = 0; c < 8; ++c) {
+                float4 const lo = tf32_lo(make_float4(pv[4 * c], pv[4 * c + 1], pv[4 * c + 2], pv[4 * c + 3]));
+                *reinterpret_cast<float4*>(plo_row + ((c ^ (r & 7)) << 4)) = lo;
             }
-            // O rescale after P is out (PV(t) is not issued before pfull)
-            if (t > 0 && __any_sync(0xffffffffu, grow)) {
+            if (t > 0 && __any_sync(0xffffffffu, grow)) {  // this half's O columns
 #pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c = 0; c < HD / 32; ++c) {
                     float ov[32];
-                    tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                    tc::tmem_ld32(tmem + lane_off + C::O_COL + h * HD + 32 * c, ov);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-                    tc::tmem_st32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                    tc::tmem_st32(tmem + lane_off + C::O_COL + h * HD + 32 * c, ov);
                 }
             }
             tc::tmem_st_wait();
             tc::fence_proxy_async_smem();
             tc::fence_before_sync();
             mbar_arrive(pfull);
+            store_v(rv);
+            mbar_arrive(vready);
+            if (t + 1 < n_kt) load(rv, vbase, a.v_t, t + 1);
         }
         if (ok && n_kt > 0) ok = mbar_wait_or_abort(pvdone, (n_kt - 1) & 1, abort);
         ok = __all_sync(0xffffffffu, ok);
+        // row sum = the two halves' parts, exchanged through the (now idle) P_lo
+        // buffer; every row thread reaches this barrier exactly once
+        float* lx = reinterpret_cast<float*>(smem + C::OFF_PLO);
+        if (ok) lx[tid] = l_part;
+        row_sync();
         if (ok) {
             tc::fence_after_sync();
+            float const l_sum = lx[r] + lx[r + kBM];
             float const inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
             float* orow = static_cast<float*>(a.out) + b * a.o_b + qi * a.o_t + hq * a.o_h;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < HD / 32; ++c) {
+                int const col = h * HD + 32 * c;
                 float ov[32];
-                tc::tmem_ld32(tmem + lane_off + C::O_COL + 32 * c, ov);
+                tc::tmem_ld32(tmem + lane_off + C::O_COL + col, ov);
                 if (qi < a.Tq) {
                     if (a.o_vec) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(orow + 32 * c + j) =
+                            *reinterpret_cast<float4*>(orow + col + j) =
                                 make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) orow[(32 * c + j) * a.o_d] = ov[j] * inv;
+                        for (int j = 0; j < 32; ++j) orow[(col + j) * a.o_d] = ov[j] * inv;
                     }
                 }
             }
