@@ -2,16 +2,12 @@
 //
 // Same pipeline and semantics as prefill.cu (attentionScores -> ops::scale ->
 // causalSoftmax with the top-left mask / softmax -> attentionApply, reference
-// test/unit/nn/attention.cpp:591-651), with both contractions on the tensor
-// cores and fp32 accuracy kept by splitting every operand x = hi + lo:
-//   hi = x as it stands: a kind::tf32 MMA reads an fp32 operand by dropping its
-//        low 13 mantissa bits, so hi*hi is one kind::tf32 MMA on the raw data;
-//   lo = x - trunc13(x), exact in fp32 (|lo| < 2^-10 |x|);
-// the corrections hi*lo + lo*hi go through one kind::f16 MMA on bf16 pairs
-// (a_hi, a_lo) . (b_lo, b_hi) packed in 32-bit words, so that a 16-element
-// bf16 k-step covers the same 8 k-indices as a tf32 k-step. Each product keeps a
-// relative error below ~2^-17 (bf16 rounding of the two corrections, 2^-18
-// each, and the dropped lo*lo, 2^-20).
+// test/unit/nn/attention.cpp:591-651), with both contractions on tcgen05.mma
+// kind::tf32 and fp32 accuracy kept by the 3xTF32 split x = hi + lo, each
+// product taken as hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-21
+// relative). A kind::tf32 MMA reads an fp32 operand by dropping its low 13
+// mantissa bits, so the raw fp32 value serves as hi as it stands and only
+// lo = x - trunc13(x) (exact in fp32, truncated again by the MMA) is computed.
 //
 // One CTA owns 128 query rows of one (batch, head) and walks its keys in tiles
 // of 64, with two warp roles:
@@ -22,21 +18,19 @@
 //               rescale (O and l are rescaled only when the running max grows by
 //               more than 8 in natural-log units, exact because O and l share
 //               the max used) over the half's 32 keys, V(t) -> shared memory,
-//               P -> TMEM (fp32) and its bf16 pairs -> shared memory, O rescale
-//               of the half's D/2 columns. K and V go global -> registers one
-//               tile ahead -> shared memory as raw fp32 and bf16 pairs, in the
-//               layouts the MMAs read (K and its pairs: K-major, 128-byte
-//               swizzle; V: MN-major, 128-byte swizzle of 32-byte chunks; V
-//               pairs: MN-major bf16 rows 2k = lo, 2k+1 = hi, 128-byte swizzle).
+//               P_hi -> TMEM, P_lo -> shared memory, O rescale of the half's D/2
+//               columns. K and V go global -> registers one tile ahead ->
+//               shared memory as hi (raw) and lo, in the layouts the MMA reads
+//               (K: K-major, 128-byte swizzle; V: MN-major, 128-byte swizzle of
+//               32-byte chunks).
 //   warp 8      one thread issues every MMA; completion comes back on mbarriers
 //               (tcgen05.commit)
-//   TMEM  [Q | Q pairs | O | S (64) | P (64)]       = 512 columns for D = 128
-//   smem  K raw/pairs x 2 buffers | V raw/pairs | P pairs = 224 KB for D = 128
+//   TMEM  [Q_hi | Q_lo | O | S (64) | P_hi (64)]   = 512 columns for D = 128
+//   smem  K hi/lo x 2 buffers | V hi/lo | P_lo     = 224 KB for D = 128
 // Tensor-pipe order S(0) S(1) PV(0) S(2) PV(1) ...: the softmax of tile t and
 // the V split run while S(t+1) and PV(t-1) execute. Per 64-key tile the MMAs
-// are S: D/8 x (tf32 M128 N64 K8 + bf16 M128 N64 K16), A = Q from TMEM, and
-// PV: 8 x (tf32 M128 N=D K8, A = P from TMEM + bf16 M128 N=D K16, A = P pairs
-// from shared memory).
+// are S: 3 x D/8 of M128 N64 K8 (A = Q from TMEM) and PV: 3 x 8 of M128 N=D K8
+// (A = P_hi from TMEM, P_lo from shared memory).
 // Every wait is bounded; on a timeout the CTA stops, waits for its issued MMAs,
 // frees its TMEM and reports ANN_DEVERR_WAIT_TIMEOUT.
 #include <cstdlib>
@@ -65,13 +59,11 @@ constexpr float kLazy2 = 8.0f * kLog2e;  // lazy-rescale threshold, log2 units
 
 template <int D>
 struct TcCfg {
-    static constexpr int TILE = kBN * D * 4;  // bytes of one K or V tile (raw, or its bf16 pairs)
+    static constexpr int TILE = kBN * D * 4;  // bytes of one K or V tile (hi or lo)
     static constexpr int BLK = kBN * 128;     // one 32-float column block of a tile: 64 rows x 128 B
-    static constexpr int OFF_K = 0;           // buffer i: raw at OFF_K + 2*i*TILE, pairs at + TILE
-    static constexpr int OFF_V = 4 * TILE;    // raw, pairs
-    static constexpr int VP_GRP = 1024;       // V pairs: 8 bf16 rows x 128 B per group,
-    static constexpr int VP_BLK = 16 * VP_GRP;  // 16 groups (128 rows) per 64-column block
-    static constexpr int OFF_PLO = 6 * TILE;  // P pairs: 128 rows x 64 keys as two 32-key blocks
+    static constexpr int OFF_K = 0;           // buffer i: hi at OFF_K + 2*i*TILE, lo at + TILE
+    static constexpr int OFF_V = 4 * TILE;    // hi, lo
+    static constexpr int OFF_PLO = 6 * TILE;  // P_lo: 128 rows x 64 keys as two 32-key blocks
     static constexpr int PLO_BLK = kBM * 128;
     static constexpr int OFF_BAR = OFF_PLO + 2 * PLO_BLK;
     // barriers: qready kready[2] vready sfull sfree pfull pvdone drain
@@ -83,13 +75,11 @@ struct TcCfg {
     static constexpr int SMEM = USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024;
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     // TMEM columns
-    static constexpr uint32_t Q_HI = 0, Q_LO = D, O_COL = 2 * D, S_COL = 3 * D, P_HI = 3 * D + kBN;  // Q_LO: pairs
+    static constexpr uint32_t Q_HI = 0, Q_LO = D, O_COL = 2 * D, S_COL = 3 * D, P_HI = 3 * D + kBN;
     static constexpr uint32_t TMEM_COLS = 512;
     static_assert(P_HI + kBN <= TMEM_COLS, "TMEM budget");
     static constexpr uint32_t IDESC_S = tc::idesc_tf32(kBM, kBN, false);
     static constexpr uint32_t IDESC_PV = tc::idesc_tf32(kBM, D, true);
-    static constexpr uint32_t IDESC_S2 = tc::idesc_bf16(kBM, kBN, false);
-    static constexpr uint32_t IDESC_PV2 = tc::idesc_bf16(kBM, D, true);
 };
 
 struct TcArgs {
@@ -108,15 +98,16 @@ struct TcArgs {
     int q_tiles;
 };
 
-// lo = x - trunc13(x), exact: the part of x that a kind::tf32 MMA drops
+// lo part of the 3xTF32 split: hi is x itself (a kind::tf32 MMA reads an fp32
+// operand by dropping its low 13 mantissa bits), lo = x - trunc13(x) is exact
+// and is in turn truncated to tf32 by the MMA, so each product keeps a relative
+// error below 2^-19 (hi*lo and lo*hi to 2^-20 each, the dropped lo*lo 2^-20).
 __device__ __forceinline__ float tf32_lo(float x) {
     return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
-// bf16 pairs of the correction MMA: the A side (Q, P) holds (x, lo), the B side
-// (K, V) holds (lo, x), so that the pair product is a_x * b_lo + a_lo * b_x.
-__device__ __forceinline__ uint32_t pair_a(float x) { return tc::pack_bf16(x, tf32_lo(x)); }
-__device__ __forceinline__ uint32_t pair_b(float x) { return tc::pack_bf16(tf32_lo(x), x); }
-__device__ __forceinline__ uint4 pair_b(float4 x) { return make_uint4(pair_b(x.x), pair_b(x.y), pair_b(x.z), pair_b(x.w)); }
+__device__ __forceinline__ float4 tf32_lo(float4 x) {
+    return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
 
 // 2^x by the ex2.approx instruction (+0 for x = -inf or below -126)
 __device__ __forceinline__ float exp2_approx(float x) {
@@ -180,7 +171,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             // so the field never carries).
             uint64_t const k_desc = tc::smem_desc(sbase + C::OFF_K, 16, 1024, tc::kSwizzle128B);
             uint64_t const v_desc = tc::smem_desc(sbase + C::OFF_V, C::BLK, 512, tc::kSwizzle128B_32B);
-            uint64_t const vp_desc = tc::smem_desc(sbase + C::OFF_V + C::TILE, C::VP_BLK, C::VP_GRP, tc::kSwizzle128B);
             uint64_t const p_desc = tc::smem_desc(sbase + C::OFF_PLO, 16, 1024, tc::kSwizzle128B);
             auto at = [](uint64_t desc, uint32_t off) { return desc + static_cast<uint64_t>(off >> 4); };
             auto issue_s = [&](int t) {  // S = Q K^T (tile t)
@@ -188,19 +178,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk) {
                     uint32_t const off = kb + (kk >> 2) * C::BLK + (kk & 3) * 32;
-                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_HI + 8 * kk, at(k_desc, off), C::IDESC_S,
-                                    kk > 0 ? 1u : 0u);
-                    tc::mma_f16_ts(tmem + C::S_COL, tmem + C::Q_LO + 8 * kk, at(k_desc, off + C::TILE), C::IDESC_S2, 1u);
+                    uint64_t const khi = at(k_desc, off), klo = at(k_desc, off + C::TILE);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_HI + 8 * kk, khi, C::IDESC_S, kk > 0 ? 1u : 0u);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_HI + 8 * kk, klo, C::IDESC_S, 1u);
+                    tc::mma_tf32_ts(tmem + C::S_COL, tmem + C::Q_LO + 8 * kk, khi, C::IDESC_S, 1u);
                 }
                 tc::mma_commit(sfull);
             };
             auto issue_pv = [&](int t) {  // O += P V (tile t)
 #pragma unroll
                 for (int kk = 0; kk < kBN / 8; ++kk) {
-                    tc::mma_tf32_ts(tmem + C::O_COL, tmem + C::P_HI + 8 * kk, at(v_desc, kk * 1024), C::IDESC_PV,
+                    uint64_t const vhi = at(v_desc, kk * 1024), vlo = at(v_desc, C::TILE + kk * 1024);
+                    uint64_t const plo = at(p_desc, (kk >> 2) * C::PLO_BLK + (kk & 3) * 32);
+                    tc::mma_tf32_ts(tmem + C::O_COL, tmem + C::P_HI + 8 * kk, vhi, C::IDESC_PV,
                                     (t > 0 || kk > 0) ? 1u : 0u);
-                    tc::mma_f16_ss(tmem + C::O_COL, at(p_desc, (kk >> 2) * C::PLO_BLK + (kk & 3) * 32),
-                                   at(vp_desc, kk * 2 * C::VP_GRP), C::IDESC_PV2, 1u);
+                    tc::mma_tf32_ts(tmem + C::O_COL, tmem + C::P_HI + 8 * kk, vlo, C::IDESC_PV, 1u);
+                    tc::mma_tf32_ss(tmem + C::O_COL, plo, vhi, C::IDESC_PV, 1u);
                 }
                 tc::mma_commit(pvdone);
             };
@@ -255,42 +248,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             }
         };
         auto store_k = [&](float4 const (&rg)[PER], int buf) {  // K-major, 16-byte chunks XOR (row % 8)
-            unsigned char* raw = smem + C::OFF_K + buf * 2 * C::TILE;
+            unsigned char* hi = smem + C::OFF_K + buf * 2 * C::TILE;
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
                 int const off = (c4 >> 3) * C::BLK + row * 128 + (((c4 & 7) ^ (row & 7)) << 4);
-                *reinterpret_cast<float4*>(raw + off) = rg[i];
-                *reinterpret_cast<uint4*>(raw + C::TILE + off) = pair_b(rg[i]);  // pair of k-index d at byte 4d
+                *reinterpret_cast<float4*>(hi + off) = rg[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(rg[i]);
             }
             tc::fence_proxy_async_smem();  // visible to the tensor core
         };
-        auto store_v = [&](float4 const (&rg)[PER]) {
-            unsigned char* raw = smem + C::OFF_V;
-            unsigned char* pairs = raw + C::TILE;
+        auto store_v = [&](float4 const (&rg)[PER]) {  // MN-major, 32-byte chunks XOR (row % 4)
+            unsigned char* hi = smem + C::OFF_V;
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
-                // raw: MN-major, 32-byte chunks XOR (row % 4)
                 int const off =
                     (c4 >> 3) * C::BLK + row * 128 + ((((c4 & 7) >> 1) ^ (row & 3)) << 5) + ((c4 & 1) << 4);
-                *reinterpret_cast<float4*>(raw + off) = rg[i];
-                // pairs: bf16 rows 2 * row (lo) and 2 * row + 1 (hi), 64 columns per block,
-                // 16-byte chunks XOR (bf16 row % 8); this float4 is 8 bytes of each row
-                float const x[4] = {rg[i].x, rg[i].y, rg[i].z, rg[i].w};
-                uint32_t lo2[2], hi2[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    lo2[u] = tc::pack_bf16(tf32_lo(x[2 * u]), tf32_lo(x[2 * u + 1]));
-                    hi2[u] = tc::pack_bf16(x[2 * u], x[2 * u + 1]);
-                }
-                int const blk = (c4 >> 4) * C::VP_BLK, chunk = (c4 & 15) >> 1, half = (c4 & 1) << 3;
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    int const kr = 2 * row + u;  // bf16 row: 2k = lo, 2k + 1 = hi
-                    int const poff = blk + (kr >> 3) * C::VP_GRP + (kr & 7) * 128 + ((chunk ^ (kr & 7)) << 4) + half;
-                    *reinterpret_cast<uint2*>(pairs + poff) = u == 0 ? make_uint2(lo2[0], lo2[1]) : make_uint2(hi2[0], hi2[1]);
-                }
+                *reinterpret_cast<float4*>(hi + off) = rg[i];
+                *reinterpret_cast<float4*>(hi + C::TILE + off) = tf32_lo(rg[i]);
             }
             tc::fence_proxy_async_smem();
         };
@@ -298,19 +274,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             load(rk, kbase, a.k_t, 0);
             load(rv, vbase, a.v_t, 0);
         }
-        {  // Q row half -> TMEM: raw and bf16 pairs, the A operands of S = Q K^T
+        {  // Q row half -> TMEM: hi (raw) and lo, the A operand of S = Q K^T
             float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h + h * HD;
             bool const live = qi < a.Tq;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
-                float hi[32], lo[32];  // lo: the bf16 pairs (raw bits)
+                float hi[32], lo[32];
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     float4 const x = live ? __ldg(reinterpret_cast<float4 const*>(qrow + 32 * c + j))
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
                     hi[j] = x.x, hi[j + 1] = x.y, hi[j + 2] = x.z, hi[j + 3] = x.w;
-                    lo[j] = __uint_as_float(pair_a(x.x)), lo[j + 1] = __uint_as_float(pair_a(x.y)),
-                    lo[j + 2] = __uint_as_float(pair_a(x.z)), lo[j + 3] = __uint_as_float(pair_a(x.w));
+                    lo[j] = tf32_lo(x.x), lo[j + 1] = tf32_lo(x.y), lo[j + 2] = tf32_lo(x.z),
+                    lo[j + 3] = tf32_lo(x.w);
                 }
                 tc::tmem_st32(tmem + lane_off + C::Q_HI + h * HD + 32 * c, hi);
                 tc::tmem_st32(tmem + lane_off + C::Q_LO + h * HD + 32 * c, lo);
@@ -397,12 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             if (!ok) break;
             tc::fence_after_sync();
             tc::tmem_st32(tmem + lane_off + C::P_HI + 32 * h, pv);
-            // P pairs: K-major A operand, 16-byte chunk c of row r at chunk c ^ (r % 8)
+            // P_lo: K-major A operand, 16-byte chunk c of row r at chunk c ^ (r % 8)
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                uint4 const pr = make_uint4(pair_a(pv[4 * c]), pair_a(pv[4 * c + 1]), pair_a(pv[4 * c + 2]),
-                                            pair_a(pv[4 * c + 3]));
-                *reinterpret_cast<uint4*>(plo_row + ((c ^ (r & 7)) << 4)) = pr;
+                float4 const lo = tf32_lo(make_float4(pv[4 * c], pv[4 * c + 1], pv[4 * c + 2], pv[4 * c + 3]));
+                *reinterpret_cast<float4*>(plo_row + ((c ^ (r & 7)) << 4)) = lo;
             }
             if (t > 0 && __any_sync(0xffffffffu, grow)) {  // this half's O columns
 #pragma unroll 1

@@ -117,29 +117,6 @@ __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, ui
         : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem], kind::f16 (both operands bf16 here), fp32 accumulate.
-// A in TMEM holds two 16-bit elements per 32-bit column (lower half = lower K index).
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem], kind::f16 (both operands bf16 here), fp32 accumulate.
-__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 // Arrive on `bar` once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -156,24 +133,6 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn_major)
            | (static_cast<uint32_t>(M >> 4) << 24);     // M / 16
 }
 
-// Instruction descriptor, kind::f16 with bf16 A and B, fp32 accumulator, A K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major) {
-    return (1u << 4)                                  // D format: f32
-           | (1u << 7)                                // A format: bf16
-           | (1u << 10)                               // B format: bf16
-           | (static_cast<uint32_t>(b_mn_major) << 16)  // B major: 0 = K, 1 = MN
-           | (static_cast<uint32_t>(N >> 3) << 17)      // N / 8
-           | (static_cast<uint32_t>(M >> 4) << 24);     // M / 16
-}
-
-// Two fp32 values as a bf16 pair (round to nearest): `first` in the lower half,
-// which is the lower K index of an MMA operand.
-__device__ __forceinline__ uint32_t pack_bf16(float first, float second) {
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(second), "f"(first));
-    return r;
-}
-
 // Shared-memory matrix descriptor layout types (bits 61..63).
 //  kSwizzle128B      : 16-byte chunks of each 128-byte row XOR'd with (row % 8) -- the layout TMA writes
 //                      with CU_TENSOR_MAP_SWIZZLE_128B; K-major operands (atom 8 rows x 128 B).
@@ -182,8 +141,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float first, float second) {
 constexpr uint64_t kSwizzle128B = 2, kSwizzle128B_32B = 1;
 
 // lbo / sbo in bytes: K-major -- sbo = stride between 8-row groups (lbo unused);
-// MN-major -- lbo = stride between 128-byte MN atoms, sbo = stride between K-row groups
-// (4 rows of 32-bit elements with kSwizzle128B_32B, 8 rows of 16-bit ones with kSwizzle128B).
+// MN-major -- lbo = stride between 128-byte MN atoms, sbo = stride between K-row groups.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint64_t layout) {
     return (static_cast<uint64_t>((saddr >> 4) & 0x3FFFu)) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
            (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46)  // version 1 (sm_100)
