@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
     p.add_argument("--no-extra", action="store_true", help="skip the secondary c2 measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
+    p.add_argument("--prefill-only", metavar="B,T,H,D[,f64]", default=None,
+                   help="run only the fused causal prefill on this shape (--steps launches) and print its time; "
+                        "the small case the prefill ncu captures use")
     return p.parse_args()
 
 
@@ -61,6 +64,16 @@ def peaks():
         return float(m["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tf32_peak():
+    """Dense tf32 tensor TFLOP/s: half the measured bf16 burst rate (B200 runs
+    kind::tf32 at half the kind::f16 rate), else half the 1.59 PFLOP/s fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]) / 2, "measured bf16 / 2"
+    except Exception:
+        return 1590.0 / 2, "fallback bf16 / 2"
 
 
 def ncu_traffic(workload):
@@ -361,8 +374,45 @@ def measure_prefill(name, world, rank, reps=10):
     flops = 4 * B * H * D * T * (T + 1) / 2
     del q, k, v, o
     torch.cuda.empty_cache()
-    return {"workload": p["desc"], "ms": t * 1e3, "tflops": flops / t / 1e12, "tokens_per_s": B * T / t,
-            "dtype": p["dtype"], "kernel": "prefill_kernel (FMA/DFMA flash)"}
+    res = {"workload": p["desc"], "ms": t * 1e3, "tflops": flops / t / 1e12, "tokens_per_s": B * T / t,
+           "dtype": p["dtype"]}
+    if p["dtype"] == "f32":
+        # 3xTF32: every useful flop costs three tf32 tensor flops
+        pk, kind = tf32_peak()
+        res.update(kernel=f"prefill_tc_kernel<{D}> (tcgen05 3xTF32)", tf32_peak_tflops=pk, tf32_peak_kind=kind,
+                   frac_of_3xtf32_peak=3 * res["tflops"] / world / pk)
+    else:
+        res.update(kernel=f"prefill_kernel<double,{D}> (DFMA flash)")
+    return res
+
+
+def prefill_only(args):
+    """--prefill-only B,T,H,D[,f64]: causal prefill launches on one GPU, CUDA-event timed."""
+    import torch
+
+    import alpakann_b200 as ann
+    f = args.prefill_only.split(",")
+    B, T, H, D = (int(x) for x in f[:4])
+    dt = torch.float64 if len(f) > 4 and f[4] == "f64" else torch.float32
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    q, k, v = (torch.randn((B, T, H, D), generator=gen, dtype=dt, device="cuda") for _ in range(3))
+    o = torch.empty_like(q)
+    queue = ann.Queue()
+    sc = 1.0 / math.sqrt(D)
+    for _ in range(args.warmup):
+        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+    e1.record()
+    torch.cuda.synchronize()
+    if queue.take_device_error() != 0:
+        raise SystemExit("prefill reported a device error")
+    t = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
+    flops = 4 * B * H * D * T * (T + 1) / 2
+    print(json.dumps({"prefill": args.prefill_only, "launches": args.steps, "ms": t * 1e3,
+                      "tflops": flops / t / 1e12}), flush=True)
 
 
 def main():
@@ -370,6 +420,9 @@ def main():
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)
+        return
+    if args.prefill_only:
+        prefill_only(args)
         return
     import torch
     import torch.distributed as dist
