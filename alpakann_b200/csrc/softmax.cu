@@ -151,6 +151,59 @@ __global__ void __launch_bounds__(256) scale_kernel(ScaleArgs a, T scalar) {
     }
 }
 
+// Strided views whose innermost run is unit-stride in both tensors: one warp per
+// row (the row's offsets decoded once), 16-byte vectors along the row.
+struct ScaleRowArgs {
+    const void* in;
+    void* out;
+    int64_t rows, len;  // len: elements per row, a multiple of the vector width
+    Outer2 outer;       // axes outside the row
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) scale_rows_kernel(ScaleRowArgs a, T scalar) {
+    using V = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n;
+    int const lane = threadIdx.x & 31;
+    int64_t const nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    int64_t const nvec = a.len / NV;
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < a.rows; r += nwarps) {
+        int64_t oi, oo;
+        a.outer.offsets(r, oi, oo);
+        V const* src = reinterpret_cast<V const*>(static_cast<T const*>(a.in) + oi);
+        V* dst = reinterpret_cast<V*>(static_cast<T*>(a.out) + oo);
+        for (int64_t j = lane; j < nvec; j += 32) {
+            V v = src[j];
+            if constexpr (NV == 4) {
+                v.x = v.x * scalar; v.y = v.y * scalar; v.z = v.z * scalar; v.w = v.w * scalar;
+            } else {
+                v.x = v.x * scalar; v.y = v.y * scalar;
+            }
+            dst[j] = v;
+        }
+    }
+}
+
+// Axes of (in, out) with extent 1 dropped and neighbours merged where both
+// tensors are contiguous across them; returns the merged rank.
+int merge_axes(const Dims& in, const Dims& out, int64_t* ext, int64_t* si, int64_t* so) {
+    int r = 0;
+    for (int i = 0; i < in.rank; ++i) {
+        if (in.ext[i] == 1) continue;
+        if (r > 0 && si[r - 1] == in.str[i] * in.ext[i] && so[r - 1] == out.str[i] * in.ext[i]) {
+            ext[r - 1] *= in.ext[i];  // axis i continues the previous one in both tensors
+            si[r - 1] = in.str[i];
+            so[r - 1] = out.str[i];
+            continue;
+        }
+        ext[r] = in.ext[i];
+        si[r] = in.str[i];
+        so[r] = out.str[i];
+        ++r;
+    }
+    return r;
+}
+
 template <typename T>
 int scale(ann_stream stream, const ann_view* in_v, T scalar, const ann_view* out_v) {
     Dims in, out;
@@ -171,6 +224,30 @@ int scale(ann_stream stream, const ann_view* in_v, T scalar, const ann_view* out
         same = same && (in.ext[i] == 1 || in.str[i] == out.str[i]);
     }
     bool const dense = same && in.dense() && aligned(in.data, 16) && aligned(out.data, 16);
+    if (!dense) {
+        int64_t ext[ANN_MAX_RANK], si[ANN_MAX_RANK], so[ANN_MAX_RANK];
+        int const r = merge_axes(in, out, ext, si, so);
+        constexpr int NV = Vec16<T>::n;
+        bool rows = r >= 1 && si[r - 1] == 1 && so[r - 1] == 1 && ext[r - 1] % NV == 0 && aligned(in.data, 16) &&
+                    aligned(out.data, 16);
+        for (int i = 0; rows && i < r - 1; ++i) rows = (si[i] * sizeof(T)) % 16 == 0 && (so[i] * sizeof(T)) % 16 == 0;
+        if (rows) {
+            ScaleRowArgs ra{};
+            ra.in = in.data;
+            ra.out = out.data;
+            ra.len = ext[r - 1];
+            ra.rows = a.n / ra.len;
+            ra.outer.n = r - 1;
+            for (int i = 0; i < r - 1; ++i) {
+                ra.outer.ext[i] = ext[i];
+                ra.outer.sa[i] = si[i];
+                ra.outer.sb[i] = so[i];
+            }
+            int const blocks = static_cast<int>(std::min<int64_t>(ceil_div(ra.rows, 8), 148 * 16));
+            scale_rows_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(ra, scalar);
+            return check_launch("scale");
+        }
+    }
     int const grid = grid_for(a.n, 256 * 4);
     if (dense)
         scale_kernel<T, true><<<grid, 256, 0, as_stream(stream)>>>(a, scalar);

@@ -346,36 +346,38 @@ PREFILL = {
 
 
 def measure_prefill(name, world, rank, reps=10):
-    """Fused causal prefill of this rank's heads (heads sharded over ranks),
-    timed with CUDA events; TFLOP/s counts QK^T + PV over the causal half
-    including the diagonal, 4*B*H*D*T(T+1)/2, for the whole job."""
+    """Fused causal prefill of this rank's heads (heads sharded over ranks) and,
+    for N > 1, the all-gather of the outputs into BTHD (batch b gathered while
+    batch b + 1 computes), timed with CUDA events; TFLOP/s counts QK^T + PV over
+    the causal half including the diagonal, 4*B*H*D*T(T+1)/2, for the whole job."""
     import torch
 
     import alpakann_b200 as ann
+    from alpakann_b200.sharded import HeadShard, HeadShardedPrefill
     p = PREFILL[name]
     B, T, H, D = p["B"], p["T"], p["H"], p["D"]
     dt = torch.float32 if p["dtype"] == "f32" else torch.float64
     Hl = H // world
     gen = torch.Generator(device="cuda").manual_seed(77 + rank)
     q, k, v = (torch.randn((B, T, Hl, D), generator=gen, dtype=dt, device="cuda") for _ in range(3))
-    o = torch.empty_like(q)
     queue = ann.Queue()
     sc = 1.0 / math.sqrt(D)
+    sharded = HeadShardedPrefill(HeadShard(rank, world, H, H), B, T, D, dt, "cuda")
     for _ in range(2):
-        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+        sharded.run(queue, q, k, v, sc)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        ann.onHost.nn.attentionPrefill(queue, None, q, k, v, o, sc, 1, 0, True)
+        sharded.run(queue, q, k, v, sc)
     e1.record()
     barrier(world)
     t = max_over_ranks([e0.elapsed_time(e1) / 1e3 / reps], world)[0]
     flops = 4 * B * H * D * T * (T + 1) / 2
-    del q, k, v, o
+    del q, k, v, sharded
     torch.cuda.empty_cache()
     res = {"workload": p["desc"], "ms": t * 1e3, "tflops": flops / t / 1e12, "tokens_per_s": B * T / t,
-           "dtype": p["dtype"]}
+           "dtype": p["dtype"], "gathered": world > 1}
     if p["dtype"] == "f32":
         # 3xTF32: every useful flop costs three tf32 tensor flops
         pk, kind = tf32_peak()
@@ -433,8 +435,8 @@ def main():
     torch.cuda.set_device(local)
     group = None
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=120))
+        from alpakann_b200.sharded import join
+        join(rank, world, "nccl", timeout_s=120, device=torch.device("cuda", local))
     peak, peak_kind = peaks()
 
     def run(wl, steps, warmup, with_clocks):

@@ -1,0 +1,79 @@
+"""Head sharding across two GPUs (NCCL): the gathered decode and prefill outputs
+must equal the 1-GPU outputs bit for bit -- the same kernels run the same
+per-head arithmetic, and the decode split is pinned (ANN_DECODE_SPLITS) so that
+both runs sum every row in the same order. Runs only where 2 GPUs are visible."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _two_gpus():
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), ANN_DECODE_SPLITS="2")
+    torch.cuda.set_device(rank)
+    import torch.distributed as dist
+
+    import alpakann_b200 as ann
+    from alpakann_b200.sharded import HeadShard, HeadShardedDecode, HeadShardedPrefill, join
+    join(rank, world, "nccl", timeout_s=60, device=torch.device("cuda", rank))
+    try:
+        gen = torch.Generator().manual_seed(2024)
+        res = {}
+        # ---- decode, GQA (8 query heads over 4 KV heads), BHTD cache, RoPE at position Tk
+        B, H, Hkv, Tk, D = 3, 8, 4, 700, 128
+        q, knew = (torch.randn(B, 1, H, D, generator=gen) for _ in range(2))
+        k, v = (torch.randn(B, Hkv, Tk, D, generator=gen) for _ in range(2))
+        ang = np.arange(Tk + 1)[:, None] * np.power(1e4, -2.0 * np.arange(D // 2) / D)[None]
+        cos = torch.from_numpy(np.cos(ang)).float().cuda()
+        sin = torch.from_numpy(np.sin(ang)).float().cuda()
+        sc = 1.0 / math.sqrt(D)
+        shard = HeadShard(rank, world, H, Hkv)
+        hs, ks = shard.head_slice, shard.kv_head_slice
+        dec = HeadShardedDecode(shard, B, D, torch.float32, "cuda")
+        got = dec.step(ann.Queue(), q[:, :, hs].contiguous().cuda(), knew[:, :, hs].contiguous().cuda(),
+                       k[:, ks].contiguous().cuda(), v[:, ks].contiguous().cuda(), cos, sin, Tk, sc).cpu()
+        one = HeadShardedDecode(HeadShard(0, 1, H, Hkv), B, D, torch.float32, "cuda")
+        ref = one.step(ann.Queue(), q.cuda(), knew.cuda(), k.cuda(), v.cuda(), cos, sin, Tk, sc).cpu()
+        res["decode"] = bool(torch.equal(got, ref))
+        # ---- causal prefill, fp32 (tensor cores) and fp64 (DFMA), BTHD
+        for name, dt, (B, T, H, D) in (("prefill_f32", torch.float32, (2, 300, 4, 128)),
+                                       ("prefill_f64", torch.float64, (2, 200, 4, 64))):
+            q, k, v = (torch.randn(B, T, H, D, generator=gen, dtype=dt) for _ in range(3))
+            shard = HeadShard(rank, world, H, H)
+            hs = shard.head_slice
+            sp = HeadShardedPrefill(shard, B, T, D, dt, "cuda")
+            sc = 1.0 / math.sqrt(D)
+            got = sp.run(ann.Queue(), *(x[:, :, hs].contiguous().cuda() for x in (q, k, v)), sc).cpu()
+            ref = torch.empty(B, T, H, D, dtype=dt, device="cuda")
+            ann.onHost.nn.attentionPrefill(ann.Queue(), None, q.cuda(), k.cuda(), v.cuda(), ref, sc, 1, 0, True)
+            res[name] = bool(torch.equal(got, ref.cpu()))
+        torch.cuda.synchronize()
+        res["device_error"] = ann.Queue().take_device_error()
+        result[rank] = res
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs 2 GPUs")
+def test_two_gpu_head_sharding_equals_one_gpu():
+    mgr = mp.get_context("spawn").Manager()
+    result = mgr.dict()
+    mp.start_processes(_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
+    want = {"decode": True, "prefill_f32": True, "prefill_f64": True, "device_error": 0}
+    assert dict(result) == {0: want, 1: want}

@@ -358,3 +358,31 @@ def test_decode_forced_cluster_sizes(ann, monkeypatch, T, D, splits):
     ann.onHost.nn.attentionDecode(queue, None, dev(q), dev(k), dev(v), o, scale, 1, ann.AttentionKvLayout.BHTD)
     assert_close(host(o), ref, T, f"decode splits={splits}")
     assert queue.take_device_error() == 0
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("case", ["reassembly", "sliced", "odd_rows"])
+def test_scale_strided_views_bitexact(ann, T, case):
+    """ops::scale on strided views (the row path for unit-stride inner runs and the
+    generic element path), bit for bit against the same product in numpy."""
+    import torch
+    g = rng(17)
+    s = T(0.5) if case != "reassembly" else T(1.0)
+    if case == "reassembly":   # rank-major gather [G,B,T,Hl,D] -> BTHD [B,T,G,Hl,D]
+        x = normal(g, (4, 3, 5, 2, 64), T)
+        src = dev(x).permute(1, 2, 0, 3, 4)
+        out = torch.full((3, 5, 4, 2, 64), float("nan"), dtype=src.dtype, device="cuda")
+        ref = (x.transpose(1, 2, 0, 3, 4) * s).astype(T)
+    elif case == "sliced":     # every other row of a matrix into a column-sliced output
+        x = normal(g, (40, 96), T)
+        src = dev(x)[::2, 8:72]
+        big = torch.full((20, 80), float("nan"), dtype=src.dtype, device="cuda")
+        out = big[:, 4:68]
+        ref = (x[::2, 8:72] * s).astype(T)
+    else:                      # rows of 3 elements: not a whole 16-byte vector, generic path
+        x = normal(g, (7, 9, 3), T)
+        src = dev(x).permute(1, 0, 2)
+        out = torch.full((9, 7, 3), float("nan"), dtype=src.dtype, device="cuda")
+        ref = (x.transpose(1, 0, 2) * s).astype(T)
+    ann.onHost.ops.scale(ann.Queue(), None, src, s, out)
+    assert np.array_equal(host(out), ref)

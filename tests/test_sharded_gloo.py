@@ -4,13 +4,14 @@ unsharded result exactly. The per-rank attention here is a torch fp64
 restatement (the GPU kernels are covered by the -m gpu tests)."""
 import os
 import socket
+import time
 
 import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from alpakann_b200.sharded import HeadShard, gathered_buffer, reassembly_views
+from alpakann_b200.sharded import HeadShard, ShardingError, gathered_buffer, join, reassembly_views
 
 
 def _free_port():
@@ -71,3 +72,64 @@ def test_shard_validation():
     g = gathered_buffer(s, 2, 1, 4, torch.float32, "cpu")
     with pytest.raises(ValueError):
         reassembly_views(g, torch.empty(2, 1, 63, 4))
+
+
+def _absent_peer_worker(rank, world, port, result):
+    """Rank 1 never joins; rank 0's join must end at its deadline."""
+    if rank == 1:
+        return
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    t0 = time.monotonic()
+    try:
+        join(rank, world, "gloo", timeout_s=3.0)
+        result[rank] = ("joined", time.monotonic() - t0)
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    except ShardingError:
+        result[rank] = ("ShardingError", time.monotonic() - t0)
+
+
+def test_rank_that_never_joins_ends_in_an_error():
+    mgr = mp.get_context("spawn").Manager()
+    result = mgr.dict()
+    mp.start_processes(_absent_peer_worker, args=(2, _free_port(), result), nprocs=2, join=True,
+                       start_method="spawn")
+    kind, seconds = result[0]
+    assert kind == "ShardingError"
+    assert seconds < 60
+
+
+def _leaving_peer_worker(rank, world, port, result):
+    """Both ranks join; rank 1 leaves before the all-gather of a step. Rank 0's
+    all-gather must fail (peer gone or process-group timeout), not wait for good."""
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    join(rank, world, "gloo", timeout_s=5.0)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, without a clean shutdown
+    shard = HeadShard(rank, world, 4, 4)
+    gathered = gathered_buffer(shard, 1, 1, 8, torch.float32, "cpu")
+    t0 = time.monotonic()
+    try:
+        dist.all_gather(list(gathered.unbind(0)), torch.zeros(1, 1, 2, 8))
+        result[rank] = ("completed", time.monotonic() - t0)
+    except Exception as e:  # gloo reports the closed connection or its timeout
+        result[rank] = (type(e).__name__, time.monotonic() - t0)
+    os._exit(0)
+
+
+def test_rank_that_leaves_before_the_gather_ends_in_an_error():
+    mgr = mp.get_context("spawn").Manager()
+    result = mgr.dict()
+    ctx = mp.start_processes(_leaving_peer_worker, args=(2, _free_port(), result), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 120
+    while 0 not in result and time.monotonic() < deadline:
+        time.sleep(0.2)
+    for p in ctx.processes:
+        p.join(timeout=10)
+        if p.is_alive():
+            p.kill()
+    kind, seconds = result[0]
+    assert kind != "completed"
+    assert seconds < 60
