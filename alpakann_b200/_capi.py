@@ -11,7 +11,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libann_b200.so")
 
-ANN_OK, ANN_EINVAL, ANN_ECUDA, ANN_ENOTSUP, ANN_EDEVICE = 0, 1, 2, 3, 4
+ANN_OK, ANN_EINVAL, ANN_ECUDA, ANN_ENOTSUP, ANN_EDEVICE, ANN_ENCCL = 0, 1, 2, 3, 4, 5
+COMM_ID_BYTES = 128
 ANN_DEVERR_TOKEN_ID, ANN_DEVERR_WAIT_TIMEOUT = 0x1, 0x2
 MAX_RANK = 8
 
@@ -33,10 +34,18 @@ _f = {"f32": ctypes.c_float, "f64": ctypes.c_double}
 
 # Every exported entry point and its argument types. The symbol test checks
 # this table against include/ann_b200.h.
+_C = ctypes.c_void_p  # ann_comm
+_ID = ctypes.c_char * COMM_ID_BYTES
 SIGNATURES = {
     "ann_version": ([], ctypes.c_int),
     "ann_last_error": ([], ctypes.c_char_p),
     "ann_take_device_error": ([_S, ctypes.POINTER(_u32)], ctypes.c_int),
+    "ann_comm_unique_id": ([ctypes.POINTER(_ID)], ctypes.c_int),
+    "ann_comm_init": ([ctypes.POINTER(_C), _i32, _i32, ctypes.POINTER(_ID), ctypes.c_double], ctypes.c_int),
+    "ann_comm_size": ([_C, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], ctypes.c_int),
+    "ann_comm_allgather": ([_C, _S, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "ann_comm_destroy": ([_C], ctypes.c_int),
+    "ann_comm_abort": ([_C], ctypes.c_int),
 }
 for _sfx, _ft in _f.items():
     SIGNATURES.update({
@@ -75,6 +84,10 @@ class AnnNotSupported(AnnError, NotImplementedError):
     """ANN_ENOTSUP."""
 
 
+class AnnCommError(AnnError):
+    """ANN_ENCCL: NCCL failed, or a rank did not join / finish within the deadline."""
+
+
 def check(rc: int) -> None:
     if rc == ANN_OK:
         return
@@ -83,6 +96,8 @@ def check(rc: int) -> None:
         raise AnnShapeError(rc, msg)
     if rc == ANN_ENOTSUP:
         raise AnnNotSupported(rc, msg)
+    if rc == ANN_ENCCL:
+        raise AnnCommError(rc, msg)
     raise AnnError(rc, msg)
 
 

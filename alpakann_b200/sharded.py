@@ -8,9 +8,10 @@ those heads of the KV cache. A decode step on every rank is
     ropeInPlace(Q_r, Knew_r) -> fused decode attention over its cache slice
     -> all-gather of the per-rank outputs -> re-assembly into BTHD [B,T,H,D]
 
-The all-gather concatenates rank-major ([G][B,T,H/G,D]); the re-assembly is a
-strided copy into the [B,T,G,H/G,D] view of the output (one CUDA kernel of
-this library: ops::scale by 1 with strided views).
+The all-gather (this library's NCCL communicator, alpakann_b200.comm.Comm,
+enqueued on the step's own queue) concatenates rank-major ([G][B,T,H/G,D]);
+the re-assembly is a strided copy into the [B,T,G,H/G,D] view of the output
+(one CUDA kernel of this library: ops::scale by 1 with strided views).
 
 Prefill does the same per batch index: the fused causal prefill of batch b
 on this rank's heads, then an asynchronous all-gather of that [T,H/G,D] slab
@@ -25,14 +26,6 @@ import torch
 
 class ShardingError(RuntimeError):
     """A rank did not join, or left before a collective finished, within the deadline."""
-
-
-def _check_queue(queue):
-    """torch.distributed orders a collective after torch's current stream, so the
-    kernels before it must run there too."""
-    handle = torch.cuda.current_stream().cuda_stream
-    if queue.handle != handle:
-        raise ValueError("the sharded path needs a Queue on torch's current stream (ann.Queue())")
 
 
 def join(rank: int, world: int, backend: str = "nccl", timeout_s: float = 60.0, device=None):
@@ -98,11 +91,13 @@ def reassembly_views(gathered: torch.Tensor, out: torch.Tensor):
 
 
 class HeadShardedDecode:
-    """One decode step of the head-sharded path on this rank. `group` is a
-    torch.distributed process group (NCCL on GPUs); world 1 needs none."""
+    """One decode step of the head-sharded path on this rank. `comm` is the
+    node's communicator (alpakann_b200.comm.Comm); world 1 needs none."""
 
-    def __init__(self, shard: HeadShard, B: int, D: int, dtype=torch.float32, device="cuda", group=None):
-        self.shard, self.B, self.D, self.group = shard, B, D, group
+    def __init__(self, shard: HeadShard, B: int, D: int, dtype=torch.float32, device="cuda", comm=None):
+        if shard.world > 1 and comm is None:
+            raise ValueError("a sharded step over several ranks needs a Comm")
+        self.shard, self.B, self.D, self.comm = shard, B, D, comm
         self.out_local = torch.empty((B, 1, shard.local_heads, D), dtype=dtype, device=device)
         self.out = torch.empty((B, 1, shard.heads, D), dtype=dtype, device=device)
         self.gathered = gathered_buffer(shard, B, 1, D, dtype, device) if shard.world > 1 else None
@@ -112,11 +107,7 @@ class HeadShardedDecode:
     def step(self, queue, q, knew, k_cache, v_cache, cos, sin, position, scale):
         """q, knew: [B,1,H/G,D] of this rank (rotated in place); k_cache,
         v_cache: [B, H/G, Tk, D] of this rank. Returns the full [B,1,H,D]."""
-        import torch.distributed as dist
-
         from . import AttentionKvLayout, RopeLayout, onHost
-        if self.shard.world > 1:
-            _check_queue(queue)
         g = self.shard.heads // self.shard.kv_heads
         onHost.nn.ropeInPlace(queue, None, q, knew, cos, sin, RopeLayout.BTHD, position)
         if self.shard.world == 1:
@@ -124,61 +115,65 @@ class HeadShardedDecode:
             return self.out
         onHost.nn.attentionDecode(queue, None, q, k_cache, v_cache, self.out_local, scale, g,
                                   AttentionKvLayout.BHTD)
-        dist.all_gather_into_tensor(self.gathered, self.out_local, group=self.group)
+        self.comm.all_gather(queue, self.out_local, self.gathered)
         onHost.ops.scale(queue, None, self._src, 1.0, self._dst)
         return self.out
 
 
 class HeadShardedPrefill:
     """Fused causal prefill of this rank's heads, gathered into the full BTHD
-    output. Batch index b is one chunk on its own side stream: prefill(b) ->
-    all-gather(b) (NCCL, ordered after prefill(b) only) -> re-assembly(b), so the
-    chunks' prefills run side by side and fill the GPU while finished chunks are
-    gathered; the caller's stream waits for every chunk at the end. `group` as
-    in HeadShardedDecode."""
+    output. Batch index b is one chunk on its own side stream: prefill(b), then
+    its all-gather on the communicator's stream (gathers keep one order on every
+    rank), then its re-assembly; the chunks' prefills run side by side while
+    finished chunks are gathered, and the caller's queue waits for every chunk
+    at the end. `comm` as in HeadShardedDecode."""
 
-    def __init__(self, shard: HeadShard, B: int, T: int, D: int, dtype=torch.float32, device="cuda", group=None,
+    def __init__(self, shard: HeadShard, B: int, T: int, D: int, dtype=torch.float32, device="cuda", comm=None,
                  streams: int = 4):
-        self.shard, self.B, self.T, self.D, self.group = shard, B, T, D, group
+        if shard.world > 1 and comm is None:
+            raise ValueError("a sharded prefill over several ranks needs a Comm")
+        self.shard, self.B, self.T, self.D, self.comm = shard, B, T, D, comm
         self.out = torch.empty((B, T, shard.heads, D), dtype=dtype, device=device)
         if shard.world > 1:
             self.out_local = torch.empty((B, T, shard.local_heads, D), dtype=dtype, device=device)
             # one receive slab per batch index so that gathers in flight never share a buffer
             self.gathered = torch.empty((B, shard.world, 1, T, shard.local_heads, D), dtype=dtype, device=device)
             self._views = [reassembly_views(self.gathered[b], self.out[b:b + 1]) for b in range(B)]
-            self._streams = [torch.cuda.Stream(device=device) for _ in range(max(1, min(streams, B)))]
+            self._side = [torch.cuda.Stream(device=device) for _ in range(max(1, min(streams, B)))]
+            self._comm_stream = torch.cuda.Stream(device=device)
 
     def run(self, queue, q, k, v, scale, kv_layout=None, causal=True):
         """q: [B,T,H/G,D], k/v: [B,Tk,H_kv/G,D] (BTHD) or [B,H_kv/G,Tk,D] (BHTD)
-        of this rank. Returns the full [B,T,H,D] output (ready on the caller's stream)."""
-        import torch.distributed as dist
-
+        of this rank. Returns the full [B,T,H,D] output (ready in `queue` order)."""
         from . import AttentionKvLayout, Queue, onHost
         layout = AttentionKvLayout.BTHD if kv_layout is None else kv_layout
         g = self.shard.heads // self.shard.kv_heads
         if self.shard.world == 1:
             onHost.nn.attentionPrefill(queue, None, q, k, v, self.out, scale, g, layout, causal)
             return self.out
-        _check_queue(queue)
-        main = torch.cuda.current_stream()
+        caller = queue.stream if not isinstance(queue.stream, int) else torch.cuda.ExternalStream(queue.stream)
+        comm_q = Queue(self._comm_stream)
         inputs_ready = torch.cuda.Event()
-        inputs_ready.record(main)
+        inputs_ready.record(caller)
         chunk_done = []
-        for b in range(self.B):  # every rank issues the gathers in the same order
-            side = self._streams[b % len(self._streams)]
-            with torch.cuda.stream(side):
-                side.wait_event(inputs_ready)
-                sq = Queue(side)
-                onHost.nn.attentionPrefill(sq, None, q[b:b + 1], k[b:b + 1], v[b:b + 1], self.out_local[b:b + 1],
-                                           scale, g, layout, causal)
-                work = dist.all_gather_into_tensor(self.gathered[b], self.out_local[b:b + 1], group=self.group,
-                                                   async_op=True)
-                work.wait()  # the side stream (not the host) waits for the gather
-                src, dst = self._views[b]
-                onHost.ops.scale(sq, None, src, 1.0, dst)
-                done = torch.cuda.Event()
-                done.record(side)
-                chunk_done.append(done)
+        for b in range(self.B):
+            side = self._side[b % len(self._side)]
+            sq = Queue(side)
+            side.wait_event(inputs_ready)
+            onHost.nn.attentionPrefill(sq, None, q[b:b + 1], k[b:b + 1], v[b:b + 1], self.out_local[b:b + 1],
+                                       scale, g, layout, causal)
+            computed = torch.cuda.Event()
+            computed.record(side)
+            self._comm_stream.wait_event(computed)
+            self.comm.all_gather(comm_q, self.out_local[b:b + 1], self.gathered[b])
+            gathered = torch.cuda.Event()
+            gathered.record(self._comm_stream)
+            side.wait_event(gathered)
+            src, dst = self._views[b]
+            onHost.ops.scale(sq, None, src, 1.0, dst)
+            done = torch.cuda.Event()
+            done.record(side)
+            chunk_done.append(done)
         for done in chunk_done:
-            main.wait_event(done)
+            caller.wait_event(done)
         return self.out

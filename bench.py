@@ -213,7 +213,7 @@ class DecodeBench:
     """Inputs and the two step flavours (device-resident and end-to-end) of
     the head-sharded decode workload on this rank."""
 
-    def __init__(self, w, rank, world, group):
+    def __init__(self, w, rank, world, comm):
         import numpy as np
         import torch
 
@@ -238,7 +238,8 @@ class DecodeBench:
         self.cos = torch.from_numpy(np.cos(ang)).to(f32).cuda()
         self.sin = torch.from_numpy(np.sin(ang)).to(f32).cuda()
         self.scale = 1.0 / math.sqrt(D)
-        self.sharded = HeadShardedDecode(self.shard, B, D, f32, "cuda", group)
+        self.sharded = HeadShardedDecode(self.shard, B, D, f32, "cuda", comm)
+        self.comm = comm
         self.stream = torch.cuda.current_stream()
         self.queue = ann.Queue(self.stream)
         # descriptors built once: the device-timed loop only issues C-ABI calls
@@ -248,7 +249,8 @@ class DecodeBench:
         self.vkv = [(V(k), V(v)) for k, v in self.caches]
         if world > 1:
             self.vsrc, self.vdst = V(self.sharded._src), V(self.sharded._dst)
-        self.launches_per_step = 2 if world == 1 else 3
+        self.launches_per_step = 2 if world == 1 else 3  # rope, decode (+ re-assembly); NCCL's own kernel not counted
+        self.gather_bytes = self.sharded.out_local.numel() * 4
         # pinned host buffers of the end-to-end step
         self.hq = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
         self.hk = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
@@ -263,9 +265,9 @@ class DecodeBench:
         chk(lib.ann_attention_decode_f32(sh, R(self.vq), R(vk), R(vv), R(self.vout), self.scale, 1, 1))
         if ev is not None:
             ev[1].record(self.stream)
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.sharded.gathered, self.sharded.out_local, group=self.sharded.group)
+        if self.world > 1:  # this library's NCCL all-gather, then the re-assembly kernel
+            chk(lib.ann_comm_allgather(self.comm._h, sh, self.sharded.out_local.data_ptr(),
+                                       self.sharded.gathered.data_ptr(), self.gather_bytes))
             chk(lib.ann_scale_f32(sh, R(self.vsrc), 1.0, R(self.vdst)))
 
     def e2e_step(self, i):
@@ -345,7 +347,7 @@ PREFILL = {
 }
 
 
-def measure_prefill(name, world, rank, reps=10):
+def measure_prefill(name, world, rank, comm, reps=10):
     """Fused causal prefill of this rank's heads (heads sharded over ranks) and,
     for N > 1, the all-gather of the outputs into BTHD (batch b gathered while
     batch b + 1 computes), timed with CUDA events; TFLOP/s counts QK^T + PV over
@@ -362,7 +364,7 @@ def measure_prefill(name, world, rank, reps=10):
     q, k, v = (torch.randn((B, T, Hl, D), generator=gen, dtype=dt, device="cuda") for _ in range(3))
     queue = ann.Queue()
     sc = 1.0 / math.sqrt(D)
-    sharded = HeadShardedPrefill(HeadShard(rank, world, H, H), B, T, D, dt, "cuda")
+    sharded = HeadShardedPrefill(HeadShard(rank, world, H, H), B, T, D, dt, "cuda", comm)
     for _ in range(2):
         sharded.run(queue, q, k, v, sc)
     barrier(world)
@@ -433,14 +435,16 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    group = None
-    if world > 1:
+    comm = None
+    if world > 1:  # torch.distributed: rendezvous, barriers, max over ranks; the data path uses comm
+        from alpakann_b200.comm import Comm
         from alpakann_b200.sharded import join
         join(rank, world, "nccl", timeout_s=120, device=torch.device("cuda", local))
+        comm = Comm.from_torch(timeout_s=120)
     peak, peak_kind = peaks()
 
     def run(wl, steps, warmup, with_clocks):
-        bench = DecodeBench(WORKLOADS[wl], rank, world, group)
+        bench = DecodeBench(WORKLOADS[wl], rank, world, comm)
         elapsed, kernel_s, e2e_s, e2e_steps, clk = measure(bench, steps, warmup, world, rank, with_clocks)
         ww = WORKLOADS[wl]
         B, Tk, H, D = ww["B"], ww["Tk"], ww["H"], ww["D"]
@@ -462,7 +466,7 @@ def main():
                         "ms_per_step": o["ms_per_step"], "kernel_us": o["kernel_us"],
                         "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"]}
         for name in ("c3", "c4"):
-            extra[f"{name}_prefill"] = measure_prefill(name, world, rank)
+            extra[f"{name}_prefill"] = measure_prefill(name, world, rank, comm)
 
     if rank == 0:
         r = main_res
@@ -498,7 +502,9 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        comm.close()
         dist.destroy_process_group()
 
 

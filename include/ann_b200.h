@@ -42,6 +42,7 @@ extern "C" {
 #define ANN_ECUDA 2   /* CUDA runtime error (launch, memcpy, no device)            */
 #define ANN_ENOTSUP 3 /* valid request this build does not implement               */
 #define ANN_EDEVICE 4 /* a kernel reported an error through the device error word  */
+#define ANN_ENCCL 5   /* NCCL error, or a rank that did not join / finish in time  */
 
 #define ANN_MAX_RANK 8
 
@@ -55,6 +56,8 @@ extern "C" {
 #define ANN_DEVERR_WAIT_TIMEOUT 0x2u /* a kernel gave up waiting for its own copies (1 s) */
 
 typedef void* ann_stream; /* cudaStream_t */
+typedef struct ann_comm_s* ann_comm; /* one rank of the node's NCCL communicator */
+#define ANN_COMM_ID_BYTES 128        /* size of the rendezvous id (ncclUniqueId)  */
 
 /* Strided view of a tensor: the B200 counterpart of an alpaka IMdSpan
  * (extents from getExtents(), byte pitches from getPitches(), data()). */
@@ -199,6 +202,32 @@ int ann_attention_prefill_f32(ann_stream stream, const ann_view* q, const ann_vi
 int ann_attention_prefill_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
                               const ann_view* out, double scale, uint32_t queries_per_kv_group, int32_t kv_layout,
                               int32_t causal);
+
+/* ---- head sharding across the GPUs of one node ------------------------------
+ * No reference counterpart: the reference path runs on one device. Attention
+ * heads are independent (onAcc/internal/nn/attention.hpp:28-36, 57-64 read only
+ * query head hq and KV head hq / g), so rank r of G computes heads
+ * [r*H/G, (r+1)*H/G) and the per-rank output slabs are re-assembled with one
+ * rank-major all-gather over NVLink. NCCL is loaded at first use; ANN_ENOTSUP
+ * if libnccl.so.2 cannot be loaded.
+ *
+ * ann_comm_unique_id: rank 0 creates the rendezvous id and hands the
+ *   ANN_COMM_ID_BYTES bytes to the other ranks out of band.
+ * ann_comm_init: joins the communicator on the current CUDA device. Non-blocking:
+ *   if the other ranks have not joined within timeout_s seconds, the half-built
+ *   communicator is aborted and ANN_ENCCL returned. timeout_s is also the bound
+ *   of the later calls on this communicator.
+ * ann_comm_allgather: recv = the bytes_per_rank of every rank's send, rank-major,
+ *   enqueued on `stream`.
+ * ann_comm_destroy: flushes pending work (within the deadline, else aborts) and
+ *   frees the communicator; ann_comm_abort tears it down at once (a peer died). */
+int ann_comm_unique_id(unsigned char id[ANN_COMM_ID_BYTES]);
+int ann_comm_init(ann_comm* comm, int32_t nranks, int32_t rank, const unsigned char id[ANN_COMM_ID_BYTES],
+                  double timeout_s);
+int ann_comm_size(ann_comm comm, int32_t* nranks, int32_t* rank);
+int ann_comm_allgather(ann_comm comm, ann_stream stream, const void* send, void* recv, uint64_t bytes_per_rank);
+int ann_comm_destroy(ann_comm comm);
+int ann_comm_abort(ann_comm comm);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -176,3 +176,25 @@ def test_prefill_validation(capi, sfx, T):
     assert "extents of Q" in _call_einval(capi, fp, r(q), r(kv), r(kv), r(np.ones((1, 8, 4, 32), T)), 0.1, 1, 0, 1)
     assert "does not match" in _call_einval(capi, fp, r(q), r(np.ones((1, 8, 4, 32), T)),
                                             r(np.ones((1, 8, 4, 32), T)), r(q), 0.1, 1, 0, 1)
+
+
+
+def test_comm_argument_validation():
+    """ann_comm_* reject bad arguments on the host, before NCCL is touched."""
+    import ctypes
+
+    from alpakann_b200 import _capi
+    lib = _capi.lib
+    uid = (ctypes.c_char * _capi.COMM_ID_BYTES)()
+    h = ctypes.c_void_p()
+    assert lib.ann_comm_init(ctypes.byref(h), 0, 0, ctypes.byref(uid), 10.0) == _capi.ANN_EINVAL
+    assert lib.ann_comm_init(ctypes.byref(h), 2, 2, ctypes.byref(uid), 10.0) == _capi.ANN_EINVAL
+    assert lib.ann_comm_init(ctypes.byref(h), 2, -1, ctypes.byref(uid), 10.0) == _capi.ANN_EINVAL
+    assert lib.ann_comm_init(ctypes.byref(h), 2, 0, ctypes.byref(uid), 0.0) == _capi.ANN_EINVAL
+    assert lib.ann_comm_init(None, 2, 0, ctypes.byref(uid), 10.0) == _capi.ANN_EINVAL
+    assert lib.ann_comm_unique_id(None) == _capi.ANN_EINVAL
+    assert lib.ann_comm_allgather(None, None, None, None, 16) == _capi.ANN_EINVAL
+    assert b"null communicator" in lib.ann_last_error()
+    assert lib.ann_comm_size(None, None, None) == _capi.ANN_EINVAL
+    assert lib.ann_comm_destroy(None) == _capi.ANN_OK
+    assert lib.ann_comm_abort(None) == _capi.ANN_OK

@@ -1,7 +1,11 @@
-"""Head sharding across two GPUs (NCCL): the gathered decode and prefill outputs
-must equal the 1-GPU outputs bit for bit -- the same kernels run the same
-per-head arithmetic, and the decode split is pinned (ANN_DECODE_SPLITS) so that
-both runs sum every row in the same order. Runs only where 2 GPUs are visible."""
+"""The node's communicator (ann_comm_*, NCCL) and head sharding across GPUs.
+
+On one GPU: a 1-rank communicator gathers exactly, and a rank whose peer never
+joins ends in ANN_ENCCL at its deadline (host-side bootstrap wait; no kernel
+runs). On two GPUs: the gathered decode and prefill outputs equal the 1-GPU
+outputs bit for bit -- the same kernels run the same per-head arithmetic, and the
+decode split is pinned (ANN_DECODE_SPLITS) so that both runs sum every row in
+the same order."""
 import math
 import os
 import socket
@@ -30,8 +34,10 @@ def _worker(rank, world, port, result):
     import torch.distributed as dist
 
     import alpakann_b200 as ann
+    from alpakann_b200.comm import Comm
     from alpakann_b200.sharded import HeadShard, HeadShardedDecode, HeadShardedPrefill, join
     join(rank, world, "nccl", timeout_s=60, device=torch.device("cuda", rank))
+    comm = Comm.from_torch(timeout_s=60)
     try:
         gen = torch.Generator().manual_seed(2024)
         res = {}
@@ -45,7 +51,7 @@ def _worker(rank, world, port, result):
         sc = 1.0 / math.sqrt(D)
         shard = HeadShard(rank, world, H, Hkv)
         hs, ks = shard.head_slice, shard.kv_head_slice
-        dec = HeadShardedDecode(shard, B, D, torch.float32, "cuda")
+        dec = HeadShardedDecode(shard, B, D, torch.float32, "cuda", comm)
         got = dec.step(ann.Queue(), q[:, :, hs].contiguous().cuda(), knew[:, :, hs].contiguous().cuda(),
                        k[:, ks].contiguous().cuda(), v[:, ks].contiguous().cuda(), cos, sin, Tk, sc).cpu()
         one = HeadShardedDecode(HeadShard(0, 1, H, Hkv), B, D, torch.float32, "cuda")
@@ -57,7 +63,7 @@ def _worker(rank, world, port, result):
             q, k, v = (torch.randn(B, T, H, D, generator=gen, dtype=dt) for _ in range(3))
             shard = HeadShard(rank, world, H, H)
             hs = shard.head_slice
-            sp = HeadShardedPrefill(shard, B, T, D, dt, "cuda")
+            sp = HeadShardedPrefill(shard, B, T, D, dt, "cuda", comm)
             sc = 1.0 / math.sqrt(D)
             got = sp.run(ann.Queue(), *(x[:, :, hs].contiguous().cuda() for x in (q, k, v)), sc).cpu()
             ref = torch.empty(B, T, H, D, dtype=dt, device="cuda")
@@ -67,7 +73,47 @@ def _worker(rank, world, port, result):
         res["device_error"] = ann.Queue().take_device_error()
         result[rank] = res
     finally:
+        comm.close()
         dist.destroy_process_group()
+
+
+def test_comm_single_rank_gathers_exactly():
+    import alpakann_b200 as ann
+    from alpakann_b200.comm import Comm, unique_id
+    x = torch.randn(3, 5, 7, device="cuda")
+    y = torch.full((1, 3, 5, 7), float("nan"), device="cuda")
+    with Comm(1, 0, unique_id(), timeout_s=30) as comm:
+        assert (comm.nranks, comm.rank) == (1, 0)
+        comm.all_gather(ann.Queue(), x, y)
+        torch.cuda.synchronize()
+    assert torch.equal(y[0], x)
+
+
+def _absent_peer(result):
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from alpakann_b200._capi import AnnCommError
+    from alpakann_b200.comm import Comm, unique_id
+    torch.cuda.set_device(0)
+    t0 = time.monotonic()
+    try:
+        Comm(2, 0, unique_id(), timeout_s=3.0)  # rank 1 never joins
+        result["outcome"] = ("joined", time.monotonic() - t0)
+    except AnnCommError as e:
+        result["outcome"] = ("ANN_ENCCL", time.monotonic() - t0, str(e))
+
+
+def test_comm_rank_that_never_joins_ends_in_enccl():
+    mgr = mp.get_context("spawn").Manager()
+    result = mgr.dict()
+    p = mp.get_context("spawn").Process(target=_absent_peer, args=(result,))
+    p.start()
+    p.join(timeout=120)
+    if p.is_alive():
+        p.kill()
+    kind, seconds = result["outcome"][:2]
+    assert kind == "ANN_ENCCL"
+    assert seconds < 60
 
 
 @pytest.mark.skipif(not _two_gpus(), reason="needs 2 GPUs")
