@@ -389,3 +389,79 @@ void attentionPrefill(auto& queue, auto /*exec*/, auto const& Q, auto const& K, 
 }
 
 }  // namespace alpaka::nn::onHost::nn
+
+namespace alpaka::nn::b200 {
+
+// One rank of the node's NCCL communicator (ann_comm_*), on the current CUDA
+// device. Rank 0 creates the rendezvous id with uniqueId() and hands its bytes
+// to the other ranks out of band; a rank whose peers do not all join within
+// timeoutSeconds gets std::runtime_error (ANN_ENCCL) instead of waiting for good.
+class Comm {
+public:
+    using Id = std::array<unsigned char, ANN_COMM_ID_BYTES>;
+
+    static Id uniqueId() {
+        Id id{};
+        detail::check(ann_comm_unique_id(id.data()));
+        return id;
+    }
+    Comm(int nranks, int rank, Id const& id, double timeoutSeconds = 60.0) {
+        detail::check(ann_comm_init(&comm_, nranks, rank, id.data(), timeoutSeconds));
+        nranks_ = nranks;
+        rank_ = rank;
+    }
+    Comm(Comm const&) = delete;
+    Comm& operator=(Comm const&) = delete;
+    ~Comm() {
+        if (comm_) ann_comm_destroy(comm_);
+    }
+    int size() const { return nranks_; }
+    int rank() const { return rank_; }
+
+    // recv = the bytesPerRank of every rank's send, rank-major, enqueued on queue.
+    template <typename Q>
+    void allGather(Q& queue, void const* send, void* recv, std::size_t bytesPerRank) {
+        detail::check(ann_comm_allgather(comm_, detail::stream_of(queue), send, recv, bytesPerRank));
+    }
+    // Tear down at once (a peer died); the destructor then does nothing.
+    void abort() {
+        if (comm_) ann_comm_abort(comm_);
+        comm_ = nullptr;
+    }
+
+private:
+    ann_comm comm_ = nullptr;
+    int nranks_ = 0, rank_ = 0;
+};
+
+// One decode step of the head-sharded path on this rank of comm: RoPE on q and
+// the new K row, fused decode over this rank's cache slice into outLocal
+// [B,1,H/G,D], all-gather into gathered [G,B,1,H/G,D] (rank-major), re-assembly
+// into out [B,1,H,D] (BTHD). All views dense; caches BHTD [B,H_kv/G,Tk,D].
+template <typename T_Type>
+void headShardedDecode(auto& queue, Comm& comm, View<T_Type, 4>& q, View<T_Type, 4>& knew,
+                       auto const& cosTable, auto const& sinTable, uint32_t position,
+                       View<T_Type, 4> const& kCache, View<T_Type, 4> const& vCache, View<T_Type, 4>& outLocal,
+                       View<T_Type, 5>& gathered, View<T_Type, 4>& out, T_Type scale, uint32_t queriesPerKvGroup = 1u) {
+    onHost::nn::ropeInPlace<T_Type>(queue, 0, q, knew, cosTable, sinTable, RopeLayout::BTHD, position);
+    onHost::nn::attentionDecode<T_Type>(queue, 0, q, kCache, vCache, outLocal, scale, queriesPerKvGroup,
+                                        AttentionKvLayout::BHTD);
+    auto const& le = outLocal.extents;
+    std::size_t const bytes = static_cast<std::size_t>(le[0] * le[1] * le[2] * le[3]) * sizeof(T_Type);
+    comm.allGather(queue, outLocal.data(), gathered.data(), bytes);
+    // gathered[r, b, t, h, d] -> out[b, t, r * H/G + h, d]: two strided 5-D views of the same order
+    View<T_Type, 5> src;
+    src.ptr = gathered.ptr;
+    src.extents = {gathered.extents[1], gathered.extents[2], gathered.extents[0], gathered.extents[3],
+                   gathered.extents[4]};
+    src.pitches = {gathered.pitches[1], gathered.pitches[2], gathered.pitches[0], gathered.pitches[3],
+                   gathered.pitches[4]};
+    View<T_Type, 5> dst;
+    dst.ptr = out.ptr;
+    dst.extents = src.extents;
+    dst.pitches = {out.pitches[0], out.pitches[1], out.pitches[2] * gathered.extents[3], out.pitches[2],
+                   out.pitches[3]};
+    onHost::ops::scale<T_Type>(queue, 0, src, T_Type(1), dst);
+}
+
+}  // namespace alpaka::nn::b200

@@ -363,6 +363,42 @@ static void embedding(b200::Queue& queue) {
     REQUIRE(threw);
 }
 
+// The head-sharded decode step through a 1-rank communicator: RoPE, decode,
+// all-gather and re-assembly must give exactly the plain RoPE + decode result.
+template <typename T>
+static void headShardedOneRank(b200::Queue& queue) {
+    int64_t const B = 2, H = 4, Tk = 40, D = 64;
+    Tensor<T, 4> q({B, 1, H, D}), kn({B, 1, H, D}), q2({B, 1, H, D}), kn2({B, 1, H, D});
+    Tensor<T, 4> kc({B, H, Tk, D}), vc({B, H, Tk, D}), local({B, 1, H, D}), out({B, 1, H, D}), ref({B, 1, H, D});
+    Tensor<T, 5> gathered({1, B, 1, H, D});
+    Tensor<T, 2> cosT({Tk + 1, D / 2}), sinT({Tk + 1, D / 2});
+    fill4D<T>(q, T(0.25)), fill4D<T>(kn, T(-0.5)), fill4D<T>(kc, T(0.125)), fill4D<T>(vc, T(0.75));
+    q2.host = q.host, kn2.host = kn.host;
+    for (int64_t p = 0; p <= Tk; ++p)
+        for (int64_t i = 0; i < D / 2; ++i) {
+            double const a = static_cast<double>(p) * std::pow(10000.0, -2.0 * static_cast<double>(i) / D);
+            cosT[{p, i}] = static_cast<T>(std::cos(a)), sinT[{p, i}] = static_cast<T>(std::sin(a));
+        }
+    for (auto* t : {&q, &kn, &q2, &kn2, &kc, &vc}) t->upload();
+    cosT.upload(), sinT.upload();
+    auto qv = q.view(), knv = kn.view(), q2v = q2.view(), kn2v = kn2.view(), kcv = kc.view(), vcv = vc.view();
+    auto lv = local.view(), ov = out.view(), rv = ref.view(), cv = cosT.view(), sv = sinT.view();
+    auto gv = gathered.view();
+    T const scale = static_cast<T>(0.125);
+    {
+        b200::Comm comm(1, 0, b200::Comm::uniqueId(), 30.0);
+        REQUIRE(comm.size() == 1);
+        b200::headShardedDecode<T>(queue, comm, qv, knv, cv, sv, static_cast<uint32_t>(Tk), kcv, vcv, lv, gv, ov,
+                                   scale);
+        queue.wait();
+    }
+    nn::ropeInPlace<T>(queue, nullptr, q2v, kn2v, cv, sv, alpaka::nn::RopeLayout::BTHD, static_cast<uint32_t>(Tk));
+    nn::attentionDecode<T>(queue, nullptr, q2v, kcv, vcv, rv, scale, 1u, AttentionKvLayout::BHTD);
+    queue.wait();
+    out.download(), ref.download();
+    REQUIRE(out.host == ref.host);
+}
+
 template <typename T>
 static void all(b200::Queue& queue) {
     gqaKnownAnswers<T>(queue);
@@ -372,6 +408,7 @@ static void all(b200::Queue& queue) {
     qkvRope<T>(queue);
     rmsNorm<T>(queue);
     embedding<T>(queue);
+    headShardedOneRank<T>(queue);
 }
 
 int main() {
