@@ -51,6 +51,7 @@ for _sfx, _ft in _f.items():
     SIGNATURES.update({
         f"ann_embedding_lookup_{_sfx}": ([_S, _P, _P, _P], ctypes.c_int),
         f"ann_rms_norm_{_sfx}": ([_S, _P, _P, _P, _ft], ctypes.c_int),
+        f"ann_embedding_rms_norm_{_sfx}": ([_S, _P, _P, _P, _P, _ft], ctypes.c_int),
         f"ann_rope_{_sfx}": ([_S, _P, _P, _P, _P, _i32, _u32], ctypes.c_int),
         f"ann_rope_inplace_{_sfx}": ([_S, _P, _P, _P, _P, _i32, _u32], ctypes.c_int),
         f"ann_attention_scores_{_sfx}": ([_S, _P, _P, _P, _u32, _i32], ctypes.c_int),

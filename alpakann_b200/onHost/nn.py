@@ -29,6 +29,15 @@ def rmsNorm(queue, exec, input, weight, output, epsilon):
                                                         float(epsilon)))
 
 
+def embeddingRmsNorm(queue, exec, tokenIds, embedding, weight, output, epsilon):
+    """embeddingLookup (onHost/nn/embedding.hpp:17-36) followed by rmsNorm
+    (onHost/nn/rms_norm.hpp:17-35) in one launch, bit for bit their result."""
+    if tokenIds.dtype not in (torch.int32, torch.uint32):
+        raise TypeError("embeddingLookup expects uint32 token ids")
+    check(fn("embedding_rms_norm", suffix(embedding, weight, output))(handle(queue), ref(tokenIds), ref(embedding),
+                                                                      ref(weight), ref(output), float(epsilon)))
+
+
 def qkvProjection(queue, input, Wq, Wk, Wv, Q, K, V):
     """onHost/nn/attention.hpp:38-52 (three GEMMs on cuBLAS, no exec)."""
     sfx = suffix(input, Wq, Wk, Wv, Q, K, V)

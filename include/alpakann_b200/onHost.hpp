@@ -222,6 +222,20 @@ void rmsNorm(auto& queue, auto /*exec*/, auto const& input, auto const& weight, 
         d::check(ann_rms_norm_f64(d::stream_of(queue), &i, &w, &o, epsilon));
 }
 
+// embeddingLookup (onHost/nn/embedding.hpp:17-36) then rmsNorm
+// (onHost/nn/rms_norm.hpp:17-35) in one launch, bit for bit their result.
+template <typename T_Type>
+void embeddingRmsNorm(auto& queue, auto /*exec*/, auto const& tokenIds, auto const& embedding, auto const& weight,
+                      auto& output, T_Type epsilon) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto t = d::to_ann(tokenIds), e = d::to_ann(embedding), w = d::to_ann(weight), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_embedding_rms_norm_f32(d::stream_of(queue), &t, &e, &w, &o, epsilon));
+    else
+        d::check(ann_embedding_rms_norm_f64(d::stream_of(queue), &t, &e, &w, &o, epsilon));
+}
+
 // onHost/nn/attention.hpp:38-52
 template <typename T_Type>
 void qkvProjection(auto& queue, auto const& input, auto const& Wq, auto const& Wk, auto const& Wv, auto& Q, auto& K,

@@ -89,6 +89,17 @@ int ann_embedding_lookup_f32(ann_stream stream, const ann_view* token_ids, const
 int ann_embedding_lookup_f64(ann_stream stream, const ann_view* token_ids, const ann_view* embedding,
                              const ann_view* output);
 
+/* ---- embeddingLookup -> rmsNorm, fused -----------------------------------
+ * out[t, :] = rmsNorm(embedding[ids[t], :], weight, eps) in one launch: the
+ * path's first two calls (embedding.hpp:17-36 then rms_norm.hpp:17-35) without
+ * the hidden state's round trip through memory, bit for bit their two-launch
+ * result. Throws on the conditions of either call; an id >= embedding rows
+ * gives a zero output row and ANN_DEVERR_TOKEN_ID. */
+int ann_embedding_rms_norm_f32(ann_stream stream, const ann_view* token_ids, const ann_view* embedding,
+                               const ann_view* weight, const ann_view* output, float epsilon);
+int ann_embedding_rms_norm_f64(ann_stream stream, const ann_view* token_ids, const ann_view* embedding,
+                               const ann_view* weight, const ann_view* output, double epsilon);
+
 /* ---- rmsNorm: onHost/nn/rms_norm.hpp:17-35 ----------------------------
  * y = x * rsqrt(sum(x^2)/H + eps) * w[h] along the last axis of any rank.
  * Throws on in/out extent mismatch or weight not rank-1 [H]. */

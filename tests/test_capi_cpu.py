@@ -198,3 +198,22 @@ def test_comm_argument_validation():
     assert lib.ann_comm_size(None, None, None) == _capi.ANN_EINVAL
     assert lib.ann_comm_destroy(None) == _capi.ANN_OK
     assert lib.ann_comm_abort(None) == _capi.ANN_OK
+
+
+
+def test_embedding_rms_norm_validation():
+    """The fused call throws on the conditions of embeddingLookup and rmsNorm."""
+    import numpy as np
+
+    from alpakann_b200 import _capi
+    lib = _capi.lib
+    ids = np.zeros(4, np.uint32)
+    table = np.zeros((8, 16), np.float32)
+    w = np.zeros(16, np.float32)
+    R = _capi.ref
+    assert lib.ann_embedding_rms_norm_f32(None, R(ids), R(table), R(w), R(np.zeros((4, 8), np.float32)),
+                                          1e-6) == _capi.ANN_EINVAL
+    assert lib.ann_embedding_rms_norm_f32(None, R(ids), R(table), R(np.zeros(8, np.float32)),
+                                          R(np.zeros((4, 16), np.float32)), 1e-6) == _capi.ANN_EINVAL
+    assert lib.ann_embedding_rms_norm_f32(None, R(ids.reshape(2, 2)), R(table), R(w),
+                                          R(np.zeros((4, 16), np.float32)), 1e-6) == _capi.ANN_EINVAL

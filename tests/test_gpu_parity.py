@@ -386,3 +386,31 @@ def test_scale_strided_views_bitexact(ann, T, case):
         ref = (x.transpose(1, 0, 2) * s).astype(T)
     ann.onHost.ops.scale(ann.Queue(), None, src, s, out)
     assert np.array_equal(host(out), ref)
+
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("H", [256, 2048, 300])
+def test_embedding_rms_norm_fused_equals_two_launches(ann, T, H):
+    """Fused gather + rmsNorm = embeddingLookup then rmsNorm, bit for bit (row
+    lengths for the warp path, the CTA path and the unvectorised path); an id out
+    of range gives a zero row and the token-id error bit."""
+    g = rng(23)
+    table = normal(g, (1024, H), T)
+    w = (1 + 0.02 * normal(g, (H,), T)).astype(T)
+    ids = g.integers(0, 1024, size=77, dtype=np.uint32)
+    queue = ann.Queue()
+    hidden, two, fused = empty((77, H), T), empty((77, H), T), empty((77, H), T)
+    ann.onHost.nn.embeddingLookup(queue, None, dev(ids), dev(table), hidden)
+    ann.onHost.nn.rmsNorm(queue, None, hidden, dev(w), two, 1e-6)
+    ann.onHost.nn.embeddingRmsNorm(queue, None, dev(ids), dev(table), dev(w), fused, 1e-6)
+    assert np.array_equal(host(fused), host(two))
+    ref = np.empty((77, H), T)
+    oracle.rms_norm(np.ascontiguousarray(table[ids]), w, ref, T(1e-6))
+    assert_close(host(fused), ref, T, "embeddingRmsNorm")
+    assert queue.take_device_error() == 0
+    ids[5] = 4096
+    ann.onHost.nn.embeddingRmsNorm(queue, None, dev(ids), dev(table), dev(w), fused, 1e-6)
+    h = host(fused)
+    assert (h[5] == 0).all() and np.array_equal(np.delete(h, 5, 0), np.delete(host(two), 5, 0))
+    assert queue.take_device_error() & 0x1
