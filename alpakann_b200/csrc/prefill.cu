@@ -9,7 +9,9 @@
 //   -> attentionApply (onAcc/internal/nn/attention.hpp:49-67)
 // without materialising the [B,Hq,Tq,Tk] scores / probabilities.
 //
-// This is the fp64 path (DFMA) and the fp32 SIMT path. One CTA owns 64 query
+// This is the SIMT path (FMA / DFMA), used when ANN_PREFILL_FMA=1 asks for it or
+// the tensor-core kernels (prefill_tc.cu for fp32, prefill_f64.cu for fp64)
+// cannot take the shape. One CTA owns 64 query
 // rows of one (batch, query head); K/V tiles of 64 keys stream through two
 // shared-memory stages filled by 1-D bulk copies (one per 16-byte aligned
 // row, rows padded by 16 bytes so the column-wise reads are bank-conflict
@@ -28,6 +30,8 @@ namespace ann {
 
 int prefill_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
                    uint32_t g, int layout, int causal, bool& handled);
+int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, double scale,
+                    uint32_t g, int layout, int causal, bool& handled);
 
 namespace {
 
@@ -343,9 +347,13 @@ int prefill(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const a
         al = al && (q.str[i] * eb) % 16 == 0 && (k.str[i] * eb) % 16 == 0 && (v.str[i] * eb) % 16 == 0;
     if (!unit || !al)
         return fail(ANN_ENOTSUP, "attention prefill needs unit-stride head vectors and 16-byte aligned rows.");
-    if constexpr (sizeof(T) == 4) {  // fp32: tcgen05 3xTF32 kernel when TMA can describe K and V
+    {  // fp32: tcgen05 3xTF32 kernel; fp64: FP64 tensor-core (DMMA) kernel
         bool handled = false;
-        int const rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+        int rc;
+        if constexpr (sizeof(T) == 4)
+            rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+        else
+            rc = prefill_mma_f64(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
         if (handled || rc != ANN_OK) return rc;
     }
     PrefillArgs a{};
