@@ -130,8 +130,10 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(PrefillArgs a, T scal
 
     int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int const tx = tid & 15, ty = tid >> 4;
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);  // most work first
-    int64_t const bh = blockIdx.y;
+    // blocks dispatch x-fastest: y walks the query tiles from the last (most keys)
+    // down, so every head's heaviest tile starts before any lighter one
+    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.y);
+    int64_t const bh = blockIdx.x;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int const q_rows = static_cast<int>(min64(kBM, a.Tq - q0));
@@ -309,10 +311,10 @@ int launch(ann_stream stream, PrefillArgs& a, T scale, int64_t batch_heads) {
     });
     if (attr != cudaSuccess) return fail(ANN_ECUDA, "attention prefill setup: %s", cudaGetErrorString(attr));
     int64_t const q_tiles = ceil_div(a.Tq, kBM);
-    if (q_tiles > INT32_MAX || batch_heads > 65535)
+    if (q_tiles > 65535 || batch_heads > INT32_MAX)
         return fail(ANN_ENOTSUP, "attention prefill: grid too large for this build.");
     a.q_tiles = static_cast<int>(q_tiles);
-    dim3 grid(static_cast<unsigned>(q_tiles), static_cast<unsigned>(batch_heads));
+    dim3 grid(static_cast<unsigned>(batch_heads), static_cast<unsigned>(q_tiles));
     prefill_kernel<T, D, BN><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill");
 }

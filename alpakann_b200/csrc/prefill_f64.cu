@@ -95,8 +95,10 @@ __global__ void __launch_bounds__(kThreads) prefill_f64_kernel(F64Args a, double
 
     int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int const g = lane >> 2, t = lane & 3;
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);  // most work first
-    int64_t const bh = blockIdx.y;
+    // blocks dispatch x-fastest: y walks the query tiles from the last (most keys)
+    // down, so every head's heaviest tile starts before any lighter one
+    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.y);
+    int64_t const bh = blockIdx.x;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int const q_rows = static_cast<int>(q0 + kBM <= a.Tq ? kBM : a.Tq - q0);
@@ -265,7 +267,7 @@ int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads)
     });
     if (attr != cudaSuccess)
         return fail(ANN_ECUDA, "attention prefill (fp64 MMA) setup: %s", cudaGetErrorString(attr));
-    dim3 grid(static_cast<unsigned>(a.q_tiles), static_cast<unsigned>(batch_heads));
+    dim3 grid(static_cast<unsigned>(batch_heads), static_cast<unsigned>(a.q_tiles));
     prefill_f64_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (fp64 MMA)");
 }
@@ -308,7 +310,7 @@ int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims&
     a.g = g;
     a.causal = causal;
     int64_t const q_tiles = ceil_div(a.Tq, kBM), bhs = q.ext[0] * q.ext[2];
-    if (q_tiles > INT32_MAX || bhs > 65535) return ANN_OK;  // not handled
+    if (q_tiles > 65535 || bhs > INT32_MAX) return ANN_OK;  // not handled
     a.q_tiles = static_cast<int>(q_tiles);
     handled = true;
     if (D == 64) return launch_f64<64>(stream, a, scale, bhs);

@@ -135,8 +135,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
     int const tid = threadIdx.x, warp = tid >> 5;
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.x);  // longest rows first
-    int64_t const bh = blockIdx.y;
+    // blocks dispatch x-fastest: y walks the query tiles from the last (most keys)
+    // down, so every head's heaviest tile starts before any lighter one
+    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.y);
+    int64_t const bh = blockIdx.x;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int64_t const k_end = a.causal ? (a.Tk < q0 + kBM ? a.Tk : q0 + kBM) : a.Tk;
@@ -477,10 +479,10 @@ int launch_tc(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, co
     a.causal = causal;
     int64_t const q_tiles = ceil_div(a.Tq, kBM);
     int64_t const bhs = q.ext[0] * q.ext[2];
-    if (q_tiles > INT32_MAX || bhs > 65535) return ANN_OK;  // not handled
+    if (q_tiles > 65535 || bhs > INT32_MAX) return ANN_OK;  // not handled
     a.q_tiles = static_cast<int>(q_tiles);
     handled = true;
-    dim3 grid(static_cast<unsigned>(q_tiles), static_cast<unsigned>(bhs));
+    dim3 grid(static_cast<unsigned>(bhs), static_cast<unsigned>(q_tiles));
     prefill_tc_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (tensor cores)");
 }
