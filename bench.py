@@ -386,8 +386,31 @@ def measure_prefill(name, world, rank, comm, reps=10):
         res.update(kernel=f"prefill_tc_kernel<{D}> (tcgen05 3xTF32)", tf32_peak_tflops=pk, tf32_peak_kind=kind,
                    frac_of_3xtf32_peak=3 * res["tflops"] / world / pk)
     else:
-        res.update(kernel=f"prefill_kernel<double,{D}> (DFMA flash)")
+        pk = fp64_gemm_tflops()
+        res.update(kernel=f"prefill_f64_kernel<{D}> (FP64 tensor cores, mma.sync m16n8k4)", fp64_peak_tflops=pk,
+                   fp64_peak_kind="cuBLAS DGEMM 4096^3, measured in this run",
+                   frac_of_fp64_peak=res["tflops"] / world / pk)
     return res
+
+
+def fp64_gemm_tflops():
+    """Dense fp64 TFLOP/s of cuBLAS DGEMM (torch.matmul, 4096^3, best of 5): the
+    fp64 counterpart of the measured bf16 GEMM peak, measured in this run."""
+    import torch
+    n = 4096
+    a, b = (torch.randn(n, n, dtype=torch.float64, device="cuda") for _ in range(2))
+    for _ in range(2):
+        torch.matmul(a, b)
+    best = float("inf")
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    del a, b
+    return 2.0 * n ** 3 / best / 1e12
 
 
 def prefill_only(args):
