@@ -14,7 +14,7 @@
 //   warps 0..7  two threads per query row (TMEM lane r = tid % 128, half
 //               h = tid / 128): Q -> TMEM; per tile S(t) -> registers (both
 //               halves load the whole row and take its max, so no exchange is
-//               needed), K(t+1) -> shared memory, online softmax with a lazy
+//               needed), K(t+2) -> shared memory, online softmax with a lazy
 //               rescale (O and l are rescaled only when the running max grows by
 //               more than 8 in natural-log units, exact because O and l share
 //               the max used) over the half's 32 keys, V(t) -> shared memory,
@@ -23,12 +23,15 @@
 //               shared memory as hi (raw) and lo, in the layouts the MMA reads
 //               (K: K-major, 128-byte swizzle; V: MN-major, 128-byte swizzle of
 //               32-byte chunks).
-//   warp 8      one thread issues every MMA; completion comes back on mbarriers
-//               (tcgen05.commit)
+//   warp 8      one thread issues the S = Q K^T MMAs
+//   warp 9      one thread issues the O += P V MMAs
+//               (two issuers: a single thread cannot issue MMAs as fast as the
+//               tensor pipe runs them; S and PV touch disjoint TMEM columns and
+//               complete on their own mbarriers through tcgen05.commit)
 //   TMEM  [Q_hi | Q_lo | O | S (64) | P_hi (64)]   = 512 columns for D = 128
 //   smem  K hi/lo x 2 buffers | V hi/lo | P_lo     = 224 KB for D = 128
-// Tensor-pipe order S(0) S(1) PV(0) S(2) PV(1) ...: the softmax of tile t and
-// the V split run while S(t+1) and PV(t-1) execute. Per 64-key tile the MMAs
+// S(t+1) runs alongside PV(t); the softmax of tile t and the V split run while
+// S(t+1) and PV(t-1) execute. Per 64-key tile the MMAs
 // are S: 3 x D/8 of M128 N64 K8 (A = Q from TMEM) and PV: 3 x 8 of M128 N=D K8
 // (A = P_hi from TMEM, P_lo from shared memory).
 // Every wait is bounded; on a timeout the CTA stops, waits for its issued MMAs,
@@ -53,7 +56,7 @@ __device__ unsigned int g_tc_error;
 
 constexpr int kBM = 128, kBN = 64;
 constexpr int kRowThreads = 256;  // warps 0..7
-constexpr int kThreads = kRowThreads + 32;
+constexpr int kThreads = kRowThreads + 64;  // + warp 8 (S issuer) and warp 9 (PV issuer)
 constexpr float kLog2e = 1.44269504088896341f;
 constexpr float kLazy2 = 8.0f * kLog2e;  // lazy-rescale threshold, log2 units
 
@@ -66,8 +69,8 @@ struct TcCfg {
     static constexpr int OFF_PLO = 6 * TILE;  // P_lo: 128 rows x 64 keys as two 32-key blocks
     static constexpr int PLO_BLK = kBM * 128;
     static constexpr int OFF_BAR = OFF_PLO + 2 * PLO_BLK;
-    // barriers: qready kready[2] vready sfull sfree pfull pvdone drain
-    static constexpr int NBAR = 9;
+    // barriers: qready kready[2] vready sfull sfree pfull pvdone drain_s drain_pv
+    static constexpr int NBAR = 10;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
     static constexpr int USED = OFF_SLOT + 16;
     // + 1 KB to align the base to the 1 KB swizzle atom; >= 120 KB so that a
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
     uint32_t const qready = bar, kready = bar + 8, vready = bar + 24, sfull = bar + 32, sfree = bar + 40,
-                   pfull = bar + 48, pvdone = bar + 56, drain = bar + 64;
+                   pfull = bar + 48, pvdone = bar + 56, drain_s = bar + 64, drain_pv = bar + 72;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
@@ -152,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
         mbar_init(sfree, kRowThreads);
         mbar_init(pfull, kRowThreads);
         mbar_init(pvdone, 1);
-        mbar_init(drain, 1);
+        mbar_init(drain_s, 1);
+        mbar_init(drain_pv, 1);
         fence_mbar_init();
         *abort = 0;
     }
@@ -165,8 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     tc::fence_after_sync();
     uint32_t const tmem = *slot;
 
-    if (warp == 8) {
-        // ================================ MMA issue ================================
+    if (warp >= 8) {
+        // ============================== MMA issue (8, 9) ==============================
         if ((tid & 31) == 0) {
             // Descriptors are built once; a tile or k-step offset is added to the
             // 14-bit start-address field (all of shared memory is < 2^18 bytes,
@@ -199,31 +203,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
                 }
                 tc::mma_commit(pvdone);
             };
-            bool ok = n_kt == 0 || mbar_wait_or_abort(qready, 0, abort);
-            for (int t = 0; t < n_kt && ok; ++t) {
-                ok = mbar_wait_or_abort(kready + 8 * (t & 1), (t >> 1) & 1, abort) &&
-                     (t == 0 || mbar_wait_or_abort(sfree, (t - 1) & 1, abort));
-                if (!ok) break;
-                tc::fence_after_sync();
-                issue_s(t);
-                if (t >= 1) {
-                    ok = mbar_wait_or_abort(pfull, (t - 1) & 1, abort) &&
-                         mbar_wait_or_abort(vready, (t - 1) & 1, abort);
+            if (warp == 8) {  // S(t) once K(t) is stored and softmax(t-1) has read S(t-1)
+                bool ok = n_kt == 0 || mbar_wait_or_abort(qready, 0, abort);
+                for (int t = 0; t < n_kt && ok; ++t) {
+                    ok = mbar_wait_or_abort(kready + 8 * (t & 1), (t >> 1) & 1, abort) &&
+                         (t == 0 || mbar_wait_or_abort(sfree, (t - 1) & 1, abort));
                     if (!ok) break;
                     tc::fence_after_sync();
-                    issue_pv(t - 1);
+                    issue_s(t);
                 }
-            }
-            if (ok && n_kt > 0) {
-                ok = mbar_wait_or_abort(pfull, (n_kt - 1) & 1, abort) &&
-                     mbar_wait_or_abort(vready, (n_kt - 1) & 1, abort);
-                if (ok) {
+            } else {  // PV(t) once P(t) and V(t) are in place
+                for (int t = 0; t < n_kt; ++t) {
+                    bool const ok = mbar_wait_or_abort(pfull, t & 1, abort) && mbar_wait_or_abort(vready, t & 1, abort);
+                    if (!ok) break;
                     tc::fence_after_sync();
-                    issue_pv(n_kt - 1);
+                    issue_pv(t);
                 }
             }
-            // every MMA issued above has finished reading TMEM and shared memory
-            // before either is released
+            // every MMA this thread issued has finished reading TMEM and shared
+            // memory before either is released
+            uint32_t const drain = warp == 8 ? drain_s : drain_pv;
             tc::mma_commit(drain);
             if (!mbar_wait_bounded(drain, 0)) *abort = 1;
         }
@@ -297,11 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
             tc::fence_before_sync();
             mbar_arrive(qready);
         }
-        if (n_kt > 0) {
-            store_k(rk, 0);
-            mbar_arrive(kready);
-            if (n_kt > 1) load(rk, kbase, a.k_t, 1);
+        // K runs two tiles ahead: K(0), K(1) now; K(t+2) into buffer t % 2 as soon
+        // as S(t) has landed, so that S(t+1) waits only for softmax(t) to read S(t)
+        for (int t = 0; t < (n_kt < 2 ? n_kt : 2); ++t) {
+            if (t == 1) load(rk, kbase, a.k_t, 1);
+            store_k(rk, t);
+            mbar_arrive(kready + 8 * t);
         }
+        if (n_kt > 2) load(rk, kbase, a.k_t, 2);
         unsigned char* plo_row = smem + C::OFF_PLO + h * C::PLO_BLK + r * 128;
         float const c2 = scale * kLog2e;  // scores are taken in log2 units: s * scale * log2(e)
         float m_used = Lowest<float>::value, l_part = 0.f;
@@ -310,16 +312,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
         // are warp-collective, so a warp must never split on an abort.
         for (int t = 0; t < n_kt && ok; ++t) {
             ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull, t & 1, abort));
-            if (!ok) break;  // S(t) done, and with it S(t-1): K buffer (t+1) % 2 is free
+            if (!ok) break;  // S(t) done: K buffer t % 2 is free
             tc::fence_after_sync();
             float sv[kBN];  // [0, 32): this half's keys, [32, 64): the other half's
             tc::tmem_ld32x2(tmem + lane_off + C::S_COL + 32 * h, tmem + lane_off + C::S_COL + 32 * (1 - h), sv);
             tc::fence_before_sync();
             mbar_arrive(sfree);  // S(t+1) may overwrite the accumulator
-            if (t + 1 < n_kt) {
-                store_k(rk, (t + 1) & 1);
-                mbar_arrive(kready + 8 * ((t + 1) & 1));
-                if (t + 2 < n_kt) load(rk, kbase, a.k_t, t + 2);
+            if (t + 2 < n_kt) {
+                store_k(rk, t & 1);  // K(t+2)
+                mbar_arrive(kready + 8 * (t & 1));
+                if (t + 3 < n_kt) load(rk, kbase, a.k_t, t + 3);
             }
             // live keys: kj < Tk and (not causal or kj <= qi), a prefix of the tile;
             // masking is by selects, not branches, so that the exps overlap
