@@ -111,6 +111,18 @@ struct Vec16<double> {
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// (batch, head) pairs per dispatch chunk of a prefill grid: as many as keep one
+// chunk's K+V within 32 MiB of L2, but at least two waves of CTAs per chunk
+// (`resident` CTAs per SM), so that longest-first inside a chunk still fills
+// the GPU. A chunk of all pairs means one global longest-first order.
+inline int64_t head_chunk_for(int64_t bhs, int64_t q_tiles, int64_t kv_bytes_per_head, int resident) {
+    int64_t chunk = kv_bytes_per_head > 0 ? (int64_t{32} << 20) / kv_bytes_per_head : bhs;
+    int64_t const waves = ceil_div(int64_t{2} * 148 * resident, q_tiles > 0 ? q_tiles : 1);
+    if (chunk < waves) chunk = waves;
+    if (chunk < 1) chunk = 1;
+    return chunk < bhs ? chunk : bhs;
+}
+
 inline int grid_for(int64_t work_items, int per_block, int max_blocks_per_sm = 16) {
     int64_t blocks = ceil_div(work_items, per_block);
     int64_t cap = static_cast<int64_t>(sm_count()) * max_blocks_per_sm;

@@ -54,6 +54,8 @@ struct PrefillArgs {
     uint32_t g;
     int causal;
     int q_tiles;
+    int64_t bhs;         // batch * query heads
+    int64_t head_chunk;  // (batch, head) pairs per dispatch chunk
 };
 
 template <typename T, int D, int BN>
@@ -130,10 +132,14 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(PrefillArgs a, T scal
 
     int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int const tx = tid & 15, ty = tid >> 4;
-    // blocks dispatch x-fastest: y walks the query tiles from the last (most keys)
-    // down, so every head's heaviest tile starts before any lighter one
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.y);
-    int64_t const bh = blockIdx.x;
+    // 1-D grid in chunks of a.head_chunk (batch, head) pairs (head_chunk_for):
+    // inside a chunk the query tiles go from the last (most keys) down, so the
+    // heaviest CTAs start first, while the K/V of one chunk stay in L2
+    int64_t const lin = blockIdx.x, per_chunk = a.head_chunk * a.q_tiles;
+    int64_t const chunk = lin / per_chunk, in_chunk = lin % per_chunk;
+    int64_t const chunk_bh = a.bhs - chunk * a.head_chunk < a.head_chunk ? a.bhs - chunk * a.head_chunk : a.head_chunk;
+    int const qt = a.q_tiles - 1 - static_cast<int>(in_chunk / chunk_bh);
+    int64_t const bh = chunk * a.head_chunk + in_chunk % chunk_bh;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int const q_rows = static_cast<int>(min64(kBM, a.Tq - q0));
@@ -311,10 +317,12 @@ int launch(ann_stream stream, PrefillArgs& a, T scale, int64_t batch_heads) {
     });
     if (attr != cudaSuccess) return fail(ANN_ECUDA, "attention prefill setup: %s", cudaGetErrorString(attr));
     int64_t const q_tiles = ceil_div(a.Tq, kBM);
-    if (q_tiles > 65535 || batch_heads > INT32_MAX)
+    if (q_tiles * batch_heads > INT32_MAX)
         return fail(ANN_ENOTSUP, "attention prefill: grid too large for this build.");
     a.q_tiles = static_cast<int>(q_tiles);
-    dim3 grid(static_cast<unsigned>(batch_heads), static_cast<unsigned>(q_tiles));
+    a.bhs = batch_heads;
+    a.head_chunk = head_chunk_for(batch_heads, q_tiles, 2 * a.Tk * D * static_cast<int64_t>(sizeof(T)), 1);
+    dim3 grid(static_cast<unsigned>(q_tiles * batch_heads));
     prefill_kernel<T, D, BN><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill");
 }

@@ -65,6 +65,8 @@ struct F64Args {
     int causal;
     int o_pairs;  // out rows unit-stride and 16-byte aligned: store pairs
     int q_tiles;
+    int64_t bhs;         // batch * query heads
+    int64_t head_chunk;  // (batch, head) pairs per dispatch chunk
 };
 
 __device__ __forceinline__ void dmma(double (&c)[4], double a0, double a1, double b0) {
@@ -95,10 +97,14 @@ __global__ void __launch_bounds__(kThreads) prefill_f64_kernel(F64Args a, double
 
     int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int const g = lane >> 2, t = lane & 3;
-    // blocks dispatch x-fastest: y walks the query tiles from the last (most keys)
-    // down, so every head's heaviest tile starts before any lighter one
-    int const qt = a.q_tiles - 1 - static_cast<int>(blockIdx.y);
-    int64_t const bh = blockIdx.x;
+    // 1-D grid in chunks of a.head_chunk (batch, head) pairs (head_chunk_for):
+    // inside a chunk the query tiles go from the last (most keys) down, so the
+    // heaviest CTAs start first, while the K/V of one chunk stay in L2
+    int64_t const lin = blockIdx.x, per_chunk = a.head_chunk * a.q_tiles;
+    int64_t const chunk = lin / per_chunk, in_chunk = lin % per_chunk;
+    int64_t const chunk_bh = a.bhs - chunk * a.head_chunk < a.head_chunk ? a.bhs - chunk * a.head_chunk : a.head_chunk;
+    int const qt = a.q_tiles - 1 - static_cast<int>(in_chunk / chunk_bh);
+    int64_t const bh = chunk * a.head_chunk + in_chunk % chunk_bh;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int const q_rows = static_cast<int>(q0 + kBM <= a.Tq ? kBM : a.Tq - q0);
@@ -267,7 +273,9 @@ int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads)
     });
     if (attr != cudaSuccess)
         return fail(ANN_ECUDA, "attention prefill (fp64 MMA) setup: %s", cudaGetErrorString(attr));
-    dim3 grid(static_cast<unsigned>(batch_heads), static_cast<unsigned>(a.q_tiles));
+    a.bhs = batch_heads;
+    a.head_chunk = head_chunk_for(batch_heads, a.q_tiles, 2 * a.Tk * D * 8, D == 64 ? 2 : 1);
+    dim3 grid(static_cast<unsigned>(a.q_tiles * batch_heads));
     prefill_f64_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (fp64 MMA)");
 }
@@ -310,7 +318,7 @@ int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims&
     a.g = g;
     a.causal = causal;
     int64_t const q_tiles = ceil_div(a.Tq, kBM), bhs = q.ext[0] * q.ext[2];
-    if (q_tiles > 65535 || bhs > INT32_MAX) return ANN_OK;  // not handled
+    if (q_tiles * bhs > INT32_MAX) return ANN_OK;  // not handled
     a.q_tiles = static_cast<int>(q_tiles);
     handled = true;
     if (D == 64) return launch_f64<64>(stream, a, scale, bhs);

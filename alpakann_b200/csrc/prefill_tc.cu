@@ -57,7 +57,6 @@ __device__ unsigned int g_tc_error;
 constexpr int kBM = 128, kBN = 64;
 constexpr int kRowThreads = 256;  // warps 0..7
 constexpr int kThreads = kRowThreads + 64;  // + warp 8 (S issuer) and warp 9 (PV issuer)
-constexpr int kHeadChunk = 8;  // (batch, head) pairs per dispatch chunk: their K/V stay in L2
 constexpr float kLog2e = 1.44269504088896341f;
 constexpr float kLazy2 = 8.0f * kLog2e;  // lazy-rescale threshold, log2 units
 
@@ -100,7 +99,8 @@ struct TcArgs {
     int causal;
     int o_vec;  // out rows are unit-stride and 16-byte aligned
     int q_tiles;
-    int64_t bhs;  // batch * query heads
+    int64_t bhs;         // batch * query heads
+    int64_t head_chunk;  // (batch, head) pairs per dispatch chunk
 };
 
 // lo part of the 3xTF32 split: hi is x itself (a kind::tf32 MMA reads an fp32
@@ -140,14 +140,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(TcArgs a, float
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
     int const tid = threadIdx.x, warp = tid >> 5;
-    // 1-D grid in chunks of kHeadChunk (batch, head) pairs: inside a chunk the
-    // query tiles go from the last (most keys) down, so the heaviest CTAs start
-    // first, while the K/V of one chunk stay resident in L2 for all its tiles
-    int64_t const lin = blockIdx.x, per_chunk = static_cast<int64_t>(kHeadChunk) * a.q_tiles;
+    // 1-D grid in chunks of a.head_chunk (batch, head) pairs (head_chunk_for):
+    // inside a chunk the query tiles go from the last (most keys) down, so the
+    // heaviest CTAs start first, while the K/V of one chunk stay in L2
+    int64_t const lin = blockIdx.x, per_chunk = a.head_chunk * a.q_tiles;
     int64_t const chunk = lin / per_chunk, in_chunk = lin % per_chunk;
-    int64_t const chunk_bh = a.bhs - chunk * kHeadChunk < kHeadChunk ? a.bhs - chunk * kHeadChunk : kHeadChunk;
+    int64_t const chunk_bh = a.bhs - chunk * a.head_chunk < a.head_chunk ? a.bhs - chunk * a.head_chunk : a.head_chunk;
     int const qt = a.q_tiles - 1 - static_cast<int>(in_chunk / chunk_bh);
-    int64_t const bh = chunk * kHeadChunk + in_chunk % chunk_bh;
+    int64_t const bh = chunk * a.head_chunk + in_chunk % chunk_bh;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int64_t const k_end = a.causal ? (a.Tk < q0 + kBM ? a.Tk : q0 + kBM) : a.Tk;
@@ -491,6 +491,7 @@ int launch_tc(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, co
     a.q_tiles = static_cast<int>(q_tiles);
     handled = true;
     a.bhs = bhs;
+    a.head_chunk = head_chunk_for(bhs, q_tiles, 2 * a.Tk * q.ext[3] * 4, 1);
     dim3 grid(static_cast<unsigned>(q_tiles * bhs));
     prefill_tc_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (tensor cores)");
