@@ -120,7 +120,8 @@ inline int64_t head_chunk_for(int64_t bhs, int64_t q_tiles, int64_t kv_bytes_per
     int64_t const waves = ceil_div(int64_t{2} * 148 * resident, q_tiles > 0 ? q_tiles : 1);
     if (chunk < waves) chunk = waves;
     if (chunk < 1) chunk = 1;
-    return chunk < bhs ? chunk : bhs;
+    if (chunk >= bhs) return bhs;
+    return ceil_div(bhs, ceil_div(bhs, chunk));  // chunks of equal size: no short last chunk
 }
 
 inline int grid_for(int64_t work_items, int per_block, int max_blocks_per_sm = 16) {
