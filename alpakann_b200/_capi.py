@@ -61,6 +61,8 @@ for _sfx, _ft in _f.items():
         f"ann_attention_apply_{_sfx}": ([_S, _P, _P, _P, _u32, _i32], ctypes.c_int),
         f"ann_gemm_{_sfx}": ([_S, _P, _P, _P], ctypes.c_int),
         f"ann_qkv_projection_{_sfx}": ([_S, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+        f"ann_output_projection_residual_{_sfx}": ([_S, _P, _P, _P, _P], ctypes.c_int),
+        f"ann_kv_cache_append_{_sfx}": ([_S, _P, _P, _P, _P, _P, _P, _u32], ctypes.c_int),
         f"ann_attention_decode_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32], ctypes.c_int),
         f"ann_attention_prefill_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32, _i32], ctypes.c_int),
     })

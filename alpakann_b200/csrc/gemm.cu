@@ -57,7 +57,7 @@ int handle_for_current_device(cublasHandle_t& out) {
 }
 
 template <typename T>
-int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_view* c_v) {
+int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_view* c_v, T beta = T(0)) {
     Dims a, b, c;
     ANN_TRY(to_dims(a_v, sizeof(T), "gemm A", a));
     ANN_TRY(to_dims(b_v, sizeof(T), "gemm B", b));
@@ -75,7 +75,7 @@ int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_
     ANN_TRY(handle_for_current_device(h));
     if (cublas().set_stream(h, as_stream(stream)) != CUBLAS_STATUS_SUCCESS)
         return fail(ANN_ECUDA, "gemm: cublasSetStream failed.");
-    T const one = 1, zero = 0;
+    T const one = 1;
     int const lda = static_cast<int>(a.ext[1] <= 1 ? (a.str[0] > 0 ? a.str[0] : 1) : a.str[0]);
     int const ldb = static_cast<int>(b.ext[1] <= 1 ? (b.str[0] > 0 ? b.str[0] : 1) : b.str[0]);
     int const ldc = static_cast<int>(c.ext[1] <= 1 ? (c.str[0] > 0 ? c.str[0] : 1) : c.str[0]);
@@ -83,11 +83,11 @@ int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_
     if constexpr (sizeof(T) == 4)
         st = cublas().sgemm(h, CUBLAS_OP_N, CUBLAS_OP_N, static_cast<int>(N), static_cast<int>(M),
                             static_cast<int>(K), &one, static_cast<const float*>(b.data), ldb,
-                            static_cast<const float*>(a.data), lda, &zero, static_cast<float*>(c.data), ldc);
+                            static_cast<const float*>(a.data), lda, &beta, static_cast<float*>(c.data), ldc);
     else
         st = cublas().dgemm(h, CUBLAS_OP_N, CUBLAS_OP_N, static_cast<int>(N), static_cast<int>(M),
                             static_cast<int>(K), &one, static_cast<const double*>(b.data), ldb,
-                            static_cast<const double*>(a.data), lda, &zero, static_cast<double*>(c.data), ldc);
+                            static_cast<const double*>(a.data), lda, &beta, static_cast<double*>(c.data), ldc);
     if (st != CUBLAS_STATUS_SUCCESS) return fail(ANN_ECUDA, "gemm: cuBLAS status %d.", static_cast<int>(st));
     return ANN_OK;
 }
@@ -98,6 +98,26 @@ int qkv(ann_stream s, const ann_view* x, const ann_view* wq, const ann_view* wk,
     ANN_TRY(gemm<T>(s, x, wq, q));
     ANN_TRY(gemm<T>(s, x, wk, k));
     return gemm<T>(s, x, wv, v);
+}
+
+// output = residual + input . Wo: outputProjection (onHost/nn/attention.hpp:112-116)
+// followed by ops::add (onHost/ops/elementwise.hpp:307-311) of the residual,
+// the add done by the GEMM's epilogue (beta = 1) on an output that holds the
+// residual (copied there first unless residual is output).
+template <typename T>
+int output_projection_residual(ann_stream s, const ann_view* in, const ann_view* wo, const ann_view* res,
+                               const ann_view* out) {
+    Dims r, o;
+    ANN_TRY(to_dims(res, sizeof(T), "outputProjection residual", r));
+    ANN_TRY(to_dims(out, sizeof(T), "outputProjection output", o));
+    if (!same_extents(r, o)) return fail(ANN_EINVAL, "outputProjection residual shape mismatch.");
+    bool same = r.data == o.data;
+    for (int i = 0; same && i < r.rank; ++i) same = r.ext[i] <= 1 || r.str[i] == o.str[i];
+    if (!same) {
+        int const rc = sizeof(T) == 4 ? ann_scale_f32(s, res, 1.0f, out) : ann_scale_f64(s, res, 1.0, out);
+        if (rc != ANN_OK) return rc;
+    }
+    return gemm<T>(s, in, wo, out, T(1));
 }
 
 }  // namespace
@@ -125,6 +145,20 @@ int ann_qkv_projection_f64(ann_stream s, const ann_view* x, const ann_view* wq, 
                            const ann_view* wv, const ann_view* q, const ann_view* k, const ann_view* v) {
     ANN_API_BEGIN
     return ann::qkv<double>(s, x, wq, wk, wv, q, k, v);
+    ANN_API_END
+}
+
+int ann_output_projection_residual_f32(ann_stream s, const ann_view* input, const ann_view* wo,
+                                       const ann_view* residual, const ann_view* output) {
+    ANN_API_BEGIN
+    return ann::output_projection_residual<float>(s, input, wo, residual, output);
+    ANN_API_END
+}
+
+int ann_output_projection_residual_f64(ann_stream s, const ann_view* input, const ann_view* wo,
+                                       const ann_view* residual, const ann_view* output) {
+    ANN_API_BEGIN
+    return ann::output_projection_residual<double>(s, input, wo, residual, output);
     ANN_API_END
 }
 

@@ -12,6 +12,11 @@
 // pairs (two pairs = one 16-byte vector in fp32, one pair in fp64), reads them
 // and writes them back. Products and sums are left uncontracted (no FMA), so
 // the result is bit-identical to the reference expression evaluated in order.
+//
+// kvCacheAppend writes a decode step's new K/V rows (BTHD) into BHTD caches at
+// a position -- the helper on either side of the attention path in a decoder
+// layer (one layer of an LBHTD cache, core/layout.hpp:41-45, is a BHTD view) --
+// optionally rotating K on the way, with the same expression as ropeInPlace.
 #include "common.cuh"
 #include "reduce.cuh"
 
@@ -25,6 +30,7 @@ struct RopeJob {
     int64_t npv;           // pair-vectors per head vector
     int64_t si[4], so[4];  // element strides
     int64_t items;         // e0 * e1 * e2 * npv
+    int rotate;            // 0: copy the pairs unchanged
 };
 
 struct RopeArgs {
@@ -67,6 +73,11 @@ __device__ __forceinline__ void rope_item(RopeArgs const& a, RopeJob const& j, i
     T y[2 * PV];
 #pragma unroll
     for (int k = 0; k < PV; ++k) {
+        if (!j.rotate) {
+            y[2 * k] = x[2 * k];
+            y[2 * k + 1] = x[2 * k + 1];
+            continue;
+        }
         int64_t const p = pv * PV + k;
         T const c = cosT[pos * a.cs0 + p * a.cs1];
         T const s = sinT[pos * a.ss0 + p * a.ss1];
@@ -132,6 +143,7 @@ void make_job(RopeJob& j, const Dims& in, const Dims& out, int pv) {
         j.so[i] = out.str[i];
     }
     j.items = j.e0 * j.e1 * j.e2 * j.npv;
+    j.rotate = 1;
 }
 
 template <typename T>
@@ -146,7 +158,7 @@ bool vec_ok(const Dims& in, const Dims& out) {
 
 template <typename T>
 int launch(ann_stream stream, const Dims* ins, const Dims* outs, int njobs, const Dims& c, const Dims& s, int layout,
-           uint32_t off) {
+           uint32_t off, const int* rotate = nullptr) {
     constexpr int PVV = Vec16<T>::n / 2;  // pairs per 16-byte vector
     bool vec = true;
     for (int k = 0; k < njobs; ++k) vec = vec && vec_ok<T>(ins[k], outs[k]);
@@ -155,7 +167,9 @@ int launch(ann_stream stream, const Dims* ins, const Dims* outs, int njobs, cons
     a.njobs = 0;
     for (int k = 0; k < njobs; ++k) {
         if (ins[k].numel() == 0) continue;
-        make_job<T>(a.job[a.njobs++], ins[k], outs[k], pv);
+        make_job<T>(a.job[a.njobs], ins[k], outs[k], pv);
+        if (rotate != nullptr) a.job[a.njobs].rotate = rotate[k];
+        ++a.njobs;
     }
     if (a.njobs == 0) return ANN_OK;
     a.cos = c.data;
@@ -203,10 +217,66 @@ int rope_inplace(ann_stream stream, const ann_view* q_v, const ann_view* k_v, co
     return launch<T>(stream, t, t, n, c, s, layout, off);
 }
 
+// k_new, v_new: BTHD [B, Tn, Hkv, D]; k_cache, v_cache: BHTD [B, Hkv, Tcap, D];
+// rows go to cache tokens [position, position + Tn). cos/sin NULL: no rotation.
+template <typename T>
+int kv_cache_append(ann_stream stream, const ann_view* kn_v, const ann_view* vn_v, const ann_view* kc_v,
+                    const ann_view* vc_v, const ann_view* c_v, const ann_view* s_v, uint32_t position) {
+    Dims kn, vn, kc, vc, c, s;
+    ANN_TRY(to_dims(kn_v, sizeof(T), "kvCacheAppend k_new", kn));
+    ANN_TRY(to_dims(vn_v, sizeof(T), "kvCacheAppend v_new", vn));
+    ANN_TRY(to_dims(kc_v, sizeof(T), "kvCacheAppend k_cache", kc));
+    ANN_TRY(to_dims(vc_v, sizeof(T), "kvCacheAppend v_cache", vc));
+    if (kn.rank != 4 || vn.rank != 4 || kc.rank != 4 || vc.rank != 4)
+        return fail(ANN_EINVAL, "kvCacheAppend expects rank-4 BTHD rows and BHTD caches.");
+    if (!same_extents(kn, vn) || !same_extents(kc, vc)) return fail(ANN_EINVAL, "kvCacheAppend K/V shape mismatch.");
+    if (kc.ext[0] != kn.ext[0] || kc.ext[1] != kn.ext[2] || kc.ext[3] != kn.ext[3])
+        return fail(ANN_EINVAL, "kvCacheAppend: rows %s do not match the cache %s.", extents_str(kn).c_str(),
+                    extents_str(kc).c_str());
+    if (static_cast<int64_t>(position) + kn.ext[1] > kc.ext[2])
+        return fail(ANN_EINVAL, "kvCacheAppend past the cache capacity (%lld + %lld > %lld).",
+                    static_cast<long long>(position), static_cast<long long>(kn.ext[1]),
+                    static_cast<long long>(kc.ext[2]));
+    bool const rope = c_v != nullptr || s_v != nullptr;
+    if (rope) {
+        if (c_v == nullptr || s_v == nullptr) return fail(ANN_EINVAL, "kvCacheAppend needs both RoPE tables.");
+        ANN_TRY(to_dims(c_v, sizeof(T), "rope cosine table", c));
+        ANN_TRY(to_dims(s_v, sizeof(T), "rope sine table", s));
+        ANN_TRY(validate<T>(kn, kn, c, s, ANN_LAYOUT_BTHD, position));
+    }
+    if (kn.numel() == 0) return ANN_OK;
+    // the caches seen in the rows' axis order (B, T, H, D), starting at `position`
+    Dims outs[2] = {kc, vc};
+    for (Dims* o : {&outs[0], &outs[1]}) {
+        Dims const cache = *o;
+        o->data = static_cast<T*>(cache.data) + static_cast<int64_t>(position) * cache.str[2];
+        o->ext[0] = kn.ext[0], o->ext[1] = kn.ext[1], o->ext[2] = kn.ext[2], o->ext[3] = kn.ext[3];
+        o->str[0] = cache.str[0], o->str[1] = cache.str[2], o->str[2] = cache.str[1], o->str[3] = cache.str[3];
+    }
+    Dims const ins[2] = {kn, vn};
+    int const rotate[2] = {rope ? 1 : 0, 0};
+    return launch<T>(stream, ins, outs, 2, c, s, ANN_LAYOUT_BTHD, position, rotate);
+}
+
 }  // namespace
 }  // namespace ann
 
 extern "C" {
+
+int ann_kv_cache_append_f32(ann_stream st, const ann_view* k_new, const ann_view* v_new, const ann_view* k_cache,
+                            const ann_view* v_cache, const ann_view* cos_table, const ann_view* sin_table,
+                            uint32_t position) {
+    ANN_API_BEGIN
+    return ann::kv_cache_append<float>(st, k_new, v_new, k_cache, v_cache, cos_table, sin_table, position);
+    ANN_API_END
+}
+int ann_kv_cache_append_f64(ann_stream st, const ann_view* k_new, const ann_view* v_new, const ann_view* k_cache,
+                            const ann_view* v_cache, const ann_view* cos_table, const ann_view* sin_table,
+                            uint32_t position) {
+    ANN_API_BEGIN
+    return ann::kv_cache_append<double>(st, k_new, v_new, k_cache, v_cache, cos_table, sin_table, position);
+    ANN_API_END
+}
 
 int ann_rope_f32(ann_stream st, const ann_view* in, const ann_view* c, const ann_view* s, const ann_view* out,
                  int32_t layout, uint32_t off) {

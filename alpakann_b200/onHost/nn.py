@@ -49,6 +49,24 @@ def outputProjection(queue, input, Wo, output):
     gemm(queue, input, Wo, output)
 
 
+def outputProjectionResidual(queue, input, Wo, residual, output):
+    """outputProjection (onHost/nn/attention.hpp:112-116) then ops::add of the
+    residual, fused: output = residual + input . Wo (residual may be output)."""
+    check(fn("output_projection_residual", suffix(input, Wo, residual, output))(
+        handle(queue), ref(input), ref(Wo), ref(residual), ref(output)))
+
+
+def kvCacheAppend(queue, exec, kNew, vNew, kCache, vCache, position, cosTable=None, sinTable=None):
+    """New K/V rows (BTHD [B,Tn,Hkv,D]) into BHTD caches [B,Hkv,Tcap,D] at tokens
+    [position, position + Tn); with RoPE tables K is rotated on the way (as
+    ropeInPlace). For an LBHTD cache pass the layer's sub-view."""
+    sfx = suffix(kNew, vNew, kCache, vCache)
+    c = ref(cosTable) if cosTable is not None else None
+    s = ref(sinTable) if sinTable is not None else None
+    check(fn("kv_cache_append", sfx)(handle(queue), ref(kNew), ref(vNew), ref(kCache), ref(vCache), c, s,
+                                     int(position)))
+
+
 def _split_tail(args, n_tensors):
     tensors = args[:n_tensors]
     tail = list(args[n_tensors:])

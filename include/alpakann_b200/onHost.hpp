@@ -222,6 +222,45 @@ void rmsNorm(auto& queue, auto /*exec*/, auto const& input, auto const& weight, 
         d::check(ann_rms_norm_f64(d::stream_of(queue), &i, &w, &o, epsilon));
 }
 
+// outputProjection (onHost/nn/attention.hpp:112-116) then ops::add of the
+// residual, fused: output = residual + input . Wo (residual may be output).
+template <typename T_Type>
+void outputProjectionResidual(auto& queue, auto const& input, auto const& Wo, auto const& residual, auto& output) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), w = d::to_ann(Wo), r = d::to_ann(residual), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_output_projection_residual_f32(d::stream_of(queue), &i, &w, &r, &o));
+    else
+        d::check(ann_output_projection_residual_f64(d::stream_of(queue), &i, &w, &r, &o));
+}
+
+// New K/V rows (BTHD) into BHTD caches at tokens [position, position + Tn); with
+// RoPE tables K is rotated on the way, as ropeInPlace does.
+template <typename T_Type>
+void kvCacheAppend(auto& queue, auto /*exec*/, auto const& kNew, auto const& vNew, auto& kCache, auto& vCache,
+                   uint32_t position) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto kn = d::to_ann(kNew), vn = d::to_ann(vNew), kc = d::to_ann(kCache), vc = d::to_ann(vCache);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_kv_cache_append_f32(d::stream_of(queue), &kn, &vn, &kc, &vc, nullptr, nullptr, position));
+    else
+        d::check(ann_kv_cache_append_f64(d::stream_of(queue), &kn, &vn, &kc, &vc, nullptr, nullptr, position));
+}
+template <typename T_Type>
+void kvCacheAppend(auto& queue, auto /*exec*/, auto const& kNew, auto const& vNew, auto& kCache, auto& vCache,
+                   auto const& cosTable, auto const& sinTable, uint32_t position) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto kn = d::to_ann(kNew), vn = d::to_ann(vNew), kc = d::to_ann(kCache), vc = d::to_ann(vCache);
+    auto c = d::to_ann(cosTable), s = d::to_ann(sinTable);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_kv_cache_append_f32(d::stream_of(queue), &kn, &vn, &kc, &vc, &c, &s, position));
+    else
+        d::check(ann_kv_cache_append_f64(d::stream_of(queue), &kn, &vn, &kc, &vc, &c, &s, position));
+}
+
 // embeddingLookup (onHost/nn/embedding.hpp:17-36) then rmsNorm
 // (onHost/nn/rms_norm.hpp:17-35) in one launch, bit for bit their result.
 template <typename T_Type>

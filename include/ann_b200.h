@@ -174,6 +174,32 @@ int ann_qkv_projection_f32(ann_stream stream, const ann_view* input, const ann_v
 int ann_qkv_projection_f64(ann_stream stream, const ann_view* input, const ann_view* wq, const ann_view* wk,
                            const ann_view* wv, const ann_view* q, const ann_view* k, const ann_view* v);
 
+/* ---- outputProjection + residual: onHost/nn/attention.hpp:112-116 then
+ * ops::add (onHost/ops/elementwise.hpp:307-311) -----------------------------
+ * output = residual + input . Wo (row-major [N,K] x [K,M]); the add is the
+ * cuBLAS epilogue (beta = 1), so the sum is rounded once instead of twice.
+ * residual may be output. Throws on the gemm shape conditions or a residual
+ * whose extents differ from output. */
+int ann_output_projection_residual_f32(ann_stream stream, const ann_view* input, const ann_view* wo,
+                                       const ann_view* residual, const ann_view* output);
+int ann_output_projection_residual_f64(ann_stream stream, const ann_view* input, const ann_view* wo,
+                                       const ann_view* residual, const ann_view* output);
+
+/* ---- KV-cache append (one layer of an LBHTD cache, core/layout.hpp:41-45) --
+ * The reference has no append kernel; its decode test fills the cache on the
+ * host. k_new, v_new: BTHD [B,Tn,Hkv,D]; k_cache, v_cache: BHTD [B,Hkv,Tcap,D]
+ * (for an LBHTD cache, the layer's sub-view). Writes the rows to cache tokens
+ * [position, position + Tn). With cos/sin tables K is rotated on the way, with
+ * the expression of ropeInPlace at positions position + t (bit-identical to
+ * ropeInPlace followed by a plain append); cos = sin = NULL copies K as is.
+ * Throws when the rows do not match the cache or do not fit its capacity. */
+int ann_kv_cache_append_f32(ann_stream stream, const ann_view* k_new, const ann_view* v_new, const ann_view* k_cache,
+                            const ann_view* v_cache, const ann_view* cos_table, const ann_view* sin_table,
+                            uint32_t position);
+int ann_kv_cache_append_f64(ann_stream stream, const ann_view* k_new, const ann_view* v_new, const ann_view* k_cache,
+                            const ann_view* v_cache, const ann_view* cos_table, const ann_view* sin_table,
+                            uint32_t position);
+
 /* ---- fused decode attention ----------------------------------------------
  * One launch computing the reference's decode pipeline
  *   attentionScores(q, k) -> ops::scale(scale) -> softmax(axis 3)

@@ -217,3 +217,23 @@ def test_embedding_rms_norm_validation():
                                           R(np.zeros((4, 16), np.float32)), 1e-6) == _capi.ANN_EINVAL
     assert lib.ann_embedding_rms_norm_f32(None, R(ids.reshape(2, 2)), R(table), R(w),
                                           R(np.zeros((4, 16), np.float32)), 1e-6) == _capi.ANN_EINVAL
+
+
+
+def test_kv_cache_append_and_residual_validation():
+    """Shape checks of the KV-cache append and the residual projection, before any launch."""
+    import numpy as np
+
+    from alpakann_b200 import _capi
+    lib, R = _capi.lib, _capi.ref
+    kn = np.zeros((2, 3, 4, 8), np.float32)
+    kc = np.zeros((2, 4, 10, 8), np.float32)
+    assert lib.ann_kv_cache_append_f32(None, R(kn), R(kn), R(kc), R(kc), None, None, 8) == _capi.ANN_EINVAL
+    assert b"capacity" in lib.ann_last_error()
+    bad = np.zeros((2, 5, 10, 8), np.float32)  # kv heads differ
+    assert lib.ann_kv_cache_append_f32(None, R(kn), R(kn), R(bad), R(bad), None, None, 0) == _capi.ANN_EINVAL
+    tab = np.zeros((16, 4), np.float32)
+    assert lib.ann_kv_cache_append_f32(None, R(kn), R(kn), R(kc), R(kc), R(tab), None, 0) == _capi.ANN_EINVAL
+    x, w = np.zeros((4, 8), np.float32), np.zeros((8, 6), np.float32)
+    assert lib.ann_output_projection_residual_f32(None, R(x), R(w), R(np.zeros((4, 5), np.float32)),
+                                                  R(np.zeros((4, 6), np.float32))) == _capi.ANN_EINVAL

@@ -414,3 +414,50 @@ def test_embedding_rms_norm_fused_equals_two_launches(ann, T, H):
     h = host(fused)
     assert (h[5] == 0).all() and np.array_equal(np.delete(h, 5, 0), np.delete(host(two), 5, 0))
     assert queue.take_device_error() & 0x1
+
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("rope", [False, True])
+def test_kv_cache_append(ann, T, rope):
+    """New rows land at [position, position + Tn) of a layer of an LBHTD cache,
+    everything else untouched; with RoPE tables K equals ropeInPlace + append, bit
+    for bit, and V is copied as is."""
+    import torch
+    g = rng(31)
+    L, B, Hkv, Tcap, D, Tn, pos = 2, 3, 4, 40, 64, 5, 17
+    cache_k = normal(g, (L, B, Hkv, Tcap, D), T)
+    cache_v = normal(g, (L, B, Hkv, Tcap, D), T)
+    kn, vn = normal(g, (B, Tn, Hkv, D), T), normal(g, (B, Tn, Hkv, D), T)
+    ck, cv = dev(cache_k), dev(cache_v)
+    cos, sin = rope_tables(Tcap, D, 1e4, T)
+    queue = ann.Queue()
+    if rope:
+        ann.onHost.nn.kvCacheAppend(queue, None, dev(kn), dev(vn), ck[1], cv[1], pos, dev(cos), dev(sin))
+        kr = dev(kn)
+        ann.onHost.nn.ropeInPlace(queue, None, kr, dev(cos), dev(sin), ann.RopeLayout.BTHD, pos)
+        want_k = host(kr)
+    else:
+        ann.onHost.nn.kvCacheAppend(queue, None, dev(kn), dev(vn), ck[1], cv[1], pos)
+        want_k = kn
+    hk, hv = host(ck), host(cv)
+    ek, ev = cache_k.copy(), cache_v.copy()
+    ek[1, :, :, pos:pos + Tn] = want_k.transpose(0, 2, 1, 3)
+    ev[1, :, :, pos:pos + Tn] = vn.transpose(0, 2, 1, 3)
+    assert np.array_equal(hk, ek) and np.array_equal(hv, ev)
+
+
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_output_projection_residual(ann, T, in_place):
+    """output = residual + input . Wo against an fp64 product, at the GEMM tolerance."""
+    import torch
+    g = rng(37)
+    N, K, M = 70, 256, 192
+    x, w, r = normal(g, (N, K), T), (normal(g, (K, M), T) / np.sqrt(K)).astype(T), normal(g, (N, M), T)
+    ref = r.astype(np.float64) + x.astype(np.float64) @ w.astype(np.float64)
+    dr = dev(r)
+    out = dr if in_place else empty((N, M), T)
+    ann.onHost.nn.outputProjectionResidual(ann.Queue(), dev(x), dev(w), dr, out)
+    rtol, atol = (1e-4, 1e-4) if T == np.float32 else (1e-11, 1e-11)
+    assert np.allclose(host(out), ref, rtol=rtol, atol=atol)
