@@ -11,7 +11,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libann_b200.so")
 
-ANN_OK, ANN_EINVAL, ANN_ECUDA, ANN_ENOTSUP, ANN_EDEVICE, ANN_ENCCL = 0, 1, 2, 3, 4, 5
+ANN_OK, ANN_EINVAL, ANN_ECUDA, ANN_ENOTSUP, ANN_EDEVICE, ANN_ENCCL, ANN_EIO = 0, 1, 2, 3, 4, 5, 6
 COMM_ID_BYTES = 128
 ANN_DEVERR_TOKEN_ID, ANN_DEVERR_WAIT_TIMEOUT = 0x1, 0x2
 MAX_RANK = 8
@@ -20,6 +20,13 @@ MAX_RANK = 8
 class AnnView(ctypes.Structure):
     _fields_ = [("data", ctypes.c_void_p), ("rank", ctypes.c_int32), ("reserved", ctypes.c_int32),
                 ("extents", ctypes.c_int64 * MAX_RANK), ("pitches", ctypes.c_int64 * MAX_RANK)]
+
+
+class AnnTensorSpec(ctypes.Structure):
+    """ann_tensor_spec: TensorSpec of onHost/core/binary.hpp:33-39."""
+    _fields_ = [("name", ctypes.c_char_p), ("offset_bytes", ctypes.c_uint64), ("count", ctypes.c_uint64),
+                ("shape", ctypes.POINTER(ctypes.c_uint64)), ("shape_rank", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 if not os.path.exists(LIB_PATH):
@@ -46,6 +53,17 @@ SIGNATURES = {
     "ann_comm_allgather": ([_C, _S, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
     "ann_comm_destroy": ([_C], ctypes.c_int),
     "ann_comm_abort": ([_C], ctypes.c_int),
+    "ann_cast": ([_S, _P, _i32, _P, _i32], ctypes.c_int),
+    "ann_fill": ([_S, _P, _i32, ctypes.c_void_p], ctypes.c_int),
+    "ann_mlp_forward_workspace_bytes": ([_P, _i32, _P, _P, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64)],
+                                        ctypes.c_int),
+    "ann_sha256_file": ([ctypes.c_char_p, ctypes.c_char_p], ctypes.c_int),
+    "ann_sha256_bytes": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p], ctypes.c_int),
+    "ann_load_binary_tensor": ([_S, ctypes.c_char_p, ctypes.POINTER(AnnTensorSpec), ctypes.c_size_t,
+                                ctypes.c_char_p, ctypes.c_void_p], ctypes.c_int),
+    "ann_load_binary_tensor_box": ([_S, ctypes.c_char_p, ctypes.POINTER(AnnTensorSpec), ctypes.c_size_t,
+                                    ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                    ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64], ctypes.c_int),
 }
 for _sfx, _ft in _f.items():
     SIGNATURES.update({
@@ -63,6 +81,16 @@ for _sfx, _ft in _f.items():
         f"ann_qkv_projection_{_sfx}": ([_S, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
         f"ann_output_projection_residual_{_sfx}": ([_S, _P, _P, _P, _P], ctypes.c_int),
         f"ann_kv_cache_append_{_sfx}": ([_S, _P, _P, _P, _P, _P, _P, _u32], ctypes.c_int),
+        f"ann_masked_softmax_{_sfx}": ([_S, _P, _P, _P, _u32], ctypes.c_int),
+        f"ann_unary_{_sfx}": ([_S, _i32, _P, _P, _ft], ctypes.c_int),
+        f"ann_binary_{_sfx}": ([_S, _i32, _P, _P, _P, _ft], ctypes.c_int),
+        f"ann_bias_add_{_sfx}": ([_S, _P, _P, _i32, _P], ctypes.c_int),
+        f"ann_reduce_{_sfx}": ([_S, _i32, _P, _P, _u32], ctypes.c_int),
+        f"ann_dot_{_sfx}": ([_S, _P, _P, _P, _u32], ctypes.c_int),
+        f"ann_linear_bias_{_sfx}": ([_S, _P, _P, _P, _i32, _P], ctypes.c_int),
+        f"ann_mlp_forward_{_sfx}": ([_S, _P, _i32, _P, _P, _i32, _i32, _P, ctypes.c_void_p, ctypes.c_uint64],
+                                    ctypes.c_int),
+        f"ann_mlp_{_sfx}": ([_S, _P, _P, _P, _P, _P, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
         f"ann_attention_decode_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32], ctypes.c_int),
         f"ann_attention_prefill_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32, _i32], ctypes.c_int),
     })
@@ -87,6 +115,11 @@ class AnnNotSupported(AnnError, NotImplementedError):
     """ANN_ENOTSUP."""
 
 
+class AnnIOError(AnnError):
+    """ANN_EIO: a file could not be opened / read, or its digest did not match
+    (std::runtime_error in the reference)."""
+
+
 class AnnCommError(AnnError):
     """ANN_ENCCL: NCCL failed, or a rank did not join / finish within the deadline."""
 
@@ -101,6 +134,8 @@ def check(rc: int) -> None:
         raise AnnNotSupported(rc, msg)
     if rc == ANN_ENCCL:
         raise AnnCommError(rc, msg)
+    if rc == ANN_EIO:
+        raise AnnIOError(rc, msg)
     raise AnnError(rc, msg)
 
 

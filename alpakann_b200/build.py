@@ -1,6 +1,7 @@
 """Build the sm_100a CUDA library of alpakann_b200 in-tree.
 
 alpakann_b200/csrc/*.cu -> alpakann_b200/_build/obj/*.o -> alpakann_b200/_build/libann_b200.so
+alpakann_b200/csrc/*.cpp (host-only code: file loading, hashing) -> g++ -> same library
 
 nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3, C++20, static
 cudart inside the shared library (no dependency on the runtime version a
@@ -25,6 +26,16 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC,-Wal
                      "-I", INCLUDE, "-I", CSRC]
 
 
+CXX_FLAGS = ["-O3", "-std=c++20", "-fPIC", "-Wall", "-I", INCLUDE, "-I", CSRC, "-I", "/usr/local/cuda/include"]
+
+
+def cxx():
+    for cand in (os.environ.get("CXX"), shutil.which("g++")):
+        if cand and (os.path.exists(cand) or shutil.which(cand)):
+            return cand
+    raise RuntimeError("g++ not found")
+
+
 def nvcc():
     for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
         if cand and os.path.exists(cand):
@@ -33,7 +44,7 @@ def nvcc():
 
 
 def sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
 def headers():
@@ -50,12 +61,16 @@ def _stale(target, deps):
 
 
 def _compile(src, extra):
-    obj = os.path.join(OBJ_DIR, os.path.basename(src)[:-3] + ".o")
+    base = os.path.basename(src)
+    obj = os.path.join(OBJ_DIR, base.rsplit(".", 1)[0] + (".o" if base.endswith(".cu") else ".cpp.o"))
     if _stale(obj, [src] + headers() + [__file__]):
-        cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
+        if base.endswith(".cu"):
+            cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
+        else:
+            cmd = [cxx()] + CXX_FLAGS + ["-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
-            raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
+            raise RuntimeError(f"compile failed for {base}:\n{r.stdout}\n{r.stderr}")
         if r.stderr.strip():
             sys.stderr.write(r.stderr)
     return obj

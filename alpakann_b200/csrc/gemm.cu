@@ -65,7 +65,10 @@ int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_
     if (a.rank != 2 || b.rank != 2 || c.rank != 2) return fail(ANN_EINVAL, "gemm expects rank-2 operands.");
     int64_t const M = a.ext[0], K = a.ext[1], N = b.ext[1];
     if (b.ext[0] != K || c.ext[0] != M || c.ext[1] != N) return fail(ANN_EINVAL, "gemm shape mismatch.");
-    auto row_major = [](const Dims& d) { return (d.ext[1] <= 1 || d.str[1] == 1) && d.str[0] >= d.ext[1]; };
+    // A single row may carry any row pitch (a broadcast row has pitch 0).
+    auto row_major = [](const Dims& d) {
+        return (d.ext[1] <= 1 || d.str[1] == 1) && (d.ext[0] <= 1 || d.str[0] >= d.ext[1]);
+    };
     if (!row_major(a) || !row_major(b) || !row_major(c))
         return fail(ANN_EINVAL, "gemm expects row-major operands with unit column stride.");
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(ANN_ENOTSUP, "gemm: extents exceed int32.");
@@ -76,9 +79,13 @@ int gemm(ann_stream stream, const ann_view* a_v, const ann_view* b_v, const ann_
     if (cublas().set_stream(h, as_stream(stream)) != CUBLAS_STATUS_SUCCESS)
         return fail(ANN_ECUDA, "gemm: cublasSetStream failed.");
     T const one = 1;
-    int const lda = static_cast<int>(a.ext[1] <= 1 ? (a.str[0] > 0 ? a.str[0] : 1) : a.str[0]);
-    int const ldb = static_cast<int>(b.ext[1] <= 1 ? (b.str[0] > 0 ? b.str[0] : 1) : b.str[0]);
-    int const ldc = static_cast<int>(c.ext[1] <= 1 ? (c.str[0] > 0 ? c.str[0] : 1) : c.str[0]);
+    // Leading dimension of the column-major transpose: the row pitch, or the
+    // row length when there is one row (its pitch is never used).
+    auto ld = [](const Dims& d) {
+        int64_t const l = d.ext[0] <= 1 ? d.ext[1] : d.str[0];
+        return static_cast<int>(l > 0 ? l : 1);
+    };
+    int const lda = ld(a), ldb = ld(b), ldc = ld(c);
     cublasStatus_t st;
     if constexpr (sizeof(T) == 4)
         st = cublas().sgemm(h, CUBLAS_OP_N, CUBLAS_OP_N, static_cast<int>(N), static_cast<int>(M),

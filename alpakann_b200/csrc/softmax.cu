@@ -1,5 +1,5 @@
-// softmax.cu -- softmax / causalSoftmax (reference: onHost/nn/softmax.hpp:14-80,
-// onAcc/internal/nn/softmax.hpp:15-75) and ops::scale
+// softmax.cu -- softmax / causalSoftmax / maskedSoftmax (reference:
+// onHost/nn/softmax.hpp:14-80, onAcc/internal/nn/softmax.hpp:15-116) and ops::scale
 // (onHost/ops/elementwise.hpp:64-73, 330-334).
 //
 // Softmax rows run along an arbitrary axis of a tensor of any rank. A row is
@@ -22,9 +22,14 @@ struct SoftmaxArgs {
     int causal;
     int q_is_axis, k_is_axis;        // query / key axis coincides with the softmax axis
     int64_t q_div, q_mod, k_div, k_mod;  // component of the row index on the query / key axis
+    const void* mask;                    // maskedSoftmax: additive mask, input's extents
+    int64_t s_mask;                      // its stride along the softmax axis
+    Outer2 mouter;                       // its row offsets (sa; sb unused)
 };
 
-template <typename T, int GROUP>
+// MASK: maskedSoftmax (onAcc/internal/nn/softmax.hpp:76-116), the row is
+// input + mask and nothing is skipped.
+template <typename T, int GROUP, bool MASK>
 __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
     constexpr int RPB = 256 / GROUP;
     __shared__ T scratch[8];
@@ -35,9 +40,10 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
     for (int64_t it = 0; it < iters; ++it) {
         int64_t const row = (it * gridDim.x + blockIdx.x) * RPB + threadIdx.x / GROUP;
         bool const live = row < a.rows;
-        int64_t oi = 0, oo = 0, qf = 0, kf = 0;
+        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0, unused = 0;
         if (live) {
             a.outer.offsets(row, oi, oo);
+            if constexpr (MASK) a.mouter.offsets(row, om, unused);
             qf = (row / a.q_div) % a.q_mod;
             kf = (row / a.k_div) % a.k_mod;
         }
@@ -48,21 +54,26 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
             int64_t const kv = a.k_is_axis ? i : kf;
             return qv < kv;
         };
+        T const* mk = static_cast<T const*>(a.mask);
+        auto value = [&](int64_t i) {
+            if constexpr (MASK) return add_rn(in[oi + i * a.s_in], mk[om + i * a.s_mask]);
+            else return in[oi + i * a.s_in];
+        };
         T m = Lowest<T>::value;
         if (live)
             for (int64_t i = gl; i < a.len; i += GROUP)
-                if (!masked(i)) m = fmax(m, in[oi + i * a.s_in]);
+                if (!masked(i)) m = fmax(m, value(i));
         if constexpr (GROUP == 32) m = warp_max(m);
         else m = block_max<8>(m, scratch);
         T sum{};
         if (live)
             for (int64_t i = gl; i < a.len; i += GROUP)
-                if (!masked(i)) sum += exp_t(in[oi + i * a.s_in] - m);
+                if (!masked(i)) sum += exp_t(value(i) - m);
         if constexpr (GROUP == 32) sum = warp_sum(sum);
         else sum = block_sum<8>(sum, scratch);
         if (!live) continue;
         for (int64_t i = gl; i < a.len; i += GROUP) {
-            T const v = masked(i) ? T{} : exp_t(in[oi + i * a.s_in] - m) / sum;
+            T const v = masked(i) ? T{} : exp_t(value(i) - m) / sum;
             out[oo + i * a.s_out] = v;
         }
     }
@@ -70,10 +81,14 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
 
 template <typename T>
 int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint32_t axis, bool causal,
-            uint32_t qaxis, uint32_t kaxis) {
-    Dims in, out;
+            uint32_t qaxis, uint32_t kaxis, const ann_view* mask_v = nullptr) {
+    Dims in, out, mask;
     ANN_TRY(to_dims(in_v, sizeof(T), "softmax input", in));
     ANN_TRY(to_dims(out_v, sizeof(T), "softmax output", out));
+    if (mask_v) {  // softmax.hpp:45-46
+        ANN_TRY(to_dims(mask_v, sizeof(T), "maskedSoftmax mask", mask));
+        if (!same_extents(in, out) || !same_extents(in, mask)) return fail(ANN_EINVAL, "maskedSoftmax shape mismatch.");
+    }
     if (!same_extents(in, out)) return fail(ANN_EINVAL, "softmax shape mismatch.");  // softmax.hpp:29-30
     if (axis >= static_cast<uint32_t>(in.rank)) return fail(ANN_EINVAL, "softmax axis out of range.");
     if (causal && (qaxis >= static_cast<uint32_t>(in.rank) || kaxis >= static_cast<uint32_t>(in.rank)))
@@ -103,11 +118,22 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
     };
     component(causal ? qaxis : 0, a.q_div, a.q_mod);
     component(causal ? kaxis : 0, a.k_div, a.k_mod);
+    if (mask_v) {
+        a.mask = mask.data;
+        a.s_mask = mask.str[axis];
+        a.mouter = a.outer;
+        for (int i = 0; i < in.rank; ++i) a.mouter.sa[i] = mask.str[i];
+    }
     cudaStream_t s = as_stream(stream);
+    if (mask_v) {
+        if (a.len <= 1024) softmax_kernel<T, 32, true><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+        else softmax_kernel<T, 256, true><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
+        return check_launch("maskedSoftmax");
+    }
     if (a.len <= 1024) {
-        softmax_kernel<T, 32><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+        softmax_kernel<T, 32, false><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
     } else {
-        softmax_kernel<T, 256><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
+        softmax_kernel<T, 256, false><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
     }
     return check_launch(causal ? "causalSoftmax" : "softmax");
 }
@@ -283,6 +309,22 @@ int ann_causal_softmax_f64(ann_stream s, const ann_view* in, const ann_view* out
     return ann::softmax<double>(s, in, out, axis, true, qa, ka);
     ANN_API_END
 }
+int ann_masked_softmax_f32(ann_stream s, const ann_view* in, const ann_view* mask, const ann_view* out,
+                           uint32_t axis) {
+    ANN_API_BEGIN
+    if (!mask) return ann::fail(ANN_EINVAL, "maskedSoftmax: mask is NULL.");
+    return ann::softmax<float>(s, in, out, axis, false, 0, 0, mask);
+    ANN_API_END
+}
+
+int ann_masked_softmax_f64(ann_stream s, const ann_view* in, const ann_view* mask, const ann_view* out,
+                           uint32_t axis) {
+    ANN_API_BEGIN
+    if (!mask) return ann::fail(ANN_EINVAL, "maskedSoftmax: mask is NULL.");
+    return ann::softmax<double>(s, in, out, axis, false, 0, 0, mask);
+    ANN_API_END
+}
+
 int ann_scale_f32(ann_stream s, const ann_view* in, float scalar, const ann_view* out) {
     ANN_API_BEGIN
     return ann::scale<float>(s, in, scalar, out);

@@ -1,15 +1,19 @@
-"""alpaka::nn::onHost::nn -- the attention path (reference:
-include/alpaka/nn/onHost/nn/{embedding,rms_norm,attention,rope,softmax}.hpp).
+"""alpaka::nn::onHost::nn -- the attention path and the layers around it
+(reference: include/alpaka/nn/onHost/nn/{embedding,rms_norm,attention,rope,
+softmax,mlp}.hpp).
 
 Same function names, argument order, defaults and error conditions as the
 reference; shape errors raise AnnShapeError (a ValueError), the analogue of
 std::invalid_argument. `exec` is accepted and ignored.
 """
+import ctypes
+import enum
 import math
+from dataclasses import dataclass
 
 import torch
 
-from .._capi import check, lib, ref
+from .._capi import AnnView, check, lib, ref, view
 from ._common import ext, fn, gemm, handle, suffix, trace
 
 BTHD, BHTD = 0, 1
@@ -141,6 +145,99 @@ def causalSoftmax(queue, exec, input, output, axis, queryAxis, keyAxis):
     """onHost/nn/softmax.hpp:59-80 (top-left causal mask)."""
     check(fn("causal_softmax", suffix(input, output))(handle(queue), ref(input), ref(output), int(axis),
                                                      int(queryAxis), int(keyAxis)))
+
+
+def maskedSoftmax(queue, exec, input, mask, output, axis):
+    """onHost/nn/softmax.hpp:42-57: softmax along axis of input + mask."""
+    check(fn("masked_softmax", suffix(input, mask, output))(handle(queue), ref(input), ref(mask), ref(output),
+                                                           int(axis)))
+
+
+# ---- MLP layers (onHost/nn/mlp.hpp) -----------------------------------------
+class Activation(enum.IntEnum):
+    """nn::Activation (mlp.hpp:52-58)."""
+    none = 0
+    relu = 1
+    silu = 2
+    gelu = 3
+
+
+@dataclass
+class WeightView:
+    """mlp.hpp:60-69: a layer weight [in, out]; not copied, not kept alive."""
+    view: torch.Tensor
+
+
+@dataclass
+class BiasView:
+    """mlp.hpp:71-76: a layer bias [out]."""
+    view: torch.Tensor
+
+
+def _unwrap(t):
+    return t.view if isinstance(t, (WeightView, BiasView)) else t
+
+
+def linear(queue, input, weight, output):
+    """mlp.hpp:33-37: output = input . weight (row-major [in, out]), cuBLAS."""
+    gemm(queue, input, weight, output)
+
+
+def linearBias(queue, exec, input, weight, bias, output, activation=Activation.none):
+    """mlp.hpp:42-47: output = input . weight + bias, with an optional
+    activation fused into the bias pass."""
+    check(fn("linear_bias", suffix(input, weight, bias, output))(handle(queue), ref(input), ref(weight), ref(bias),
+                                                               int(activation), ref(output)))
+
+
+def mlpForward(queue, exec, input, weights, biases, *args, workspace=None):
+    """mlp.hpp:150-246. mlpForward(queue, exec, input, weights, biases,
+    activation, output) or (..., hiddenActivation, lastActivation, output).
+    weights / biases: sequences of tensors or WeightView / BiasView."""
+    if len(args) == 2:
+        hidden, last, output = args[0], args[0], args[1]
+    elif len(args) == 3:
+        hidden, last, output = args
+    else:
+        raise TypeError("mlpForward(queue, exec, input, weights, biases, [hidden,] activation, output)")
+    ws = [_unwrap(w) for w in weights]
+    bs = [_unwrap(b) for b in biases]
+    if len(ws) == 0:
+        raise_shape("mlpForward: at least one layer is required.")
+    if len(ws) != len(bs):
+        raise_shape("mlpForward: weights and biases must have the same length.")
+    sfx = suffix(input, output, *ws, *bs)
+    wv = (AnnView * len(ws))(*[view(w) for w in ws])
+    bv = (AnnView * len(bs))(*[view(b) for b in bs])
+    wptr = workspace.data_ptr() if workspace is not None else None
+    wbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(fn("mlp_forward", sfx)(handle(queue), ref(input), len(ws), wv, bv, int(hidden), int(last), ref(output),
+                                 wptr, wbytes))
+
+
+def mlpForwardWorkspaceBytes(input, weights, biases, output):
+    """Bytes of scratch mlpForward needs for these shapes (0 for one layer)."""
+    ws = [_unwrap(w) for w in weights]
+    bs = [_unwrap(b) for b in biases]
+    wv = (AnnView * max(1, len(ws)))(*[view(w) for w in ws])
+    bv = (AnnView * max(1, len(bs)))(*[view(b) for b in bs])
+    out = ctypes.c_uint64(0)
+    check(lib.ann_mlp_forward_workspace_bytes(ref(input), len(ws), wv, bv, ref(output), input.element_size(),
+                                              ctypes.byref(out)))
+    return out.value
+
+
+def decodeLatent(queue, exec, latent, weight, output):
+    """mlp.hpp:277-282: output = latent . weight (no bias, no activation)."""
+    gemm(queue, latent, weight, output)
+
+
+def mlp(queue, exec, input, Wgate, Wup, Wdown, output, workspace=None):
+    """mlp.hpp:307-337: output = swiglu(input . Wgate, input . Wup) . Wdown."""
+    sfx = suffix(input, Wgate, Wup, Wdown, output)
+    wptr = workspace.data_ptr() if workspace is not None else None
+    wbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(fn("mlp", sfx)(handle(queue), ref(input), ref(Wgate), ref(Wup), ref(Wdown), ref(output), wptr, wbytes))
 
 
 def attentionDecode(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1, kvLayout=BHTD):

@@ -53,6 +53,9 @@ def parse():
     p.add_argument("--prefill-only", metavar="B,T,H,D[,f64]", default=None,
                    help="run only the fused causal prefill on this shape (--steps launches) and print its time; "
                         "the small case the prefill ncu captures use")
+    p.add_argument("--loader", metavar="MIB", type=int, default=None,
+                   help="measure only the model-artifact loader on a MIB-sized float32 file (page-cached): "
+                        "sha256File, loadBinaryTensor, a 1/8 column shard, against pinned and pageable copies")
     return p.parse_args()
 
 
@@ -442,8 +445,79 @@ def prefill_only(args):
                       "tflops": flops / t / 1e12}), flush=True)
 
 
+def loader_only(args):
+    """--loader MIB: GB/s of the artifact loader (onHost/core/binary.hpp) with
+    the file in the page cache. Denominators measured in the same run: a
+    pinned host->device copy (the copy-engine ceiling) and the reference's
+    route (whole tensor read into one pageable host buffer, then copied)."""
+    import tempfile
+    import time
+
+    import numpy as np
+    import torch
+
+    from alpakann_b200.onHost import core
+    mib = args.loader
+    n = (mib << 20) // 4
+    rows, cols = 4096, n // 4096
+    n = rows * cols
+    nbytes = n * 4
+    d = tempfile.mkdtemp(prefix="ann_loader_")
+    path = os.path.join(d, "w.bin")
+    rng = np.random.default_rng(1)
+    rng.standard_normal(n, dtype=np.float32).tofile(path)
+    spec = core.TensorSpec("w", 0, n, (rows, cols))
+    torch.cuda.init()
+    reps = max(args.steps, 1)
+
+    def timed(fn):
+        fn()  # warm: page cache, staging buffers, allocator
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        return best
+
+    try:
+        t_sha = timed(lambda: core.sha256File(path))
+        out = {}
+        t_load = timed(lambda: out.__setitem__("w", core.loadBinaryTensor(None, path, spec)))
+        shard_cols = cols // 8
+        t_box = timed(lambda: out.__setitem__("b", core.loadBinaryTensorBox(None, path, spec, (0, rows),
+                                                                             (3 * shard_cols, shard_cols))))
+        host_pinned = torch.empty(n, dtype=torch.float32, pin_memory=True)
+        dev = torch.empty(n, dtype=torch.float32, device="cuda")
+        t_h2d = timed(lambda: dev.copy_(host_pinned, non_blocking=True))
+
+        def reference_route():
+            host = np.fromfile(path, dtype=np.float32, count=n)  # one pageable host buffer
+            dev.copy_(torch.from_numpy(host))
+        t_ref = timed(reference_route)
+        ok = torch.equal(out["w"].view(rows, cols)[:, 3 * shard_cols:4 * shard_cols], out["b"])
+    finally:
+        os.remove(path)
+        os.rmdir(d)
+    gbs = lambda b, t: round(b / t / 1e9, 2)  # noqa: E731
+    print(json.dumps({
+        "loader": {"file_mib": mib, "shape": [rows, cols], "dtype": "f32", "reps": reps, "timing": "best of reps, "
+                   "wall clock around the call plus a device synchronize"},
+        "sha256File_GBps": gbs(nbytes, t_sha),
+        "loadBinaryTensor_GBps": gbs(nbytes, t_load),
+        "box_1of8_columns_GBps": gbs(nbytes // 8, t_box),
+        "pinned_h2d_GBps": gbs(nbytes, t_h2d),
+        "reference_route_GBps": gbs(nbytes, t_ref),
+        "load_frac_of_pinned_h2d": round(t_h2d / t_load, 3),
+        "box_equals_slice": bool(ok)}), flush=True)
+
+
 def main():
     args = parse()
+    if args.loader:
+        loader_only(args)
+        return
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)

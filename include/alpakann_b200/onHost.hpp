@@ -28,6 +28,8 @@
 #include <stdexcept>
 #include <string>
 #include <type_traits>
+#include <utility>
+#include <vector>
 
 #include "../ann_b200.h"
 
@@ -99,6 +101,47 @@ View<T, R> subView(View<T, R> const& src, std::array<int64_t, R> const& offset, 
     v.extents = ext;
     return v;
 }
+
+// Owning one-dimensional device allocation: what alpaka::onHost::alloc<T>(
+// device, Vec{n}) returns to loadBinaryTensor's caller. Allocated on the
+// current device; freed (cudaFree) when it goes out of scope.
+template <typename T>
+class DeviceBuffer {
+public:
+    using value_type = T;
+    DeviceBuffer() = default;
+    explicit DeviceBuffer(int64_t n) : extents_{n}, pitches_{static_cast<int64_t>(sizeof(T))} {
+        if (n > 0 && cudaMalloc(reinterpret_cast<void**>(&ptr_), static_cast<std::size_t>(n) * sizeof(T)) != cudaSuccess) {
+            ptr_ = nullptr;
+            throw std::runtime_error("alpakann_b200: cudaMalloc failed");
+        }
+    }
+    DeviceBuffer(DeviceBuffer&& o) noexcept : ptr_(std::exchange(o.ptr_, nullptr)), extents_(o.extents_), pitches_(o.pitches_) {}
+    DeviceBuffer& operator=(DeviceBuffer&& o) noexcept {
+        if (this != &o) {
+            reset();
+            ptr_ = std::exchange(o.ptr_, nullptr);
+            extents_ = o.extents_;
+            pitches_ = o.pitches_;
+        }
+        return *this;
+    }
+    DeviceBuffer(DeviceBuffer const&) = delete;
+    DeviceBuffer& operator=(DeviceBuffer const&) = delete;
+    ~DeviceBuffer() { reset(); }
+    T* data() const { return ptr_; }
+    std::array<int64_t, 1> const& getExtents() const { return extents_; }
+    std::array<int64_t, 1> const& getPitches() const { return pitches_; }
+
+private:
+    void reset() {
+        if (ptr_) cudaFree(ptr_);
+        ptr_ = nullptr;
+    }
+    T* ptr_ = nullptr;
+    std::array<int64_t, 1> extents_{};
+    std::array<int64_t, 1> pitches_{};
+};
 
 namespace detail {
 template <typename E>
@@ -178,6 +221,57 @@ void gemm(auto& queue, auto const& A, auto const& B, auto& C) {
         d::check(ann_gemm_f64(d::stream_of(queue), &a, &b, &c));
 }
 
+}  // namespace alpaka::nn::onHost
+
+namespace alpaka::nn::onHost {
+// onHost/core/binary.hpp:33-39
+struct TensorSpec {
+    std::string name;
+    std::size_t offsetBytes;
+    std::size_t count;
+    std::vector<std::size_t> shape;
+};
+
+namespace detail {
+inline ann_tensor_spec to_ann(TensorSpec const& spec, std::vector<uint64_t>& shape) {
+    shape.assign(spec.shape.begin(), spec.shape.end());
+    ann_tensor_spec s{};
+    s.name = spec.name.c_str();
+    s.offset_bytes = spec.offsetBytes;
+    s.count = spec.count;
+    s.shape = shape.empty() ? nullptr : shape.data();
+    s.shape_rank = static_cast<int32_t>(shape.size());
+    return s;
+}
+}  // namespace detail
+
+// sha256File (onHost/core/binary.hpp:212-232): 64 lowercase hex digits;
+// std::runtime_error if the file cannot be opened or read.
+inline std::string sha256File(std::string const& path) {
+    char hex[65] = {};
+    b200::detail::check(ann_sha256_file(path.c_str(), hex));
+    return std::string(hex);
+}
+
+// loadBinaryTensor<T> (onHost/core/binary.hpp:234-323): the tensor's count
+// elements in a new device buffer on the current device, copied on `queue`.
+// std::invalid_argument for a bad layout, std::runtime_error for file errors
+// and a digest mismatch, all raised before the buffer is allocated.
+template <typename T_Type>
+auto loadBinaryTensor(auto& queue, std::string const& path, TensorSpec const& spec,
+                      std::string const& expectedSha256 = std::string{}) {
+    static_assert(std::is_same_v<T_Type, float> || std::is_same_v<T_Type, double>,
+                  "alpaka::nn::onHost::loadBinaryTensor supports only float32 and float64 tensors.");
+    std::vector<uint64_t> shape;
+    ann_tensor_spec const s = detail::to_ann(spec, shape);
+    // Every check (and the digest) with nothing allocated yet, then the load.
+    b200::detail::check(ann_load_binary_tensor(b200::detail::stream_of(queue), path.c_str(), &s, sizeof(T_Type),
+                                               expectedSha256.c_str(), nullptr));
+    b200::DeviceBuffer<T_Type> buffer(static_cast<int64_t>(spec.count));
+    b200::detail::check(
+        ann_load_binary_tensor(b200::detail::stream_of(queue), path.c_str(), &s, sizeof(T_Type), "", buffer.data()));
+    return buffer;
+}
 }  // namespace alpaka::nn::onHost
 
 namespace alpaka::nn::onHost::ops {

@@ -43,6 +43,7 @@ extern "C" {
 #define ANN_ENOTSUP 3 /* valid request this build does not implement               */
 #define ANN_EDEVICE 4 /* a kernel reported an error through the device error word  */
 #define ANN_ENCCL 5   /* NCCL error, or a rank that did not join / finish in time  */
+#define ANN_EIO 6     /* file error or digest mismatch (std::runtime_error in the reference) */
 
 #define ANN_MAX_RANK 8
 
@@ -155,6 +156,16 @@ int ann_causal_softmax_f32(ann_stream stream, const ann_view* in, const ann_view
 int ann_causal_softmax_f64(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis,
                            uint32_t query_axis, uint32_t key_axis);
 
+/* ---- maskedSoftmax: onHost/nn/softmax.hpp:42-57 -------------------------
+ * Softmax along `axis` of in + mask (an additive mask with the input's
+ * extents, e.g. 0 / -inf): max from lowest() over every element, exp of
+ * (in + mask - max), divided by the row sum. ANN_EINVAL "maskedSoftmax shape
+ * mismatch." unless in, mask and out share extents. */
+int ann_masked_softmax_f32(ann_stream stream, const ann_view* in, const ann_view* mask, const ann_view* out,
+                           uint32_t axis);
+int ann_masked_softmax_f64(ann_stream stream, const ann_view* in, const ann_view* mask, const ann_view* out,
+                           uint32_t axis);
+
 /* ---- attentionApply: onHost/nn/attention.hpp:83-110 -------------------
  * out[b,i,hq,d] = sum_j probs[b,hq,i,j] * V(b,j,hq/g,d) over all Tk keys. */
 int ann_attention_apply_f32(ann_stream stream, const ann_view* probs, const ann_view* values, const ann_view* out,
@@ -199,6 +210,110 @@ int ann_kv_cache_append_f32(ann_stream stream, const ann_view* k_new, const ann_
 int ann_kv_cache_append_f64(ann_stream stream, const ann_view* k_new, const ann_view* v_new, const ann_view* k_cache,
                             const ann_view* v_cache, const ann_view* cos_table, const ann_view* sin_table,
                             uint32_t position);
+
+/* ---- elementwise ops: onHost/ops/elementwise.hpp ---------------------------
+ * unaryOp / binaryOp over views of any rank and pitch with equal extents
+ * (ANN_EINVAL "<op> shape mismatch." otherwise, elementwise.hpp:205-212).
+ * Same expression order as the reference's operators, rounded per operation
+ * (no fused multiply-add): copy/scale/add/sub/mul/div/axpy/relu/sqrt are
+ * bit-identical to the reference's host arithmetic; exp, rsqrt, sigmoid,
+ * silu, gelu and swiglu use the device math functions. In-place calls
+ * (in == out) are allowed. */
+#define ANN_UNARY_COPY 0    /* ops::copy            x                              */
+#define ANN_UNARY_SCALE 1   /* ops::scale           x * scalar                     */
+#define ANN_UNARY_EXP 2     /* ops::exp                                            */
+#define ANN_UNARY_SQRT 3    /* ops::sqrt                                           */
+#define ANN_UNARY_RSQRT 4   /* ops::rsqrt                                          */
+#define ANN_UNARY_RELU 5    /* ops::relu            x > 0 ? x : 0                  */
+#define ANN_UNARY_SIGMOID 6 /* ops::sigmoid         1 / (1 + exp(-x))              */
+#define ANN_UNARY_SILU 7    /* ops::silu            x * sigmoid(x)                 */
+#define ANN_UNARY_GELU 8    /* ops::gelu            0.5 * x * (1 + erf(x / sqrt 2)) */
+int ann_unary_f32(ann_stream stream, int32_t op, const ann_view* in, const ann_view* out, float scalar);
+int ann_unary_f64(ann_stream stream, int32_t op, const ann_view* in, const ann_view* out, double scalar);
+
+#define ANN_BINARY_ADD 0    /* ops::add     l + r                      */
+#define ANN_BINARY_SUB 1    /* ops::sub     l - r                      */
+#define ANN_BINARY_MUL 2    /* ops::mul     l * r                      */
+#define ANN_BINARY_DIV 3    /* ops::div     l / r                      */
+#define ANN_BINARY_AXPY 4   /* ops::axpy    alpha * l + r              */
+#define ANN_BINARY_SWIGLU 5 /* ops::swiglu  l * sigmoid(l) * r         */
+int ann_binary_f32(ann_stream stream, int32_t op, const ann_view* lhs, const ann_view* rhs, const ann_view* out,
+                   float alpha);
+int ann_binary_f64(ann_stream stream, int32_t op, const ann_view* lhs, const ann_view* rhs, const ann_view* out,
+                   double alpha);
+
+/* ops::biasAdd (elementwise.hpp:348-366): out[..., h] = in[..., h] + bias[h],
+ * bias 1-D with the extent of the last axis, then optionally an activation
+ * in the same pass (nn::Activation, mlp.hpp:52-58): the result of biasAdd
+ * followed by the activation in place, in one read and one write. */
+#define ANN_ACT_NONE 0
+#define ANN_ACT_RELU 1
+#define ANN_ACT_SILU 2
+#define ANN_ACT_GELU 3
+int ann_bias_add_f32(ann_stream stream, const ann_view* in, const ann_view* bias, int32_t act, const ann_view* out);
+int ann_bias_add_f64(ann_stream stream, const ann_view* in, const ann_view* bias, int32_t act, const ann_view* out);
+
+/* ops::cast<T_Out> (elementwise.hpp:368-374) and ops::fill (:250-254): element
+ * types by code; `value` points to one element of `dtype`. */
+#define ANN_DTYPE_F32 0
+#define ANN_DTYPE_F64 1
+#define ANN_DTYPE_I32 2
+#define ANN_DTYPE_U32 3
+#define ANN_DTYPE_I64 4
+int ann_cast(ann_stream stream, const ann_view* in, int32_t in_dtype, const ann_view* out, int32_t out_dtype);
+int ann_fill(ann_stream stream, const ann_view* out, int32_t dtype, const void* value);
+
+/* ---- axis reductions: onHost/ops/reduction.hpp ------------------------------
+ * out has the input's rank and extents with extent 1 on `axis`
+ * (validateReduction, reduction.hpp:173-188). Sums are formed in a different
+ * order than the reference's sequential loop (within the reference tests'
+ * 1e-5 / 1e-12); max is exact. mean divides by the axis extent. */
+#define ANN_REDUCE_SUM 0
+#define ANN_REDUCE_MAX 1
+#define ANN_REDUCE_MEAN 2
+#define ANN_REDUCE_SUM_SQUARES 3
+#define ANN_REDUCE_DOT 4 /* ann_dot_* only */
+int ann_reduce_f32(ann_stream stream, int32_t op, const ann_view* in, const ann_view* out, uint32_t axis);
+int ann_reduce_f64(ann_stream stream, int32_t op, const ann_view* in, const ann_view* out, uint32_t axis);
+/* ops::dot (reduction.hpp:259-283): sum over `axis` of lhs * rhs. */
+int ann_dot_f32(ann_stream stream, const ann_view* lhs, const ann_view* rhs, const ann_view* out, uint32_t axis);
+int ann_dot_f64(ann_stream stream, const ann_view* lhs, const ann_view* rhs, const ann_view* out, uint32_t axis);
+
+/* ---- MLP layers: onHost/nn/mlp.hpp ------------------------------------------
+ * Weights are row-major [in, out] (model format row_major_in_out), biases
+ * 1-D [out]; activations ANN_ACT_*. GEMMs on cuBLAS; bias + activation in
+ * one pass over the GEMM output.
+ * linearBias (mlp.hpp:42-47) followed by an optional activation:
+ * output = act(input . weight + bias). linear (:33-37) and decodeLatent
+ * (:277-282) are ann_gemm_*. */
+int ann_linear_bias_f32(ann_stream stream, const ann_view* input, const ann_view* weight, const ann_view* bias,
+                        int32_t act, const ann_view* output);
+int ann_linear_bias_f64(ann_stream stream, const ann_view* input, const ann_view* weight, const ann_view* bias,
+                        int32_t act, const ann_view* output);
+/* mlpForward (mlp.hpp:150-218): n_layers layers of
+ * hidden = act(hidden . weights[l] + biases[l]), hidden_act on every layer but
+ * the last, last_act on the last (the single-activation overload passes the
+ * same value twice). Shape errors as the reference's, before anything is
+ * enqueued. Scratch for the hidden activations: `workspace` of
+ * workspace_bytes (ann_mlp_forward_workspace_bytes tells how many; 0 for one
+ * layer), or NULL for a stream-ordered allocation on `stream`. */
+int ann_mlp_forward_workspace_bytes(const ann_view* input, int32_t n_layers, const ann_view* weights,
+                                    const ann_view* biases, const ann_view* output, size_t element_size,
+                                    uint64_t* bytes);
+int ann_mlp_forward_f32(ann_stream stream, const ann_view* input, int32_t n_layers, const ann_view* weights,
+                        const ann_view* biases, int32_t hidden_act, int32_t last_act, const ann_view* output,
+                        void* workspace, uint64_t workspace_bytes);
+int ann_mlp_forward_f64(ann_stream stream, const ann_view* input, int32_t n_layers, const ann_view* weights,
+                        const ann_view* biases, int32_t hidden_act, int32_t last_act, const ann_view* output,
+                        void* workspace, uint64_t workspace_bytes);
+/* mlp (mlp.hpp:307-337), the gated MLP:
+ * output = swiglu(input . wgate, input . wup) . wdown. Scratch: two
+ * [batch, hidden] buffers (2 * batch * hidden * element size bytes) in
+ * `workspace`, or NULL for a stream-ordered allocation on `stream`. */
+int ann_mlp_f32(ann_stream stream, const ann_view* input, const ann_view* wgate, const ann_view* wup,
+                const ann_view* wdown, const ann_view* output, void* workspace, uint64_t workspace_bytes);
+int ann_mlp_f64(ann_stream stream, const ann_view* input, const ann_view* wgate, const ann_view* wup,
+                const ann_view* wdown, const ann_view* output, void* workspace, uint64_t workspace_bytes);
 
 /* ---- fused decode attention ----------------------------------------------
  * One launch computing the reference's decode pipeline
@@ -266,6 +381,53 @@ int ann_comm_size(ann_comm comm, int32_t* nranks, int32_t* rank);
 int ann_comm_allgather(ann_comm comm, ann_stream stream, const void* send, void* recv, uint64_t bytes_per_rank);
 int ann_comm_destroy(ann_comm comm);
 int ann_comm_abort(ann_comm comm);
+
+/* ---- flat model artifacts: onHost/core/binary.hpp ------------------------
+ * TensorSpec (binary.hpp:33-39): one tensor of a little-endian ".bin" file of
+ * the neural-bunch model format v1. `shape` (row-major, informational) may be
+ * NULL when shape_rank is 0. */
+typedef struct ann_tensor_spec {
+    const char* name;
+    uint64_t offset_bytes;
+    uint64_t count;
+    const uint64_t* shape;
+    int32_t shape_rank;
+    int32_t reserved;
+} ann_tensor_spec;
+
+/* sha256File (binary.hpp:212-232): SHA-256 of the whole file as 64 lowercase
+ * hex digits plus a NUL in hex_out. ANN_EIO if the file cannot be opened or
+ * read. Host only, no device. */
+int ann_sha256_file(const char* path, char hex_out[65]);
+/* SHA-256 of a host buffer (the digest sha256File computes over a file). */
+int ann_sha256_bytes(const void* data, size_t bytes, char hex_out[65]);
+
+/* loadBinaryTensor<T> (binary.hpp:234-323), T = float (element_size 4) or
+ * double (8): the spec's count elements at offset_bytes of `path` into
+ * device_out (count * element_size bytes the caller allocated on the stream's
+ * device, which must be current). Checks, in the reference's order and before
+ * the payload is read: count != 0 (ANN_EINVAL); shape product == count
+ * (ANN_EINVAL); the file can be stat'ed (ANN_EIO); offset_bytes % 64 == 0
+ * (ANN_EINVAL); count * element_size does not overflow (ANN_EINVAL); the
+ * byte range lies inside the file (ANN_EINVAL); when expected_sha256 is
+ * non-empty, the file's digest equals it ignoring case (ANN_EIO). The copy is
+ * enqueued on `stream`; the call returns once the payload has been read from
+ * the file and handed to the copy engine (host staging is the library's).
+ * device_out NULL: run the checks (digest included) and read nothing, so that
+ * a wrapper can fail before it allocates, as the reference does. */
+int ann_load_binary_tensor(ann_stream stream, const char* path, const ann_tensor_spec* spec, size_t element_size,
+                           const char* expected_sha256, void* device_out);
+/* One rank's rectangle of a tensor stored row-major as [rows, cols], rows =
+ * spec->shape[0], cols = count / rows: rows [row_begin, row_begin+row_count)
+ * x columns [col_begin, col_begin+col_count), written with a row pitch of
+ * out_row_pitch_bytes. Loads a column-parallel (Wq/Wk/Wv) or row-parallel
+ * (Wo) shard without reading the other ranks' columns. Same checks as
+ * ann_load_binary_tensor, plus the box inside the tensor (ANN_EINVAL). The
+ * reference loads whole tensors only. */
+int ann_load_binary_tensor_box(ann_stream stream, const char* path, const ann_tensor_spec* spec,
+                               size_t element_size, const char* expected_sha256, int64_t row_begin,
+                               int64_t row_count, int64_t col_begin, int64_t col_count, void* device_out,
+                               int64_t out_row_pitch_bytes);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -52,6 +52,11 @@ def lib():
             getattr(_lib, f"oracle_softmax_{sfx}").argtypes = [P, P, ctypes.c_uint32, ctypes.c_int,
                                                                 ctypes.c_uint32, ctypes.c_uint32]
             getattr(_lib, f"oracle_gemm_{sfx}").argtypes = [P, P, P]
+            getattr(_lib, f"oracle_masked_softmax_{sfx}").argtypes = [P, P, P, ctypes.c_uint32]
+            getattr(_lib, f"oracle_unary_{sfx}").argtypes = [P, P, ctypes.c_int, ct]
+            getattr(_lib, f"oracle_binary_{sfx}").argtypes = [P, P, P, ctypes.c_int, ct]
+            getattr(_lib, f"oracle_bias_add_{sfx}").argtypes = [P, P, P, ctypes.c_int]
+            getattr(_lib, f"oracle_reduce_{sfx}").argtypes = [P, P, P, ctypes.c_int, ctypes.c_uint32]
             getattr(_lib, f"oracle_attention_rows_{sfx}").argtypes = [
                 P, P, P, ctypes.c_void_p, ctypes.c_int64, ct, ctypes.c_uint32, ctypes.c_int, ctypes.c_int,
                 ctypes.c_void_p]
@@ -135,3 +140,64 @@ def attention_rows(q, k, v, rows, scale_value, g=1, layout=0, causal=False):
 
 def library_path() -> str:
     return _build.OUT if os.path.exists(_build.OUT) else _build.build()
+
+
+def masked_softmax(x, mask, out, axis):
+    """onAcc/internal/nn/softmax.hpp:76-116."""
+    getattr(lib(), f"oracle_masked_softmax_{_sfx(x)}")(view(x), view(mask), view(out), axis)
+    return out
+
+
+# operator codes of include/ann_b200.h (ANN_UNARY_*, ANN_BINARY_*, ANN_ACT_*, ANN_REDUCE_*)
+UNARY = {"copy": 0, "scale": 1, "exp": 2, "sqrt": 3, "rsqrt": 4, "relu": 5, "sigmoid": 6, "silu": 7, "gelu": 8}
+BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3, "axpy": 4, "swiglu": 5}
+ACT = {"none": 0, "relu": 1, "silu": 2, "gelu": 3}
+REDUCE = {"sum": 0, "max": 1, "mean": 2, "sum_squares": 3, "dot": 4}
+
+
+def unary(x, out, op, scalar=0.0):
+    """onHost/ops/elementwise.hpp:15-178, one operator per element."""
+    getattr(lib(), f"oracle_unary_{_sfx(x)}")(view(x), view(out), UNARY[op], scalar)
+    return out
+
+
+def binary(lhs, rhs, out, op, alpha=0.0):
+    getattr(lib(), f"oracle_binary_{_sfx(lhs)}")(view(lhs), view(rhs), view(out), BINARY[op], alpha)
+    return out
+
+
+def bias_add(x, bias, out, act="none"):
+    """biasAdd (elementwise.hpp:216-228), then the activation as a second pass."""
+    getattr(lib(), f"oracle_bias_add_{_sfx(x)}")(view(x), view(bias), view(out), ACT[act])
+    return out
+
+
+def reduce(x, out, op, axis, rhs=None):
+    """reduction.hpp:52-114: ascending loop over the axis per output."""
+    r = view(rhs) if rhs is not None else None
+    getattr(lib(), f"oracle_reduce_{_sfx(x)}")(view(x), ctypes.byref(r) if r is not None else None, view(out),
+                                               REDUCE[op], axis)
+    return out
+
+
+def mlp_forward(x, weights, biases, hidden_act, last_act):
+    """mlpForward (onHost/nn/mlp.hpp:150-218): per layer gemm, biasAdd, then the
+    activation; hidden_act on every layer but the last."""
+    h = np.ascontiguousarray(x)
+    for i, (w, b) in enumerate(zip(weights, biases)):
+        out = np.empty((h.shape[0], w.shape[1]), h.dtype)
+        gemm(h, w, out)
+        bias_add(out, b, out, last_act if i + 1 == len(weights) else hidden_act)
+        h = out
+    return h
+
+
+def gated_mlp(x, wg, wu, wd):
+    """mlp (onHost/nn/mlp.hpp:307-337): swiglu(x.Wg, x.Wu) . Wd."""
+    g = np.empty((x.shape[0], wg.shape[1]), x.dtype)
+    u = np.empty_like(g)
+    gemm(x, wg, g)
+    gemm(x, wu, u)
+    h = binary(g, u, np.empty_like(g), "swiglu")
+    out = np.empty((x.shape[0], wd.shape[1]), x.dtype)
+    return gemm(h, wd, out)

@@ -8,6 +8,9 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstring>
+#include <filesystem>
+#include <fstream>
 #include <limits>
 #include <vector>
 
@@ -399,6 +402,55 @@ static void headShardedOneRank(b200::Queue& queue) {
     REQUIRE(out.host == ref.host);
 }
 
+// core/binary.cpp:70-121 (roundtrip behind a 64-byte poison prefix, digest
+// checked) and :182-235 (every rejected layout, and the exception type).
+template <typename T>
+static void binaryTensor(b200::Queue& queue) {
+    namespace onHost = alpaka::nn::onHost;
+    auto const path = (std::filesystem::temp_directory_path() / "alpakann_b200_dropin_binary.bin").string();
+    std::vector<T> values(6);
+    for (std::size_t i = 0; i < values.size(); ++i) values[i] = static_cast<T>(i) * T(0.5) - T(1.25);
+    {
+        std::vector<unsigned char> bytes(64, 0xab);
+        bytes.resize(64 + values.size() * sizeof(T));
+        std::memcpy(bytes.data() + 64, values.data(), values.size() * sizeof(T));
+        std::ofstream f(path, std::ios::binary | std::ios::trunc);
+        f.write(reinterpret_cast<char const*>(bytes.data()), static_cast<std::streamsize>(bytes.size()));
+    }
+    onHost::TensorSpec const spec{"t", 64u, 6u, {2u, 3u}};
+    auto const sha = onHost::sha256File(path);
+    REQUIRE(sha.size() == 64u);
+    auto buffer = onHost::loadBinaryTensor<T>(queue, path, spec, sha);
+    queue.wait();
+    std::vector<T> back(6);
+    cudaMemcpy(back.data(), buffer.data(), sizeof(T) * back.size(), cudaMemcpyDeviceToHost);
+    REQUIRE(back == values);
+    REQUIRE(buffer.getExtents()[0] == 6);
+
+    auto throwsAs = [&](auto fn, bool invalidArgument) {
+        bool ok = false;
+        try {
+            fn();
+        } catch (std::invalid_argument const&) {
+            ok = invalidArgument;
+        } catch (std::runtime_error const&) {
+            ok = !invalidArgument;
+        }
+        REQUIRE(ok);
+    };
+    auto mk = [](std::size_t off, std::size_t count, std::vector<std::size_t> shape = {}) {
+        return onHost::TensorSpec{"spec", off, count, std::move(shape)};
+    };
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(8u, 4u)); }, true);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(0u, 6u, {2u, 4u})); }, true);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(0u, 1000u)); }, true);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(0u, std::numeric_limits<std::size_t>::max() / sizeof(T) + 1u)); }, true);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(0u, 0u)); }, true);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path, mk(0u, 4u), std::string(64u, '0')); }, false);
+    throwsAs([&] { onHost::loadBinaryTensor<T>(queue, path + ".missing", mk(0u, 4u)); }, false);
+    std::filesystem::remove(path);
+}
+
 template <typename T>
 static void all(b200::Queue& queue) {
     gqaKnownAnswers<T>(queue);
@@ -409,6 +461,7 @@ static void all(b200::Queue& queue) {
     rmsNorm<T>(queue);
     embedding<T>(queue);
     headShardedOneRank<T>(queue);
+    binaryTensor<T>(queue);
 }
 
 int main() {
