@@ -30,7 +30,7 @@ class AnnTensorSpec(ctypes.Structure):
 
 
 if not os.path.exists(LIB_PATH):
-    raise ImportError(f"alpakann_b200: {LIB_PATH} is missing; build it with `python -m alpakann_b200.build`")
+    raise ImportError(f"alpakann_b200: {LIB_PATH} is missing; build it with `python alpakann_b200/build.py`")
 
 lib = ctypes.CDLL(LIB_PATH)
 

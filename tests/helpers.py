@@ -7,6 +7,17 @@ import os
 import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_cases.json")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def build_library() -> str:
+    """Builds (if stale) the CUDA library by loading alpakann_b200/build.py by
+    path: importing the package would load the library before it is rebuilt."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ann_build", os.path.join(ROOT, "alpakann_b200", "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build()
 
 
 def load_cases():

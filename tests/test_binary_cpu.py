@@ -20,8 +20,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 @pytest.fixture(scope="module")
 def core():
-    from alpakann_b200 import build
-    build.build()
+    from tests.helpers import build_library
+    build_library()
     from alpakann_b200.onHost import core
     return core
 

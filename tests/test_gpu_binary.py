@@ -13,8 +13,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(scope="module")
 def core():
-    from alpakann_b200 import build
-    build.build()
+    from tests.helpers import build_library
+    build_library()
     from alpakann_b200.onHost import core
     return core
 

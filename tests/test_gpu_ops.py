@@ -31,8 +31,8 @@ SOFTMAX_TOL = {np.float32: dict(rtol=1e-5, atol=1e-7), np.float64: dict(rtol=1e-
 
 @pytest.fixture(scope="module")
 def ann():
-    from alpakann_b200 import build
-    build.build()
+    from tests.helpers import build_library
+    build_library()
     import alpakann_b200 as a
     return a
 
