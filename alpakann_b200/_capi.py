@@ -54,6 +54,7 @@ SIGNATURES = {
     "ann_comm_destroy": ([_C], ctypes.c_int),
     "ann_comm_abort": ([_C], ctypes.c_int),
     "ann_cast": ([_S, _P, _i32, _P, _i32], ctypes.c_int),
+    "ann_mlp_static_scratch": ([_S, _i32, _P, _P, _P, _P, _P], ctypes.c_int),
     "ann_fill": ([_S, _P, _i32, ctypes.c_void_p], ctypes.c_int),
     "ann_mlp_forward_workspace_bytes": ([_P, _i32, _P, _P, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64)],
                                         ctypes.c_int),

@@ -315,6 +315,20 @@ int ann_mlp_f32(ann_stream stream, const ann_view* input, const ann_view* wgate,
 int ann_mlp_f64(ann_stream stream, const ann_view* input, const ann_view* wgate, const ann_view* wup,
                 const ann_view* wdown, const ann_view* output, void* workspace, uint64_t workspace_bytes);
 
+/* The gated MLP of ann_mlp_* for callers that cannot allocate device memory
+ * while they run (a fixed memory budget, an allocator that must not be
+ * re-entered). No counterpart in the reference, whose mlp allocates three
+ * buffers per call. This call allocates nothing: the [batch, hidden]
+ * activations go to a buffer that is part of the library image (8 MiB per
+ * device, so batch * hidden * element size <= 8388608 bytes, else
+ * ANN_EINVAL), and both GEMMs are the library's own kernels, not cuBLAS.
+ * dtype: ANN_DTYPE_F32 or ANN_DTYPE_F64. The first call on each device looks
+ * up the buffer's address (cudaGetSymbolAddress); make it before any stream
+ * capture. Nothing in the buffer needs to start at zero. Calls whose work
+ * overlaps on the GPU (different streams, no ordering) race on the buffer. */
+int ann_mlp_static_scratch(ann_stream stream, int32_t dtype, const ann_view* input, const ann_view* wgate,
+                           const ann_view* wup, const ann_view* wdown, const ann_view* output);
+
 /* ---- fused decode attention ----------------------------------------------
  * One launch computing the reference's decode pipeline
  *   attentionScores(q, k) -> ops::scale(scale) -> softmax(axis 3)
