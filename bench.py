@@ -53,6 +53,9 @@ def parse():
     p.add_argument("--prefill-only", metavar="B,T,H,D[,f64]", default=None,
                    help="run only the fused causal prefill on this shape (--steps launches) and print its time; "
                         "the small case the prefill ncu captures use")
+    p.add_argument("--ops", action="store_true",
+                   help="measure only the HBM-bound ops (elementwise, bias+activation, reductions, maskedSoftmax) "
+                        "and the MLP layers on 1 GiB operands; one JSON line per op")
     p.add_argument("--loader", metavar="MIB", type=int, default=None,
                    help="measure only the model-artifact loader on a MIB-sized float32 file (page-cached): "
                         "sha256File, loadBinaryTensor, a 1/8 column shard, against pinned and pageable copies")
@@ -445,6 +448,80 @@ def prefill_only(args):
                       "tflops": flops / t / 1e12}), flush=True)
 
 
+def ops_only(args):
+    """--ops: device time per launch (CUDA events, median of --steps after
+    --warmup, operands larger than L2) and algorithmic bytes / time against
+    the measured HBM copy peak, for the ops of onHost/ops and onHost/nn/mlp.hpp."""
+    import torch
+
+    import alpakann_b200 as ann
+    ops, nn = ann.onHost.ops, ann.onHost.nn
+    peak, kind = peaks()
+    torch.manual_seed(0)
+    dev = "cuda"
+    f32 = torch.float32
+    G = 1 << 28  # elements: 1 GiB of float32 per operand
+    a = torch.randn(G, device=dev)
+    b = torch.randn(G, device=dev)
+    o = torch.empty(G, device=dev)
+    rows = a.view(65536, 4096)
+    bias = torch.randn(4096, device=dev)
+    red_rows = torch.empty((65536, 1), device=dev)
+    red_cols = torch.empty((1, 4096), device=dev)
+    sm_in = a[:1 << 27].view(4, 32, 1024, 1024)
+    sm_mask = b[:1 << 27].view(4, 32, 1024, 1024)
+    sm_out = o[:1 << 27].view(4, 32, 1024, 1024)
+
+    def timed(fn, reps=max(args.steps, 5), warm=max(args.warmup, 3)):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return sorted(ts)[len(ts) // 2]
+
+    cases = [
+        ("add", 3 * 4 * G, lambda: ops.add(None, None, a, b, o)),
+        ("axpy", 3 * 4 * G, lambda: ops.axpy(None, None, 0.5, a, b, o)),
+        ("silu", 2 * 4 * G, lambda: ops.silu(None, None, a, o)),
+        ("gelu", 2 * 4 * G, lambda: ops.gelu(None, None, a, o)),
+        ("swiglu", 3 * 4 * G, lambda: ops.swiglu(None, None, a, b, o)),
+        ("biasAdd+silu [65536,4096]", 2 * 4 * G,
+         lambda: ann._capi.check(ann._capi.lib.ann_bias_add_f32(
+             None, ann._capi.ref(rows), ann._capi.ref(bias), 2, ann._capi.ref(o.view(65536, 4096))))),
+        ("reduceSum axis 1 [65536,4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_rows, 1)),
+        ("reduceSum axis 0 [65536,4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_cols, 0)),
+        ("maskedSoftmax [4,32,1024,1024]", 3 * 4 * (1 << 27),
+         lambda: nn.maskedSoftmax(None, None, sm_in, sm_mask, sm_out, 3)),
+    ]
+    for name, nbytes, fn in cases:
+        t = timed(fn)
+        print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 4), "GBps": round(nbytes / t / 1e9, 1),
+                          "frac_of_hbm_peak": round(nbytes / t / 1e9 / peak, 3), "peak_GBps": peak,
+                          "peak_kind": kind, "bytes_per_launch": nbytes}), flush=True)
+    del a, b, o
+    torch.cuda.empty_cache()
+    # the gated MLP and a 3-layer mlpForward at decoder-like shapes: cuBLAS
+    # GEMMs plus this library's fused passes
+    M, K, F = 4096, 4096, 14336
+    x = torch.randn((M, K), device=dev) / 8
+    wg, wu = torch.randn((K, F), device=dev) / 64, torch.randn((K, F), device=dev) / 64
+    wd = torch.randn((F, K), device=dev) / 120
+    out = torch.empty((M, K), device=dev)
+    ws = torch.empty(2 * M * F * 4, dtype=torch.uint8, device=dev)
+    t = timed(lambda: nn.mlp(None, None, x, wg, wu, wd, out, workspace=ws), reps=5, warm=2)
+    flops = 2 * M * K * F * 3
+    t_sw = timed(lambda: ops.swiglu(None, None, ws.view(f32)[:M * F], ws.view(f32)[M * F:], ws.view(f32)[:M * F]))
+    print(json.dumps({"op": f"mlp (gated) x[{M},{K}] W[{K},{F}]", "dtype": "f32", "ms": round(t * 1e3, 3),
+                      "TFLOPs": round(flops / t / 1e12, 1), "swiglu_pass_ms": round(t_sw * 1e3, 3),
+                      "swiglu_share": round(t_sw / t, 3)}), flush=True)
+
+
 def loader_only(args):
     """--loader MIB: GB/s of the artifact loader (onHost/core/binary.hpp) with
     the file in the page cache. Denominators measured in the same run: a
@@ -515,6 +592,9 @@ def loader_only(args):
 
 def main():
     args = parse()
+    if args.ops:
+        ops_only(args)
+        return
     if args.loader:
         loader_only(args)
         return

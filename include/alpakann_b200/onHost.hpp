@@ -24,6 +24,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <span>
 #include <sstream>
 #include <stdexcept>
 #include <string>
@@ -192,6 +193,46 @@ constexpr void require_float() {
     static_assert(is_f32<T> || is_f64<T>, "alpakann_b200 supports float and double");
 }
 
+// Element type of a view (its data() pointee) and its ANN_DTYPE_* code.
+template <typename V>
+using elem_of = std::remove_cv_t<std::remove_pointer_t<decltype(std::declval<V const&>().data())>>;
+template <typename E>
+constexpr int32_t dtype_code() {
+    if constexpr (std::is_same_v<E, float>) return ANN_DTYPE_F32;
+    else if constexpr (std::is_same_v<E, double>) return ANN_DTYPE_F64;
+    else if constexpr (std::is_same_v<E, int32_t>) return ANN_DTYPE_I32;
+    else if constexpr (std::is_same_v<E, uint32_t>) return ANN_DTYPE_U32;
+    else {
+        static_assert(std::is_same_v<E, int64_t>, "alpakann_b200: float, double, int32, uint32 or int64 elements");
+        return ANN_DTYPE_I64;
+    }
+}
+
+template <typename T, typename Q>
+void unary(Q& queue, int32_t op, ann_view const& i, ann_view const& o, T scalar = T(0)) {
+    require_float<T>();
+    if constexpr (is_f32<T>)
+        check(ann_unary_f32(stream_of(queue), op, &i, &o, scalar));
+    else
+        check(ann_unary_f64(stream_of(queue), op, &i, &o, scalar));
+}
+template <typename T, typename Q>
+void binary(Q& queue, int32_t op, ann_view const& l, ann_view const& r, ann_view const& o, T alpha = T(0)) {
+    require_float<T>();
+    if constexpr (is_f32<T>)
+        check(ann_binary_f32(stream_of(queue), op, &l, &r, &o, alpha));
+    else
+        check(ann_binary_f64(stream_of(queue), op, &l, &r, &o, alpha));
+}
+template <typename T, typename Q>
+void reduce(Q& queue, int32_t op, ann_view const& i, ann_view const& o, uint32_t axis) {
+    require_float<T>();
+    if constexpr (is_f32<T>)
+        check(ann_reduce_f32(stream_of(queue), op, &i, &o, axis));
+    else
+        check(ann_reduce_f64(stream_of(queue), op, &i, &o, axis));
+}
+
 // ALPAKANN_DEBUG_ATTENTION_TRACE (onHost/nn/attention.hpp:24-34)
 inline bool attention_trace_enabled() {
     auto const* env = std::getenv("ALPAKANN_DEBUG_ATTENTION_TRACE");
@@ -286,6 +327,132 @@ void scale(auto& queue, auto /*exec*/, auto const& in, T_Type scalar, auto& out)
         d::check(ann_scale_f32(d::stream_of(queue), &i, scalar, &o));
     else
         d::check(ann_scale_f64(d::stream_of(queue), &i, scalar, &o));
+}
+
+// onHost/ops/elementwise.hpp:250-254: every element of out = value, in out's element type.
+template <typename T_Value>
+void fill(auto& queue, auto /*exec*/, auto& out, T_Value value) {
+    namespace d = alpaka::nn::b200::detail;
+    using E = d::elem_of<std::remove_cvref_t<decltype(out)>>;
+    E const v = static_cast<E>(value);
+    auto o = d::to_ann(out);
+    d::check(ann_fill(d::stream_of(queue), &o, d::dtype_code<E>(), &v));
+}
+
+// :256-268
+void copy(auto& queue, auto /*exec*/, auto const& in, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    using E = d::elem_of<std::remove_cvref_t<decltype(out)>>;
+    d::unary<E>(queue, ANN_UNARY_COPY, d::to_ann(in), d::to_ann(out));
+}
+
+// :306-337
+template <typename T_Type>
+void add(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_ADD, d::to_ann(lhs), d::to_ann(rhs), d::to_ann(out));
+}
+template <typename T_Type>
+void sub(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_SUB, d::to_ann(lhs), d::to_ann(rhs), d::to_ann(out));
+}
+template <typename T_Type>
+void mul(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_MUL, d::to_ann(lhs), d::to_ann(rhs), d::to_ann(out));
+}
+template <typename T_Type>
+void div(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_DIV, d::to_ann(lhs), d::to_ann(rhs), d::to_ann(out));
+}
+template <typename T_Type>
+void axpy(auto& queue, auto /*exec*/, T_Type alpha, auto const& x, auto const& y, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_AXPY, d::to_ann(x), d::to_ann(y), d::to_ann(out), alpha);
+}
+
+// :338-353
+void biasAdd(auto& queue, auto /*exec*/, auto const& input, auto const& bias, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    using E = d::elem_of<std::remove_cvref_t<decltype(out)>>;
+    d::require_float<E>();
+    auto i = d::to_ann(input), b = d::to_ann(bias), o = d::to_ann(out);
+    if constexpr (d::is_f32<E>)
+        d::check(ann_bias_add_f32(d::stream_of(queue), &i, &b, ANN_ACT_NONE, &o));
+    else
+        d::check(ann_bias_add_f64(d::stream_of(queue), &i, &b, ANN_ACT_NONE, &o));
+}
+
+// :355-361
+template <typename T_Out>
+void cast(auto& queue, auto /*exec*/, auto const& in, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    using In = d::elem_of<std::remove_cvref_t<decltype(in)>>;
+    static_assert(std::is_same_v<T_Out, d::elem_of<std::remove_cvref_t<decltype(out)>>>,
+                  "cast<T_Out>: out must hold T_Out elements");
+    auto i = d::to_ann(in), o = d::to_ann(out);
+    d::check(ann_cast(d::stream_of(queue), &i, d::dtype_code<In>(), &o, d::dtype_code<T_Out>()));
+}
+
+// :363-414, the transcendental and activation operators
+#define ANN_B200_UNARY(name, code)                                                     \
+    template <typename T_Type>                                                         \
+    void name(auto& queue, auto /*exec*/, auto const& in, auto& out) {                 \
+        namespace d = alpaka::nn::b200::detail;                                        \
+        d::unary<T_Type>(queue, code, d::to_ann(in), d::to_ann(out));                  \
+    }
+ANN_B200_UNARY(exp, ANN_UNARY_EXP)
+ANN_B200_UNARY(sqrt, ANN_UNARY_SQRT)
+ANN_B200_UNARY(rsqrt, ANN_UNARY_RSQRT)
+ANN_B200_UNARY(relu, ANN_UNARY_RELU)
+ANN_B200_UNARY(sigmoid, ANN_UNARY_SIGMOID)
+ANN_B200_UNARY(silu, ANN_UNARY_SILU)
+ANN_B200_UNARY(gelu, ANN_UNARY_GELU)
+#undef ANN_B200_UNARY
+
+template <typename T_Type>
+void swiglu(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out) {
+    namespace d = alpaka::nn::b200::detail;
+    d::binary<T_Type>(queue, ANN_BINARY_SWIGLU, d::to_ann(lhs), d::to_ann(rhs), d::to_ann(out));
+}
+
+// onHost/ops/reduction.hpp:190-289
+template <typename T_Type>
+void reduceSum(auto& queue, auto /*exec*/, auto const& in, auto& out, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::reduce<T_Type>(queue, ANN_REDUCE_SUM, d::to_ann(in), d::to_ann(out), axis);
+}
+template <typename T_Type>
+void reduceMax(auto& queue, auto /*exec*/, auto const& in, auto& out, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::reduce<T_Type>(queue, ANN_REDUCE_MAX, d::to_ann(in), d::to_ann(out), axis);
+}
+template <typename T_Type>
+void reduceMean(auto& queue, auto /*exec*/, auto const& in, auto& out, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::reduce<T_Type>(queue, ANN_REDUCE_MEAN, d::to_ann(in), d::to_ann(out), axis);
+}
+template <typename T_Type>
+void reduceSumSquares(auto& queue, auto /*exec*/, auto const& in, auto& out, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::reduce<T_Type>(queue, ANN_REDUCE_SUM_SQUARES, d::to_ann(in), d::to_ann(out), axis);
+}
+template <typename T_Type>
+void dot(auto& queue, auto /*exec*/, auto const& lhs, auto const& rhs, auto& out, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto l = d::to_ann(lhs), r = d::to_ann(rhs), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_dot_f32(d::stream_of(queue), &l, &r, &o, axis));
+    else
+        d::check(ann_dot_f64(d::stream_of(queue), &l, &r, &o, axis));
+}
+// reduction.hpp:285-288
+inline auto makeReducedExtents(auto extents, uint32_t axis) {
+    extents[axis] = 1;
+    return extents;
 }
 
 }  // namespace alpaka::nn::onHost::ops
@@ -449,6 +616,112 @@ void causalSoftmax(auto& queue, auto /*exec*/, auto const& input, auto& output, 
         d::check(ann_causal_softmax_f32(d::stream_of(queue), &i, &o, axis, queryAxis, keyAxis));
     else
         d::check(ann_causal_softmax_f64(d::stream_of(queue), &i, &o, axis, queryAxis, keyAxis));
+}
+
+// onHost/nn/softmax.hpp:42-57
+template <typename T_Type>
+void maskedSoftmax(auto& queue, auto /*exec*/, auto const& input, auto const& mask, auto& output, uint32_t axis) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), m = d::to_ann(mask), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_masked_softmax_f32(d::stream_of(queue), &i, &m, &o, axis));
+    else
+        d::check(ann_masked_softmax_f64(d::stream_of(queue), &i, &m, &o, axis));
+}
+
+// ---- MLP layers: onHost/nn/mlp.hpp --------------------------------------------
+// :33-37
+template <typename T_Type>
+void linear(auto& queue, auto const& input, auto const& weight, auto& output) {
+    alpaka::nn::onHost::gemm<T_Type>(queue, input, weight, output);
+}
+
+// :52-58
+enum class Activation { none = ANN_ACT_NONE, relu = ANN_ACT_RELU, silu = ANN_ACT_SILU, gelu = ANN_ACT_GELU };
+
+// :60-76
+template <typename T_View>
+struct WeightView {
+    T_View view;
+};
+template <typename T_View>
+struct BiasView {
+    T_View view;
+};
+
+// :42-47, the bias add and an optional activation in one pass after the GEMM
+template <typename T_Type>
+void linearBias(auto& queue, auto /*exec*/, auto const& input, auto const& weight, auto const& bias, auto& output,
+                Activation activation = Activation::none) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), w = d::to_ann(weight), b = d::to_ann(bias), o = d::to_ann(output);
+    int32_t const act = static_cast<int32_t>(activation);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_linear_bias_f32(d::stream_of(queue), &i, &w, &b, act, &o));
+    else
+        d::check(ann_linear_bias_f64(d::stream_of(queue), &i, &w, &b, act, &o));
+}
+
+// :150-218 (hidden / last activation), scratch from a stream-ordered allocation
+template <typename T_Type, typename T_WeightView, typename T_BiasView>
+void mlpForward(auto& queue, auto /*exec*/, auto const& input, std::span<WeightView<T_WeightView> const> weights,
+                std::span<BiasView<T_BiasView> const> biases, Activation hiddenActivation, Activation lastActivation,
+                auto& output) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    if (weights.empty()) throw std::invalid_argument{"mlpForward: at least one layer is required."};
+    if (weights.size() != biases.size())
+        throw std::invalid_argument{"mlpForward: weights and biases must have the same length."};
+    std::vector<ann_view> w, b;
+    for (auto const& x : weights) w.push_back(d::to_ann(x.view));
+    for (auto const& x : biases) b.push_back(d::to_ann(x.view));
+    auto i = d::to_ann(input), o = d::to_ann(output);
+    int32_t const n = static_cast<int32_t>(w.size());
+    int32_t const ha = static_cast<int32_t>(hiddenActivation), la = static_cast<int32_t>(lastActivation);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_mlp_forward_f32(d::stream_of(queue), &i, n, w.data(), b.data(), ha, la, &o, nullptr, 0));
+    else
+        d::check(ann_mlp_forward_f64(d::stream_of(queue), &i, n, w.data(), b.data(), ha, la, &o, nullptr, 0));
+}
+// :141-148 (one activation for every layer)
+template <typename T_Type, typename T_WeightView, typename T_BiasView>
+void mlpForward(auto& queue, auto exec, auto const& input, std::span<WeightView<T_WeightView> const> weights,
+                std::span<BiasView<T_BiasView> const> biases, Activation activation, auto& output) {
+    mlpForward<T_Type>(queue, exec, input, weights, biases, activation, activation, output);
+}
+// :248-275 (compile-time depth)
+template <typename T_Type, typename T_WeightView, typename T_BiasView, std::size_t T_Depth>
+void mlpForward(auto& queue, auto exec, auto const& input, std::array<WeightView<T_WeightView>, T_Depth> const& weights,
+                std::array<BiasView<T_BiasView>, T_Depth> const& biases, Activation hiddenActivation,
+                Activation lastActivation, auto& output) {
+    mlpForward<T_Type>(queue, exec, input, std::span<WeightView<T_WeightView> const>{weights},
+                       std::span<BiasView<T_BiasView> const>{biases}, hiddenActivation, lastActivation, output);
+}
+template <typename T_Type, typename T_WeightView, typename T_BiasView, std::size_t T_Depth>
+void mlpForward(auto& queue, auto exec, auto const& input, std::array<WeightView<T_WeightView>, T_Depth> const& weights,
+                std::array<BiasView<T_BiasView>, T_Depth> const& biases, Activation activation, auto& output) {
+    mlpForward<T_Type>(queue, exec, input, weights, biases, activation, activation, output);
+}
+
+// :277-282
+template <typename T_Type>
+void decodeLatent(auto& queue, auto /*exec*/, auto const& latent, auto const& weight, auto& output) {
+    alpaka::nn::onHost::gemm<T_Type>(queue, latent, weight, output);
+}
+
+// :307-337, the gated MLP; scratch from a stream-ordered allocation
+template <typename T_Type>
+void mlp(auto& queue, auto /*exec*/, auto const& input, auto const& Wgate, auto const& Wup, auto const& Wdown,
+         auto& output) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto i = d::to_ann(input), g = d::to_ann(Wgate), u = d::to_ann(Wup), w = d::to_ann(Wdown), o = d::to_ann(output);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_mlp_f32(d::stream_of(queue), &i, &g, &u, &w, &o, nullptr, 0));
+    else
+        d::check(ann_mlp_f64(d::stream_of(queue), &i, &g, &u, &w, &o, nullptr, 0));
 }
 
 // onHost/nn/rope.hpp:49-62

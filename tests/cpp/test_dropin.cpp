@@ -451,6 +451,210 @@ static void binaryTensor(b200::Queue& queue) {
     std::filesystem::remove(path);
 }
 
+// ops/elementwise.cpp:31-130: the elementwise chain on [2,4], biasAdd, cast,
+// and the activations on padded views (row pitch 8).
+template <typename T>
+static void elementwise(b200::Queue& queue) {
+    Tensor<T, 2> a({2, 4}), b({2, 4}), out({2, 4});
+    T v = T(-3);
+    for (auto& x : a.host) x = v, v += T(0.5);
+    for (std::size_t i = 0; i < b.host.size(); ++i) b.host[i] = a.host[i] + T(1);
+    a.upload(), b.upload();
+    auto av = a.view(), bv = b.view(), ov = out.view();
+    ops::fill(queue, nullptr, ov, T(2));
+    ops::copy(queue, nullptr, av, ov);
+    ops::add<T>(queue, nullptr, av, bv, ov);
+    queue.wait(), out.download();
+    for (std::size_t i = 0; i < 8; ++i) checkValue(out.host[i], T(a.host[i] + b.host[i]), 1e-5, 1e-6, "add");
+    ops::sub<T>(queue, nullptr, bv, av, ov);
+    ops::mul<T>(queue, nullptr, av, bv, ov);
+    ops::div<T>(queue, nullptr, bv, av, ov);
+    ops::scale<T>(queue, nullptr, av, T(3), ov);
+    ops::axpy<T>(queue, nullptr, T(2), av, bv, ov);
+    queue.wait(), out.download();
+    for (std::size_t i = 0; i < 8; ++i) checkValue(out.host[i], T(T(2) * a.host[i] + b.host[i]), 1e-5, 1e-6, "axpy");
+    Tensor<T, 1> bias({4});
+    for (int i = 0; i < 4; ++i) bias.host[static_cast<std::size_t>(i)] = static_cast<T>(i);
+    bias.upload();
+    auto biv = bias.view();
+    ops::biasAdd(queue, nullptr, av, biv, ov);
+    queue.wait(), out.download();
+    for (std::size_t i = 0; i < 8; ++i) checkValue(out.host[i], T(a.host[i] + bias.host[i % 4]), 1e-5, 1e-6, "bias");
+    int* idev = nullptr;
+    cudaMalloc(&idev, 8 * sizeof(int));
+    auto iv = b200::makeView<int, 2>(idev, {2, 4});
+    ops::cast<int>(queue, nullptr, av, iv);
+    queue.wait();
+    int ih[8];
+    cudaMemcpy(ih, idev, sizeof(ih), cudaMemcpyDeviceToHost);
+    for (std::size_t i = 0; i < 8; ++i) REQUIRE(ih[i] == static_cast<int>(a.host[i]));
+    cudaFree(idev);
+    // padded views: 24 elements, [2,4] with row pitch 8 elements
+    Tensor<T, 1> pin({24}), pout({24});
+    for (int r = 0; r < 2; ++r)
+        for (int c = 0; c < 4; ++c) pin.host[static_cast<std::size_t>(r * 8 + c)] = a.host[static_cast<std::size_t>(r * 4 + c)];
+    pin.upload(), pout.upload();
+    b200::View<T, 2> vin{pin.dev, {2, 4}, {8 * int64_t(sizeof(T)), int64_t(sizeof(T))}};
+    b200::View<T, 2> vout{pout.dev, {2, 4}, {8 * int64_t(sizeof(T)), int64_t(sizeof(T))}};
+    ops::exp<T>(queue, nullptr, vin, vout);
+    ops::sqrt<T>(queue, nullptr, vout, vout);
+    ops::rsqrt<T>(queue, nullptr, vout, vout);
+    ops::relu<T>(queue, nullptr, vin, vout);
+    ops::sigmoid<T>(queue, nullptr, vin, vout);
+    ops::silu<T>(queue, nullptr, vin, vout);
+    ops::gelu<T>(queue, nullptr, vin, vout);
+    ops::swiglu<T>(queue, nullptr, vin, vin, vout);
+    queue.wait(), pout.download();
+    double const eps = std::is_same_v<T, float> ? 1e-5 : 1e-9;
+    for (int r = 0; r < 2; ++r)
+        for (int c = 0; c < 4; ++c) {
+            T const x = a.host[static_cast<std::size_t>(r * 4 + c)];
+            T const sig = T(1) / (T(1) + std::exp(-x));
+            checkValue(pout.host[static_cast<std::size_t>(r * 8 + c)], T(x * sig * x), eps, eps, "swiglu padded");
+            REQUIRE(pout.host[static_cast<std::size_t>(r * 8 + c + 4)] == T(0));
+        }
+}
+
+// ops/reduction.cpp:33-124
+template <typename T>
+static void reductions(b200::Queue& queue) {
+    Tensor<T, 3> in({2, 3, 4}), out({2, 3, 1});
+    for (std::size_t i = 0; i < in.host.size(); ++i) in.host[i] = static_cast<T>(i + 1);
+    in.upload();
+    auto iv = in.view(), ov = out.view();
+    REQUIRE((ops::makeReducedExtents(iv.getExtents(), 2u) == std::array<int64_t, 3>{2, 3, 1}));
+    double const eps = std::is_same_v<T, float> ? 1e-5 : 1e-12;
+    ops::reduceSum<T>(queue, nullptr, iv, ov, 2u);
+    queue.wait(), out.download();
+    for (int r = 0; r < 6; ++r) {
+        T sum{};
+        for (int k = 0; k < 4; ++k) sum += in.host[static_cast<std::size_t>(r * 4 + k)];
+        checkValue(out.host[static_cast<std::size_t>(r)], sum, eps, eps, "reduceSum");
+    }
+    ops::reduceMean<T>(queue, nullptr, iv, ov, 2u);
+    ops::reduceMax<T>(queue, nullptr, iv, ov, 2u);
+    queue.wait(), out.download();
+    for (int r = 0; r < 6; ++r) REQUIRE(out.host[static_cast<std::size_t>(r)] == in.host[static_cast<std::size_t>(r * 4 + 3)]);
+    ops::reduceSumSquares<T>(queue, nullptr, iv, ov, 2u);
+    queue.wait(), out.download();
+    for (int r = 0; r < 6; ++r) {
+        T sum{};
+        for (int k = 0; k < 4; ++k) sum += in.host[static_cast<std::size_t>(r * 4 + k)] * in.host[static_cast<std::size_t>(r * 4 + k)];
+        checkValue(out.host[static_cast<std::size_t>(r)], sum, eps, eps, "reduceSumSquares");
+    }
+    Tensor<T, 3> dotOut({2, 1, 4});
+    auto dv = dotOut.view();
+    ops::dot<T>(queue, nullptr, iv, iv, dv, 1u);
+    queue.wait(), dotOut.download();
+    for (int b = 0; b < 2; ++b)
+        for (int k = 0; k < 4; ++k) {
+            T sum{};
+            for (int j = 0; j < 3; ++j) {
+                T const x = in.host[static_cast<std::size_t>(b * 12 + j * 4 + k)];
+                sum += x * x;
+            }
+            checkValue(dotOut.host[static_cast<std::size_t>(b * 4 + k)], sum, eps, eps, "dot");
+        }
+    bool threw = false;
+    try {
+        ops::reduceSum<T>(queue, nullptr, iv, iv, 2u);
+    } catch (std::invalid_argument const&) {
+        threw = true;
+    }
+    REQUIRE(threw);
+}
+
+// nn/mlp.cpp:20-68 and nn/mlp_forward.cpp:60-216
+template <typename T>
+static void mlpCases(b200::Queue& queue) {
+    Tensor<T, 2> x({1, 4}), wg({4, 6}), wu({4, 6}), wd({6, 4}), out({1, 4});
+    for (int k = 0; k < 4; ++k) x.host[static_cast<std::size_t>(k)] = static_cast<T>(k + 1);
+    for (int k = 0; k < 4; ++k)
+        for (int c = 0; c < 6; ++c) {
+            wg[{k, c}] = T(0.05) * static_cast<T>(k + c + 1);
+            wu[{k, c}] = T(0.04) * static_cast<T>(k + c + 1);
+        }
+    for (int k = 0; k < 6; ++k)
+        for (int c = 0; c < 4; ++c) wd[{k, c}] = T(0.03) * static_cast<T>(k + c + 1);
+    for (auto* t : {&x, &wg, &wu, &wd}) t->upload();
+    auto xv = x.view(), gv = wg.view(), uv = wu.view(), dv = wd.view(), ov = out.view();
+    nn::mlp<T>(queue, nullptr, xv, gv, uv, dv, ov);
+    queue.wait(), out.download();
+    T hidden[6];
+    for (int c = 0; c < 6; ++c) {
+        T a{}, b{};
+        for (int k = 0; k < 4; ++k) a += x.host[static_cast<std::size_t>(k)] * wg[{k, c}], b += x.host[static_cast<std::size_t>(k)] * wu[{k, c}];
+        hidden[c] = a / (T(1) + std::exp(-a)) * b;
+    }
+    for (int c = 0; c < 4; ++c) {
+        T e{};
+        for (int k = 0; k < 6; ++k) e += hidden[k] * wd[{k, c}];
+        checkValue(out.host[static_cast<std::size_t>(c)], e, 1e-5, 1e-6, "mlp");
+    }
+
+    auto fillDet = [](auto& t, T scale, T shift) {
+        for (std::size_t i = 0; i < t.host.size(); ++i) t.host[i] = scale * static_cast<T>(i + 1) + shift;
+        t.upload();
+    };
+    auto silu = [](T v) { return v / (T(1) + std::exp(-v)); };
+    // three layers, silu hidden, none last (mlp_forward.cpp:112-182)
+    Tensor<T, 2> in({2, 3}), w0({3, 5}), w1({5, 4}), w2({4, 2}), res({2, 2});
+    Tensor<T, 1> b0({5}), b1({4}), b2({2});
+    fillDet(in, T(0.2), T(-0.3)), fillDet(w0, T(0.09), T(-0.2)), fillDet(w1, T(0.07), T(-0.1));
+    fillDet(w2, T(0.05), T(-0.05)), fillDet(b0, T(0.03), T(0.01)), fillDet(b1, T(0.02), T(-0.01));
+    fillDet(b2, T(0.01), T(0.02));
+    using W = nn::WeightView<b200::View<T, 2>>;
+    using B = nn::BiasView<b200::View<T, 1>>;
+    std::array<W, 3> ws{W{w0.view()}, W{w1.view()}, W{w2.view()}};
+    std::array<B, 3> bs{B{b0.view()}, B{b1.view()}, B{b2.view()}};
+    auto inv = in.view(), rv = res.view();
+    nn::mlpForward<T>(queue, nullptr, inv, ws, bs, nn::Activation::silu, nn::Activation::none, rv);
+    queue.wait(), res.download();
+    for (int r = 0; r < 2; ++r) {
+        T l0[5], l1[4];
+        for (int c = 0; c < 5; ++c) {
+            T v = b0.host[static_cast<std::size_t>(c)];
+            for (int k = 0; k < 3; ++k) v += in[{r, k}] * w0[{k, c}];
+            l0[c] = silu(v);
+        }
+        for (int c = 0; c < 4; ++c) {
+            T v = b1.host[static_cast<std::size_t>(c)];
+            for (int k = 0; k < 5; ++k) v += l0[k] * w1[{k, c}];
+            l1[c] = silu(v);
+        }
+        for (int c = 0; c < 2; ++c) {
+            T v = b2.host[static_cast<std::size_t>(c)];
+            for (int k = 0; k < 4; ++k) v += l1[k] * w2[{k, c}];
+            checkValue(res[{r, c}], v, 1e-5, 1e-6, "mlpForward 3 layers");
+        }
+    }
+    // decodeLatent (mlp_forward.cpp:184-216)
+    Tensor<T, 2> lat({1, 3}), wl({3, 5}), lo({1, 5});
+    fillDet(lat, T(0.4), T(-0.6)), fillDet(wl, T(0.08), T(-0.3));
+    auto lav = lat.view(), wlv = wl.view(), lov = lo.view();
+    nn::decodeLatent<T>(queue, nullptr, lav, wlv, lov);
+    queue.wait(), lo.download();
+    for (int c = 0; c < 5; ++c) {
+        T e{};
+        for (int k = 0; k < 3; ++k) e += lat.host[static_cast<std::size_t>(k)] * wl[{k, c}];
+        checkValue(lo.host[static_cast<std::size_t>(c)], e, 1e-5, 1e-6, "decodeLatent");
+    }
+    // maskedSoftmax with a -inf mask: masked entries 0, the rest sum to 1
+    Tensor<T, 2> sIn({2, 5}), sMask({2, 5}), sOut({2, 5});
+    for (int i = 0; i < 10; ++i) {
+        sIn.host[static_cast<std::size_t>(i)] = static_cast<T>(i % 5);
+        sMask.host[static_cast<std::size_t>(i)] = (i % 5 >= 3) ? -std::numeric_limits<T>::infinity() : T(0);
+    }
+    sIn.upload(), sMask.upload();
+    auto siv = sIn.view(), smv = sMask.view(), sov = sOut.view();
+    nn::maskedSoftmax<T>(queue, nullptr, siv, smv, sov, 1u);
+    queue.wait(), sOut.download();
+    T const z = std::exp(T(-2)) + std::exp(T(-1)) + T(1);
+    for (int r = 0; r < 2; ++r)
+        for (int c = 0; c < 5; ++c)
+            checkValue(sOut[{r, c}], c >= 3 ? T(0) : T(std::exp(static_cast<T>(c - 2)) / z), 1e-5, 1e-7, "maskedSoftmax");
+}
+
 template <typename T>
 static void all(b200::Queue& queue) {
     gqaKnownAnswers<T>(queue);
@@ -462,6 +666,9 @@ static void all(b200::Queue& queue) {
     embedding<T>(queue);
     headShardedOneRank<T>(queue);
     binaryTensor<T>(queue);
+    elementwise<T>(queue);
+    reductions<T>(queue);
+    mlpCases<T>(queue);
 }
 
 int main() {
