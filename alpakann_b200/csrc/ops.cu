@@ -15,14 +15,22 @@
 //  - biasAdd + activation fuse into one pass (the reference's mlpForward runs
 //    biasAdd, then the activation in place: two passes with the same two
 //    roundings).
-//  - Reductions: a row along a unit-stride axis is reduced by a warp (or a
-//    256-thread CTA for long rows) with vector loads; any other axis by 32
-//    adjacent outputs per CTA, eight warps splitting the axis, so the loads
-//    of a warp are adjacent in memory whenever the output's last axis is.
+//  - Reductions: a row along a unit-stride axis is reduced by a warp with
+//    16-byte loads, four in flight per lane, when the rows are 16-byte
+//    aligned (else a warp or a 256-thread CTA with element loads); any other
+//    axis by 32 adjacent outputs per CTA, eight warps splitting the axis, so
+//    the loads of a warp are adjacent in memory whenever the output's last
+//    axis is -- and when those tiles are too few to fill the GPU, by a
+//    cluster of eight CTAs per tile that split the axis and combine through
+//    distributed shared memory.
+#include <cooperative_groups.h>
+
 #include <cstring>
 
 #include "common.cuh"
 #include "reduce.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace ann {
 namespace {
@@ -188,23 +196,47 @@ __global__ void __launch_bounds__(kThreads) binary_strided(T const* l, T const* 
 }
 
 // out[..., h] = act(in[..., h] + bias[h]); dense rows of length H.
-template <int ACT, typename T>
-__global__ void __launch_bounds__(kThreads) bias_dense(T const* in, T const* bias,
-                                                       T* out, int64_t n, int64_t H, int vec_ok) {
+// FIXED_COL: the grid stride is a whole number of rows, so every vector a
+// thread touches has the same column: its bias vector is loaded once. Two
+// vectors per thread per iteration keep two loads in flight.
+template <int ACT, typename T, bool FIXED_COL>
+__global__ void __launch_bounds__(kThreads) bias_dense(T const* in, T const* bias, T* out, int64_t n, int64_t H,
+                                                       int vec_ok) {
     using V = typename Vec16<T>::type;
     constexpr int NV = Vec16<T>::n;
     int64_t const tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     int64_t const stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     if (vec_ok) {  // H % NV == 0: a vector never straddles two rows
-        int64_t const nv = n / NV;
-        for (int64_t i = tid; i < nv; i += stride) {
-            V x = reinterpret_cast<V const*>(in)[i];
-            V const b = reinterpret_cast<V const*>(bias)[(i * NV % H) / NV];
+        int64_t const nv = n / NV, hv = H / NV;
+        V const* vi = reinterpret_cast<V const*>(in);
+        V const* vb = reinterpret_cast<V const*>(bias);
+        V* vo = reinterpret_cast<V*>(out);
+        auto apply = [](V x, V const& b) {
             T* e = reinterpret_cast<T*>(&x);
             T const* eb = reinterpret_cast<T const*>(&b);
 #pragma unroll
             for (int k = 0; k < NV; ++k) e[k] = activate<ACT>(add_rn(e[k], eb[k]));
-            reinterpret_cast<V*>(out)[i] = x;
+            return x;
+        };
+        if constexpr (FIXED_COL) {
+            V const b = vb[tid % hv];
+            int64_t i = tid;
+            for (; i + stride < nv; i += 2 * stride) {
+                V const x0 = vi[i], x1 = vi[i + stride];
+                vo[i] = apply(x0, b);
+                vo[i + stride] = apply(x1, b);
+            }
+            if (i < nv) vo[i] = apply(vi[i], b);
+        } else {
+            // column of vector i, advanced by the stride's remainder each
+            // iteration instead of a 64-bit modulo per vector
+            int64_t col = tid % hv;
+            int64_t const step = stride % hv;
+            for (int64_t i = tid; i < nv; i += stride) {
+                vo[i] = apply(vi[i], vb[col]);
+                col += step;
+                if (col >= hv) col -= hv;
+            }
         }
         return;
     }
@@ -312,8 +344,28 @@ void launch_bias(cudaStream_t s, const Dims& in, const Dims& bias, const Dims& o
     if (dense_alike(in, out) && bias.str[0] == 1) {
         int const vec = vec_aligned(in.data) && vec_aligned(out.data) && vec_aligned(bias.data) &&
                         H % Vec16<T>::n == 0;
-        bias_dense<ACT, T><<<blocks_for(n, vec ? Vec16<T>::n : 1), kThreads, 0, s>>>(
-            static_cast<T const*>(in.data), static_cast<T const*>(bias.data), static_cast<T*>(out.data), n, H, vec);
+        int grid = blocks_for(n, vec ? Vec16<T>::n : 1);
+        T const* pi = static_cast<T const*>(in.data);
+        T const* pb = static_cast<T const*>(bias.data);
+        T* po = static_cast<T*>(out.data);
+        if (vec) {
+            // A grid whose stride (grid * kThreads vectors) is a multiple of
+            // the row's hv vectors keeps each thread on one column.
+            int64_t const hv = H / Vec16<T>::n;
+            int64_t g = hv, t = kThreads;  // g = hv / gcd(hv, kThreads)
+            while (t != 0) {
+                int64_t const r = g % t;
+                g = t;
+                t = r;
+            }
+            int64_t const period = hv / g;
+            if (period <= grid) {
+                grid = static_cast<int>(grid / period * period);
+                bias_dense<ACT, T, true><<<grid, kThreads, 0, s>>>(pi, pb, po, n, H, 1);
+                return;
+            }
+        }
+        bias_dense<ACT, T, false><<<grid, kThreads, 0, s>>>(pi, pb, po, n, H, vec);
     } else {
         bias_strided<ACT, T><<<blocks_for(n, 1), kThreads, 0, s>>>(
             static_cast<T const*>(in.data), static_cast<T const*>(bias.data), bias.str[0], static_cast<T*>(out.data),
@@ -428,6 +480,60 @@ struct ReduceArgs {
     Walk3 w;                   // output extents; strides of out, a, b
 };
 
+// One warp per output, the axis unit-stride and every row start 16-byte
+// aligned in a (and b): 16-byte loads, four in flight per lane.
+template <int OP, typename T>
+__global__ void __launch_bounds__(kThreads) reduce_rows_vec(ReduceArgs r) {
+    using V = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n;
+    T const* A = static_cast<T const*>(r.a);
+    T const* Bp = static_cast<T const*>(r.b);
+    T* out = static_cast<T*>(r.out);
+    int const lane = threadIdx.x & 31;
+    int64_t const warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+    int64_t const nv = r.len / NV;
+    for (int64_t o = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + threadIdx.x / 32; o < r.outputs;
+         o += warps) {
+        int64_t oo, oa, ob;
+        r.w.offsets(o, oo, oa, ob);
+        V const* va = reinterpret_cast<V const*>(A + oa);
+        V const* vb = reinterpret_cast<V const*>(Bp + ob);
+        T acc = reduce_init<OP, T>();
+        int64_t i = lane;
+        for (; i + 96 < nv; i += 128) {  // four vectors per lane in flight
+            V xa[4], xb[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                xa[u] = va[i + 32 * u];
+                if constexpr (OP == ANN_REDUCE_DOT) xb[u] = vb[i + 32 * u];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                T const* ea = reinterpret_cast<T const*>(&xa[u]);
+                T const* eb = reinterpret_cast<T const*>(&xb[u]);
+#pragma unroll
+                for (int k = 0; k < NV; ++k)
+                    acc = combine<OP>(acc, transform<OP>(ea[k], OP == ANN_REDUCE_DOT ? eb[k] : T(0)));
+            }
+        }
+        for (; i < nv; i += 32) {
+            V const xa = va[i];
+            V xb{};
+            if constexpr (OP == ANN_REDUCE_DOT) xb = vb[i];
+            T const* ea = reinterpret_cast<T const*>(&xa);
+            T const* eb = reinterpret_cast<T const*>(&xb);
+#pragma unroll
+            for (int k = 0; k < NV; ++k)
+                acc = combine<OP>(acc, transform<OP>(ea[k], OP == ANN_REDUCE_DOT ? eb[k] : T(0)));
+        }
+        for (int64_t e = nv * NV + lane; e < r.len; e += 32)  // tail elements
+            acc = combine<OP>(acc, transform<OP>(A[oa + e], OP == ANN_REDUCE_DOT ? Bp[ob + e] : T(0)));
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) acc = combine<OP>(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+        if (lane == 0) out[oo] = finalize<OP>(acc, r.len);
+    }
+}
+
 // One GROUP-thread team per output; the axis has unit stride in a (and b).
 template <int OP, typename T, int GROUP>
 __global__ void __launch_bounds__(kThreads) reduce_rows(ReduceArgs r) {
@@ -494,6 +600,85 @@ __global__ void __launch_bounds__(kThreads) reduce_cols(ReduceArgs r) {
     }
 }
 
+// The same 32 adjacent outputs per tile, but a cluster of kColSplit CTAs per
+// tile: CTA k of the cluster reduces the k-th slice of the axis (its 8 warps
+// interleaved over the slice, four loads in flight per thread) and CTA 0 then
+// combines the slices' partials in rank order through distributed shared
+// memory. Eight times the CTAs of reduce_cols for the same outputs, which is
+// what a long axis with few outputs needs to keep HBM busy; the combine order
+// is fixed, so results do not depend on timing.
+constexpr int kColSplit = 8;
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(kThreads) reduce_cols_cluster(ReduceArgs r) {
+    __shared__ T part[8][33];
+    __shared__ T cta[32];
+    cg::cluster_group cluster = cg::this_cluster();
+    int const rank = static_cast<int>(cluster.block_rank());
+    T const* A = static_cast<T const*>(r.a);
+    T const* Bp = static_cast<T const*>(r.b);
+    T* out = static_cast<T*>(r.out);
+    int const lane = threadIdx.x & 31, wy = threadIdx.x >> 5;
+    int64_t const tiles = ceil_div(r.outputs, 32);
+    int64_t const clusters = gridDim.x / kColSplit;
+    int64_t const per = ceil_div(r.len, kColSplit);
+    int64_t const lo = rank * per < r.len ? rank * per : r.len;
+    int64_t const hi = lo + per < r.len ? lo + per : r.len;
+    for (int64_t t = blockIdx.x / kColSplit; t < tiles; t += clusters) {  // same trip count in every CTA
+        int64_t const o = t * 32 + lane;
+        T acc = reduce_init<OP, T>();
+        int64_t oo = 0, oa = 0, ob = 0;
+        if (o < r.outputs) {
+            r.w.offsets(o, oo, oa, ob);
+            auto term = [&](int64_t i) {
+                return transform<OP>(A[oa + i * r.sa_axis], OP == ANN_REDUCE_DOT ? Bp[ob + i * r.sb_axis] : T(0));
+            };
+            int64_t i = lo + wy;
+            for (; i + 24 < hi; i += 32) {
+                T const t0 = term(i), t1 = term(i + 8), t2 = term(i + 16), t3 = term(i + 24);
+                acc = combine<OP>(combine<OP>(combine<OP>(combine<OP>(acc, t0), t1), t2), t3);
+            }
+            for (; i < hi; i += 8) acc = combine<OP>(acc, term(i));
+        }
+        part[wy][lane] = acc;
+        __syncthreads();
+        if (wy == 0) {
+            T v = part[0][lane];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) v = combine<OP>(v, part[k][lane]);
+            cta[lane] = v;
+        }
+        cluster.sync();
+        if (rank == 0 && wy == 0 && o < r.outputs) {
+            T v = cta[lane];
+            for (int k = 1; k < kColSplit; ++k) v = combine<OP>(v, cluster.map_shared_rank(cta, k)[lane]);
+            out[oo] = finalize<OP>(v, r.len);
+        }
+        cluster.sync();  // the peers' partials must outlive rank 0's reads
+    }
+}
+
+template <int OP, typename T>
+int launch_cols_cluster(cudaStream_t s, ReduceArgs const& r) {
+    int64_t const tiles = ceil_div(r.outputs, 32);
+    int64_t clusters = static_cast<int64_t>(sm_count()) * 8 / kColSplit;
+    if (clusters > tiles) clusters = tiles;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = kColSplit;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * kColSplit));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = s;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, reduce_cols_cluster<OP, T>, r);
+    if (e != cudaSuccess) return fail(ANN_ECUDA, "reduce: %s", cudaGetErrorString(e));
+    return ANN_OK;
+}
+
 char const* reduce_name(int op) {
     switch (op) {
         case ANN_REDUCE_SUM: return "reduceSum";
@@ -505,14 +690,19 @@ char const* reduce_name(int op) {
 }
 
 template <int OP, typename T>
-void launch_reduce(cudaStream_t s, ReduceArgs const& r, bool rows) {
+int launch_reduce(cudaStream_t s, ReduceArgs const& r, bool rows, bool vec) {
     if (!rows) {
+        // few output tiles against a long axis: split the axis over a cluster
+        if (r.len >= 256 && ceil_div(r.outputs, 32) < 4 * sm_count()) return launch_cols_cluster<OP, T>(s, r);
         reduce_cols<OP, T><<<grid_for(ceil_div(r.outputs, 32), 1, 8), kThreads, 0, s>>>(r);
+    } else if (vec && (r.len <= 65536 || r.outputs >= 4 * sm_count())) {
+        reduce_rows_vec<OP, T><<<grid_for(r.outputs, kThreads / 32, 8), kThreads, 0, s>>>(r);
     } else if (r.len <= 2048) {
         reduce_rows<OP, T, 32><<<grid_for(r.outputs, kThreads / 32, 8), kThreads, 0, s>>>(r);
     } else {
         reduce_rows<OP, T, kThreads><<<grid_for(r.outputs, 1, 8), kThreads, 0, s>>>(r);
     }
+    return ANN_OK;
 }
 
 // validateReduction (reduction.hpp:173-188) and the launch.
@@ -544,13 +734,20 @@ int reduce(ann_stream stream, int op, const ann_view* a_v, const ann_view* b_v, 
     r.sb_axis = op == ANN_REDUCE_DOT ? b.str[axis] : a.str[axis];
     r.w = walk_of(out, &out, &a, op == ANN_REDUCE_DOT ? &b : &a);
     bool const rows = r.sa_axis == 1 && r.sb_axis == 1 && r.len >= 16;
+    // 16-byte vectors need every row start aligned: the base pointers and
+    // every non-reduced stride a multiple of the vector width.
+    bool vec = rows && aligned(a.data, 16) && (op != ANN_REDUCE_DOT || aligned(b.data, 16));
+    for (int i = 0; vec && i < a.rank; ++i) {
+        if (i == static_cast<int>(axis) || a.ext[i] == 1) continue;
+        vec = a.str[i] % Vec16<T>::n == 0 && (op != ANN_REDUCE_DOT || b.str[i] % Vec16<T>::n == 0);
+    }
     cudaStream_t s = as_stream(stream);
     switch (op) {
-        case ANN_REDUCE_SUM: launch_reduce<ANN_REDUCE_SUM, T>(s, r, rows); break;
-        case ANN_REDUCE_MAX: launch_reduce<ANN_REDUCE_MAX, T>(s, r, rows); break;
-        case ANN_REDUCE_MEAN: launch_reduce<ANN_REDUCE_MEAN, T>(s, r, rows); break;
-        case ANN_REDUCE_SUM_SQUARES: launch_reduce<ANN_REDUCE_SUM_SQUARES, T>(s, r, rows); break;
-        default: launch_reduce<ANN_REDUCE_DOT, T>(s, r, rows); break;
+        case ANN_REDUCE_SUM: ANN_TRY((launch_reduce<ANN_REDUCE_SUM, T>(s, r, rows, vec))); break;
+        case ANN_REDUCE_MAX: ANN_TRY((launch_reduce<ANN_REDUCE_MAX, T>(s, r, rows, vec))); break;
+        case ANN_REDUCE_MEAN: ANN_TRY((launch_reduce<ANN_REDUCE_MEAN, T>(s, r, rows, vec))); break;
+        case ANN_REDUCE_SUM_SQUARES: ANN_TRY((launch_reduce<ANN_REDUCE_SUM_SQUARES, T>(s, r, rows, vec))); break;
+        default: ANN_TRY((launch_reduce<ANN_REDUCE_DOT, T>(s, r, rows, vec))); break;
     }
     return check_launch(name);
 }

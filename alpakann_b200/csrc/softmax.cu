@@ -2,12 +2,15 @@
 // onHost/nn/softmax.hpp:14-80, onAcc/internal/nn/softmax.hpp:15-116) and ops::scale
 // (onHost/ops/elementwise.hpp:64-73, 330-334).
 //
-// Softmax rows run along an arbitrary axis of a tensor of any rank. A row is
-// owned by one warp (rows up to 1024 elements) or by a whole 256-thread CTA
-// (longer rows): max over the unmasked entries from lowest(), sum of
-// exp(x - max), then out = exp(x - max) / sum with masked entries written as 0
-// -- the reference's three passes, with the passes' reductions done by warp
-// shuffles instead of one thread per row. Re-reads of a row come from L1/L2.
+// Softmax rows run along an arbitrary axis of a tensor of any rank. A row of
+// up to 2048 elements is owned by one to eight warps and held in their
+// registers, eight elements per lane (one read, one write); a longer row by a
+// whole 256-thread CTA, re-read from L1/L2. Either way: max over the unmasked entries from lowest(), sum of
+// exp(x - max), then out = exp(x - max) / sum with masked entries written as
+// 0 -- the reference's three passes, with the passes' reductions done by warp
+// shuffles instead of one thread per row.
+#include <type_traits>
+
 #include "common.cuh"
 #include "reduce.cuh"
 
@@ -25,7 +28,146 @@ struct SoftmaxArgs {
     const void* mask;                    // maskedSoftmax: additive mask, input's extents
     int64_t s_mask;                      // its stride along the softmax axis
     Outer2 mouter;                       // its row offsets (sa; sb unused)
+    int uniform;                         // rows equally spaced in every operand:
+    int64_t row_in, row_out, row_mask;   //   row r starts at r * row_* (no index division)
 };
+
+// Row starts of row r in input, output and mask.
+__device__ __forceinline__ void row_offsets(SoftmaxArgs const& a, int64_t row, int64_t& oi, int64_t& oo,
+                                            int64_t& om) {
+    if (a.uniform) {
+        oi = row * a.row_in;
+        oo = row * a.row_out;
+        om = row * a.row_mask;
+        return;
+    }
+    a.outer.offsets(row, oi, oo);
+    int64_t unused;
+    if (a.mask) a.mouter.offsets(row, om, unused);
+}
+
+// A row of at most WPR * 32 * CH * VEC elements, owned by WPR warps and held
+// in their registers: one read of the row, one write, nothing re-read. Lane
+// l of warp w (of the row's WPR) owns the VEC-element pieces
+// c * 32 * WPR + 32 w + l; with VEC > 1 (unit-stride, 16-byte aligned rows)
+// each piece is one 16-byte load. All loads of a lane are issued before any
+// of them is used. Max and sum: per lane in piece order, across the warp by
+// shuffles, across the row's warps through shared memory in warp order.
+template <typename T, int VEC>
+struct Piece {
+    using type = typename Vec16<T>::type;
+};
+template <typename T>
+struct Piece<T, 1> {
+    using type = T;
+};
+
+template <typename T, int CH, int VEC, int WPR, bool MASK>
+__global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
+    using P = typename Piece<T, VEC>::type;
+    constexpr int N = CH * VEC;  // elements per lane
+    constexpr int RPB = 8 / WPR;  // rows per CTA and iteration
+    static_assert(N <= 64 && 8 % WPR == 0, "keep mask is 64 bits; WPR divides 8");
+    // Partials of the row's warps, double-buffered by iteration parity, so
+    // each reduction needs one barrier of the row's warps (named barrier
+    // 1 + row group, 32 * WPR threads) and rows of a CTA never wait on each
+    // other.
+    __shared__ T red_max[2][8], red_sum[2][8];
+    T const* in = static_cast<T const*>(a.in);
+    T const* mk = static_cast<T const*>(a.mask);
+    T* out = static_cast<T*>(a.out);
+    int const lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int const part = warp % WPR, first = warp - part;  // this warp's slice; the row's first warp
+    int64_t const per_iter = static_cast<int64_t>(gridDim.x) * RPB;
+    int64_t const iters = ceil_div(a.rows, per_iter);
+    for (int64_t it = 0; it < iters; ++it) {  // same trip count in every warp of the CTA
+        int64_t const row = it * per_iter + static_cast<int64_t>(blockIdx.x) * RPB + warp / WPR;
+        bool const live = row < a.rows;
+        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0;
+        if (live) {
+            row_offsets(a, row, oi, oo, om);
+            if (a.causal) {
+                qf = (row / a.q_div) % a.q_mod;
+                kf = (row / a.k_div) % a.k_mod;
+            }
+        }
+        auto elem0 = [&](int c) { return (c * 32 * WPR + 32 * part + lane) * VEC; };  // < 2048 + 256
+        T v[N];
+        int const len = static_cast<int>(a.len);  // <= 2048 on this path
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            int const e0 = elem0(c);
+            bool const in_row = live && e0 < len;  // with VEC > 1, len is a multiple of VEC
+            P x{}, y{};
+            if constexpr (VEC > 1) {
+                if (in_row) x = *reinterpret_cast<P const*>(in + oi + e0);
+                if constexpr (MASK)
+                    if (in_row) y = *reinterpret_cast<P const*>(mk + om + e0);
+            } else {
+                if (in_row) x = in[oi + e0 * a.s_in];
+                if constexpr (MASK)
+                    if (in_row) y = mk[om + e0 * a.s_mask];
+            }
+            T const* xe = reinterpret_cast<T const*>(&x);
+            T const* ye = reinterpret_cast<T const*>(&y);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                if constexpr (MASK) v[c * VEC + k] = add_rn(xe[k], ye[k]);
+                else v[c * VEC + k] = xe[k];
+            }
+        }
+        uint64_t keep = 0;  // bit j: element j of this lane is in the row and not masked
+        T m = Lowest<T>::value;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            int const e = elem0(j / VEC) + j % VEC;
+            bool ok = live && e < len;
+            if (a.causal) ok = ok && (a.q_is_axis ? e : qf) >= (a.k_is_axis ? e : kf);
+            if (ok) {
+                m = fmax(m, v[j]);
+                keep |= uint64_t{1} << j;
+            }
+        }
+        int const buf = static_cast<int>(it & 1);
+        auto row_barrier = [&]() {
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / WPR), "r"(32 * WPR) : "memory");
+        };
+        m = warp_max(m);
+        if constexpr (WPR > 1) {
+            if (lane == 0) red_max[buf][warp] = m;
+            row_barrier();
+            m = red_max[buf][first];
+#pragma unroll
+            for (int w = 1; w < WPR; ++w) m = fmax(m, red_max[buf][first + w]);
+        }
+        T sum{};
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            v[j] = (keep >> j & 1u) ? exp_t(v[j] - m) : T(0);
+            sum += v[j];
+        }
+        sum = warp_sum(sum);
+        if constexpr (WPR > 1) {
+            if (lane == 0) red_sum[buf][warp] = sum;
+            row_barrier();
+            sum = red_sum[buf][first];
+#pragma unroll
+            for (int w = 1; w < WPR; ++w) sum += red_sum[buf][first + w];
+        }
+        if (!live) continue;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            int const e0 = elem0(c);
+            if (e0 >= len) continue;
+            P r;
+            T* re = reinterpret_cast<T*>(&r);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) re[k] = (keep >> (c * VEC + k) & 1u) ? v[c * VEC + k] / sum : T{};
+            if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = r;
+            else out[oo + e0 * a.s_out] = r;
+        }
+    }
+}
 
 // MASK: maskedSoftmax (onAcc/internal/nn/softmax.hpp:76-116), the row is
 // input + mask and nothing is skipped.
@@ -40,12 +182,13 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
     for (int64_t it = 0; it < iters; ++it) {
         int64_t const row = (it * gridDim.x + blockIdx.x) * RPB + threadIdx.x / GROUP;
         bool const live = row < a.rows;
-        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0, unused = 0;
+        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0;
         if (live) {
-            a.outer.offsets(row, oi, oo);
-            if constexpr (MASK) a.mouter.offsets(row, om, unused);
-            qf = (row / a.q_div) % a.q_mod;
-            kf = (row / a.k_div) % a.k_mod;
+            row_offsets(a, row, oi, oo, om);
+            if (a.causal) {
+                qf = (row / a.q_div) % a.q_mod;
+                kf = (row / a.k_div) % a.k_mod;
+            }
         }
         // masked(i) <=> probe[queryAxis] < probe[keyAxis] with probe[axis] = i
         auto masked = [&](int64_t i) {
@@ -124,18 +267,60 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
         a.mouter = a.outer;
         for (int i = 0; i < in.rank; ++i) a.mouter.sa[i] = mask.str[i];
     }
+    // Equally spaced rows: the non-axis axes (extent > 1) merge into one, in
+    // every operand, i.e. each one's stride is the next one's times its extent.
+    {
+        int prev = -1;
+        bool uni = true;
+        for (int i = 0; i < in.rank && uni; ++i) {
+            if (i == static_cast<int>(axis) || in.ext[i] == 1) continue;
+            if (prev >= 0) {
+                uni = in.str[prev] == in.str[i] * in.ext[i] && out.str[prev] == out.str[i] * out.ext[i] &&
+                      (!mask_v || mask.str[prev] == mask.str[i] * mask.ext[i]);
+            }
+            prev = i;
+        }
+        int last = -1;  // the innermost non-axis axis sets the row spacing
+        for (int i = 0; i < in.rank; ++i)
+            if (i != static_cast<int>(axis) && in.ext[i] != 1) last = i;
+        a.uniform = uni ? 1 : 0;
+        a.row_in = last >= 0 ? in.str[last] : 0;
+        a.row_out = last >= 0 ? out.str[last] : 0;
+        a.row_mask = (last >= 0 && mask_v) ? mask.str[last] : 0;
+    }
     cudaStream_t s = as_stream(stream);
-    if (mask_v) {
-        if (a.len <= 1024) softmax_kernel<T, 32, true><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
-        else softmax_kernel<T, 256, true><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
-        return check_launch("maskedSoftmax");
+    char const* name = mask_v ? "maskedSoftmax" : causal ? "causalSoftmax" : "softmax";
+    // 16-byte pieces: unit stride along the axis in every operand, the row
+    // length a multiple of the piece, every row start 16-byte aligned.
+    constexpr int NV = Vec16<T>::n;
+    bool vec = a.s_in == 1 && a.s_out == 1 && a.len % NV == 0 && aligned(in.data, 16) && aligned(out.data, 16);
+    if (mask_v) vec = vec && a.s_mask == 1 && aligned(mask.data, 16);
+    for (int i = 0; vec && i < in.rank; ++i) {
+        if (i == static_cast<int>(axis) || in.ext[i] == 1) continue;
+        vec = in.str[i] % NV == 0 && out.str[i] % NV == 0 && (!mask_v || mask.str[i] % NV == 0);
     }
-    if (a.len <= 1024) {
-        softmax_kernel<T, 32, false><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
-    } else {
-        softmax_kernel<T, 256, false><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
-    }
-    return check_launch(causal ? "causalSoftmax" : "softmax");
+    // Up to 2048 elements a row stays in registers, 8 per lane: 1, 2, 4 or 8
+    // warps per row. Longer rows stream through L1/L2.
+    auto launch = [&](auto mask_tag) {
+        constexpr bool M = decltype(mask_tag)::value;
+        constexpr int CV = 8 / NV;  // 16-byte pieces per lane
+        if (vec) {
+            if (a.len <= 256) softmax_regs<T, CV, NV, 1, M><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+            else if (a.len <= 512) softmax_regs<T, CV, NV, 2, M><<<grid_for(a.rows, 4), 256, 0, s>>>(a);
+            else if (a.len <= 1024) softmax_regs<T, CV, NV, 4, M><<<grid_for(a.rows, 2), 256, 0, s>>>(a);
+            else if (a.len <= 2048) softmax_regs<T, CV, NV, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else softmax_kernel<T, 256, M><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
+        } else {
+            if (a.len <= 256) softmax_regs<T, 8, 1, 1, M><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+            else if (a.len <= 512) softmax_regs<T, 8, 1, 2, M><<<grid_for(a.rows, 4), 256, 0, s>>>(a);
+            else if (a.len <= 1024) softmax_regs<T, 8, 1, 4, M><<<grid_for(a.rows, 2), 256, 0, s>>>(a);
+            else if (a.len <= 2048) softmax_regs<T, 8, 1, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else softmax_kernel<T, 256, M><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
+        }
+    };
+    if (mask_v) launch(std::true_type{});
+    else launch(std::false_type{});
+    return check_launch(name);
 }
 
 // ---- ops::scale ----------------------------------------------------------

@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--ops", action="store_true",
                    help="measure only the HBM-bound ops (elementwise, bias+activation, reductions, maskedSoftmax) "
                         "and the MLP layers on 1 GiB operands; one JSON line per op")
+    p.add_argument("--ops-elems", type=int, default=1 << 28,
+                   help="elements per operand of --ops (default 2^28 = 1 GiB of float32); a smaller value also skips "
+                        "the MLP lines (the small case ncu captures use)")
     p.add_argument("--loader", metavar="MIB", type=int, default=None,
                    help="measure only the model-artifact loader on a MIB-sized float32 file (page-cached): "
                         "sha256File, loadBinaryTensor, a 1/8 column shard, against pinned and pageable copies")
@@ -460,30 +463,34 @@ def ops_only(args):
     torch.manual_seed(0)
     dev = "cuda"
     f32 = torch.float32
-    G = 1 << 28  # elements: 1 GiB of float32 per operand
+    G = max(args.ops_elems // (1 << 21), 1) << 21  # elements per operand, a multiple of 4096 * 512
+    R = G // 4096
     a = torch.randn(G, device=dev)
     b = torch.randn(G, device=dev)
     o = torch.empty(G, device=dev)
-    rows = a.view(65536, 4096)
+    rows = a.view(R, 4096)
     bias = torch.randn(4096, device=dev)
-    red_rows = torch.empty((65536, 1), device=dev)
+    red_rows = torch.empty((R, 1), device=dev)
     red_cols = torch.empty((1, 4096), device=dev)
-    sm_in = a[:1 << 27].view(4, 32, 1024, 1024)
-    sm_mask = b[:1 << 27].view(4, 32, 1024, 1024)
-    sm_out = o[:1 << 27].view(4, 32, 1024, 1024)
+    S = G // 2 // (1024 * 1024)  # softmax rows of 1024: half of an operand
+    sm_in = a[:S << 20].view(S, 1, 1024, 1024)
+    sm_mask = b[:S << 20].view(S, 1, 1024, 1024)
+    sm_out = o[:S << 20].view(S, 1, 1024, 1024)
 
     def timed(fn, reps=max(args.steps, 5), warm=max(args.warmup, 3)):
+        """Mean device time of `reps` back-to-back launches between two
+        events, so the host's launch work overlaps the previous kernel
+        instead of being counted as device time."""
         for _ in range(warm):
             fn()
-        ts = []
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         for _ in range(reps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
             fn()
-            e1.record()
-            e1.synchronize()
-            ts.append(e0.elapsed_time(e1) / 1e3)
-        return sorted(ts)[len(ts) // 2]
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
 
     cases = [
         ("add", 3 * 4 * G, lambda: ops.add(None, None, a, b, o)),
@@ -491,13 +498,14 @@ def ops_only(args):
         ("silu", 2 * 4 * G, lambda: ops.silu(None, None, a, o)),
         ("gelu", 2 * 4 * G, lambda: ops.gelu(None, None, a, o)),
         ("swiglu", 3 * 4 * G, lambda: ops.swiglu(None, None, a, b, o)),
-        ("biasAdd+silu [65536,4096]", 2 * 4 * G,
+        (f"biasAdd+silu [{R},4096]", 2 * 4 * G,
          lambda: ann._capi.check(ann._capi.lib.ann_bias_add_f32(
-             None, ann._capi.ref(rows), ann._capi.ref(bias), 2, ann._capi.ref(o.view(65536, 4096))))),
-        ("reduceSum axis 1 [65536,4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_rows, 1)),
-        ("reduceSum axis 0 [65536,4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_cols, 0)),
-        ("maskedSoftmax [4,32,1024,1024]", 3 * 4 * (1 << 27),
+             None, ann._capi.ref(rows), ann._capi.ref(bias), 2, ann._capi.ref(o.view(R, 4096))))),
+        (f"reduceSum axis 1 [{R},4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_rows, 1)),
+        (f"reduceSum axis 0 [{R},4096]", 4 * G, lambda: ops.reduceSum(None, None, rows, red_cols, 0)),
+        (f"maskedSoftmax [{S},1,1024,1024]", 3 * 4 * (S << 20),
          lambda: nn.maskedSoftmax(None, None, sm_in, sm_mask, sm_out, 3)),
+        (f"softmax [{S},1,1024,1024]", 2 * 4 * (S << 20), lambda: nn.softmax(None, None, sm_in, sm_out, 3)),
     ]
     for name, nbytes, fn in cases:
         t = timed(fn)
@@ -506,6 +514,8 @@ def ops_only(args):
                           "peak_kind": kind, "bytes_per_launch": nbytes}), flush=True)
     del a, b, o
     torch.cuda.empty_cache()
+    if args.ops_elems != 1 << 28:
+        return
     # the gated MLP and a 3-layer mlpForward at decoder-like shapes: cuBLAS
     # GEMMs plus this library's fused passes
     M, K, F = 4096, 4096, 14336
