@@ -22,6 +22,8 @@
 // with the most key tiles are dispatched first.
 #include <mutex>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "reduce.cuh"
 #include "tma.cuh"
@@ -30,6 +32,8 @@ namespace ann {
 
 int prefill_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
                    uint32_t g, int layout, int causal, bool& handled);
+int prefill_tc_pair_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
+                        uint32_t g, int layout, int causal, bool& handled);
 int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, double scale,
                     uint32_t g, int layout, int causal, bool& handled);
 
@@ -357,12 +361,16 @@ int prefill(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const a
         al = al && (q.str[i] * eb) % 16 == 0 && (k.str[i] * eb) % 16 == 0 && (v.str[i] * eb) % 16 == 0;
     if (!unit || !al)
         return fail(ANN_ENOTSUP, "attention prefill needs unit-stride head vectors and 16-byte aligned rows.");
-    {  // fp32: tcgen05 3xTF32 kernel; fp64: FP64 tensor-core (DMMA) kernel
+    {  // fp32: tcgen05 3xTF32 kernel on SM pairs, else on single SMs; fp64: FP64 tensor-core (DMMA) kernel
         bool handled = false;
         int rc;
-        if constexpr (sizeof(T) == 4)
-            rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
-        else
+        if constexpr (sizeof(T) == 4) {
+            rc = ANN_OK;
+            if (!std::getenv("ANN_PREFILL_FMA") || std::getenv("ANN_PREFILL_FMA")[0] != '1')
+                rc = prefill_tc_pair_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+            if (!handled && rc == ANN_OK)
+                rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+        } else
             rc = prefill_mma_f64(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
         if (handled || rc != ANN_OK) return rc;
     }

@@ -29,6 +29,43 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// ---- 2-CTA clusters ------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of this CTA's shared address `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t map_cluster(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// Arrival on an mbarrier given by its shared::cluster address (any CTA of the
+// cluster), with the default release semantics at CTA scope: the arriving
+// thread's earlier writes are performed before the arrival. A cluster-scope
+// release would also wait for the thread's global loads still in flight.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// All threads of all CTAs of the cluster (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// try_wait with acquire semantics at cluster scope: for barriers that threads of
+// another CTA of the cluster arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
@@ -61,15 +98,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 }
 
 // As mbar_wait_bounded, but also gives up as soon as *abort becomes non-zero
-// (another thread of the CTA has already given up).
+// (another thread of the CTA has already given up). CLUSTER: the barrier's
+// arrivals come from other CTAs of the cluster too (acquire at cluster scope).
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort,
                                                    uint64_t limit_ns = 1000000000ull) {
-    if (mbar_try_wait(bar, parity)) return true;
+    auto probe = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+    if (probe()) return true;
     uint64_t const t0 = global_timer_ns();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+            if (probe()) return true;
         if (*abort) return false;
         if (global_timer_ns() - t0 > limit_ns) {
             *abort = 1;

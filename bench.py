@@ -392,7 +392,10 @@ def measure_prefill(name, world, rank, comm, reps=10):
     if p["dtype"] == "f32":
         # 3xTF32: every useful flop costs three tf32 tensor flops
         pk, kind = tf32_peak()
-        res.update(kernel=f"prefill_tc_kernel<{D}> (tcgen05 3xTF32)", tf32_peak_tflops=pk, tf32_peak_kind=kind,
+        pair = os.environ.get("ANN_PREFILL_TC_PAIR", "1")[:1] != "0"
+        name = (f"prefill_pair_kernel<{D}> (tcgen05 cta_group::2 on SM pairs, 3xTF32)" if pair
+                else f"prefill_tc_kernel<{D}> (tcgen05 3xTF32)")
+        res.update(kernel=name, tf32_peak_tflops=pk, tf32_peak_kind=kind,
                    frac_of_3xtf32_peak=3 * res["tflops"] / world / pk)
     else:
         pk = fp64_gemm_tflops()

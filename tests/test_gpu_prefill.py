@@ -20,14 +20,18 @@ def ann():
     return alpakann_b200
 
 
-@pytest.fixture(params=["tensor", "fma"], autouse=True)
+@pytest.fixture(params=["tensor", "tensor-1sm", "fma"], autouse=True)
 def kernel(request, monkeypatch):
-    """fp32 runs on the tcgen05 3xTF32 kernel by default; ANN_PREFILL_FMA=1
-    selects the FMA kernel (fp64 always runs on DFMA)."""
+    """fp32 runs on the tcgen05 3xTF32 kernel on SM pairs by default;
+    ANN_PREFILL_TC_PAIR=0 keeps it on one SM per CTA, ANN_PREFILL_FMA=1
+    selects the FMA kernel (fp64 runs on the FP64 tensor cores, or on DFMA
+    with ANN_PREFILL_FMA=1)."""
+    monkeypatch.delenv("ANN_PREFILL_FMA", raising=False)
+    monkeypatch.delenv("ANN_PREFILL_TC_PAIR", raising=False)
     if request.param == "fma":
         monkeypatch.setenv("ANN_PREFILL_FMA", "1")
-    else:
-        monkeypatch.delenv("ANN_PREFILL_FMA", raising=False)
+    elif request.param == "tensor-1sm":
+        monkeypatch.setenv("ANN_PREFILL_TC_PAIR", "0")
     return request.param
 
 
