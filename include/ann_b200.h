@@ -360,9 +360,11 @@ int ann_attention_decode_f64(ann_stream stream, const ann_view* q, const ann_vie
  * Tq != Tk. q, out: BTHD [B,Tq,Hq,D]; k, v: `kv_layout` with Tk keys.
  * Requires unit innermost stride, 16-byte aligned rows, D in {64, 128}.
  * fp32 runs on the tensor cores (tcgen05 kind::tf32 with the 3xTF32 split,
- * fp32-level accuracy); ANN_PREFILL_FMA=1 in the environment selects the
- * FP32-pipe kernel instead. fp64 runs on the FP64 tensor cores (mma.sync
- * m16n8k4.f64; ANN_PREFILL_FMA=1 selects the DFMA kernel). */
+ * fp32-level accuracy), by default on pairs of SMs that share every MMA
+ * (cta_group::2); ANN_PREFILL_TC_PAIR=0 keeps one SM per CTA, and
+ * ANN_PREFILL_FMA=1 selects the FP32-pipe kernel instead. fp64 runs on the
+ * FP64 tensor cores (mma.sync m16n8k4.f64; ANN_PREFILL_FMA=1 selects the DFMA
+ * kernel). */
 int ann_attention_prefill_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
                               const ann_view* out, float scale, uint32_t queries_per_kv_group, int32_t kv_layout,
                               int32_t causal);
