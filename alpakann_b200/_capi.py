@@ -47,6 +47,7 @@ SIGNATURES = {
     "ann_version": ([], ctypes.c_int),
     "ann_last_error": ([], ctypes.c_char_p),
     "ann_take_device_error": ([_S, ctypes.POINTER(_u32)], ctypes.c_int),
+    "ann_selftest_wait": ([_S, _i32, ctypes.c_uint64], ctypes.c_int),
     "ann_comm_unique_id": ([ctypes.POINTER(_ID)], ctypes.c_int),
     "ann_comm_init": ([ctypes.POINTER(_C), _i32, _i32, ctypes.POINTER(_ID), ctypes.c_double], ctypes.c_int),
     "ann_comm_size": ([_C, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], ctypes.c_int),

@@ -90,6 +90,7 @@ int ann_take_device_error(ann_stream stream, uint32_t* bits) {
     ANN_TRY(ann::take_prefill_error(s, &value));
     ANN_TRY(ann::take_prefill_tc_error(s, &value));
     ANN_TRY(ann::take_prefill_tc2_error(s, &value));
+    ANN_TRY(ann::take_selftest_error(s, &value));
     ANN_TRY(ann::take_rms_error(s, &value));
     ANN_TRY(ann::take_prefill_f64_error(s, &value));
     *bits = value;

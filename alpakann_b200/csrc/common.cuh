@@ -31,6 +31,7 @@ int take_decode_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_tc_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_tc2_error(cudaStream_t s, uint32_t* bits);
+int take_selftest_error(cudaStream_t s, uint32_t* bits);
 int take_rms_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_f64_error(cudaStream_t s, uint32_t* bits);
 

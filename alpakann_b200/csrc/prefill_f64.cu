@@ -6,7 +6,7 @@
 // mma.sync.m16n8k4.f64 (fp64 products, fp64 accumulation).
 //
 // One CTA = 64 query rows of one (batch, head), 4 warps of 16 rows; K/V tiles of
-// 32 keys stream through two shared-memory stages filled by 1-D bulk copies,
+// 32 (or 16, see FCfg) keys stream through two shared-memory stages filled by 1-D bulk copies,
 // rows padded by 16 bytes (pitch = 16 mod 128 bytes), which makes every
 // fragment read below hit each bank at most twice per 256 bytes.
 // Fragment layout of m16n8k4.f64 (g = lane / 4, t = lane % 4):
@@ -36,13 +36,20 @@ namespace {
 
 __device__ unsigned int g_f64_error;
 
-constexpr int kBM = 64, kBN = 32, kThreads = 128;
+constexpr int kBM = 64, kThreads = 128;
 
-template <int D>
+// BN keys per tile. D = 64 with 16-key tiles needs 158 registers and 68 KB of
+// shared memory, room for 3 CTAs (12 warps) per SM that keep the DMMA pipe
+// fed on long grids; with 32-key tiles (2 CTAs per SM) half as many tiles carry
+// the per-tile softmax cost, which wins on short grids (launch_f64 picks).
+// D = 128: 32-key tiles, one CTA per SM.
+template <int D, int BN_ = 32>
 struct FCfg {
+    static constexpr int BN = BN_;
+    static constexpr int MIN_CTAS = D <= 64 ? (BN <= 16 ? 3 : 2) : 1;
     static constexpr int LD = D + 2;  // row pitch in doubles: 16 bytes of padding
     static constexpr int ROWB = D * 8;
-    static constexpr size_t TILE = static_cast<size_t>(kBN) * LD;  // doubles per K or V stage
+    static constexpr size_t TILE = static_cast<size_t>(BN) * LD;  // doubles per K or V stage
     static constexpr size_t OFF_Q = 0;
     static constexpr size_t OFF_K = OFF_Q + static_cast<size_t>(kBM) * LD * 8;
     static constexpr size_t OFF_V = OFF_K + 2 * TILE * 8;
@@ -84,9 +91,10 @@ __device__ __forceinline__ double quad_sum(double x) {
     return x + __shfl_xor_sync(0xffffffffu, x, 2);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads) prefill_f64_kernel(F64Args a, double scale) {
-    using C = FCfg<D>;
+template <int D, int BN>
+__global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_kernel(F64Args a, double scale) {
+    using C = FCfg<D, BN>;
+    constexpr int kBN = C::BN;
     constexpr int NJ = kBN / 8;  // key blocks of 8 per tile
     constexpr int NO = D / 8;    // output column blocks of 8
     extern __shared__ __align__(128) unsigned char smem[];
@@ -262,22 +270,32 @@ __global__ void __launch_bounds__(kThreads) prefill_f64_kernel(F64Args a, double
     }
 }
 
-template <int D>
-int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads) {
-    using C = FCfg<D>;
+template <int D, int BN>
+int launch_f64_bn(ann_stream stream, F64Args& a, double scale, int64_t batch_heads) {
+    using C = FCfg<D, BN>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(prefill_f64_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr = cudaFuncSetAttribute(prefill_f64_kernel<D, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::SMEM));
     });
     if (attr != cudaSuccess)
         return fail(ANN_ECUDA, "attention prefill (fp64 MMA) setup: %s", cudaGetErrorString(attr));
     a.bhs = batch_heads;
-    a.head_chunk = head_chunk_for(batch_heads, a.q_tiles, 2 * a.Tk * D * 8, D == 64 ? 2 : 1);
+    a.head_chunk = head_chunk_for(batch_heads, a.q_tiles, 2 * a.Tk * D * 8, C::MIN_CTAS);
     dim3 grid(static_cast<unsigned>(a.q_tiles * batch_heads));
-    prefill_f64_kernel<D><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
+    prefill_f64_kernel<D, BN><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
     return check_launch("attention prefill (fp64 MMA)");
+}
+
+template <int D>
+int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads) {
+    if constexpr (D <= 64) {
+        // 16-key tiles once the grid fills at least four waves of 3-CTA slots
+        if (static_cast<int64_t>(a.q_tiles) * batch_heads >= int64_t{4} * 3 * sm_count())
+            return launch_f64_bn<D, 16>(stream, a, scale, batch_heads);
+    }
+    return launch_f64_bn<D, 32>(stream, a, scale, batch_heads);
 }
 
 }  // namespace

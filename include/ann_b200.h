@@ -78,6 +78,12 @@ const char* ann_last_error(void);
 /* Reads and clears the device error word of the current device; synchronises
  * `stream` first. *bits receives the ANN_DEVERR_* bits that were set. */
 int ann_take_device_error(ann_stream stream, uint32_t* bits);
+/* Self-test of the failure-detection path the kernels share: one CTA waits on
+ * an mbarrier with the kernels' bounded wait. arrive != 0: the barrier is
+ * arrived on first and the wait completes; arrive == 0: nothing arrives, the
+ * wait gives up after limit_ns (at most 2 s) and ANN_DEVERR_WAIT_TIMEOUT shows
+ * up in the next ann_take_device_error; the context stays usable. */
+int ann_selftest_wait(ann_stream stream, int32_t arrive, uint64_t limit_ns);
 
 /* ---- embeddingLookup: onHost/nn/embedding.hpp:17-36 --------------------
  * out[t, h] = embedding[ids[t], h]. ids: rank-1 uint32; embedding, output:

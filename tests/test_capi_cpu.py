@@ -237,3 +237,9 @@ def test_kv_cache_append_and_residual_validation():
     x, w = np.zeros((4, 8), np.float32), np.zeros((8, 6), np.float32)
     assert lib.ann_output_projection_residual_f32(None, R(x), R(w), R(np.zeros((4, 5), np.float32)),
                                                   R(np.zeros((4, 6), np.float32))) == _capi.ANN_EINVAL
+
+
+def test_selftest_limit_validated(capi):
+    """The wait self-test refuses limits above 2 s before launching anything."""
+    rc = capi.lib.ann_selftest_wait(None, 0, 3_000_000_000)
+    assert rc == capi.ANN_EINVAL and "2 s" in capi.lib.ann_last_error().decode()

@@ -141,6 +141,11 @@ def test_prefill_c4_fp64_sampled(ann):
     _sampled(ann, np.float64, 2, 1024, 16, 64, 4)
 
 
+def test_prefill_fp64_long_grid_sampled(ann):
+    """fp64 D = 64 on a grid long enough for the 16-key-tile variant (2048 CTAs)."""
+    _sampled(ann, np.float64, 4, 2048, 16, 64, 5)
+
+
 def test_prefill_c3_fp32_sampled(ann):
     """c3: batch 4, seq 4096, 32 heads x 128, fp32, causal."""
     _sampled(ann, np.float32, 4, 4096, 32, 128, 3)
