@@ -11,8 +11,10 @@
 //    image itself (a file-scope __device__ array, created when the module is
 //    loaded on a device), so no call asks any allocator for memory;
 //  - its two GEMMs are this file's own kernels, not a library's.
-// The price is a size limit (kScratchBytes of hidden activations) and plain
-// SIMT FMA GEMMs, slower than cuBLAS on large shapes.
+// The price is a size limit (kScratchBytes of hidden activations), plain
+// SIMT FMA GEMMs, slower than cuBLAS on large shapes, and kScratchBytes of
+// device memory that every GPU which loads the library holds until the process
+// exits, whether or not it ever calls this entry point.
 //
 // The first call on a device looks the buffer's address up with
 // cudaGetSymbolAddress (no allocation) and remembers it; make that first call

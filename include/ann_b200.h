@@ -327,7 +327,8 @@ int ann_mlp_f64(ann_stream stream, const ann_view* input, const ann_view* wgate,
  * buffers per call. This call allocates nothing: the [batch, hidden]
  * activations go to a buffer that is part of the library image (8 MiB per
  * device, so batch * hidden * element size <= 8388608 bytes, else
- * ANN_EINVAL), and both GEMMs are the library's own kernels, not cuBLAS.
+ * ANN_EINVAL; every GPU that loads the library holds those 8 MiB until the
+ * process exits, whether or not it calls this), and both GEMMs are the library's own kernels, not cuBLAS.
  * dtype: ANN_DTYPE_F32 or ANN_DTYPE_F64. The first call on each device looks
  * up the buffer's address (cudaGetSymbolAddress); make it before any stream
  * capture. Nothing in the buffer needs to start at zero. Calls whose work
