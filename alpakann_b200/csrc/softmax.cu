@@ -3,12 +3,18 @@
 // (onHost/ops/elementwise.hpp:64-73, 330-334).
 //
 // Softmax rows run along an arbitrary axis of a tensor of any rank. A row of
-// up to 2048 elements is owned by one to eight warps and held in their
-// registers, eight elements per lane (one read, one write); a longer row by a
-// whole 256-thread CTA, re-read from L1/L2. Either way: max over the unmasked entries from lowest(), sum of
-// exp(x - max), then out = exp(x - max) / sum with masked entries written as
-// 0 -- the reference's three passes, with the passes' reductions done by warp
-// shuffles instead of one thread per row.
+// up to 8192 elements is owned by one to eight warps and held in their
+// registers, 8, 16 or 32 elements per lane (one read, one write); a row of up
+// to 96 KB by a 256-thread CTA that keeps it in shared memory (one read, one
+// write); a longer row by a 256-thread CTA that re-reads it from L1/L2. In
+// every case: max over the unmasked entries from lowest(), sum of
+// exp(x - max), then out = exp(x - max) * (1 / sum) with masked entries
+// written as 0 -- the reference's three passes, with the passes' reductions
+// done by warp shuffles instead of one thread per row, and one division per
+// row instead of one per element (the product is within an ulp of the
+// reference's quotient; the per-element division made these kernels
+// instruction-bound). The kept elements of a causal row are one index range,
+// tested with one compare per element.
 #include <type_traits>
 
 #include "common.cuh"
@@ -44,6 +50,24 @@ __device__ __forceinline__ void row_offsets(SoftmaxArgs const& a, int64_t row, i
     a.outer.offsets(row, oi, oo);
     int64_t unused;
     if (a.mask) a.mouter.offsets(row, om, unused);
+}
+
+// Elements of row `row` that the causal test keeps, as one range [lo, hi).
+// An element e is kept when probe[queryAxis] >= probe[keyAxis] with
+// probe[axis] = e, so with q, k the row's own query / key indices:
+//   softmax axis = key axis only     e <= q   ->  [0, min(len, q + 1))
+//   softmax axis = query axis only   e >= k   ->  [min(k, len), len)
+//   softmax axis = both              always   ->  [0, len)
+//   neither                          q >= k   ->  [0, len), else nothing.
+// Without a causal mask every element is kept.
+__device__ __forceinline__ void kept_range(SoftmaxArgs const& a, int64_t row, int64_t& lo, int64_t& hi) {
+    lo = 0;
+    hi = a.len;
+    if (!a.causal) return;
+    int64_t const q = (row / a.q_div) % a.q_mod, k = (row / a.k_div) % a.k_mod;
+    if (a.k_is_axis && !a.q_is_axis) hi = q + 1 < a.len ? q + 1 : a.len;
+    else if (a.q_is_axis && !a.k_is_axis) lo = k < a.len ? k : a.len;
+    else if (!a.q_is_axis && !a.k_is_axis && q < k) hi = 0;
 }
 
 // A row of at most WPR * 32 * CH * VEC elements, owned by WPR warps and held
@@ -83,17 +107,18 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
     for (int64_t it = 0; it < iters; ++it) {  // same trip count in every warp of the CTA
         int64_t const row = it * per_iter + static_cast<int64_t>(blockIdx.x) * RPB + warp / WPR;
         bool const live = row < a.rows;
-        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0;
+        int64_t oi = 0, oo = 0, om = 0, lo64 = 0, hi64 = 0;
         if (live) {
             row_offsets(a, row, oi, oo, om);
-            if (a.causal) {
-                qf = (row / a.q_div) % a.q_mod;
-                kf = (row / a.k_div) % a.k_mod;
-            }
+            kept_range(a, row, lo64, hi64);
         }
-        auto elem0 = [&](int c) { return (c * 32 * WPR + 32 * part + lane) * VEC; };  // < 2048 + 256
+        auto elem0 = [&](int c) { return (c * 32 * WPR + 32 * part + lane) * VEC; };  // < 8192 + 256
         T v[N];
-        int const len = static_cast<int>(a.len);  // <= 2048 on this path
+        int const len = static_cast<int>(a.len);  // <= 8192 on this path
+        // element e is kept iff lo <= e < hi: one unsigned compare
+        int const lo = static_cast<int>(lo64);
+        unsigned const span = hi64 > lo64 ? static_cast<unsigned>(hi64 - lo64) : 0u;
+        auto kept = [&](int e) { return static_cast<unsigned>(e - lo) < span; };
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             int const e0 = elem0(c);
@@ -116,18 +141,10 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
                 else v[c * VEC + k] = xe[k];
             }
         }
-        uint64_t keep = 0;  // bit j: element j of this lane is in the row and not masked
         T m = Lowest<T>::value;
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-            int const e = elem0(j / VEC) + j % VEC;
-            bool ok = live && e < len;
-            if (a.causal) ok = ok && (a.q_is_axis ? e : qf) >= (a.k_is_axis ? e : kf);
-            if (ok) {
-                m = fmax(m, v[j]);
-                keep |= uint64_t{1} << j;
-            }
-        }
+        for (int j = 0; j < N; ++j)
+            if (kept(elem0(j / VEC) + j % VEC)) m = fmax(m, v[j]);
         int const buf = static_cast<int>(it & 1);
         auto row_barrier = [&]() {
             asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / WPR), "r"(32 * WPR) : "memory");
@@ -143,7 +160,7 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
         T sum{};
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-            v[j] = (keep >> j & 1u) ? exp_t(v[j] - m) : T(0);
+            v[j] = kept(elem0(j / VEC) + j % VEC) ? exp_t(v[j] - m) : T(0);
             sum += v[j];
         }
         sum = warp_sum(sum);
@@ -155,6 +172,7 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
             for (int w = 1; w < WPR; ++w) sum += red_sum[buf][first + w];
         }
         if (!live) continue;
+        T const inv = T(1) / sum;  // one division per row; x * (1 / sum) is within an ulp of x / sum
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             int const e0 = elem0(c);
@@ -162,9 +180,92 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
             P r;
             T* re = reinterpret_cast<T*>(&r);
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) re[k] = (keep >> (c * VEC + k) & 1u) ? v[c * VEC + k] / sum : T{};
+            for (int k = 0; k < VEC; ++k) re[k] = kept(e0 + k) ? v[c * VEC + k] * inv : T{};
             if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = r;
             else out[oo + e0 * a.s_out] = r;
+        }
+    }
+}
+
+// Rows longer than the register path holds but at most kSmemRowBytes: one
+// 256-thread CTA per row, the row (input + mask for maskedSoftmax) kept in
+// dynamic shared memory between the three passes, so it is read from HBM once
+// and written once. Thread t owns the VEC-element pieces t, t + 256, ... in
+// every pass, so no thread reads an element another one wrote and the only
+// barriers are the two inside the block reductions. Loads go out kBatch
+// pieces at a time before any of them is used.
+constexpr int64_t kSmemRowBytes = int64_t{96} << 10;
+constexpr int kBatch = 4;
+
+template <typename T, int VEC, bool MASK>
+__global__ void __launch_bounds__(256) softmax_smem(SoftmaxArgs a) {
+    using P = typename Piece<T, VEC>::type;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* buf = reinterpret_cast<T*>(smem_raw);
+    __shared__ T scratch[8];
+    T const* in = static_cast<T const*>(a.in);
+    T const* mk = static_cast<T const*>(a.mask);
+    T* out = static_cast<T*>(a.out);
+    int64_t const pieces = a.len / VEC;  // with VEC > 1, len is a multiple of VEC
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {  // same trip count in the whole CTA
+        int64_t oi = 0, oo = 0, om = 0, lo = 0, hi = 0;
+        row_offsets(a, row, oi, oo, om);
+        kept_range(a, row, lo, hi);
+        auto masked = [&](int64_t e) { return e < lo || e >= hi; };
+        T m = Lowest<T>::value;
+        for (int64_t p0 = threadIdx.x; p0 < pieces; p0 += 256 * kBatch) {
+            P x[kBatch], y[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                int64_t const e0 = (p0 + 256 * u) * VEC;
+                x[u] = P{};
+                y[u] = P{};
+                if (p0 + 256 * u >= pieces) continue;
+                if constexpr (VEC > 1) {
+                    x[u] = *reinterpret_cast<P const*>(in + oi + e0);
+                    if constexpr (MASK) y[u] = *reinterpret_cast<P const*>(mk + om + e0);
+                } else {
+                    x[u] = in[oi + e0 * a.s_in];
+                    if constexpr (MASK) y[u] = mk[om + e0 * a.s_mask];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                int64_t const e0 = (p0 + 256 * u) * VEC;
+                if (p0 + 256 * u >= pieces) continue;
+                T* xe = reinterpret_cast<T*>(&x[u]);
+                T const* ye = reinterpret_cast<T const*>(&y[u]);
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) {
+                    if constexpr (MASK) xe[k] = add_rn(xe[k], ye[k]);
+                    if (!masked(e0 + k)) m = fmax(m, xe[k]);
+                }
+                *reinterpret_cast<P*>(buf + e0) = x[u];
+            }
+        }
+        m = block_max<8>(m, scratch);
+        T sum{};
+        for (int64_t p = threadIdx.x; p < pieces; p += 256) {
+            int64_t const e0 = p * VEC;
+            P x = *reinterpret_cast<P const*>(buf + e0);
+            T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                xe[k] = masked(e0 + k) ? T(0) : exp_t(xe[k] - m);
+                sum += xe[k];
+            }
+            *reinterpret_cast<P*>(buf + e0) = x;
+        }
+        sum = block_sum<8>(sum, scratch);
+        T const inv = T(1) / sum;  // one division per row; x * (1 / sum) is within an ulp of x / sum
+        for (int64_t p = threadIdx.x; p < pieces; p += 256) {
+            int64_t const e0 = p * VEC;
+            P x = *reinterpret_cast<P const*>(buf + e0);
+            T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) xe[k] = masked(e0 + k) ? T(0) : xe[k] * inv;
+            if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = x;
+            else out[oo + e0 * a.s_out] = x;
         }
     }
 }
@@ -182,21 +283,12 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
     for (int64_t it = 0; it < iters; ++it) {
         int64_t const row = (it * gridDim.x + blockIdx.x) * RPB + threadIdx.x / GROUP;
         bool const live = row < a.rows;
-        int64_t oi = 0, oo = 0, qf = 0, kf = 0, om = 0;
+        int64_t oi = 0, oo = 0, om = 0, lo = 0, hi = 0;
         if (live) {
             row_offsets(a, row, oi, oo, om);
-            if (a.causal) {
-                qf = (row / a.q_div) % a.q_mod;
-                kf = (row / a.k_div) % a.k_mod;
-            }
+            kept_range(a, row, lo, hi);
         }
-        // masked(i) <=> probe[queryAxis] < probe[keyAxis] with probe[axis] = i
-        auto masked = [&](int64_t i) {
-            if (!a.causal) return false;
-            int64_t const qv = a.q_is_axis ? i : qf;
-            int64_t const kv = a.k_is_axis ? i : kf;
-            return qv < kv;
-        };
+        auto masked = [&](int64_t i) { return i < lo || i >= hi; };
         T const* mk = static_cast<T const*>(a.mask);
         auto value = [&](int64_t i) {
             if constexpr (MASK) return add_rn(in[oi + i * a.s_in], mk[om + i * a.s_mask]);
@@ -215,8 +307,9 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
         if constexpr (GROUP == 32) sum = warp_sum(sum);
         else sum = block_sum<8>(sum, scratch);
         if (!live) continue;
+        T const inv = T(1) / sum;  // one division per row; x * (1 / sum) is within an ulp of x / sum
         for (int64_t i = gl; i < a.len; i += GROUP) {
-            T const v = masked(i) ? T{} : exp_t(value(i) - m) / sum;
+            T const v = masked(i) ? T{} : exp_t(value(i) - m) * inv;
             out[oo + i * a.s_out] = v;
         }
     }
@@ -300,21 +393,43 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
         vec = in.str[i] % NV == 0 && out.str[i] % NV == 0 && (!mask_v || mask.str[i] % NV == 0);
     }
     // Up to 2048 elements a row stays in registers, 8 per lane: 1, 2, 4 or 8
-    // warps per row. Longer rows stream through L1/L2.
+    // warps per row; up to 8192 in the registers of a whole CTA, 16 or 32 per
+    // lane; up to kSmemRowBytes in one CTA's shared memory. Longer rows stream
+    // through L1/L2.
+    int64_t const row_bytes = a.len * static_cast<int64_t>(sizeof(T));
+    bool const smem_row = a.len > 8192 && row_bytes <= kSmemRowBytes;
+    if (smem_row && row_bytes > (48 << 10)) {
+        cudaError_t e = cudaSuccess;
+        if (vec)
+            e = cudaFuncSetAttribute(mask_v ? softmax_smem<T, NV, true> : softmax_smem<T, NV, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemRowBytes));
+        else
+            e = cudaFuncSetAttribute(mask_v ? softmax_smem<T, 1, true> : softmax_smem<T, 1, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemRowBytes));
+        if (e != cudaSuccess) return fail(ANN_ECUDA, "softmax: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
     auto launch = [&](auto mask_tag) {
         constexpr bool M = decltype(mask_tag)::value;
         constexpr int CV = 8 / NV;  // 16-byte pieces per lane
-        if (vec) {
+        if (smem_row) {
+            size_t const bytes = static_cast<size_t>(row_bytes);
+            if (vec) softmax_smem<T, NV, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);
+            else softmax_smem<T, 1, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);
+        } else if (vec) {
             if (a.len <= 256) softmax_regs<T, CV, NV, 1, M><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
             else if (a.len <= 512) softmax_regs<T, CV, NV, 2, M><<<grid_for(a.rows, 4), 256, 0, s>>>(a);
             else if (a.len <= 1024) softmax_regs<T, CV, NV, 4, M><<<grid_for(a.rows, 2), 256, 0, s>>>(a);
             else if (a.len <= 2048) softmax_regs<T, CV, NV, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else if (a.len <= 4096) softmax_regs<T, 2 * CV, NV, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else if (a.len <= 8192) softmax_regs<T, 4 * CV, NV, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
             else softmax_kernel<T, 256, M><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
         } else {
             if (a.len <= 256) softmax_regs<T, 8, 1, 1, M><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
             else if (a.len <= 512) softmax_regs<T, 8, 1, 2, M><<<grid_for(a.rows, 4), 256, 0, s>>>(a);
             else if (a.len <= 1024) softmax_regs<T, 8, 1, 4, M><<<grid_for(a.rows, 2), 256, 0, s>>>(a);
             else if (a.len <= 2048) softmax_regs<T, 8, 1, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else if (a.len <= 4096) softmax_regs<T, 16, 1, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
+            else if (a.len <= 8192) softmax_regs<T, 32, 1, 8, M><<<grid_for(a.rows, 1), 256, 0, s>>>(a);
             else softmax_kernel<T, 256, M><<<grid_for(a.rows, 1, 8), 256, 0, s>>>(a);
         }
     };

@@ -510,6 +510,14 @@ def ops_only(args):
          lambda: nn.maskedSoftmax(None, None, sm_in, sm_mask, sm_out, 3)),
         (f"softmax [{S},1,1024,1024]", 2 * 4 * (S << 20), lambda: nn.softmax(None, None, sm_in, sm_out, 3)),
     ]
+    if S >= 16:  # rows of 4096 (one CTA's registers) and 16384 (one CTA's shared memory)
+        S4, S16 = S // 4, S // 16
+        r4_in, r4_out = a[:S4 << 22].view(S4, 1, 1024, 4096), o[:S4 << 22].view(S4, 1, 1024, 4096)
+        r16_in, r16_out = a[:S16 << 24].view(S16, 1, 1024, 16384), o[:S16 << 24].view(S16, 1, 1024, 16384)
+        cases.append((f"causalSoftmax [{S4},1,1024,4096]", 2 * 4 * (S4 << 22),
+                      lambda: nn.causalSoftmax(None, None, r4_in, r4_out, 3, 2, 3)))
+        cases.append((f"softmax [{S16},1,1024,16384]", 2 * 4 * (S16 << 24),
+                      lambda: nn.softmax(None, None, r16_in, r16_out, 3)))
     for name, nbytes, fn in cases:
         t = timed(fn)
         print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 4), "GBps": round(nbytes / t / 1e9, 1),

@@ -364,6 +364,50 @@ def test_masked_softmax_parity(ann, dtype, np_t, shape, axis):
     np.testing.assert_allclose(host(out), want, **SOFTMAX_TOL[np_t])
 
 
+@pytest.mark.parametrize("dtype,np_t", DT)
+@pytest.mark.parametrize("shape,axis,causal", [((1, 2, 9, 4096), 3, False), ((1, 2, 9, 4096), 3, True),
+                                               ((1, 2, 3, 2051), 3, False), ((1, 2, 3, 2051), 3, True),
+                                               ((1, 1, 2, 8192), 3, True), ((1, 1, 3000, 4), 2, False),
+                                               ((1, 1, 3000, 4), 2, True), ((1, 2, 3, 9000), 3, True),
+                                               ((1, 1, 3, 20000), 3, False), ((1, 1, 9001, 2), 2, True),
+                                               ((1, 1, 2, 30001), 3, True)])
+def test_long_softmax_rows(ann, dtype, np_t, shape, axis, causal):
+    """Rows longer than 2048: in a CTA's registers up to 8192 elements, in
+    shared memory up to 96 KB a row (36 KB, 72 KB and 80 KB rows here, past
+    the 48 KB default), streamed beyond that; vectorised when the row is
+    unit-stride and a multiple of 16 bytes, element-wise otherwise (2051,
+    9001, 30001 and the axis-2 rows). Causal masks with the query axis before
+    the key axis (queries 2, keys 3) and, for the axis-2 rows, the softmax
+    axis as the query axis.
+
+    The reference sums a row's exponentials one after another, so its own
+    rounding error grows like sqrt(len) eps and scales the whole row by one
+    factor; the relative tolerance grows with the row the same way (4 eps
+    sqrt(len), at least the short-row tolerance), and in fp32 the GPU result
+    must be no further from the softmax evaluated in fp64 than the oracle's."""
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal(shape) * 6).astype(np_t)
+    out = torch.empty_like(dev(x))
+
+    def run_oracle(v):
+        if causal:
+            return oracle.causal_softmax(v, np.empty_like(v), axis, 2, 3)
+        return oracle.softmax(v, np.empty_like(v), axis)
+
+    want = run_oracle(x)
+    if causal:
+        ann.onHost.nn.causalSoftmax(None, None, dev(x), out, axis, 2, 3)
+    else:
+        ann.onHost.nn.softmax(None, None, dev(x), out, axis)
+    got = host(out)
+    tol = dict(SOFTMAX_TOL[np_t])
+    tol["rtol"] = max(tol["rtol"], 4 * float(np.finfo(np_t).eps) * math.sqrt(shape[axis]))
+    np.testing.assert_allclose(got, want, **tol)
+    if np_t == np.float32:
+        exact = run_oracle(x.astype(np.float64))
+        assert np.abs(got - exact).max() <= np.abs(want - exact).max() * 1.5 + 1e-12
+
+
 def test_masked_softmax_all_masked_row_matches_reference(ann):
     """A row that is all -inf: max stays lowest(), every exp is 0, 0/0 = NaN
     (onAcc/internal/nn/softmax.hpp:90-113)."""
