@@ -34,6 +34,7 @@ int take_prefill_tc2_error(cudaStream_t s, uint32_t* bits);
 int take_selftest_error(cudaStream_t s, uint32_t* bits);
 int take_rms_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_f64_error(cudaStream_t s, uint32_t* bits);
+int take_softmax_error(cudaStream_t s, uint32_t* bits);
 
 // ---------------------------------------------------------------------------
 // Views: ann_view with byte pitches -> element strides, validated.

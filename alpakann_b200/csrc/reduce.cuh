@@ -58,6 +58,10 @@ struct Lowest<double> {
     static constexpr double value = -DBL_MAX;
 };
 
+// -infinity of T (exp of it is exactly 0).
+__device__ __forceinline__ float neg_inf(float) { return __int_as_float(0xff800000); }
+__device__ __forceinline__ double neg_inf(double) { return __longlong_as_double(static_cast<long long>(0xfff0000000000000ull)); }
+
 // 1/sqrt: rsqrtf for fp32 (within 2 ulp), correctly rounded sqrt and divide
 // for fp64 so the 1e-11 budget is not spent here.
 __device__ __forceinline__ float rsqrt_t(float x) { return rsqrtf(x); }

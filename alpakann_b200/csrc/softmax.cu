@@ -19,9 +19,15 @@
 
 #include "common.cuh"
 #include "reduce.cuh"
+#include "tma.cuh"
 
 namespace ann {
+
+int take_softmax_error(cudaStream_t s, uint32_t* bits);
+
 namespace {
+
+__device__ unsigned int g_softmax_error;  // ANN_DEVERR_WAIT_TIMEOUT from softmax_ring
 
 struct SoftmaxArgs {
     const void* in;
@@ -141,10 +147,17 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
                 else v[c * VEC + k] = xe[k];
             }
         }
+        // Elements outside [lo, hi), and slots past the row's end, become
+        // -inf once, here: max ignores them and exp gives them exactly 0, so
+        // the later passes need no tests. Rows with every slot kept skip it.
+        bool const full = lo == 0 && span >= static_cast<unsigned>(32 * WPR * N);  // same in the whole row
+        if (!full)
+#pragma unroll
+            for (int j = 0; j < N; ++j)
+                if (!kept(elem0(j / VEC) + j % VEC)) v[j] = neg_inf(T{});
         T m = Lowest<T>::value;
 #pragma unroll
-        for (int j = 0; j < N; ++j)
-            if (kept(elem0(j / VEC) + j % VEC)) m = fmax(m, v[j]);
+        for (int j = 0; j < N; ++j) m = fmax(m, v[j]);
         int const buf = static_cast<int>(it & 1);
         auto row_barrier = [&]() {
             asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / WPR), "r"(32 * WPR) : "memory");
@@ -157,11 +170,23 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
 #pragma unroll
             for (int w = 1; w < WPR; ++w) m = fmax(m, red_max[buf][first + w]);
         }
+        // exp; in a row that is not fully kept, pieces wholly past the kept
+        // range are 0 without evaluating exp (three quarters of a causal row
+        // of 4096 against 1024 queries)
+        int const hi = lo + static_cast<int>(span);
         T sum{};
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-            v[j] = kept(elem0(j / VEC) + j % VEC) ? exp_t(v[j] - m) : T(0);
-            sum += v[j];
+            for (int j = 0; j < N; ++j) {
+                v[j] = exp_t(v[j] - m);
+                sum += v[j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                v[j] = elem0(j / VEC) < hi ? exp_t(v[j] - m) : T(0);
+                sum += v[j];
+            }
         }
         sum = warp_sum(sum);
         if constexpr (WPR > 1) {
@@ -172,18 +197,230 @@ __global__ void __launch_bounds__(256) softmax_regs(SoftmaxArgs a) {
             for (int w = 1; w < WPR; ++w) sum += red_sum[buf][first + w];
         }
         if (!live) continue;
-        T const inv = T(1) / sum;  // one division per row; x * (1 / sum) is within an ulp of x / sum
+        // One division per row; x * (1 / sum) is within an ulp of x / sum.
+        // sum >= 1 whenever a kept element is finite (the maximum contributes
+        // exp(0)); otherwise (nothing kept, or only -inf / NaN kept) the
+        // unkept slots are written as 0 explicitly, as the reference does.
+        T const inv = T(1) / sum;
+        auto store = [&](auto exact_tag) {
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                int const e0 = elem0(c);
+                if (e0 >= len) continue;
+                P r;
+                T* re = reinterpret_cast<T*>(&r);
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) {
+                    if constexpr (decltype(exact_tag)::value) re[k] = kept(e0 + k) ? v[c * VEC + k] * inv : T{};
+                    else re[k] = v[c * VEC + k] * inv;
+                }
+                if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = r;
+                else out[oo + e0 * a.s_out] = r;
+            }
+        };
+        if (sum >= T(1)) store(std::false_type{});
+        else store(std::true_type{});
+    }
+}
+
+// Aligned rows of up to 8192 elements: softmax_regs' row groups and register
+// layout, fed by a ring of bulk copies (TMA) instead of loads issued by the
+// row's own threads. Warp 0 copies the input (and mask) rows of iteration
+// it + STAGES - 1 into shared memory while the CTA computes iteration it, so a
+// CTA keeps STAGES - 1 iterations of rows in flight whatever its threads are
+// doing; the loads into registers then come from shared memory. Every wait is
+// bounded: a copy that has not landed after 1 s sets ANN_DEVERR_WAIT_TIMEOUT,
+// the CTA drains its copies in flight (bounded too) and returns.
+template <typename T, int CH, int WPR, bool MASK>
+struct RingCfg {
+    static constexpr int NV = Vec16<T>::n;
+    static constexpr int CAP = 32 * WPR * CH * NV;  // elements of one row slot
+    static constexpr int RPB = 8 / WPR;              // rows a CTA takes per iteration
+    static constexpr int OPS = MASK ? 2 : 1;         // input (+ mask) rows
+    static constexpr int STAGE = RPB * CAP * OPS * static_cast<int>(sizeof(T));  // bytes
+    static constexpr int STAGES = STAGE <= (8 << 10) ? 4 : STAGE <= (16 << 10) ? 3 : 2;
+    static constexpr int SMEM = STAGE * STAGES;
+};
+
+template <typename T, int CH, int WPR, bool MASK>
+__global__ void __launch_bounds__(256) softmax_ring(SoftmaxArgs a) {
+    using C = RingCfg<T, CH, WPR, MASK>;
+    using P = typename Vec16<T>::type;
+    constexpr int NV = C::NV, N = CH * NV, RPB = C::RPB;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t full[C::STAGES];
+    __shared__ T red_max[2][8], red_sum[2][8];
+    T const* in = static_cast<T const*>(a.in);
+    T const* mk = static_cast<T const*>(a.mask);
+    T* out = static_cast<T*>(a.out);
+    int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int const part = warp % WPR, first = warp - part, group = warp / WPR;
+    int64_t const per_iter = static_cast<int64_t>(gridDim.x) * RPB;
+    int64_t const iters = ceil_div(a.rows, per_iter);
+    int const len = static_cast<int>(a.len);  // <= CAP, a multiple of NV
+    uint32_t const row_bytes = static_cast<uint32_t>(len) * sizeof(T);
+    uint32_t const bar0 = smem_u32(full), ring0 = smem_u32(ring);
+
+    // Warp 0: the rows of iteration `it` into stage it % STAGES. One arrival
+    // with the iteration's byte count, then one copy per row and operand.
+    auto issue = [&](int64_t it) {
+        int const st = static_cast<int>(it % C::STAGES);
+        uint32_t const bar = bar0 + 8u * st;
+        uint32_t const dst = ring0 + static_cast<uint32_t>(st) * C::STAGE;
+        int64_t const r0 = it * per_iter + static_cast<int64_t>(blockIdx.x) * RPB;
+        int64_t const left = a.rows - r0;  // the last iteration may hold fewer rows, or none
+        int const live = static_cast<int>(left <= 0 ? 0 : left < RPB ? left : RPB);
+        if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(live) * row_bytes * C::OPS);
+        __syncwarp();
+        if (lane < live) {
+            int64_t oi, oo, om = 0;
+            row_offsets(a, r0 + lane, oi, oo, om);
+            bulk_copy_g2s(dst + static_cast<uint32_t>(lane * C::CAP * sizeof(T)), in + oi, row_bytes, bar);
+            if constexpr (MASK)
+                bulk_copy_g2s(dst + static_cast<uint32_t>((RPB + lane) * C::CAP * sizeof(T)), mk + om, row_bytes, bar);
+        }
+    };
+
+    if (tid == 0) {
+        for (int st = 0; st < C::STAGES; ++st) mbar_init(bar0 + 8u * st, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int64_t it = 0; it < iters && it < C::STAGES; ++it) issue(it);
+
+    auto row_barrier = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(32 * WPR) : "memory"); };
+    auto elem0 = [&](int c) { return (c * 32 * WPR + 32 * part + lane) * NV; };
+    for (int64_t it = 0; it < iters; ++it) {
+        int const st = static_cast<int>(it % C::STAGES);
+        bool const ok = mbar_wait_bounded(bar0 + 8u * st, static_cast<uint32_t>((it / C::STAGES) & 1));
+        // All threads agree on giving up; the barrier also retires every read
+        // of the stage that iteration it - 1 used, which is refilled next.
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicOr(&g_softmax_error, ANN_DEVERR_WAIT_TIMEOUT);
+                for (int64_t u = it; u < iters && u < it - 1 + C::STAGES; ++u)  // copies in flight (bounded)
+                    mbar_wait_bounded(bar0 + 8u * static_cast<uint32_t>(u % C::STAGES),
+                                      static_cast<uint32_t>((u / C::STAGES) & 1));
+            }
+            return;
+        }
+        if (it >= 1 && warp == 0 && it - 1 + C::STAGES < iters) issue(it - 1 + C::STAGES);
+
+        int64_t const row = it * per_iter + static_cast<int64_t>(blockIdx.x) * RPB + group;
+        bool const live = row < a.rows;
+        int64_t oi = 0, oo = 0, om = 0, lo64 = 0, hi64 = 0;
+        if (live) {
+            row_offsets(a, row, oi, oo, om);
+            kept_range(a, row, lo64, hi64);
+        }
+        int const lo = static_cast<int>(lo64);
+        unsigned const span = hi64 > lo64 ? static_cast<unsigned>(hi64 - lo64) : 0u;
+        auto kept = [&](int e) { return static_cast<unsigned>(e - lo) < span; };
+        T const* xs = reinterpret_cast<T const*>(ring + st * C::STAGE) + group * C::CAP;
+        T const* ys = xs + RPB * C::CAP;
+        T v[N];
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             int const e0 = elem0(c);
-            if (e0 >= len) continue;
-            P r;
-            T* re = reinterpret_cast<T*>(&r);
+            P x{}, y{};
+            if (live && e0 < len) {
+                x = *reinterpret_cast<P const*>(xs + e0);
+                if constexpr (MASK) y = *reinterpret_cast<P const*>(ys + e0);
+            }
+            T const* xe = reinterpret_cast<T const*>(&x);
+            T const* ye = reinterpret_cast<T const*>(&y);
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) re[k] = kept(e0 + k) ? v[c * VEC + k] * inv : T{};
-            if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = r;
-            else out[oo + e0 * a.s_out] = r;
+            for (int k = 0; k < NV; ++k) {
+                if constexpr (MASK) v[c * NV + k] = add_rn(xe[k], ye[k]);
+                else v[c * NV + k] = xe[k];
+            }
         }
+        bool const full = lo == 0 && span >= static_cast<unsigned>(C::CAP);  // as in softmax_regs
+        if (!full)
+#pragma unroll
+            for (int j = 0; j < N; ++j)
+                if (!kept(elem0(j / NV) + j % NV)) v[j] = neg_inf(T{});
+        T m = Lowest<T>::value;
+#pragma unroll
+        for (int j = 0; j < N; ++j) m = fmax(m, v[j]);
+        int const buf = static_cast<int>(it & 1);
+        m = warp_max(m);
+        if constexpr (WPR > 1) {
+            if (lane == 0) red_max[buf][warp] = m;
+            row_barrier();
+            m = red_max[buf][first];
+#pragma unroll
+            for (int w = 1; w < WPR; ++w) m = fmax(m, red_max[buf][first + w]);
+        }
+        int const hi = lo + static_cast<int>(span);  // as in softmax_regs
+        T sum{};
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                v[j] = exp_t(v[j] - m);
+                sum += v[j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                v[j] = elem0(j / NV) < hi ? exp_t(v[j] - m) : T(0);
+                sum += v[j];
+            }
+        }
+        sum = warp_sum(sum);
+        if constexpr (WPR > 1) {
+            if (lane == 0) red_sum[buf][warp] = sum;
+            row_barrier();
+            sum = red_sum[buf][first];
+#pragma unroll
+            for (int w = 1; w < WPR; ++w) sum += red_sum[buf][first + w];
+        }
+        if (!live) continue;
+        T const inv = T(1) / sum;  // as in softmax_regs
+        auto store = [&](auto exact_tag) {
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                int const e0 = elem0(c);
+                if (e0 >= len) continue;
+                P r;
+                T* re = reinterpret_cast<T*>(&r);
+#pragma unroll
+                for (int k = 0; k < NV; ++k) {
+                    if constexpr (decltype(exact_tag)::value) re[k] = kept(e0 + k) ? v[c * NV + k] * inv : T{};
+                    else re[k] = v[c * NV + k] * inv;
+                }
+                *reinterpret_cast<P*>(out + oo + e0) = r;
+            }
+        };
+        if (sum >= T(1)) store(std::false_type{});
+        else store(std::true_type{});
+    }
+}
+
+// Launches softmax_ring on a grid of resident CTAs (each streams its rows
+// through its ring), or returns false when its ring does not fit a CTA.
+template <typename T, int CH, int WPR, bool MASK>
+bool launch_ring(SoftmaxArgs const& a, cudaStream_t s) {
+    using C = RingCfg<T, CH, WPR, MASK>;
+    if constexpr (C::SMEM > (200 << 10)) {
+        return false;
+    } else {
+        auto kernel = softmax_ring<T, CH, WPR, MASK>;
+        if (C::SMEM > (48 << 10) &&
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+            return false;
+        static int per_sm = 0;  // same kernel, same B200 on every device of the process
+        if (per_sm == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, C::SMEM) != cudaSuccess ||
+                            per_sm < 1)) {
+            per_sm = 0;
+            cudaGetLastError();
+            return false;
+        }
+        int64_t const blocks = ceil_div(a.rows, static_cast<int64_t>(C::RPB));
+        int64_t const cap = static_cast<int64_t>(sm_count()) * per_sm;
+        kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, C::SMEM, s>>>(a);
+        return true;
     }
 }
 
@@ -238,7 +475,8 @@ __global__ void __launch_bounds__(256) softmax_smem(SoftmaxArgs a) {
 #pragma unroll
                 for (int k = 0; k < VEC; ++k) {
                     if constexpr (MASK) xe[k] = add_rn(xe[k], ye[k]);
-                    if (!masked(e0 + k)) m = fmax(m, xe[k]);
+                    if (masked(e0 + k)) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
+                    m = fmax(m, xe[k]);
                 }
                 *reinterpret_cast<P*>(buf + e0) = x[u];
             }
@@ -251,19 +489,22 @@ __global__ void __launch_bounds__(256) softmax_smem(SoftmaxArgs a) {
             T* xe = reinterpret_cast<T*>(&x);
 #pragma unroll
             for (int k = 0; k < VEC; ++k) {
-                xe[k] = masked(e0 + k) ? T(0) : exp_t(xe[k] - m);
+                xe[k] = exp_t(xe[k] - m);
                 sum += xe[k];
             }
             *reinterpret_cast<P*>(buf + e0) = x;
         }
         sum = block_sum<8>(sum, scratch);
-        T const inv = T(1) / sum;  // one division per row; x * (1 / sum) is within an ulp of x / sum
+        // one division per row; x * (1 / sum) is within an ulp of x / sum;
+        // unkept slots tested only when sum < 1 (see softmax_regs)
+        T const inv = T(1) / sum;
+        bool const exact = !(sum >= T(1));
         for (int64_t p = threadIdx.x; p < pieces; p += 256) {
             int64_t const e0 = p * VEC;
             P x = *reinterpret_cast<P const*>(buf + e0);
             T* xe = reinterpret_cast<T*>(&x);
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) xe[k] = masked(e0 + k) ? T(0) : xe[k] * inv;
+            for (int k = 0; k < VEC; ++k) xe[k] = exact && masked(e0 + k) ? T(0) : xe[k] * inv;
             if constexpr (VEC > 1) *reinterpret_cast<P*>(out + oo + e0) = x;
             else out[oo + e0 * a.s_out] = x;
         }
@@ -313,6 +554,19 @@ __global__ void __launch_bounds__(256) softmax_kernel(SoftmaxArgs a) {
             out[oo + i * a.s_out] = v;
         }
     }
+}
+
+// softmax_ring for an aligned row of at most 8192 elements: the tier of
+// softmax_regs that the row length picks (CV 16-byte pieces a lane at up to
+// 2048 elements).
+template <typename T, int CV, bool M>
+bool ring_launched(SoftmaxArgs const& a, cudaStream_t s) {
+    if (a.len <= 256) return launch_ring<T, CV, 1, M>(a, s);
+    if (a.len <= 512) return launch_ring<T, CV, 2, M>(a, s);
+    if (a.len <= 1024) return launch_ring<T, CV, 4, M>(a, s);
+    if (a.len <= 2048) return launch_ring<T, CV, 8, M>(a, s);
+    if (a.len <= 4096) return launch_ring<T, 2 * CV, 8, M>(a, s);
+    return launch_ring<T, 4 * CV, 8, M>(a, s);
 }
 
 template <typename T>
@@ -415,6 +669,8 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
             size_t const bytes = static_cast<size_t>(row_bytes);
             if (vec) softmax_smem<T, NV, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);
             else softmax_smem<T, 1, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);
+        } else if (vec && a.len <= 8192 && ring_launched<T, CV, M>(a, s)) {
+            // rows through a bulk-copy ring (softmax_ring)
         } else if (vec) {
             if (a.len <= 256) softmax_regs<T, CV, NV, 1, M><<<grid_for(a.rows, 8), 256, 0, s>>>(a);
             else if (a.len <= 512) softmax_regs<T, CV, NV, 2, M><<<grid_for(a.rows, 4), 256, 0, s>>>(a);
@@ -583,6 +839,17 @@ int scale(ann_stream stream, const ann_view* in_v, T scalar, const ann_view* out
 }
 
 }  // namespace
+
+int take_softmax_error(cudaStream_t s, uint32_t* bits) {
+    unsigned int value = 0, zero = 0;
+    if (cudaMemcpyFromSymbolAsync(&value, g_softmax_error, sizeof value, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyToSymbolAsync(g_softmax_error, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return fail(ANN_ECUDA, "device error word: %s", cudaGetErrorString(cudaGetLastError()));
+    *bits |= value;
+    return ANN_OK;
+}
+
 }  // namespace ann
 
 extern "C" {

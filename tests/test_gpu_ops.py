@@ -408,6 +408,50 @@ def test_long_softmax_rows(ann, dtype, np_t, shape, axis, causal):
         assert np.abs(got - exact).max() <= np.abs(want - exact).max() * 1.5 + 1e-12
 
 
+@pytest.mark.parametrize("dtype,np_t", DT)
+@pytest.mark.parametrize("shape,kind", [((30001, 64), "softmax"), ((30001, 64), "masked"),
+                                        ((1, 8, 1023, 1024), "causal"), ((3, 1, 700, 2048), "masked"),
+                                        ((2, 1, 999, 4096), "causal")])
+def test_softmax_many_rows(ann, dtype, np_t, shape, kind):
+    """Many more rows than one pass of resident CTAs takes, so each CTA's ring
+    of bulk copies wraps around several times, and a row count that leaves
+    the last pass partly (or, for some CTAs, wholly) empty."""
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal(shape) * 5).astype(np_t)
+    out = torch.empty_like(dev(x))
+    axis = len(shape) - 1
+    if kind == "causal":
+        want = oracle.causal_softmax(x, np.empty_like(x), axis, axis - 1, axis)
+        ann.onHost.nn.causalSoftmax(None, None, dev(x), out, axis, axis - 1, axis)
+    elif kind == "masked":
+        mask = np.where(rng.random(shape) < 0.2, -np.inf, rng.standard_normal(shape)).astype(np_t)
+        mask[..., 0] = 0
+        want = oracle.masked_softmax(x, mask, np.empty_like(x), axis)
+        ann.onHost.nn.maskedSoftmax(None, None, dev(x), dev(mask), out, axis)
+    else:
+        want = oracle.softmax(x, np.empty_like(x), axis)
+        ann.onHost.nn.softmax(None, None, dev(x), out, axis)
+    np.testing.assert_allclose(host(out), want, **SOFTMAX_TOL[np_t])
+    assert ann.take_device_error(torch.cuda.current_stream().cuda_stream) == 0  # no wait gave up
+
+
+@pytest.mark.parametrize("dtype,np_t", DT)
+@pytest.mark.parametrize("T", [64, 1024, 4096, 2051, 9000])
+def test_causal_softmax_minus_inf_rows_match_reference(ann, dtype, np_t, T):
+    """causalSoftmax on rows whose kept entries are all -inf (sum of exps 0):
+    the reference gives 0/0 = NaN on kept entries and writes 0 on masked
+    ones; a second row group mixes finite and -inf kept entries."""
+    x = np.full((1, 2, 5, T), -np.inf, np_t)
+    x[0, 1, :, ::3] = np.arange(len(range(0, T, 3)), dtype=np_t)[None, :] / np_t(7)
+    want = oracle.causal_softmax(x, np.empty_like(x), 3, 2, 3)
+    out = torch.empty_like(dev(x))
+    ann.onHost.nn.causalSoftmax(None, None, dev(x), out, 3, 2, 3)
+    got = host(out)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    fin = ~np.isnan(want)
+    np.testing.assert_allclose(got[fin], want[fin], **SOFTMAX_TOL[np_t])
+
+
 def test_masked_softmax_all_masked_row_matches_reference(ann):
     """A row that is all -inf: max stays lowest(), every exp is 0, 0/0 = NaN
     (onAcc/internal/nn/softmax.hpp:90-113)."""
