@@ -518,6 +518,30 @@ def ops_only(args):
                       lambda: nn.causalSoftmax(None, None, r4_in, r4_out, 3, 2, 3)))
         cases.append((f"softmax [{S16},1,1024,16384]", 2 * 4 * (S16 << 24),
                       lambda: nn.softmax(None, None, r16_in, r16_out, 3)))
+    # the attention path's own HBM-bound calls: embeddingLookup, rmsNorm, the
+    # two fused into one launch, ropeInPlace on Q and K, ops::scale
+    H = 4096
+    ntok = R // 2  # gathered rows: half of a [R, 4096] table
+    table = a.view(R, H)
+    ids = torch.randint(0, R, (ntok,), device=dev, dtype=torch.int32)
+    emb_out = o[:ntok * H].view(ntok, H)
+    norm_w = torch.rand(H, device=dev) + 0.5
+    heads, hd = 32, 128
+    T = G // 2 // (heads * hd)  # Q and K: half of an operand each
+    rq, rk = a[:G // 2].view(1, T, heads, hd), b[:G // 2].view(1, T, heads, hd)
+    ang = torch.arange(T, device=dev, dtype=torch.float64)[:, None] * torch.pow(
+        10000.0, -2.0 * torch.arange(hd // 2, device=dev, dtype=torch.float64) / hd)[None, :]
+    cos_t, sin_t = torch.cos(ang).float(), torch.sin(ang).float()
+    cases += [
+        (f"embeddingLookup [{ntok}] of [{R},{H}]", 2 * 4 * ntok * H + 4 * ntok,
+         lambda: nn.embeddingLookup(None, None, ids, table, emb_out)),
+        (f"rmsNorm [{R},{H}]", 2 * 4 * G, lambda: nn.rmsNorm(None, None, rows, norm_w, o.view(R, H), 1e-5)),
+        (f"embeddingLookup+rmsNorm [{ntok}] of [{R},{H}]", 2 * 4 * ntok * H + 4 * ntok,
+         lambda: nn.embeddingRmsNorm(None, None, ids, table, norm_w, emb_out, 1e-5)),
+        (f"ropeInPlace Q,K [1,{T},{heads},{hd}]", 2 * 2 * 4 * (G // 2) + 2 * 4 * T * (hd // 2),
+         lambda: nn.ropeInPlace(None, None, rq, rk, cos_t, sin_t)),
+        ("scale", 2 * 4 * G, lambda: ops.scale(None, None, a, 0.5, o)),
+    ]
     for name, nbytes, fn in cases:
         t = timed(fn)
         print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 4), "GBps": round(nbytes / t / 1e9, 1),
