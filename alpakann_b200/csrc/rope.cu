@@ -100,6 +100,108 @@ __device__ __forceinline__ void rope_item(RopeArgs const& a, RopeJob const& j, i
     }
 }
 
+// Division of n < 2^31 by an invariant d >= 1 as a multiply and a shift
+// (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", 1994): with l = ceil(log2 d) and m = ceil(2^(31+l) / d),
+// which fits in 32 bits, n / d = (n * m) >> (31 + l) for every n < 2^31.
+struct FastDiv {
+    uint32_t d, m, shift;
+    static FastDiv make(uint32_t d) {
+        uint32_t l = 0;
+        while ((uint64_t{1} << l) < d) ++l;
+        uint64_t const num = uint64_t{1} << (31 + l);
+        return FastDiv{d, static_cast<uint32_t>((num + d - 1) / d), 31 + l};
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return static_cast<uint32_t>((static_cast<uint64_t>(n) * m) >> shift);
+    }
+};
+
+// The aligned path when every index fits in 31 bits (the normal case): the
+// flat item index splits into (a0, a1, a2, pair-vector) with three FastDiv
+// steps instead of three 64-bit divisions (which made the kernel
+// instruction-bound), and the PV cos/sin entries of an item are one vector
+// load each when the tables allow it.
+struct RopeFast {
+    FastDiv npv[2], e2[2], e1[2];
+    int tab_vec;  // cos/sin entries of one item contiguous and 8-byte aligned (fp32 only)
+};
+
+template <typename T, int PV>
+__device__ __forceinline__ void rope_item_fast(RopeArgs const& a, RopeJob const& j, int jk, RopeFast const& f,
+                                               uint32_t flat) {
+    uint32_t const r = f.npv[jk].div(flat);
+    uint32_t const pv = flat - r * f.npv[jk].d;
+    uint32_t const r2 = f.e2[jk].div(r);
+    uint32_t const a2 = r - r2 * f.e2[jk].d;
+    uint32_t const a0 = f.e1[jk].div(r2);
+    uint32_t const a1 = r2 - a0 * f.e1[jk].d;
+    int64_t const tok = a.layout == ANN_LAYOUT_BTHD ? a1 : a2;
+    int64_t const pos = a.pos_off + tok;
+    using V = typename Vec16<T>::type;
+    T const* in = static_cast<T const*>(j.in) + a0 * j.si[0] + a1 * j.si[1] + a2 * j.si[2];
+    T* out = static_cast<T*>(j.out) + a0 * j.so[0] + a1 * j.so[1] + a2 * j.so[2];
+    V const v = *reinterpret_cast<V const*>(in + 2 * PV * static_cast<int64_t>(pv));
+    T x[2 * PV];
+    if constexpr (PV == 2) {
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    } else {
+        x[0] = v.x; x[1] = v.y;
+    }
+    T y[2 * PV];
+    if (!j.rotate) {  // a copied job (V of kvCacheAppend) may come with no tables at all
+#pragma unroll
+        for (int e = 0; e < 2 * PV; ++e) y[e] = x[e];
+    } else {
+        T c[PV], sn[PV];
+        T const* cosT = static_cast<T const*>(a.cos);
+        T const* sinT = static_cast<T const*>(a.sin);
+        int64_t const p0 = static_cast<int64_t>(pv) * PV;
+        bool done = false;
+        if constexpr (PV == 2 && sizeof(T) == 4) {
+            if (f.tab_vec) {
+                float2 const cc = *reinterpret_cast<float2 const*>(cosT + pos * a.cs0 + p0);
+                float2 const ss = *reinterpret_cast<float2 const*>(sinT + pos * a.ss0 + p0);
+                c[0] = cc.x; c[1] = cc.y; sn[0] = ss.x; sn[1] = ss.y;
+                done = true;
+            }
+        }
+        if (!done) {
+#pragma unroll
+            for (int k = 0; k < PV; ++k) {
+                c[k] = cosT[pos * a.cs0 + (p0 + k) * a.cs1];
+                sn[k] = sinT[pos * a.ss0 + (p0 + k) * a.ss1];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < PV; ++k) {
+            T const even = x[2 * k], odd = x[2 * k + 1];
+            y[2 * k] = sub_rn(mul_rn(even, c[k]), mul_rn(odd, sn[k]));
+            y[2 * k + 1] = add_rn(mul_rn(even, sn[k]), mul_rn(odd, c[k]));
+        }
+    }
+    V w;
+    if constexpr (PV == 2) {
+        w.x = y[0]; w.y = y[1]; w.z = y[2]; w.w = y[3];
+    } else {
+        w.x = y[0]; w.y = y[1];
+    }
+    *reinterpret_cast<V*>(out + 2 * PV * static_cast<int64_t>(pv)) = w;
+}
+
+template <typename T, int PV>
+__global__ void __launch_bounds__(256) rope_kernel_fast(RopeArgs a, RopeFast f) {
+    uint32_t const n0 = static_cast<uint32_t>(a.job[0].items);
+    uint32_t const total = n0 + (a.njobs > 1 ? static_cast<uint32_t>(a.job[1].items) : 0u);  // < 2^31
+    uint32_t const step = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        if (i < n0)
+            rope_item_fast<T, PV>(a, a.job[0], 0, f, i);
+        else
+            rope_item_fast<T, PV>(a, a.job[1], 1, f, i - n0);
+    }
+}
+
 template <typename T, int PV, bool VEC>
 __global__ void __launch_bounds__(256) rope_kernel(RopeArgs a) {
     int64_t const total = a.job[0].items + (a.njobs > 1 ? a.job[1].items : 0);
@@ -182,7 +284,20 @@ int launch(ann_stream stream, const Dims* ins, const Dims* outs, int njobs, cons
     a.pos_off = off;
     int64_t const total = a.job[0].items + (a.njobs > 1 ? a.job[1].items : 0);
     int const grid = grid_for(total, 256);
-    if (vec)
+    bool fast = vec && total < (int64_t{1} << 31);
+    for (int k = 0; fast && k < a.njobs; ++k)
+        fast = a.job[k].npv >= 1 && a.job[k].e2 >= 1 && a.job[k].e1 >= 1;
+    if (fast) {
+        RopeFast f{};
+        for (int k = 0; k < a.njobs; ++k) {
+            f.npv[k] = FastDiv::make(static_cast<uint32_t>(a.job[k].npv));
+            f.e2[k] = FastDiv::make(static_cast<uint32_t>(a.job[k].e2));
+            f.e1[k] = FastDiv::make(static_cast<uint32_t>(a.job[k].e1));
+        }
+        f.tab_vec = sizeof(T) == 4 && a.cs1 == 1 && a.ss1 == 1 && a.cs0 % 2 == 0 && a.ss0 % 2 == 0 &&
+                    aligned(a.cos, 8) && aligned(a.sin, 8);
+        rope_kernel_fast<T, PVV><<<grid, 256, 0, as_stream(stream)>>>(a, f);
+    } else if (vec)
         rope_kernel<T, PVV, true><<<grid, 256, 0, as_stream(stream)>>>(a);
     else
         rope_kernel<T, 1, false><<<grid, 256, 0, as_stream(stream)>>>(a);
