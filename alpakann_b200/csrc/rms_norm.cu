@@ -34,6 +34,81 @@ struct RmsArgs {
     int64_t s_ids, s_row, vocab;
 };
 
+// Aligned rows of at most GROUP * CH 16-byte vectors: the row is held in
+// registers, CH vectors a thread (v = gl + GROUP c), all loads issued before
+// the first is used, and the second pass reads the registers instead of the
+// row again. The squares are summed in the same order as rms_norm_kernel's
+// loop (the extra terms are +0), so both give the same bits.
+template <typename T, int GROUP, int CH, bool GATHER>
+__global__ void __launch_bounds__(256) rms_norm_regs(RmsArgs a, T eps) {
+    using V = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n;
+    constexpr int RPB = 256 / GROUP;
+    __shared__ T scratch[8];
+    int const gl = threadIdx.x % GROUP;
+    T const* in = static_cast<T const*>(a.in);
+    V const* wv = static_cast<V const*>(a.w);
+    T* out = static_cast<T*>(a.out);
+    int const nvec = static_cast<int>(a.hidden / NV);  // <= GROUP * CH
+    int64_t const iters = ceil_div(a.rows, static_cast<int64_t>(gridDim.x) * RPB);
+    for (int64_t it = 0; it < iters; ++it) {
+        int64_t const row = (it * gridDim.x + blockIdx.x) * RPB + threadIdx.x / GROUP;
+        bool const live = row < a.rows;
+        bool valid = live;
+        int64_t oi = 0, oo = 0;
+        if (live) {
+            a.outer.offsets(row, oi, oo);
+            if constexpr (GATHER) {
+                uint32_t const id = a.ids[row * a.s_ids];
+                valid = id < a.vocab;
+                if (!valid && gl == 0) atomicOr(&g_rms_error, ANN_DEVERR_TOKEN_ID);
+                oi = static_cast<int64_t>(id) * a.s_row;
+            }
+        }
+        V const* x = reinterpret_cast<V const*>(in + oi);
+        V xr[CH];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            int const v = gl + GROUP * c;
+            xr[c] = (valid && v < nvec) ? x[v] : V{};
+        }
+        T sum{};
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            V const xv = xr[c];
+            if constexpr (NV == 4) {
+                sum += xv.x * xv.x; sum += xv.y * xv.y; sum += xv.z * xv.z; sum += xv.w * xv.w;
+            } else {
+                sum += xv.x * xv.x; sum += xv.y * xv.y;
+            }
+        }
+        if constexpr (GROUP == 32) {
+            sum = warp_sum(sum);
+        } else {
+            sum = block_sum<8>(sum, scratch);
+        }
+        if (!live) continue;
+        T const rms = rsqrt_t(sum / static_cast<T>(a.hidden) + eps);
+        V* y = reinterpret_cast<V*>(out + oo);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            int const v = gl + GROUP * c;
+            if (v >= nvec) continue;
+            V r{};
+            if (valid) {  // an id out of range gives a zero row, as embeddingLookup writes
+                V const xv = xr[c];
+                V const ww = __ldg(wv + v);
+                if constexpr (NV == 4) {
+                    r.x = xv.x * rms * ww.x; r.y = xv.y * rms * ww.y; r.z = xv.z * rms * ww.z; r.w = xv.w * rms * ww.w;
+                } else {
+                    r.x = xv.x * rms * ww.x; r.y = xv.y * rms * ww.y;
+                }
+            }
+            y[v] = r;
+        }
+    }
+}
+
 template <typename T, int GROUP, bool VEC, bool GATHER>
 __global__ void __launch_bounds__(256) rms_norm_kernel(RmsArgs a, T eps) {
     using V = typename Vec16<T>::type;
@@ -154,13 +229,16 @@ int rms_norm(ann_stream stream, const ann_view* in_v, const ann_view* w_v, const
 template <typename T, bool GATHER>
 int launch_rms(ann_stream stream, RmsArgs const& a, bool vec, T eps, const char* what) {
     cudaStream_t s = as_stream(stream);
+    constexpr int NV = Vec16<T>::n;
     if (a.hidden <= 1024) {
         int const grid = grid_for(a.rows, 8);
-        if (vec) rms_norm_kernel<T, 32, true, GATHER><<<grid, 256, 0, s>>>(a, eps);
+        if (vec && a.hidden <= 32 * 8 * NV) rms_norm_regs<T, 32, 8, GATHER><<<grid, 256, 0, s>>>(a, eps);
+        else if (vec) rms_norm_kernel<T, 32, true, GATHER><<<grid, 256, 0, s>>>(a, eps);
         else rms_norm_kernel<T, 32, false, GATHER><<<grid, 256, 0, s>>>(a, eps);
     } else {
         int const grid = grid_for(a.rows, 1, 8);
-        if (vec) rms_norm_kernel<T, 256, true, GATHER><<<grid, 256, 0, s>>>(a, eps);
+        if (vec && a.hidden <= 256 * 8 * NV) rms_norm_regs<T, 256, 8, GATHER><<<grid, 256, 0, s>>>(a, eps);
+        else if (vec) rms_norm_kernel<T, 256, true, GATHER><<<grid, 256, 0, s>>>(a, eps);
         else rms_norm_kernel<T, 256, false, GATHER><<<grid, 256, 0, s>>>(a, eps);
     }
     return check_launch(what);
