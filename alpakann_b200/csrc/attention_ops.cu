@@ -87,10 +87,144 @@ __global__ void __launch_bounds__(256) bgemm_kernel(BgemmArgs a) {
     }
 }
 
+// fp32 at sizes that fill the GPU: 128-column x (16 TM)-row output tiles, 8-deep
+// k slices, each thread TM x 8 outputs in four quadrants (rows ty*TM/2 + i and
+// BM/2 + ty*TM/2 + i, columns tx*4 + j and 64 + tx*4 + j) read from shared
+// memory as 16-byte vectors. Two shared-memory buffers: the global loads of
+// slice s + 1 go out before slice s is computed and land in the other buffer
+// after it, one barrier per slice. Every output still accumulates k in
+// ascending order with FMA, as bgemm_kernel does.
+constexpr int BK8 = 8, BN128 = 128, PAD = 4;
+
+template <int TM>
+__global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
+    constexpr int BMW = 16 * TM;
+    constexpr int LA = BMW * BK8 / 256, LB = BN128 * BK8 / 256;  // loads a thread makes per slice
+    __shared__ __align__(16) float As[2][BK8][BMW + PAD];
+    __shared__ __align__(16) float Bs[2][BK8][BN128 + PAD];
+    int const tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+    int64_t const z = blockIdx.z;
+    int64_t const b = z / a.heads, hq = z % a.heads;
+    int64_t const kvh = hq / a.g;
+    float const* A = static_cast<float const*>(a.A) + b * a.a_b + hq * a.a_h;
+    float const* B = static_cast<float const*>(a.B) + b * a.b_b + kvh * a.b_h;
+    float* C = static_cast<float*>(a.C) + b * a.c_b + hq * a.c_h;
+    int64_t const m0 = static_cast<int64_t>(blockIdx.y) * BMW, n0 = static_cast<int64_t>(blockIdx.x) * BN128;
+    float ra[LA], rb[LB];
+    auto load = [&](int64_t k0) {
+#pragma unroll
+        for (int e = 0; e < LA; ++e) {
+            int const lin = tid + e * 256;
+            int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
+            int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
+            int64_t const gm = m0 + m, gk = k0 + k;
+            ra[e] = (gm < a.M && gk < a.K) ? A[gm * a.am + gk * a.ak] : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < LB; ++e) {
+            int const lin = tid + e * 256;
+            int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
+            int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
+            int64_t const gn = n0 + n, gk = k0 + k;
+            rb[e] = (gn < a.N && gk < a.K) ? B[gk * a.bk + gn * a.bn] : 0.f;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int e = 0; e < LA; ++e) {
+            int const lin = tid + e * 256;
+            int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
+            int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
+            As[buf][k][m] = ra[e];
+        }
+#pragma unroll
+        for (int e = 0; e < LB; ++e) {
+            int const lin = tid + e * 256;
+            int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
+            int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
+            Bs[buf][k][n] = rb[e];
+        }
+    };
+    float acc[TM][8];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    int64_t const slices = ceil_div(a.K, static_cast<int64_t>(BK8));
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int64_t sl = 0; sl < slices; ++sl) {
+        int const buf = static_cast<int>(sl & 1);
+        if (sl + 1 < slices) load((sl + 1) * BK8);
+#pragma unroll
+        for (int k = 0; k < BK8; ++k) {
+            float av[TM], bv[8];
+            if constexpr (TM == 8) {  // 4 rows from each half: 16-byte aligned (ty * 4 floats)
+                float4 const a0 = *reinterpret_cast<float4 const*>(&As[buf][k][ty * 4]);
+                float4 const a1 = *reinterpret_cast<float4 const*>(&As[buf][k][BMW / 2 + ty * 4]);
+                av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+                av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+            } else {  // TM == 4: 2 rows from each half, 8-byte aligned (ty * 2 floats)
+                float2 const a0 = *reinterpret_cast<float2 const*>(&As[buf][k][ty * 2]);
+                float2 const a1 = *reinterpret_cast<float2 const*>(&As[buf][k][BMW / 2 + ty * 2]);
+                av[0] = a0.x; av[1] = a0.y; av[2] = a1.x; av[3] = a1.y;
+            }
+            float4 const b0 = *reinterpret_cast<float4 const*>(&Bs[buf][k][tx * 4]);
+            float4 const b1 = *reinterpret_cast<float4 const*>(&Bs[buf][k][64 + tx * 4]);
+            bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+            bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (sl + 1 < slices) store(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        int const half = i / (TM / 2), r = i % (TM / 2);
+        int64_t const gm = m0 + half * (BMW / 2) + ty * (TM / 2) + r;
+        if (gm >= a.M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int64_t const gn = n0 + h * 64 + tx * 4;
+            float* c = C + gm * a.cm;
+            if (vec_c && gn + 3 < a.N) {
+                *reinterpret_cast<float4*>(c + gn) =
+                    make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (gn + j < a.N) c[(gn + j) * a.cn] = acc[i][4 * h + j];
+            }
+        }
+    }
+}
+
 template <typename T>
 int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* what) {
     a.a_k_unit = a.ak == 1 ? 1 : 0;
     a.b_k_unit = a.bk == 1 ? 1 : 0;
+    if constexpr (sizeof(T) == 4) {
+        // wide tiles once the problem fills the GPU; 64-row tiles when 128-row
+        // ones would leave it under two waves (attentionApply: N = D)
+        int64_t const gx = ceil_div(a.N, static_cast<int64_t>(BN128));
+        int64_t const tiles128 = gx * ceil_div(a.M, int64_t{128}) * batches;
+        int64_t const slots = static_cast<int64_t>(sm_count()) * 2;
+        if (a.M >= 64 && a.N >= 64 && tiles128 >= slots / 2 && batches <= 65535) {
+            int const vec_c = a.cn == 1 && a.cm % 4 == 0 && a.c_b % 4 == 0 && a.c_h % 4 == 0 && aligned(a.C, 16);
+            bool const tall = tiles128 >= 2 * slots;
+            int64_t const gy = ceil_div(a.M, tall ? int64_t{128} : int64_t{64});
+            if (gy <= 65535) {
+                dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batches));
+                if (tall) bgemm_wide<8><<<grid, 256, 0, as_stream(stream)>>>(a, vec_c);
+                else bgemm_wide<4><<<grid, 256, 0, as_stream(stream)>>>(a, vec_c);
+                return check_launch(what);
+            }
+        }
+    }
     int64_t const gx = ceil_div(a.N, BN), gy = ceil_div(a.M, BM);
     if (gy > 65535 || batches > 65535) return fail(ANN_ENOTSUP, "%s: grid too large for this build.", what);
     dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batches));

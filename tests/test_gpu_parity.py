@@ -340,6 +340,45 @@ def test_scores_apply_gqa_bthd_ragged(ann, T):
         assert_close(host(o), ro, T, "apply")
 
 
+@pytest.mark.parametrize("case", ["scores_bthd", "scores_bhtd_gqa", "apply_bthd", "apply_bhtd_gqa"])
+def test_scores_apply_wide_tiles(ann, case):
+    """fp32 scores / apply at sizes that fill the GPU, so they run on the
+    128-column tiles (8 x 8 outputs a thread for scores, 4 x 8 for apply):
+    ragged edges, GQA, both K/V layouts, against the oracle. Sums of
+    hundreds of products can cancel to near 0, where FMA and the oracle's
+    separate multiply-add round differently; each output may differ by the
+    dot-product rounding bound 4 eps sqrt(K) sum|a b| on top of the usual
+    tolerance (sum|a b| from the oracle on |a| and |b|)."""
+    g = rng(41)
+    T = np.float32
+    layout = 1 if "bhtd" in case else 0
+    gq = 2 if "gqa" in case else 1
+    if case.startswith("scores"):
+        B, Tq, Tk, Hq, D = 1, 1100, 1037, 8, 72
+    else:
+        B, Tq, Tk, Hq, D = 1, 700, 611, 48, 128
+    Hkv = Hq // gq
+    kshape = (B, Tk, Hkv, D) if layout == 0 else (B, Hkv, Tk, D)
+    if case.startswith("scores"):
+        q, k = normal(g, (B, Tq, Hq, D), T), normal(g, kshape, T)
+        want = oracle.attention_scores(q, k, np.empty((B, Hq, Tq, Tk), T), gq, layout)
+        s = empty(want.shape, T)
+        ann.onHost.nn.attentionScores(ann.Queue(), None, dev(q), dev(k), s, gq, layout)
+        got, K = host(s), D
+        absdot = oracle.attention_scores(np.abs(q), np.abs(k), np.empty_like(want), gq, layout)
+    else:
+        p, v = normal(g, (B, Hq, Tq, Tk), T), normal(g, kshape, T)
+        want = oracle.attention_apply(p, v, np.empty((B, Tq, Hq, D), T), gq, layout)
+        o = empty(want.shape, T)
+        ann.onHost.nn.attentionApply(ann.Queue(), None, dev(p), dev(v), o, gq, layout)
+        got, K = host(o), Tk
+        absdot = oracle.attention_apply(np.abs(p), np.abs(v), np.empty_like(want), gq, layout)
+    rtol, atol = 1e-4, 1e-5
+    err = np.abs(got.astype(np.float64) - want)
+    bound = rtol * np.abs(want.astype(np.float64)) + atol + 4 * np.finfo(T).eps * np.sqrt(K) * absdot
+    assert (err <= bound).all(), (case, float((err - bound).max()), int((err > bound).sum()))
+
+
 @pytest.mark.parametrize("T,D", [(np.float32, 128), (np.float64, 64)])
 @pytest.mark.parametrize("splits", [1, 2, 5, 8, 16])
 def test_decode_forced_cluster_sizes(ann, monkeypatch, T, D, splits):
