@@ -96,10 +96,14 @@ __global__ void __launch_bounds__(256) bgemm_kernel(BgemmArgs a) {
 // ascending order with FMA, as bgemm_kernel does.
 constexpr int BK8 = 8, BN128 = 128, PAD = 4;
 
-template <int TM>
+// VL: both operands are loaded as 16-byte vectors (unit stride along the
+// walked axis, 4-element aligned rows and extents), one or two a thread per
+// slice, instead of TM + 4 scalar loads with their index arithmetic.
+template <int TM, bool VL>
 __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     constexpr int BMW = 16 * TM;
-    constexpr int LA = BMW * BK8 / 256, LB = BN128 * BK8 / 256;  // loads a thread makes per slice
+    constexpr int LA = VL ? 1 : BMW * BK8 / 256, LB = VL ? 1 : BN128 * BK8 / 256;  // loads a thread makes per slice
+    constexpr int QA = BMW * BK8 / 4;  // 16-byte pieces of an A slice (256 or 128)
     __shared__ __align__(16) float As[2][BK8][BMW + PAD];
     __shared__ __align__(16) float Bs[2][BK8][BN128 + PAD];
     int const tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
@@ -111,7 +115,42 @@ __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     float* C = static_cast<float*>(a.C) + b * a.c_b + hq * a.c_h;
     int64_t const m0 = static_cast<int64_t>(blockIdx.y) * BMW, n0 = static_cast<int64_t>(blockIdx.x) * BN128;
     float ra[LA], rb[LB];
+    float4 va{}, vb{};
+    auto load_vec = [&](int64_t k0) {
+        if (tid < QA) {
+            int64_t gm, gk;
+            if (a.a_k_unit) gm = m0 + tid / 2, gk = k0 + (tid % 2) * 4;
+            else gm = m0 + (tid % (BMW / 4)) * 4, gk = k0 + tid / (BMW / 4);
+            bool const in = a.a_k_unit ? (gm < a.M && gk < a.K) : (gk < a.K && gm < a.M);
+            va = in ? *reinterpret_cast<float4 const*>(A + gm * a.am + gk * a.ak) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        int64_t gn, gk;
+        if (a.b_k_unit) gn = n0 + tid / 2, gk = k0 + (tid % 2) * 4;
+        else gn = n0 + (tid % (BN128 / 4)) * 4, gk = k0 + tid / (BN128 / 4);
+        bool const in = gn < a.N && gk < a.K;
+        vb = in ? *reinterpret_cast<float4 const*>(B + gk * a.bk + gn * a.bn) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto store_vec = [&](int buf) {
+        if (tid < QA) {
+            if (a.a_k_unit) {
+                int const m = tid / 2, k = (tid % 2) * 4;
+                As[buf][k][m] = va.x; As[buf][k + 1][m] = va.y; As[buf][k + 2][m] = va.z; As[buf][k + 3][m] = va.w;
+            } else {
+                *reinterpret_cast<float4*>(&As[buf][tid / (BMW / 4)][(tid % (BMW / 4)) * 4]) = va;
+            }
+        }
+        if (a.b_k_unit) {
+            int const n = tid / 2, k = (tid % 2) * 4;
+            Bs[buf][k][n] = vb.x; Bs[buf][k + 1][n] = vb.y; Bs[buf][k + 2][n] = vb.z; Bs[buf][k + 3][n] = vb.w;
+        } else {
+            *reinterpret_cast<float4*>(&Bs[buf][tid / (BN128 / 4)][(tid % (BN128 / 4)) * 4]) = vb;
+        }
+    };
     auto load = [&](int64_t k0) {
+        if constexpr (VL) {
+            load_vec(k0);
+            return;
+        }
 #pragma unroll
         for (int e = 0; e < LA; ++e) {
             int const lin = tid + e * 256;
@@ -130,6 +169,10 @@ __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
         }
     };
     auto store = [&](int buf) {
+        if constexpr (VL) {
+            store_vec(buf);
+            return;
+        }
 #pragma unroll
         for (int e = 0; e < LA; ++e) {
             int const lin = tid + e * 256;
@@ -217,10 +260,25 @@ int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* w
             int const vec_c = a.cn == 1 && a.cm % 4 == 0 && a.c_b % 4 == 0 && a.c_h % 4 == 0 && aligned(a.C, 16);
             bool const tall = tiles128 >= 2 * slots;
             int64_t const gy = ceil_div(a.M, tall ? int64_t{128} : int64_t{64});
+            // 16-byte loads: along k (stride 1, row pitch and batch / head
+            // strides multiples of 4, K a multiple of 4) or along m / n (the
+            // same with M / N)
+            auto vec_ok = [&](const void* base, int k_unit, int64_t s_k, int64_t s_o, int64_t sb, int64_t sh,
+                              int64_t ext_o) {
+                int64_t const unit = k_unit ? s_k : s_o, other = k_unit ? s_o : s_k;
+                int64_t const walked = k_unit ? a.K : ext_o;
+                return unit == 1 && other % 4 == 0 && sb % 4 == 0 && sh % 4 == 0 && walked % 4 == 0 &&
+                       aligned(base, 16);
+            };
+            bool const vl = vec_ok(a.A, a.a_k_unit, a.ak, a.am, a.a_b, a.a_h, a.M) &&
+                            vec_ok(a.B, a.b_k_unit, a.bk, a.bn, a.b_b, a.b_h, a.N);
             if (gy <= 65535) {
                 dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batches));
-                if (tall) bgemm_wide<8><<<grid, 256, 0, as_stream(stream)>>>(a, vec_c);
-                else bgemm_wide<4><<<grid, 256, 0, as_stream(stream)>>>(a, vec_c);
+                cudaStream_t st = as_stream(stream);
+                if (tall && vl) bgemm_wide<8, true><<<grid, 256, 0, st>>>(a, vec_c);
+                else if (tall) bgemm_wide<8, false><<<grid, 256, 0, st>>>(a, vec_c);
+                else if (vl) bgemm_wide<4, true><<<grid, 256, 0, st>>>(a, vec_c);
+                else bgemm_wide<4, false><<<grid, 256, 0, st>>>(a, vec_c);
                 return check_launch(what);
             }
         }
