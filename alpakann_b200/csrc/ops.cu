@@ -689,8 +689,101 @@ char const* reduce_name(int op) {
     }
 }
 
+// The plain column case: the reduced axis is the outermost one and the rest
+// is one contiguous run in a, b and out (output o at offset o everywhere),
+// 16-byte aligned. A cluster of kColSplit CTAs splits the axis; a CTA owns
+// 16 * NV columns, each half-warp one row at a time (16 lanes x 16 bytes),
+// four rows in flight a thread, the 16 half-warps' partials then combined
+// in order through shared memory and the cluster's in rank order through
+// distributed shared memory.
 template <int OP, typename T>
-int launch_reduce(cudaStream_t s, ReduceArgs const& r, bool rows, bool vec) {
+__global__ void __launch_bounds__(kThreads) reduce_cols_vec(ReduceArgs r) {
+    using V = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n, TC = 16 * NV;
+    __shared__ T part[16][TC + 1];
+    __shared__ T cta[TC];
+    cg::cluster_group cluster = cg::this_cluster();
+    int const rank = static_cast<int>(cluster.block_rank());
+    T const* A = static_cast<T const*>(r.a);
+    T const* Bp = static_cast<T const*>(r.b);
+    T* out = static_cast<T*>(r.out);
+    int const l16 = threadIdx.x & 15, half = threadIdx.x >> 4;
+    int64_t const tiles = r.outputs / TC;  // outputs is a multiple of TC here
+    int64_t const clusters = gridDim.x / kColSplit;
+    int64_t const per = ceil_div(r.len, kColSplit);
+    int64_t const lo = rank * per < r.len ? rank * per : r.len;
+    int64_t const hi = lo + per < r.len ? lo + per : r.len;
+    auto term = [&](V x, V y, T* acc) {
+        T const* xe = reinterpret_cast<T const*>(&x);
+        T const* ye = reinterpret_cast<T const*>(&y);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) acc[k] = combine<OP>(acc[k], transform<OP>(xe[k], ye[k]));
+    };
+    for (int64_t t = blockIdx.x / kColSplit; t < tiles; t += clusters) {  // same trip count in every CTA
+        int64_t const c0 = t * TC + l16 * NV;
+        T acc[NV];
+#pragma unroll
+        for (int k = 0; k < NV; ++k) acc[k] = reduce_init<OP, T>();
+        int64_t i = lo + half;
+        for (; i + 48 < hi; i += 64) {
+            V x[4], y[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                x[u] = *reinterpret_cast<V const*>(A + (i + 16 * u) * r.sa_axis + c0);
+                y[u] = OP == ANN_REDUCE_DOT ? *reinterpret_cast<V const*>(Bp + (i + 16 * u) * r.sb_axis + c0) : V{};
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) term(x[u], y[u], acc);
+        }
+        for (; i < hi; i += 16) {
+            V const x = *reinterpret_cast<V const*>(A + i * r.sa_axis + c0);
+            V const y = OP == ANN_REDUCE_DOT ? *reinterpret_cast<V const*>(Bp + i * r.sb_axis + c0) : V{};
+            term(x, y, acc);
+        }
+#pragma unroll
+        for (int k = 0; k < NV; ++k) part[half][l16 * NV + k] = acc[k];
+        __syncthreads();
+        if (threadIdx.x < TC) {
+            T v = part[0][threadIdx.x];
+#pragma unroll
+            for (int h = 1; h < 16; ++h) v = combine<OP>(v, part[h][threadIdx.x]);
+            cta[threadIdx.x] = v;
+        }
+        cluster.sync();
+        if (rank == 0 && threadIdx.x < TC) {
+            T v = cta[threadIdx.x];
+            for (int k = 1; k < kColSplit; ++k) v = combine<OP>(v, cluster.map_shared_rank(cta, k)[threadIdx.x]);
+            out[t * TC + threadIdx.x] = finalize<OP>(v, r.len);
+        }
+        cluster.sync();  // the peers' partials must outlive rank 0's reads, and part is reused
+    }
+}
+
+template <int OP, typename T>
+int launch_cols_vec(cudaStream_t s, ReduceArgs const& r) {
+    constexpr int TC = 16 * Vec16<T>::n;
+    int64_t const tiles = r.outputs / TC;
+    int64_t clusters = static_cast<int64_t>(sm_count()) * 8 / kColSplit;
+    if (clusters > tiles) clusters = tiles;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = kColSplit;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * kColSplit));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = s;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, reduce_cols_vec<OP, T>, r);
+    if (e != cudaSuccess) return fail(ANN_ECUDA, "reduce: %s", cudaGetErrorString(e));
+    return ANN_OK;
+}
+
+template <int OP, typename T>
+int launch_reduce(cudaStream_t s, ReduceArgs const& r, bool rows, bool vec, bool plain_cols = false) {
+    if (!rows && plain_cols) return launch_cols_vec<OP, T>(s, r);
     if (!rows) {
         // few output tiles against a long axis: split the axis over a cluster
         if (r.len >= 256 && ceil_div(r.outputs, 32) < 4 * sm_count()) return launch_cols_cluster<OP, T>(s, r);
@@ -741,13 +834,32 @@ int reduce(ann_stream stream, int op, const ann_view* a_v, const ann_view* b_v, 
         if (i == static_cast<int>(axis) || a.ext[i] == 1) continue;
         vec = a.str[i] % Vec16<T>::n == 0 && (op != ANN_REDUCE_DOT || b.str[i] % Vec16<T>::n == 0);
     }
+    // The plain column case for reduce_cols_vec: every non-reduced axis of
+    // extent > 1 row-major contiguous, innermost first, in a, b and out, the
+    // reduced axis outermost of them, 16-byte aligned rows, the outputs a
+    // whole number of column tiles and an axis long enough to split.
+    bool plain = !rows && r.len >= 256;
+    {
+        int64_t expect = 1;
+        for (int i = a.rank - 1; plain && i >= 0; --i) {
+            if (i == static_cast<int>(axis) || a.ext[i] == 1) continue;
+            plain = a.str[i] == expect && out.str[i] == expect && (op != ANN_REDUCE_DOT || b.str[i] == expect) &&
+                    static_cast<int>(axis) < i;
+            expect *= a.ext[i];
+        }
+        constexpr int NV = Vec16<T>::n;
+        plain = plain && r.outputs % (16 * NV) == 0 && r.sa_axis % NV == 0 && r.sb_axis % NV == 0 &&
+                aligned(a.data, 16) && aligned(out.data, 16) && (op != ANN_REDUCE_DOT || aligned(b.data, 16));
+    }
     cudaStream_t s = as_stream(stream);
     switch (op) {
-        case ANN_REDUCE_SUM: ANN_TRY((launch_reduce<ANN_REDUCE_SUM, T>(s, r, rows, vec))); break;
-        case ANN_REDUCE_MAX: ANN_TRY((launch_reduce<ANN_REDUCE_MAX, T>(s, r, rows, vec))); break;
-        case ANN_REDUCE_MEAN: ANN_TRY((launch_reduce<ANN_REDUCE_MEAN, T>(s, r, rows, vec))); break;
-        case ANN_REDUCE_SUM_SQUARES: ANN_TRY((launch_reduce<ANN_REDUCE_SUM_SQUARES, T>(s, r, rows, vec))); break;
-        default: ANN_TRY((launch_reduce<ANN_REDUCE_DOT, T>(s, r, rows, vec))); break;
+        case ANN_REDUCE_SUM: ANN_TRY((launch_reduce<ANN_REDUCE_SUM, T>(s, r, rows, vec, plain))); break;
+        case ANN_REDUCE_MAX: ANN_TRY((launch_reduce<ANN_REDUCE_MAX, T>(s, r, rows, vec, plain))); break;
+        case ANN_REDUCE_MEAN: ANN_TRY((launch_reduce<ANN_REDUCE_MEAN, T>(s, r, rows, vec, plain))); break;
+        case ANN_REDUCE_SUM_SQUARES:
+            ANN_TRY((launch_reduce<ANN_REDUCE_SUM_SQUARES, T>(s, r, rows, vec, plain)));
+            break;
+        default: ANN_TRY((launch_reduce<ANN_REDUCE_DOT, T>(s, r, rows, vec, plain))); break;
     }
     return check_launch(name);
 }

@@ -317,7 +317,8 @@ def test_fill(ann, dtype, value):
 
 @pytest.mark.parametrize("dtype,np_t", DT)
 @pytest.mark.parametrize("shape,axis", [((7, 33, 4099), 2), ((7, 33, 300), 2), ((7, 33, 5), 2), ((7, 33, 301), 1),
-                                        ((4099, 3, 2), 0), ((1, 1, 1), 0), ((5, 0, 3), 1)])
+                                        ((4099, 3, 2), 0), ((1, 1, 1), 0), ((5, 0, 3), 1),
+                                        ((3001, 4, 64), 0), ((1, 777, 128), 1), ((20000, 192), 0)])
 def test_reduction_parity(ann, dtype, np_t, shape, axis):
     rng = np.random.default_rng(5)
     x = rng.standard_normal(shape).astype(np_t)
@@ -345,6 +346,37 @@ def test_reduction_parity(ann, dtype, np_t, shape, axis):
         if op == "max" or shape[axis] == 0:
             assert np.array_equal(got, want, equal_nan=True), op
         else:
+            assert (np.abs(got.astype(np.float64) - want) <= bound).all(), op
+
+
+@pytest.mark.parametrize("dtype,np_t", DT)
+def test_column_reduction_padded_rows(ann, dtype, np_t):
+    """Columns [:, :128] of a [600, 192] tensor reduced over axis 0 (row
+    pitch 192, 16-byte aligned): the split-axis column path with a pitch
+    wider than the run, for sum, max and dot."""
+    rng = np.random.default_rng(12)
+    big = rng.standard_normal((600, 192)).astype(np_t)
+    other = rng.standard_normal((600, 192)).astype(np_t)
+    x, y = big[:, :128], other[:, :128]
+    dx, dy = dev(big)[:, :128], dev(other)[:, :128]
+    o = ann.onHost.ops
+    eps = np.finfo(np_t).eps
+    for op in ["sum", "max", "dot"]:
+        want = np.empty((1, 128), np_t)
+        oracle.reduce(np.ascontiguousarray(x), want, op, 0, rhs=np.ascontiguousarray(y) if op == "dot" else None)
+        out = torch.full((1, 128), 123.0, dtype=dtype, device="cuda")
+        if op == "dot":
+            o.dot(None, None, dx, dy, out, 0)
+        elif op == "sum":
+            o.reduceSum(None, None, dx, out, 0)
+        else:
+            o.reduceMax(None, None, dx, out, 0)
+        got = host(out)
+        if op == "max":
+            assert np.array_equal(got, want), op
+        else:
+            terms = (x * y if op == "dot" else x).astype(np.float64)
+            bound = 4 * eps * math.sqrt(600) * np.abs(terms).sum(0, keepdims=True)
             assert (np.abs(got.astype(np.float64) - want) <= bound).all(), op
 
 
