@@ -170,15 +170,23 @@ __global__ void __launch_bounds__(kThreads) binary_dense(T const* l, T const* r,
     int64_t done = 0;
     if (vec_ok) {
         int64_t const nv = n / NV;
-        for (int64_t i = tid; i < nv; i += stride) {
-            V a = reinterpret_cast<V const*>(l)[i];
-            V const b = reinterpret_cast<V const*>(r)[i];
+        V const* vl = reinterpret_cast<V const*>(l);
+        V const* vr = reinterpret_cast<V const*>(r);
+        V* vo = reinterpret_cast<V*>(out);
+        auto apply = [&](V a, V const& b) {
             T* ea = reinterpret_cast<T*>(&a);
             T const* eb = reinterpret_cast<T const*>(&b);
 #pragma unroll
             for (int k = 0; k < NV; ++k) ea[k] = binary<OP>(ea[k], eb[k], alpha);
-            reinterpret_cast<V*>(out)[i] = a;
+            return a;
+        };
+        int64_t i = tid;
+        for (; i + stride < nv; i += 2 * stride) {  // four loads in flight
+            V const a0 = vl[i], b0 = vr[i], a1 = vl[i + stride], b1 = vr[i + stride];
+            vo[i] = apply(a0, b0);
+            vo[i + stride] = apply(a1, b1);
         }
+        if (i < nv) vo[i] = apply(vl[i], vr[i]);
         done = nv * NV;
     }
     for (int64_t i = done + tid; i < n; i += stride) out[i] = binary<OP>(l[i], r[i], alpha);
@@ -197,8 +205,8 @@ __global__ void __launch_bounds__(kThreads) binary_strided(T const* l, T const* 
 
 // out[..., h] = act(in[..., h] + bias[h]); dense rows of length H.
 // FIXED_COL: the grid stride is a whole number of rows, so every vector a
-// thread touches has the same column: its bias vector is loaded once. Two
-// vectors per thread per iteration keep two loads in flight.
+// thread touches has the same column: its bias vector is loaded once. Four
+// vectors per thread per iteration keep four loads in flight.
 template <int ACT, typename T, bool FIXED_COL>
 __global__ void __launch_bounds__(kThreads) bias_dense(T const* in, T const* bias, T* out, int64_t n, int64_t H,
                                                        int vec_ok) {
@@ -221,12 +229,14 @@ __global__ void __launch_bounds__(kThreads) bias_dense(T const* in, T const* bia
         if constexpr (FIXED_COL) {
             V const b = vb[tid % hv];
             int64_t i = tid;
-            for (; i + stride < nv; i += 2 * stride) {
-                V const x0 = vi[i], x1 = vi[i + stride];
+            for (; i + 3 * stride < nv; i += 4 * stride) {
+                V const x0 = vi[i], x1 = vi[i + stride], x2 = vi[i + 2 * stride], x3 = vi[i + 3 * stride];
                 vo[i] = apply(x0, b);
                 vo[i + stride] = apply(x1, b);
+                vo[i + 2 * stride] = apply(x2, b);
+                vo[i + 3 * stride] = apply(x3, b);
             }
-            if (i < nv) vo[i] = apply(vi[i], b);
+            for (; i < nv; i += stride) vo[i] = apply(vi[i], b);
         } else {
             // column of vector i, advanced by the stride's remainder each
             // iteration instead of a 64-bit modulo per vector
