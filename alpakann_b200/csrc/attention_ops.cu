@@ -252,13 +252,13 @@ int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* w
     a.b_k_unit = a.bk == 1 ? 1 : 0;
     if constexpr (sizeof(T) == 4) {
         // wide tiles once the problem fills the GPU; 64-row tiles when 128-row
-        // ones would leave it under two waves (attentionApply: N = D)
+        // ones would leave over a quarter of the CTA slots idle
         int64_t const gx = ceil_div(a.N, static_cast<int64_t>(BN128));
         int64_t const tiles128 = gx * ceil_div(a.M, int64_t{128}) * batches;
         int64_t const slots = static_cast<int64_t>(sm_count()) * 2;
         if (a.M >= 64 && a.N >= 64 && tiles128 >= slots / 2 && batches <= 65535) {
             int const vec_c = a.cn == 1 && a.cm % 4 == 0 && a.c_b % 4 == 0 && a.c_h % 4 == 0 && aligned(a.C, 16);
-            bool const tall = tiles128 >= 2 * slots;
+            bool const tall = 4 * tiles128 >= 3 * slots;
             int64_t const gy = ceil_div(a.M, tall ? int64_t{128} : int64_t{64});
             // 16-byte loads: along k (stride 1, row pitch and batch / head
             // strides multiples of 4, K a multiple of 4) or along m / n (the

@@ -473,7 +473,10 @@ def test_softmax_rows_not_equally_spaced(ann, dtype, np_t, L):
     """Aligned rows whose starts are not equally spaced (the two outer axes
     of a [3, 5, 7, L] tensor swapped in the view): every row's offset is
     decoded from its index in the bulk-copy issuer and in the kernel; plain,
-    causal and masked."""
+    causal and masked. Relative tolerance scaled with the row as in
+    test_long_softmax_rows (the reference's sequential sum)."""
+    tol = dict(SOFTMAX_TOL[np_t])
+    tol["rtol"] = max(tol["rtol"], 4 * float(np.finfo(np_t).eps) * math.sqrt(L))
     rng = np.random.default_rng(13)
     base = (rng.standard_normal((3, 5, 7, L)) * 4).astype(np_t)
     x = base.transpose(1, 0, 2, 3)  # [5, 3, 7, L], outer strides not nested
@@ -482,16 +485,16 @@ def test_softmax_rows_not_equally_spaced(ann, dtype, np_t, L):
     out = torch.empty(x.shape, dtype=dtype, device="cuda")
     nn.softmax(None, None, dx, out, 3)
     np.testing.assert_allclose(host(out), oracle.softmax(np.ascontiguousarray(x), np.empty(x.shape, np_t), 3),
-                               **SOFTMAX_TOL[np_t])
+                               **tol)
     nn.causalSoftmax(None, None, dx, out, 3, 2, 3)
     np.testing.assert_allclose(host(out), oracle.causal_softmax(np.ascontiguousarray(x), np.empty(x.shape, np_t), 3, 2,
-                                                                3), **SOFTMAX_TOL[np_t])
+                                                                3), **tol)
     mbase = np.where(rng.random((3, 5, 7, L)) < 0.25, -np.inf, rng.standard_normal((3, 5, 7, L))).astype(np_t)
     mbase[..., 0] = 0
     m = mbase.transpose(1, 0, 2, 3)
     nn.maskedSoftmax(None, None, dx, dev(mbase).permute(1, 0, 2, 3), out, 3)
     np.testing.assert_allclose(host(out), oracle.masked_softmax(np.ascontiguousarray(x), np.ascontiguousarray(m),
-                                                                np.empty(x.shape, np_t), 3), **SOFTMAX_TOL[np_t])
+                                                                np.empty(x.shape, np_t), 3), **tol)
     assert ann.take_device_error(torch.cuda.current_stream().cuda_stream) == 0
 
 
