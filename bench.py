@@ -551,22 +551,21 @@ def ops_only(args):
     # reference does): one c3-like slice, B 1, T 4096, 8 heads of 128, fp32,
     # against the nominal FP32 SIMT peak (148 SMs x 128 lanes x 2 x 1965 MHz);
     # a fixed shape (512 MiB of scores) whatever --ops-elems is
-    if True:
-        Tq, Hs, Dh = 4096, 8, 128
-        q4 = torch.randn((1, Tq, Hs, Dh), device=dev)
-        k4 = torch.randn((1, Tq, Hs, Dh), device=dev)
-        s4 = torch.empty((1, Hs, Tq, Tq), device=dev)
-        o4 = torch.empty((1, Tq, Hs, Dh), device=dev)
-        simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-        flops = 2 * Hs * Tq * Tq * Dh
-        for name, fn in ((f"attentionScores Q,K [1,{Tq},{Hs},{Dh}] -> S [1,{Hs},{Tq},{Tq}]",
-                          lambda: nn.attentionScores(None, None, q4, k4, s4)),
-                         (f"attentionApply P [1,{Hs},{Tq},{Tq}], V [1,{Tq},{Hs},{Dh}]",
-                          lambda: nn.attentionApply(None, None, s4, k4, o4))):
-            t = timed(fn, reps=5, warm=2)
-            print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 3), "TFLOPs": round(flops / t / 1e12, 2),
-                              "frac_of_fp32_simt_nominal": round(flops / t / 1e12 / simt_peak, 3)}), flush=True)
-        del q4, k4, s4, o4
+    Tq, Hs, Dh = 4096, 8, 128
+    q4 = torch.randn((1, Tq, Hs, Dh), device=dev)
+    k4 = torch.randn((1, Tq, Hs, Dh), device=dev)
+    s4 = torch.empty((1, Hs, Tq, Tq), device=dev)
+    o4 = torch.empty((1, Tq, Hs, Dh), device=dev)
+    simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    flops = 2 * Hs * Tq * Tq * Dh
+    for name, fn in ((f"attentionScores Q,K [1,{Tq},{Hs},{Dh}] -> S [1,{Hs},{Tq},{Tq}]",
+                      lambda: nn.attentionScores(None, None, q4, k4, s4)),
+                     (f"attentionApply P [1,{Hs},{Tq},{Tq}], V [1,{Tq},{Hs},{Dh}]",
+                      lambda: nn.attentionApply(None, None, s4, k4, o4))):
+        t = timed(fn, reps=5, warm=2)
+        print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 3), "TFLOPs": round(flops / t / 1e12, 2),
+                          "frac_of_fp32_simt_nominal": round(flops / t / 1e12 / simt_peak, 3)}), flush=True)
+    del q4, k4, s4, o4
     del a, b, o
     torch.cuda.empty_cache()
     if args.ops_elems != 1 << 28:
