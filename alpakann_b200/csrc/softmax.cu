@@ -714,15 +714,21 @@ __global__ void __launch_bounds__(256) scale_kernel(ScaleArgs a, T scalar) {
         int64_t const nv = a.n / NV;
         V const* iv = reinterpret_cast<V const*>(in);
         V* ov = reinterpret_cast<V*>(out);
-        for (int64_t i = i0; i < nv; i += step) {
-            V v = iv[i];
+        auto mul = [&](V v) {
             if constexpr (NV == 4) {
                 v.x = v.x * scalar; v.y = v.y * scalar; v.z = v.z * scalar; v.w = v.w * scalar;
             } else {
                 v.x = v.x * scalar; v.y = v.y * scalar;
             }
-            ov[i] = v;
+            return v;
+        };
+        int64_t i = i0;
+        for (; i + step < nv; i += 2 * step) {  // two loads in flight
+            V const v0 = iv[i], v1 = iv[i + step];
+            ov[i] = mul(v0);
+            ov[i + step] = mul(v1);
         }
+        if (i < nv) ov[i] = mul(iv[i]);
         for (int64_t i = nv * NV + i0; i < a.n; i += step) out[i] = in[i] * scalar;
     } else {
         for (int64_t i = i0; i < a.n; i += step) {
