@@ -149,43 +149,43 @@ __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     auto load = [&](int64_t k0) {
         if constexpr (VL) {
             load_vec(k0);
-            return;
-        }
+        } else {
 #pragma unroll
-        for (int e = 0; e < LA; ++e) {
-            int const lin = tid + e * 256;
-            int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
-            int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
-            int64_t const gm = m0 + m, gk = k0 + k;
-            ra[e] = (gm < a.M && gk < a.K) ? A[gm * a.am + gk * a.ak] : 0.f;
-        }
+            for (int e = 0; e < LA; ++e) {
+                int const lin = tid + e * 256;
+                int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
+                int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
+                int64_t const gm = m0 + m, gk = k0 + k;
+                ra[e] = (gm < a.M && gk < a.K) ? A[gm * a.am + gk * a.ak] : 0.f;
+            }
 #pragma unroll
-        for (int e = 0; e < LB; ++e) {
-            int const lin = tid + e * 256;
-            int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
-            int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
-            int64_t const gn = n0 + n, gk = k0 + k;
-            rb[e] = (gn < a.N && gk < a.K) ? B[gk * a.bk + gn * a.bn] : 0.f;
+            for (int e = 0; e < LB; ++e) {
+                int const lin = tid + e * 256;
+                int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
+                int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
+                int64_t const gn = n0 + n, gk = k0 + k;
+                rb[e] = (gn < a.N && gk < a.K) ? B[gk * a.bk + gn * a.bn] : 0.f;
+            }
         }
     };
     auto store = [&](int buf) {
         if constexpr (VL) {
             store_vec(buf);
-            return;
-        }
+        } else {
 #pragma unroll
-        for (int e = 0; e < LA; ++e) {
-            int const lin = tid + e * 256;
-            int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
-            int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
-            As[buf][k][m] = ra[e];
-        }
+            for (int e = 0; e < LA; ++e) {
+                int const lin = tid + e * 256;
+                int const m = a.a_k_unit ? lin / BK8 : lin % BMW;
+                int const k = a.a_k_unit ? lin % BK8 : lin / BMW;
+                As[buf][k][m] = ra[e];
+            }
 #pragma unroll
-        for (int e = 0; e < LB; ++e) {
-            int const lin = tid + e * 256;
-            int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
-            int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
-            Bs[buf][k][n] = rb[e];
+            for (int e = 0; e < LB; ++e) {
+                int const lin = tid + e * 256;
+                int const n = a.b_k_unit ? lin / BK8 : lin % BN128;
+                int const k = a.b_k_unit ? lin % BK8 : lin / BN128;
+                Bs[buf][k][n] = rb[e];
+            }
         }
     };
     float acc[TM][8];
