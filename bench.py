@@ -566,6 +566,27 @@ def ops_only(args):
         print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 3), "TFLOPs": round(flops / t / 1e12, 2),
                           "frac_of_fp32_simt_nominal": round(flops / t / 1e12 / simt_peak, 3)}), flush=True)
     del q4, k4, s4, o4
+    # the same two ops in fp64 at the c4 prefill shape (B 2, T 1024, 16 heads
+    # of 64), against the DGEMM rate cuBLAS reaches on this GPU
+    Tq, Hs, Dh = 1024, 16, 64
+    q4 = torch.randn((2, Tq, Hs, Dh), device=dev, dtype=torch.float64)
+    k4 = torch.randn((2, Tq, Hs, Dh), device=dev, dtype=torch.float64)
+    s4 = torch.empty((2, Hs, Tq, Tq), device=dev, dtype=torch.float64)
+    o4 = torch.empty((2, Tq, Hs, Dh), device=dev, dtype=torch.float64)
+    ga, gb = torch.randn((4096, 4096), device=dev, dtype=torch.float64), torch.randn((4096, 4096), device=dev,
+                                                                                   dtype=torch.float64)
+    dgemm = 2 * 4096 ** 3 / timed(lambda: torch.mm(ga, gb), reps=3, warm=1) / 1e12
+    del ga, gb
+    flops = 2 * 2 * Hs * Tq * Tq * Dh
+    for name, fn in ((f"attentionScores Q,K [2,{Tq},{Hs},{Dh}] -> S [2,{Hs},{Tq},{Tq}] f64",
+                      lambda: nn.attentionScores(None, None, q4, k4, s4)),
+                     (f"attentionApply P [2,{Hs},{Tq},{Tq}], V [2,{Tq},{Hs},{Dh}] f64",
+                      lambda: nn.attentionApply(None, None, s4, k4, o4))):
+        t = timed(fn, reps=5, warm=2)
+        print(json.dumps({"op": name, "dtype": "f64", "ms": round(t * 1e3, 4), "TFLOPs": round(flops / t / 1e12, 2),
+                          "frac_of_cublas_dgemm": round(flops / t / 1e12 / dgemm, 3),
+                          "cublas_dgemm_tflops": round(dgemm, 1)}), flush=True)
+    del q4, k4, s4, o4
     del a, b, o
     torch.cuda.empty_cache()
     if args.ops_elems != 1 << 28:
