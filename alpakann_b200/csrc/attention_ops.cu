@@ -246,6 +246,117 @@ __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     }
 }
 
+// fp64 on the FP64 tensor cores: mma.sync.m16n8k4.f64 (fp64 products and
+// accumulation). 64 x 64 output tiles, 4 warps of 32 x 32 (2 x 4 MMA tiles of
+// 16 x 8 each), 16-deep k slices in shared memory with k contiguous and a row
+// pitch of 18 doubles (16 mod 128 bytes: each fragment read hits a bank at
+// most twice per 256 bytes), two buffers, the next slice's global loads issued
+// before the current one is computed. Fragments of m16n8k4.f64 (g = lane / 4,
+// t = lane % 4): a0 = A[g][t], a1 = A[g + 8][t], b0 = B[t][g]; c0 = C[g][2t],
+// c1 = C[g][2t + 1], c2 = C[g + 8][2t], c3 = C[g + 8][2t + 1].
+constexpr int DM = 64, DN = 64, DK = 16, DP = DK + 2, kDThreads = 128;
+
+__device__ __forceinline__ void dmma_acc(double (&c)[4], double a0, double a1, double b0) {
+    asm volatile("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                 : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+                 : "d"(a0), "d"(a1), "d"(b0));
+}
+
+__global__ void __launch_bounds__(kDThreads, 3) bgemm_dmma(BgemmArgs a) {
+    constexpr int LA = DM * DK / kDThreads, LB = DN * DK / kDThreads;  // 8 loads each per slice
+    __shared__ __align__(16) double As[2][DM][DP];
+    __shared__ __align__(16) double Bs[2][DN][DP];
+    int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int const g = lane >> 2, t = lane & 3;
+    int const wm = warp >> 1, wn = warp & 1;
+    int64_t const z = blockIdx.z;
+    int64_t const b = z / a.heads, hq = z % a.heads;
+    int64_t const kvh = hq / a.g;
+    double const* A = static_cast<double const*>(a.A) + b * a.a_b + hq * a.a_h;
+    double const* B = static_cast<double const*>(a.B) + b * a.b_b + kvh * a.b_h;
+    double* C = static_cast<double*>(a.C) + b * a.c_b + hq * a.c_h;
+    int64_t const m0 = static_cast<int64_t>(blockIdx.y) * DM, n0 = static_cast<int64_t>(blockIdx.x) * DN;
+    double ra[LA], rb[LB];
+    auto load = [&](int64_t k0) {
+#pragma unroll
+        for (int e = 0; e < LA; ++e) {
+            int const lin = tid + e * kDThreads;
+            int const m = a.a_k_unit ? lin / DK : lin % DM;
+            int const k = a.a_k_unit ? lin % DK : lin / DM;
+            int64_t const gm = m0 + m, gk = k0 + k;
+            ra[e] = (gm < a.M && gk < a.K) ? A[gm * a.am + gk * a.ak] : 0.0;
+        }
+#pragma unroll
+        for (int e = 0; e < LB; ++e) {
+            int const lin = tid + e * kDThreads;
+            int const n = a.b_k_unit ? lin / DK : lin % DN;
+            int const k = a.b_k_unit ? lin % DK : lin / DN;
+            int64_t const gn = n0 + n, gk = k0 + k;
+            rb[e] = (gn < a.N && gk < a.K) ? B[gk * a.bk + gn * a.bn] : 0.0;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int e = 0; e < LA; ++e) {
+            int const lin = tid + e * kDThreads;
+            int const m = a.a_k_unit ? lin / DK : lin % DM;
+            int const k = a.a_k_unit ? lin % DK : lin / DM;
+            As[buf][m][k] = ra[e];
+        }
+#pragma unroll
+        for (int e = 0; e < LB; ++e) {
+            int const lin = tid + e * kDThreads;
+            int const n = a.b_k_unit ? lin / DK : lin % DN;
+            int const k = a.b_k_unit ? lin % DK : lin / DN;
+            Bs[buf][n][k] = rb[e];
+        }
+    };
+    double acc[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0;
+    int64_t const slices = ceil_div(a.K, static_cast<int64_t>(DK));
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int64_t sl = 0; sl < slices; ++sl) {
+        int const buf = static_cast<int>(sl & 1);
+        if (sl + 1 < slices) load((sl + 1) * DK);
+#pragma unroll
+        for (int kk = 0; kk < DK / 4; ++kk) {
+            double a0[2], a1[2], b0[4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                a0[i] = As[buf][wm * 32 + 16 * i + g][4 * kk + t];
+                a1[i] = As[buf][wm * 32 + 16 * i + g + 8][4 * kk + t];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b0[j] = Bs[buf][wn * 32 + 8 * j + g][4 * kk + t];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_acc(acc[i][j], a0[i], a1[i], b0[j]);
+        }
+        if (sl + 1 < slices) store(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int64_t const gm = m0 + wm * 32 + 16 * i + g + 8 * h;
+                if (gm >= a.M) continue;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    int64_t const gn = n0 + wn * 32 + 8 * j + 2 * t + c;
+                    if (gn < a.N) C[gm * a.cm + gn * a.cn] = acc[i][j][2 * h + c];
+                }
+            }
+}
+
 template <typename T>
 int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* what) {
     a.a_k_unit = a.ak == 1 ? 1 : 0;
@@ -282,6 +393,13 @@ int launch_bgemm(ann_stream stream, BgemmArgs& a, int64_t batches, const char* w
                 return check_launch(what);
             }
         }
+    }
+    if constexpr (sizeof(T) == 8) {  // fp64: the FP64 tensor cores
+        int64_t const gx = ceil_div(a.N, static_cast<int64_t>(DN)), gy = ceil_div(a.M, static_cast<int64_t>(DM));
+        if (gy > 65535 || batches > 65535) return fail(ANN_ENOTSUP, "%s: grid too large for this build.", what);
+        dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batches));
+        bgemm_dmma<<<grid, kDThreads, 0, as_stream(stream)>>>(a);
+        return check_launch(what);
     }
     int64_t const gx = ceil_div(a.N, BN), gy = ceil_div(a.M, BM);
     if (gy > 65535 || batches > 65535) return fail(ANN_ENOTSUP, "%s: grid too large for this build.", what);

@@ -340,22 +340,28 @@ def test_scores_apply_gqa_bthd_ragged(ann, T):
         assert_close(host(o), ro, T, "apply")
 
 
+@pytest.mark.parametrize("T", [np.float32, np.float64])
 @pytest.mark.parametrize("case", ["scores_bthd", "scores_bhtd_gqa", "apply_bthd", "apply_bhtd_gqa"])
-def test_scores_apply_wide_tiles(ann, case):
+def test_scores_apply_wide_tiles(ann, case, T):
     """fp32 scores / apply at sizes that fill the GPU, so they run on the
     128-column tiles (8 x 8 outputs a thread for scores, 4 x 8 for apply):
     ragged edges, GQA, both K/V layouts, against the oracle. Sums of
     hundreds of products can cancel to near 0, where FMA and the oracle's
     separate multiply-add round differently; each output may differ by the
     dot-product rounding bound 4 eps sqrt(K) sum|a b| on top of the usual
-    tolerance (sum|a b| from the oracle on |a| and |b|)."""
+    tolerance (sum|a b| from the oracle on |a| and |b|). fp64 runs on the
+    FP64 tensor-core tiles (64 x 64, mma.sync m16n8k4) at smaller sizes."""
     g = rng(41)
-    T = np.float32
     layout = 1 if "bhtd" in case else 0
     gq = 2 if "gqa" in case else 1
-    # D = 72 and Tk = 612 take the 16-byte-load variant, D = 70 and Tk = 611
-    # the scalar-load one
-    if case.startswith("scores"):
+    # fp32: D = 72 and Tk = 612 take the 16-byte-load variant, D = 70 and
+    # Tk = 611 the scalar-load one
+    if T == np.float64:
+        if case.startswith("scores"):
+            B, Tq, Tk, Hq, D = 2, 301, 277, 4, (64 if gq > 1 else 37)
+        else:
+            B, Tq, Tk, Hq, D = 2, 290, (256 if gq > 1 else 283), 4, 64
+    elif case.startswith("scores"):
         B, Tq, Tk, Hq, D = 1, 1100, 1037, 8, (72 if gq > 1 else 70)
     else:
         B, Tq, Tk, Hq, D = 1, 700, (612 if gq > 1 else 611), 48, 128
@@ -375,7 +381,7 @@ def test_scores_apply_wide_tiles(ann, case):
         ann.onHost.nn.attentionApply(ann.Queue(), None, dev(p), dev(v), o, gq, layout)
         got, K = host(o), Tk
         absdot = oracle.attention_apply(np.abs(p), np.abs(v), np.empty_like(want), gq, layout)
-    rtol, atol = 1e-4, 1e-5
+    rtol, atol = (1e-4, 1e-5) if T == np.float32 else (1e-11, 1e-12)
     err = np.abs(got.astype(np.float64) - want)
     bound = rtol * np.abs(want.astype(np.float64)) + atol + 4 * np.finfo(T).eps * np.sqrt(K) * absdot
     assert (err <= bound).all(), (case, float((err - bound).max()), int((err > bound).sum()))
