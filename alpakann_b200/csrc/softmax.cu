@@ -4,9 +4,11 @@
 //
 // Softmax rows run along an arbitrary axis of a tensor of any rank. A row of
 // up to 8192 elements is owned by one to eight warps and held in their
-// registers, 8, 16 or 32 elements per lane (one read, one write); a row of up
-// to 96 KB by a 256-thread CTA that keeps it in shared memory (one read, one
-// write); a longer row by a 256-thread CTA that re-reads it from L1/L2. In
+// registers, 8, 16 or 32 elements per lane (one read, one write); a longer
+// aligned row of up to 200 KB by a 256-thread CTA that brings it into shared
+// memory with one bulk copy (one read, one write); an unaligned row of up to
+// 96 KB by a CTA that loads it into shared memory itself; a longer row by a
+// 256-thread CTA that re-reads it from L1/L2. In
 // every case: max over the unmasked entries from lowest(), sum of
 // exp(x - max), then out = exp(x - max) * (1 / sum) with masked entries
 // written as 0 -- the reference's three passes, with the passes' reductions
@@ -511,6 +513,144 @@ __global__ void __launch_bounds__(256) softmax_smem(SoftmaxArgs a) {
     }
 }
 
+// Aligned rows longer than the register path holds, up to kBulkBytes of
+// input (+ mask): one CTA per row, the whole row brought into shared memory by
+// ONE bulk copy (TMA) -- all of it in flight at once, where per-thread loads
+// keep a few pieces a thread in flight -- and, with two stages, the next
+// row's copy issued while this one is computed. Then softmax_smem's passes
+// over shared memory (masked slots -inf from the first pass on, one
+// reciprocal a row). Every wait is bounded: a copy that has not landed after
+// 1 s sets ANN_DEVERR_WAIT_TIMEOUT, the CTA drains its copies in flight
+// (bounded too) and returns.
+constexpr int64_t kBulkBytes = int64_t{200} << 10;
+
+template <typename T, bool MASK>
+__global__ void __launch_bounds__(256) softmax_bulk(SoftmaxArgs a, int stages, uint32_t stage_bytes) {
+    using P = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n;
+    extern __shared__ __align__(128) unsigned char rows_smem[];
+    __shared__ __align__(8) uint64_t full[2];
+    __shared__ T scratch[8];
+    T const* in = static_cast<T const*>(a.in);
+    T const* mk = static_cast<T const*>(a.mask);
+    T* out = static_cast<T*>(a.out);
+    int const tid = threadIdx.x;
+    int64_t const pieces = a.len / NV;
+    uint32_t const row_bytes = static_cast<uint32_t>(a.len) * sizeof(T);
+    int64_t const iters = ceil_div(a.rows - static_cast<int64_t>(blockIdx.x), static_cast<int64_t>(gridDim.x));
+    uint32_t const bar0 = smem_u32(full), base0 = smem_u32(rows_smem);
+    auto issue = [&](int64_t it) {  // thread 0: row blockIdx.x + it * gridDim.x into stage it % stages
+        int const st = static_cast<int>(it % stages);
+        int64_t const row = static_cast<int64_t>(blockIdx.x) + it * gridDim.x;
+        int64_t oi, oo, om = 0;
+        row_offsets(a, row, oi, oo, om);
+        uint32_t const bar = bar0 + 8u * st, dst = base0 + static_cast<uint32_t>(st) * stage_bytes;
+        mbar_arrive_expect_tx(bar, row_bytes * (MASK ? 2u : 1u));
+        bulk_copy_g2s(dst, in + oi, row_bytes, bar);
+        if constexpr (MASK) bulk_copy_g2s(dst + row_bytes, mk + om, row_bytes, bar);
+    };
+    if (tid == 0) {
+        for (int st = 0; st < stages; ++st) mbar_init(bar0 + 8u * st, 1);
+        fence_mbar_init();
+        for (int64_t it = 0; it < iters && it < stages; ++it) issue(it);
+    }
+    __syncthreads();
+    for (int64_t it = 0; it < iters; ++it) {
+        int const st = static_cast<int>(it % stages);
+        bool const ok = mbar_wait_bounded(bar0 + 8u * st, static_cast<uint32_t>((it / stages) & 1));
+        if (__syncthreads_or(!ok)) {  // all threads agree on giving up
+            if (tid == 0) {
+                atomicOr(&g_softmax_error, ANN_DEVERR_WAIT_TIMEOUT);
+                for (int64_t u = it; u < iters && u < it + stages; ++u)  // copies in flight (bounded)
+                    mbar_wait_bounded(bar0 + 8u * static_cast<uint32_t>(u % stages),
+                                      static_cast<uint32_t>((u / stages) & 1));
+            }
+            return;
+        }
+        int64_t const row = static_cast<int64_t>(blockIdx.x) + it * gridDim.x;
+        int64_t oi, oo, om = 0, lo, hi;
+        row_offsets(a, row, oi, oo, om);
+        kept_range(a, row, lo, hi);
+        T* buf = reinterpret_cast<T*>(rows_smem + static_cast<size_t>(st) * stage_bytes);
+        T const* mbuf = buf + a.len;
+        T m = Lowest<T>::value;
+        for (int64_t p = tid; p < pieces; p += 256) {
+            int64_t const e0 = p * NV;
+            P x = *reinterpret_cast<P const*>(buf + e0);
+            T* xe = reinterpret_cast<T*>(&x);
+            if constexpr (MASK) {
+                P const y = *reinterpret_cast<P const*>(mbuf + e0);
+                T const* ye = reinterpret_cast<T const*>(&y);
+#pragma unroll
+                for (int k = 0; k < NV; ++k) xe[k] = add_rn(xe[k], ye[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                if (e0 + k < lo || e0 + k >= hi) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
+                m = fmax(m, xe[k]);
+            }
+            *reinterpret_cast<P*>(buf + e0) = x;
+        }
+        m = block_max<8>(m, scratch);
+        T sum{};
+        for (int64_t p = tid; p < pieces; p += 256) {
+            int64_t const e0 = p * NV;
+            P x = *reinterpret_cast<P const*>(buf + e0);
+            T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                xe[k] = exp_t(xe[k] - m);
+                sum += xe[k];
+            }
+            *reinterpret_cast<P*>(buf + e0) = x;
+        }
+        sum = block_sum<8>(sum, scratch);
+        // one division per row; unkept slots tested only when sum < 1 (see softmax_regs)
+        T const inv = T(1) / sum;
+        bool const exact = !(sum >= T(1));
+        for (int64_t p = tid; p < pieces; p += 256) {
+            int64_t const e0 = p * NV;
+            P x = *reinterpret_cast<P const*>(buf + e0);
+            T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) xe[k] = exact && (e0 + k < lo || e0 + k >= hi) ? T(0) : xe[k] * inv;
+            *reinterpret_cast<P*>(out + oo + e0) = x;
+        }
+        // every read of stage st is done: refill it with the row `stages`
+        // iterations on (issued here, not at the next iteration's start, so
+        // that one stage works too)
+        __syncthreads();
+        if (tid == 0 && it + stages < iters) issue(it + stages);
+    }
+}
+
+// Launches softmax_bulk on a grid of resident CTAs; false when one row does
+// not fit. One row stage a CTA: several CTAs an SM, each with a whole row in
+// flight, kept more bytes in flight than two stages in fewer CTAs (rows of
+// 16384 fp32: 0.85 of the copy peak against 0.67).
+template <typename T, bool MASK>
+bool bulk_launched(SoftmaxArgs const& a, cudaStream_t s) {
+    int64_t const stage = ceil_div(a.len * static_cast<int64_t>(sizeof(T)) * (MASK ? 2 : 1), int64_t{128}) * 128;
+    if (stage > kBulkBytes) return false;
+    int const stages = 1;
+    int const smem = static_cast<int>(stage * stages);
+    auto kernel = softmax_bulk<T, MASK>;
+    if (smem > (48 << 10) &&
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    int64_t const cap = static_cast<int64_t>(sm_count()) * per_sm;
+    kernel<<<static_cast<unsigned>(a.rows < cap ? a.rows : cap), 256, smem, s>>>(a, stages,
+                                                                              static_cast<uint32_t>(stage));
+    return true;
+}
+
 // MASK: maskedSoftmax (onAcc/internal/nn/softmax.hpp:76-116), the row is
 // input + mask and nothing is skipped.
 template <typename T, int GROUP, bool MASK>
@@ -665,7 +805,9 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
     auto launch = [&](auto mask_tag) {
         constexpr bool M = decltype(mask_tag)::value;
         constexpr int CV = 8 / NV;  // 16-byte pieces per lane
-        if (smem_row) {
+        if (vec && a.len > 8192 && bulk_launched<T, M>(a, s)) {
+            // whole rows by bulk copy (softmax_bulk)
+        } else if (smem_row) {
             size_t const bytes = static_cast<size_t>(row_bytes);
             if (vec) softmax_smem<T, NV, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);
             else softmax_smem<T, 1, M><<<grid_for(a.rows, 1, 8), 256, bytes, s>>>(a);

@@ -518,6 +518,9 @@ def ops_only(args):
                       lambda: nn.causalSoftmax(None, None, r4_in, r4_out, 3, 2, 3)))
         cases.append((f"softmax [{S16},1,1024,16384]", 2 * 4 * (S16 << 24),
                       lambda: nn.softmax(None, None, r16_in, r16_out, 3)))
+    if S >= 64:  # decode-shaped rows of 32768 keys (128 KiB, streamed): c5's softmax, twice over
+        r32_in, r32_out = a[:1 << 26].view(32, 64, 1, 32768), o[:1 << 26].view(32, 64, 1, 32768)
+        cases.append(("softmax [32,64,1,32768]", 2 * 4 * (1 << 26), lambda: nn.softmax(None, None, r32_in, r32_out, 3)))
     # the attention path's own HBM-bound calls: embeddingLookup, rmsNorm, the
     # two fused into one launch, ropeInPlace on Q and K, ops::scale
     H = 4096
