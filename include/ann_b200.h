@@ -150,9 +150,9 @@ int ann_scale_f64(ann_stream stream, const ann_view* in, double scalar, const an
 
 /* ---- softmax: onHost/nn/softmax.hpp:26-40 ------------------------------
  * Row softmax along `axis` (max-subtracted, exp, divide by the sum; here one
- * reciprocal of the sum per row, within an ulp of the quotient). Rows of up
- * to 8192 elements that are 16-byte aligned are streamed into shared memory
- * by bulk copies with bounded waits (also for causalSoftmax and
+ * reciprocal of the sum per row, within an ulp of the quotient). Rows that
+ * are 16-byte aligned, of up to 200 KB (input + mask), are brought into shared
+ * memory by bulk copies with bounded waits (also for causalSoftmax and
  * maskedSoftmax): a copy that has not landed after 1 s sets
  * ANN_DEVERR_WAIT_TIMEOUT (ann_take_device_error). */
 int ann_softmax_f32(ann_stream stream, const ann_view* in, const ann_view* out, uint32_t axis);
