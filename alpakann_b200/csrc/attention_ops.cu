@@ -87,14 +87,14 @@ __global__ void __launch_bounds__(256) bgemm_kernel(BgemmArgs a) {
     }
 }
 
-// fp32 at sizes that fill the GPU: 128-column x (16 TM)-row output tiles, 8-deep
-// k slices, each thread TM x 8 outputs in four quadrants (rows ty*TM/2 + i and
+// fp32 at sizes that fill the GPU: 128-column x (16 TM)-row output tiles, 16-deep
+// k slices (8-deep with scalar loads), each thread TM x 8 outputs in four quadrants (rows ty*TM/2 + i and
 // BM/2 + ty*TM/2 + i, columns tx*4 + j and 64 + tx*4 + j) read from shared
 // memory as 16-byte vectors. Two shared-memory buffers: the global loads of
 // slice s + 1 go out before slice s is computed and land in the other buffer
 // after it, one barrier per slice. Every output still accumulates k in
 // ascending order with FMA, as bgemm_kernel does.
-constexpr int BK8 = 8, BN128 = 128, PAD = 4;
+constexpr int BN128 = 128, PAD = 4;
 
 // VL: both operands are loaded as 16-byte vectors (unit stride along the
 // walked axis, 4-element aligned rows and extents), one or two a thread per
@@ -102,8 +102,11 @@ constexpr int BK8 = 8, BN128 = 128, PAD = 4;
 template <int TM, bool VL>
 __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     constexpr int BMW = 16 * TM;
-    constexpr int LA = VL ? 1 : BMW * BK8 / 256, LB = VL ? 1 : BN128 * BK8 / 256;  // loads a thread makes per slice
-    constexpr int QA = BMW * BK8 / 4;  // 16-byte pieces of an A slice (256 or 128)
+    constexpr int BK8 = VL ? 16 : 8;  // slice depth: 16 with 16-byte loads, 8 with scalar ones
+    constexpr int LA = VL ? 1 : BMW * BK8 / 256, LB = VL ? 1 : BN128 * BK8 / 256;  // scalar loads a thread per slice
+    constexpr int QA = BMW * BK8 / 4, QB = BN128 * BK8 / 4;  // 16-byte pieces of an A / B slice
+    constexpr int VA = (QA + 255) / 256, VB = QB / 256;        // ... a thread (A: 2 or 1, B: 2)
+    constexpr int PR = BK8 / 4;                                // pieces along k of one row
     __shared__ __align__(16) float As[2][BK8][BMW + PAD];
     __shared__ __align__(16) float Bs[2][BK8][BN128 + PAD];
     int const tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
@@ -115,35 +118,54 @@ __global__ void __launch_bounds__(256, 2) bgemm_wide(BgemmArgs a, int vec_c) {
     float* C = static_cast<float*>(a.C) + b * a.c_b + hq * a.c_h;
     int64_t const m0 = static_cast<int64_t>(blockIdx.y) * BMW, n0 = static_cast<int64_t>(blockIdx.x) * BN128;
     float ra[LA], rb[LB];
-    float4 va{}, vb{};
+    float4 va[VA], vb[VB];
+    // piece q of a slice: along k, row q / PR at k (q % PR) * 4; along m / n,
+    // k row q / (extent / 4) at (q % (extent / 4)) * 4
     auto load_vec = [&](int64_t k0) {
-        if (tid < QA) {
-            int64_t gm, gk;
-            if (a.a_k_unit) gm = m0 + tid / 2, gk = k0 + (tid % 2) * 4;
-            else gm = m0 + (tid % (BMW / 4)) * 4, gk = k0 + tid / (BMW / 4);
-            bool const in = a.a_k_unit ? (gm < a.M && gk < a.K) : (gk < a.K && gm < a.M);
-            va = in ? *reinterpret_cast<float4 const*>(A + gm * a.am + gk * a.ak) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        int64_t gn, gk;
-        if (a.b_k_unit) gn = n0 + tid / 2, gk = k0 + (tid % 2) * 4;
-        else gn = n0 + (tid % (BN128 / 4)) * 4, gk = k0 + tid / (BN128 / 4);
-        bool const in = gn < a.N && gk < a.K;
-        vb = in ? *reinterpret_cast<float4 const*>(B + gk * a.bk + gn * a.bn) : make_float4(0.f, 0.f, 0.f, 0.f);
-    };
-    auto store_vec = [&](int buf) {
-        if (tid < QA) {
-            if (a.a_k_unit) {
-                int const m = tid / 2, k = (tid % 2) * 4;
-                As[buf][k][m] = va.x; As[buf][k + 1][m] = va.y; As[buf][k + 2][m] = va.z; As[buf][k + 3][m] = va.w;
-            } else {
-                *reinterpret_cast<float4*>(&As[buf][tid / (BMW / 4)][(tid % (BMW / 4)) * 4]) = va;
+#pragma unroll
+        for (int e = 0; e < VA; ++e) {
+            int const q = tid + 256 * e;
+            va[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (q < QA) {
+                int64_t gm, gk;
+                if (a.a_k_unit) gm = m0 + q / PR, gk = k0 + (q % PR) * 4;
+                else gm = m0 + (q % (BMW / 4)) * 4, gk = k0 + q / (BMW / 4);
+                if (gm < a.M && gk < a.K) va[e] = *reinterpret_cast<float4 const*>(A + gm * a.am + gk * a.ak);
             }
         }
-        if (a.b_k_unit) {
-            int const n = tid / 2, k = (tid % 2) * 4;
-            Bs[buf][k][n] = vb.x; Bs[buf][k + 1][n] = vb.y; Bs[buf][k + 2][n] = vb.z; Bs[buf][k + 3][n] = vb.w;
-        } else {
-            *reinterpret_cast<float4*>(&Bs[buf][tid / (BN128 / 4)][(tid % (BN128 / 4)) * 4]) = vb;
+#pragma unroll
+        for (int e = 0; e < VB; ++e) {
+            int const q = tid + 256 * e;
+            int64_t gn, gk;
+            if (a.b_k_unit) gn = n0 + q / PR, gk = k0 + (q % PR) * 4;
+            else gn = n0 + (q % (BN128 / 4)) * 4, gk = k0 + q / (BN128 / 4);
+            vb[e] = (gn < a.N && gk < a.K) ? *reinterpret_cast<float4 const*>(B + gk * a.bk + gn * a.bn)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_vec = [&](int buf) {
+#pragma unroll
+        for (int e = 0; e < VA; ++e) {
+            int const q = tid + 256 * e;
+            if (q >= QA) continue;
+            if (a.a_k_unit) {
+                int const m = q / PR, k = (q % PR) * 4;
+                As[buf][k][m] = va[e].x; As[buf][k + 1][m] = va[e].y; As[buf][k + 2][m] = va[e].z;
+                As[buf][k + 3][m] = va[e].w;
+            } else {
+                *reinterpret_cast<float4*>(&As[buf][q / (BMW / 4)][(q % (BMW / 4)) * 4]) = va[e];
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < VB; ++e) {
+            int const q = tid + 256 * e;
+            if (a.b_k_unit) {
+                int const n = q / PR, k = (q % PR) * 4;
+                Bs[buf][k][n] = vb[e].x; Bs[buf][k + 1][n] = vb[e].y; Bs[buf][k + 2][n] = vb[e].z;
+                Bs[buf][k + 3][n] = vb[e].w;
+            } else {
+                *reinterpret_cast<float4*>(&Bs[buf][q / (BN128 / 4)][(q % (BN128 / 4)) * 4]) = vb[e];
+            }
         }
     };
     auto load = [&](int64_t k0) {
