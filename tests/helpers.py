@@ -47,9 +47,9 @@ def assert_approx(actual, expected, eps, margin, what=""):
         raise AssertionError(f"{what}: {int((~ok).sum())} of {ok.size} elements outside tolerance: {detail}")
 
 
-# Tolerance of the attention path against the oracle (BASELINE: fp32 1e-4
-# max relative error, fp64 1e-11), written as |a-b| <= rtol*|b| + atol with an
-# absolute floor for values near zero.
+# Tolerance of the attention path against the oracle (fp32: 1e-4 relative,
+# fp64: 1e-11 relative, the parity targets of this path), written as
+# |a-b| <= rtol*|b| + atol with an absolute floor for values near zero.
 TOL = {np.float32: (1e-4, 1e-5), np.float64: (1e-11, 1e-12)}
 
 
