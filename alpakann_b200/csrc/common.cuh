@@ -120,7 +120,7 @@ __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + 
 // the GPU. A chunk of all pairs means one global longest-first order.
 inline int64_t head_chunk_for(int64_t bhs, int64_t q_tiles, int64_t kv_bytes_per_head, int resident) {
     int64_t chunk = kv_bytes_per_head > 0 ? (int64_t{32} << 20) / kv_bytes_per_head : bhs;
-    int64_t const waves = ceil_div(int64_t{2} * 148 * resident, q_tiles > 0 ? q_tiles : 1);
+    int64_t const waves = ceil_div(int64_t{2} * sm_count() * resident, q_tiles > 0 ? q_tiles : 1);
     if (chunk < waves) chunk = waves;
     if (chunk < 1) chunk = 1;
     if (chunk >= bhs) return bhs;

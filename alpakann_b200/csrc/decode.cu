@@ -240,7 +240,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicOr(&g_decode_error, ANN_DEVERR_WAIT_TIMEOUT);
-                for (int u = t + 1; u < min(total, t - 1 + kStages); ++u)  // drain copies in flight (bounded)
+                // drain every copy still in flight, tile t's own included, before
+                // the stages are reused as reduction scratch (each wait bounded)
+                for (int u = t; u < min(total, t - 1 + kStages); ++u)
                     mbar_wait_bounded(bar0 + (u % kStages) * 8, (u / kStages) & 1);
             }
             break;  // still joins the cluster barriers below

@@ -8,20 +8,29 @@
 // an allocator that must not be re-entered from this call site, a process
 // that is not allowed to grow its footprint. This variant allocates nothing:
 //  - the hidden activations live in one buffer that belongs to the library
-//    image itself (a file-scope __device__ array, created when the module is
-//    loaded on a device), so no call asks any allocator for memory;
+//    image itself (a file-scope __device__ array of kScratchBytes), so no call
+//    asks any allocator for memory;
 //  - its two GEMMs are this file's own kernels, not a library's.
-// The price is a size limit (kScratchBytes of hidden activations), plain
-// SIMT FMA GEMMs, slower than cuBLAS on large shapes, and kScratchBytes of
-// device memory that every GPU which loads the library holds until the process
-// exits, whether or not it ever calls this entry point.
+// The price is a size limit (kScratchBytes of hidden activations) and plain
+// SIMT FMA GEMMs, slower than cuBLAS on large shapes.
 //
-// The first call on a device looks the buffer's address up with
-// cudaGetSymbolAddress (no allocation) and remembers it; make that first call
-// before any stream capture. Nothing in the buffer has to start at zero: the
-// first kernel writes every element the second one reads. There is one buffer
-// per device: two calls whose kernels overlap on the GPU (different streams,
-// no ordering between them) race on it.
+// When the buffer is reserved: the CUDA runtime creates a module's __device__
+// arrays when it loads the module on a device. Under lazy module loading (the
+// default of CUDA 12 and what PyTorch sets) that is the first use of this
+// file's code on the device, i.e. the first call of ann_mlp_static_scratch
+// there; with CUDA_MODULE_LOADING=EAGER it is context creation. So the first
+// call on each device takes kScratchBytes of device memory and later calls
+// take none: make the first call at start-up, before a memory budget is fixed
+// and before any stream capture. The memory stays reserved until the process
+// exits.
+//
+// The first call on a device also looks the buffer's address up with
+// cudaGetSymbolAddress (no allocation) and keeps it for that device ordinal
+// for the life of the process; the kept address does not survive a
+// cudaDeviceReset of that device. Nothing in the buffer has to start at zero:
+// the first kernel writes every element the second one reads. There is one
+// buffer per device: two calls whose kernels overlap on the GPU (different
+// streams, no ordering between them) race on it.
 #include <mutex>
 
 #include "common.cuh"

@@ -1,6 +1,9 @@
 // tcgen05.cuh -- sm_100a tensor-core (tcgen05 / TMEM) and tensor-TMA helpers, inline PTX.
 //
-// Only CTA-local forms (cta_group::1, no multicast) are used.
+// cta_group::1 forms for single-SM kernels and cta_group::2 forms for kernels
+// on SM pairs (a 2-CTA cluster sharing each MMA). No TMA load here or anywhere
+// in the library uses cluster multicast; the only `.multicast::cluster` is
+// tcgen05.commit's mbarrier signal to both CTAs of a pair.
 #pragma once
 
 #include <cuda.h>

@@ -332,12 +332,18 @@ int ann_mlp_f64(ann_stream stream, const ann_view* input, const ann_view* wgate,
  * buffers per call. This call allocates nothing: the [batch, hidden]
  * activations go to a buffer that is part of the library image (8 MiB per
  * device, so batch * hidden * element size <= 8388608 bytes, else
- * ANN_EINVAL; every GPU that loads the library holds those 8 MiB until the
- * process exits, whether or not it calls this), and both GEMMs are the library's own kernels, not cuBLAS.
- * dtype: ANN_DTYPE_F32 or ANN_DTYPE_F64. The first call on each device looks
- * up the buffer's address (cudaGetSymbolAddress); make it before any stream
- * capture. Nothing in the buffer needs to start at zero. Calls whose work
- * overlaps on the GPU (different streams, no ordering) race on the buffer. */
+ * ANN_EINVAL), and both GEMMs are the library's own kernels, not cuBLAS.
+ * dtype: ANN_DTYPE_F32 or ANN_DTYPE_F64.
+ * The 8 MiB are reserved when the CUDA runtime loads this code on a device:
+ * under lazy module loading (CUDA 12's default, and what PyTorch sets) that is
+ * the FIRST call on each device, so make that call at start-up, before a
+ * memory budget is fixed and before any stream capture; later calls reserve
+ * nothing, and the memory stays held until the process exits. The first call
+ * on a device also looks up the buffer's address (cudaGetSymbolAddress) and
+ * keeps it for that device for the life of the process; it does not survive a
+ * cudaDeviceReset. Nothing in the buffer needs to start at zero. Calls whose
+ * work overlaps on the GPU (different streams, no ordering) race on the
+ * buffer. */
 int ann_mlp_static_scratch(ann_stream stream, int32_t dtype, const ann_view* input, const ann_view* wgate,
                            const ann_view* wup, const ann_view* wdown, const ann_view* output);
 

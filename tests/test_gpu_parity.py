@@ -468,8 +468,9 @@ def test_embedding_rms_norm_fused_equals_two_launches(ann, T, H):
 @pytest.mark.parametrize("rope", [False, True])
 def test_kv_cache_append(ann, T, rope):
     """New rows land at [position, position + Tn) of a layer of an LBHTD cache,
-    everything else untouched; with RoPE tables K equals ropeInPlace + append, bit
-    for bit, and V is copied as is."""
+    everything else untouched; with RoPE tables K equals ropeInPlace + append and
+    the oracle's rope (onAcc/internal/nn/rope.hpp:35-46), bit for bit, and V is
+    copied as is."""
     import torch
     g = rng(31)
     L, B, Hkv, Tcap, D, Tn, pos = 2, 3, 4, 40, 64, 5, 17
@@ -484,6 +485,8 @@ def test_kv_cache_append(ann, T, rope):
         kr = dev(kn)
         ann.onHost.nn.ropeInPlace(queue, None, kr, dev(cos), dev(sin), ann.RopeLayout.BTHD, pos)
         want_k = host(kr)
+        oracle_k = oracle.rope(kn, cos, sin, np.empty_like(kn), 0, pos)
+        assert np.array_equal(want_k, oracle_k)
     else:
         ann.onHost.nn.kvCacheAppend(queue, None, dev(kn), dev(vn), ck[1], cv[1], pos)
         want_k = kn
