@@ -59,6 +59,8 @@ SIGNATURES = {
     "ann_fill": ([_S, _P, _i32, ctypes.c_void_p], ctypes.c_int),
     "ann_mlp_forward_workspace_bytes": ([_P, _i32, _P, _P, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64)],
                                         ctypes.c_int),
+    "ann_signal_barrier": ([_S, ctypes.c_void_p, ctypes.c_void_p, _i32, _i32, _u32, ctypes.c_uint64],
+                           ctypes.c_int),
     "ann_sha256_file": ([ctypes.c_char_p, ctypes.c_char_p], ctypes.c_int),
     "ann_sha256_bytes": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p], ctypes.c_int),
     "ann_load_binary_tensor": ([_S, ctypes.c_char_p, ctypes.POINTER(AnnTensorSpec), ctypes.c_size_t,
@@ -95,6 +97,9 @@ for _sfx, _ft in _f.items():
         f"ann_mlp_{_sfx}": ([_S, _P, _P, _P, _P, _P, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
         f"ann_attention_decode_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32], ctypes.c_int),
         f"ann_attention_prefill_{_sfx}": ([_S, _P, _P, _P, _P, _ft, _u32, _i32, _i32], ctypes.c_int),
+        f"ann_attention_decode_mirror_{_sfx}": ([_S, _P, _P, _P, _P, ctypes.c_void_p, _ft, _u32, _i32], ctypes.c_int),
+        f"ann_attention_prefill_mirror_{_sfx}": ([_S, _P, _P, _P, _P, ctypes.c_void_p, _ft, _u32, _i32, _i32],
+                                                 ctypes.c_int),
     })
 
 for _name, (_args, _res) in SIGNATURES.items():

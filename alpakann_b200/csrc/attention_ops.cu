@@ -13,6 +13,14 @@
 #include "common.cuh"
 
 namespace ann {
+
+// fp32 on the tensor cores (attention_tc.cu); `handled` = false when the
+// shapes do not allow it and the FP32-pipe kernels below run instead
+int scores_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& s, uint32_t g, int layout,
+                  bool& handled);
+int apply_tc_f32(ann_stream stream, const Dims& p, const Dims& v, const Dims& o, uint32_t g, int layout,
+                 bool& handled);
+
 namespace {
 
 struct BgemmArgs {
@@ -455,6 +463,11 @@ int attention_scores(ann_stream stream, const ann_view* q_v, const ann_view* k_v
         k.ext[head] <= (Hq - 1) / static_cast<int64_t>(g) || k.ext[3] < D)
         return fail(ANN_EINVAL, "attentionScores: Q %s / K %s do not cover scores %s.", extents_str(q).c_str(),
                     extents_str(k).c_str(), extents_str(s).c_str());
+    if constexpr (sizeof(T) == 4) {
+        bool handled = false;
+        int const rc = scores_tc_f32(stream, q, k, s, g, layout, handled);
+        if (handled || rc != ANN_OK) return rc;
+    }
     BgemmArgs a{};
     a.A = q.data;
     a.B = k.data;
@@ -498,6 +511,11 @@ int attention_apply(ann_stream stream, const ann_view* p_v, const ann_view* v_v,
         v.ext[head] <= (Hq - 1) / static_cast<int64_t>(g) || v.ext[3] < D)
         return fail(ANN_EINVAL, "attentionApply: probs %s / values %s do not cover out %s.", extents_str(p).c_str(),
                     extents_str(v).c_str(), extents_str(o).c_str());
+    if constexpr (sizeof(T) == 4) {
+        bool handled = false;
+        int const rc = apply_tc_f32(stream, p, v, o, g, layout, handled);
+        if (handled || rc != ANN_OK) return rc;
+    }
     BgemmArgs a{};
     a.A = p.data;
     a.B = v.data;

@@ -94,6 +94,8 @@ int ann_take_device_error(ann_stream stream, uint32_t* bits) {
     ANN_TRY(ann::take_rms_error(s, &value));
     ANN_TRY(ann::take_prefill_f64_error(s, &value));
     ANN_TRY(ann::take_softmax_error(s, &value));
+    ANN_TRY(ann::take_multicast_error(s, &value));
+    ANN_TRY(ann::take_attention_tc_error(s, &value));
     *bits = value;
     return ANN_OK;
 }

@@ -35,6 +35,8 @@ int take_selftest_error(cudaStream_t s, uint32_t* bits);
 int take_rms_error(cudaStream_t s, uint32_t* bits);
 int take_prefill_f64_error(cudaStream_t s, uint32_t* bits);
 int take_softmax_error(cudaStream_t s, uint32_t* bits);
+int take_multicast_error(cudaStream_t s, uint32_t* bits);
+int take_attention_tc_error(cudaStream_t s, uint32_t* bits);
 
 // ---------------------------------------------------------------------------
 // Views: ann_view with byte pitches -> element strides, validated.

@@ -35,6 +35,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "multimem.cuh"
 #include "reduce.cuh"
 #include "tma.cuh"
 
@@ -57,6 +58,7 @@ struct DecodeArgs {
     const void* k;
     const void* v;
     void* out;
+    void* mirror;                // multicast address of out[0] (stores reach every rank's copy), or null
     int64_t q_b, q_t, q_h;       // element strides of Q (unit stride along d)
     int64_t o_b, o_t, o_h, o_d;  // element strides of out
     int64_t k_b, k_h, k_t;       // element strides of K by batch, kv head, token
@@ -313,14 +315,19 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
             *reinterpret_cast<V*>(red + warp * D + (pv_vec + 32 * m) * C::NV) = acc[m];
     }
     __syncthreads();
-    T* out = static_cast<T*>(a.out) + b * a.o_b + tq * a.o_t + hq * a.o_h;
+    int64_t const out_off = b * a.o_b + tq * a.o_t + hq * a.o_h;
+    T* out = static_cast<T*>(a.out) + out_off;
+    T* mout = a.mirror ? static_cast<T*>(a.mirror) + out_off : nullptr;
     if (a.splits == 1) {
         for (int d = tid; d < D; d += kThreads) {
             T s{};
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) s += red[w * D + d];
-            out[d * a.o_d] = l_run > T{} ? s / l_run : T{};
+            T const val = l_run > T{} ? s / l_run : T{};
+            if (mout) mc::store(mout + d * a.o_d, val);
+            else out[d * a.o_d] = val;
         }
+        if (mout) __threadfence_system();  // performed at system scope before the CTA retires
         return;
     }
     for (int d = tid; d < D; d += kThreads) {
@@ -350,8 +357,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
             L += w * px[D + 1];
             o += w * px[lo + tid];
         }
-        out[(lo + tid) * a.o_d] = L > T{} ? o / L : T{};
+        T const val = L > T{} ? o / L : T{};
+        if (mout) mc::store(mout + (lo + tid) * a.o_d, val);
+        else out[(lo + tid) * a.o_d] = val;
     }
+    if (mout) __threadfence_system();  // performed at system scope before the CTA retires
     cluster.sync();  // peers' shared memory must outlive the reads above
 }
 
@@ -465,7 +475,7 @@ int launch(ann_stream stream, DecodeArgs& a, T scale) {
 
 template <typename T>
 int decode(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const ann_view* v_v, const ann_view* o_v,
-           T scale, uint32_t g, int layout) {
+           T scale, uint32_t g, int layout, void* mirror = nullptr) {
     if (g == 0u) return fail(ANN_EINVAL, "attention decode requires queriesPerKvGroup > 0.");
     if (layout != ANN_LAYOUT_BTHD && layout != ANN_LAYOUT_BHTD)
         return fail(ANN_EINVAL, "attention decode: invalid kv layout.");
@@ -501,6 +511,9 @@ int decode(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const an
     a.k = k.data;
     a.v = v.data;
     a.out = o.data;
+    a.mirror = mirror;
+    if (mirror != nullptr && !aligned(mirror, sizeof(T)))
+        return fail(ANN_EINVAL, "attention decode: the output mirror is misaligned.");
     a.q_b = q.str[0];
     a.q_t = q.str[1];
     a.q_h = q.str[2];
@@ -556,6 +569,24 @@ int ann_attention_decode_f64(ann_stream s, const ann_view* q, const ann_view* k,
                              const ann_view* out, double scale, uint32_t g, int32_t layout) {
     ANN_API_BEGIN
     return ann::decode<double>(s, q, k, v, out, scale, g, layout);
+    ANN_API_END
+}
+
+int ann_attention_decode_mirror_f32(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
+                                    const ann_view* out, void* out_mirror, float scale, uint32_t g,
+                                    int32_t layout) {
+    ANN_API_BEGIN
+    if (out_mirror == nullptr) return ann::fail(ANN_EINVAL, "attention decode: the output mirror is NULL.");
+    return ann::decode<float>(s, q, k, v, out, scale, g, layout, out_mirror);
+    ANN_API_END
+}
+
+int ann_attention_decode_mirror_f64(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
+                                    const ann_view* out, void* out_mirror, double scale, uint32_t g,
+                                    int32_t layout) {
+    ANN_API_BEGIN
+    if (out_mirror == nullptr) return ann::fail(ANN_EINVAL, "attention decode: the output mirror is NULL.");
+    return ann::decode<double>(s, q, k, v, out, scale, g, layout, out_mirror);
     ANN_API_END
 }
 

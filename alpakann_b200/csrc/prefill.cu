@@ -33,9 +33,9 @@ namespace ann {
 int prefill_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
                    uint32_t g, int layout, int causal, bool& handled);
 int prefill_tc_pair_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
-                        uint32_t g, int layout, int causal, bool& handled);
+                        uint32_t g, int layout, int causal, bool& handled, void* mirror);
 int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, double scale,
-                    uint32_t g, int layout, int causal, bool& handled);
+                    uint32_t g, int layout, int causal, bool& handled, void* mirror);
 
 namespace {
 
@@ -333,7 +333,7 @@ int launch(ann_stream stream, PrefillArgs& a, T scale, int64_t batch_heads) {
 
 template <typename T>
 int prefill(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const ann_view* v_v, const ann_view* o_v,
-            T scale, uint32_t g, int layout, int causal) {
+            T scale, uint32_t g, int layout, int causal, void* mirror = nullptr) {
     if (g == 0u) return fail(ANN_EINVAL, "attention prefill requires queriesPerKvGroup > 0.");
     if (layout != ANN_LAYOUT_BTHD && layout != ANN_LAYOUT_BHTD)
         return fail(ANN_EINVAL, "attention prefill: invalid kv layout.");
@@ -364,15 +364,20 @@ int prefill(ann_stream stream, const ann_view* q_v, const ann_view* k_v, const a
     {  // fp32: tcgen05 3xTF32 kernel on SM pairs, else on single SMs; fp64: FP64 tensor-core (DMMA) kernel
         bool handled = false;
         int rc;
+        if (mirror != nullptr && !aligned(mirror, sizeof(T)))
+            return fail(ANN_EINVAL, "attention prefill: the output mirror is misaligned.");
         if constexpr (sizeof(T) == 4) {
             rc = ANN_OK;
-            if (!std::getenv("ANN_PREFILL_FMA") || std::getenv("ANN_PREFILL_FMA")[0] != '1')
-                rc = prefill_tc_pair_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
-            if (!handled && rc == ANN_OK)
+            if (mirror || !std::getenv("ANN_PREFILL_FMA") || std::getenv("ANN_PREFILL_FMA")[0] != '1')
+                rc = prefill_tc_pair_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled, mirror);
+            if (!handled && rc == ANN_OK && mirror == nullptr)
                 rc = prefill_tc_f32(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
         } else
-            rc = prefill_mma_f64(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled);
+            rc = prefill_mma_f64(stream, q, k, v, o, scale, g, layout, causal ? 1 : 0, handled, mirror);
         if (handled || rc != ANN_OK) return rc;
+        if (mirror != nullptr)
+            return fail(ANN_ENOTSUP, "attention prefill: the multicast output needs the tensor-core kernels "
+                                     "(head dim 64 or 128).");
     }
     PrefillArgs a{};
     a.q = q.data;
@@ -430,6 +435,24 @@ int ann_attention_prefill_f64(ann_stream s, const ann_view* q, const ann_view* k
                               const ann_view* out, double scale, uint32_t g, int32_t layout, int32_t causal) {
     ANN_API_BEGIN
     return ann::prefill<double>(s, q, k, v, out, scale, g, layout, causal);
+    ANN_API_END
+}
+
+int ann_attention_prefill_mirror_f32(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
+                                     const ann_view* out, void* out_mirror, float scale, uint32_t g, int32_t layout,
+                                     int32_t causal) {
+    ANN_API_BEGIN
+    if (out_mirror == nullptr) return ann::fail(ANN_EINVAL, "attention prefill: the output mirror is NULL.");
+    return ann::prefill<float>(s, q, k, v, out, scale, g, layout, causal, out_mirror);
+    ANN_API_END
+}
+
+int ann_attention_prefill_mirror_f64(ann_stream s, const ann_view* q, const ann_view* k, const ann_view* v,
+                                     const ann_view* out, void* out_mirror, double scale, uint32_t g,
+                                     int32_t layout, int32_t causal) {
+    ANN_API_BEGIN
+    if (out_mirror == nullptr) return ann::fail(ANN_EINVAL, "attention prefill: the output mirror is NULL.");
+    return ann::prefill<double>(s, q, k, v, out, scale, g, layout, causal, out_mirror);
     ANN_API_END
 }
 

@@ -23,13 +23,14 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "multimem.cuh"
 #include "reduce.cuh"
 #include "tma.cuh"
 
 namespace ann {
 
 int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, double scale,
-                    uint32_t g, int layout, int causal, bool& handled);
+                    uint32_t g, int layout, int causal, bool& handled, void* mirror);
 int take_prefill_f64_error(cudaStream_t s, uint32_t* bits);
 
 namespace {
@@ -63,6 +64,7 @@ struct F64Args {
     const double* k;
     const double* v;
     double* out;
+    double* mirror;  // multicast address of out[0] (every O store goes to all ranks' copies), or null
     int64_t q_b, q_t, q_h;
     int64_t o_b, o_t, o_h, o_d;
     int64_t k_b, k_h, k_t;
@@ -249,18 +251,27 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         }
         return;
     }
-    double* obase = a.out + b * a.o_b + q0 * a.o_t + hq * a.o_h;
+    int64_t const obase_off = b * a.o_b + q0 * a.o_t + hq * a.o_h;
+    double* obase = a.out + obase_off;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         int const r = r0 + 8 * h;
         if (r >= q_rows) continue;
         double const inv = l_run[h] > 0.0 ? 1.0 / l_run[h] : 0.0;
         double* orow = obase + r * a.o_t;
+        double* mrow = a.mirror ? a.mirror + obase_off + r * a.o_t : nullptr;
 #pragma unroll
         for (int n = 0; n < NO; ++n) {
             int const d = 8 * n + 2 * t;
             double const x0 = o[n][2 * h] * inv, x1 = o[n][2 * h + 1] * inv;
-            if (a.o_pairs) {
+            if (mrow) {
+                if (a.o_pairs) {
+                    mc::store(mrow + d, make_double2(x0, x1));
+                } else {
+                    mc::store(mrow + d * a.o_d, x0);
+                    mc::store(mrow + (d + 1) * a.o_d, x1);
+                }
+            } else if (a.o_pairs) {
                 *reinterpret_cast<double2*>(orow + d) = make_double2(x0, x1);
             } else {
                 orow[d * a.o_d] = x0;
@@ -268,6 +279,9 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
             }
         }
     }
+    // the multicast stores are performed at system scope before the CTA
+    // retires (the barrier that follows the kernel publishes them)
+    if (a.mirror) __threadfence_system();
 }
 
 template <int D, int BN>
@@ -303,10 +317,10 @@ int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads)
 // fp64 prefill on the FP64 tensor cores for D 64 / 128 (the caller has checked
 // unit-stride, 16-byte aligned Q/K/V rows); `handled` = false otherwise.
 int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, double scale,
-                    uint32_t g, int layout, int causal, bool& handled) {
+                    uint32_t g, int layout, int causal, bool& handled, void* mirror) {
     handled = false;
     if (const char* env = std::getenv("ANN_PREFILL_FMA"))
-        if (env[0] == '1') return ANN_OK;
+        if (env[0] == '1' && mirror == nullptr) return ANN_OK;
     int64_t const D = q.ext[3];
     if (D != 64 && D != 128) return ANN_OK;
     int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
@@ -315,6 +329,7 @@ int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims&
     a.k = static_cast<const double*>(k.data);
     a.v = static_cast<const double*>(v.data);
     a.out = static_cast<double*>(o.data);
+    a.mirror = static_cast<double*>(mirror);
     a.q_b = q.str[0];
     a.q_t = q.str[1];
     a.q_h = q.str[2];
@@ -323,7 +338,7 @@ int prefill_mma_f64(ann_stream stream, const Dims& q, const Dims& k, const Dims&
     a.o_h = o.str[2];
     a.o_d = o.str[3];
     a.o_pairs = o.str[3] == 1 && reinterpret_cast<uintptr_t>(o.data) % 16 == 0 && o.str[0] % 2 == 0 &&
-                o.str[1] % 2 == 0 && o.str[2] % 2 == 0;
+                o.str[1] % 2 == 0 && o.str[2] % 2 == 0 && (mirror == nullptr || aligned(mirror, 16));
     a.k_b = k.str[0];
     a.k_h = k.str[head];
     a.k_t = k.str[tok];

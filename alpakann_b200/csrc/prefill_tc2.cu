@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "multimem.cuh"
 #include "reduce.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
@@ -32,7 +33,7 @@
 namespace ann {
 
 int prefill_tc_pair_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
-                        uint32_t g, int layout, int causal, bool& handled);
+                        uint32_t g, int layout, int causal, bool& handled, void* mirror);
 int take_prefill_tc2_error(cudaStream_t s, uint32_t* bits);
 
 namespace {
@@ -78,6 +79,7 @@ struct PairCfg {
 
 struct PairArgs {
     void* out;
+    float* mirror;  // multicast address of out[0] (every O store goes to all ranks' copies), or null
     const float* q;
     const float* k;
     const float* v;
@@ -446,7 +448,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
             tc::fence_after_sync();
             float const l_sum = lx[r] + lx[r + kBM];
             float const inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-            float* orow = static_cast<float*>(a.out) + b * a.o_b + qi * a.o_t + hq * a.o_h;
+            int64_t const orow_off = b * a.o_b + qi * a.o_t + hq * a.o_h;
+            float* orow = static_cast<float*>(a.out) + orow_off;
+            float* mrow = a.mirror ? a.mirror + orow_off : nullptr;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
                 int const col = h * HD + 32 * c;
@@ -455,15 +459,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                 if (qi < a.Tq) {
                     if (a.o_vec) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(orow + col + j) =
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 const val =
                                 make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                            if (mrow) mc::store(mrow + col + j, val);
+                            else *reinterpret_cast<float4*>(orow + col + j) = val;
+                        }
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) orow[(col + j) * a.o_d] = ov[j] * inv;
+                        for (int j = 0; j < 32; ++j) {
+                            if (mrow) mc::store(mrow + (col + j) * a.o_d, ov[j] * inv);
+                            else orow[(col + j) * a.o_d] = ov[j] * inv;
+                        }
                     }
                 }
             }
+            // the multicast stores are performed at system scope before this
+            // CTA retires (the barrier that follows the kernel publishes them)
+            if (mrow) __threadfence_system();
         }
     }
 
@@ -482,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
 
 template <int D>
 int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
-                uint32_t g, int layout, int causal, bool& handled) {
+                uint32_t g, int layout, int causal, bool& handled, void* mirror) {
     using C = PairCfg<D>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
@@ -493,6 +506,7 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
     int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
     PairArgs a{};
     a.out = o.data;
+    a.mirror = static_cast<float*>(mirror);
     a.q = static_cast<const float*>(q.data);
     a.k = static_cast<const float*>(k.data);
     a.v = static_cast<const float*>(v.data);
@@ -510,7 +524,7 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
     a.o_h = o.str[2];
     a.o_d = o.str[3];
     a.o_vec = o.str[3] == 1 && reinterpret_cast<uintptr_t>(o.data) % 16 == 0 && o.str[0] % 4 == 0 &&
-              o.str[1] % 4 == 0 && o.str[2] % 4 == 0;
+              o.str[1] % 4 == 0 && o.str[2] % 4 == 0 && (mirror == nullptr || aligned(mirror, 16));
     a.Tq = q.ext[1];
     a.Tk = k.ext[tok];
     a.Hq = q.ext[2];
@@ -551,12 +565,12 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
 // 16-byte aligned Q/K/V rows); `handled` = false when it does not run (other D,
 // ANN_PREFILL_TC_PAIR=0, or no 2-CTA cluster of it can be resident).
 int prefill_tc_pair_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, const Dims& o, float scale,
-                        uint32_t g, int layout, int causal, bool& handled) {
+                        uint32_t g, int layout, int causal, bool& handled, void* mirror) {
     handled = false;
     if (const char* env = std::getenv("ANN_PREFILL_TC_PAIR"))
-        if (env[0] == '0') return ANN_OK;
-    if (q.ext[3] == 64) return launch_pair<64>(stream, q, k, v, o, scale, g, layout, causal, handled);
-    if (q.ext[3] == 128) return launch_pair<128>(stream, q, k, v, o, scale, g, layout, causal, handled);
+        if (env[0] == '0' && mirror == nullptr) return ANN_OK;
+    if (q.ext[3] == 64) return launch_pair<64>(stream, q, k, v, o, scale, g, layout, causal, handled, mirror);
+    if (q.ext[3] == 128) return launch_pair<128>(stream, q, k, v, o, scale, g, layout, causal, handled, mirror);
     return ANN_OK;
 }
 

@@ -263,6 +263,31 @@ def attentionPrefill(queue, exec, Q, K, V, out, scale=None, queriesPerKvGroup=1,
                                        int(queriesPerKvGroup), int(kvLayout), 1 if causal else 0))
 
 
+def attentionDecodeMirror(queue, exec, Q, K, V, out, outMirror, scale=None, queriesPerKvGroup=1, kvLayout=BHTD):
+    """attentionDecode whose results are stored through `outMirror`, the NVLink
+    multicast address of out's first element, into every rank's copy of the
+    output (include/ann_b200.h, multicast outputs); follow it with the buffer's
+    barrier on every rank."""
+    sfx = suffix(Q, K, V, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.shape[3])
+    check(fn("attention_decode_mirror", sfx)(handle(queue), ref(Q), ref(K), ref(V), ref(out),
+                                             ctypes.c_void_p(int(outMirror)), float(scale), int(queriesPerKvGroup),
+                                             int(kvLayout)))
+
+
+def attentionPrefillMirror(queue, exec, Q, K, V, out, outMirror, scale=None, queriesPerKvGroup=1, kvLayout=BTHD,
+                           causal=True):
+    """attentionPrefill with the results stored through the multicast address
+    `outMirror` into every rank's copy (see attentionDecodeMirror)."""
+    sfx = suffix(Q, K, V, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.shape[3])
+    check(fn("attention_prefill_mirror", sfx)(handle(queue), ref(Q), ref(K), ref(V), ref(out),
+                                              ctypes.c_void_p(int(outMirror)), float(scale), int(queriesPerKvGroup),
+                                              int(kvLayout), 1 if causal else 0))
+
+
 def raise_shape(msg):
     from .._capi import ANN_EINVAL, AnnShapeError
     raise AnnShapeError(ANN_EINVAL, msg)

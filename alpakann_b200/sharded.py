@@ -17,6 +17,13 @@ Prefill does the same per batch index: the fused causal prefill of batch b
 on this rank's heads, then an asynchronous all-gather of that [T,H/G,D] slab
 while batch b+1 computes, then re-assembly. (Chunks along T are not possible:
 the reference's top-left causal mask has no query offset.)
+
+Where the node supports NVLink multicast (NVSwitch NVLS), both steps gather
+without a collective instead (gather='multicast', alpakann_b200.mirror): the
+output lives in memory every rank has bound to one multicast object, each
+rank's kernel stores its heads through the multicast address into every
+rank's copy while it computes, and one signal barrier per step publishes
+them. No re-assembly pass: the stores land at their BTHD positions.
 """
 from dataclasses import dataclass
 from datetime import timedelta
@@ -90,14 +97,39 @@ def reassembly_views(gathered: torch.Tensor, out: torch.Tensor):
     return gathered.permute(1, 2, 0, 3, 4), out.view(B, T, G, Hl, D)
 
 
+def choose_gather(gather: str, world: int) -> str:
+    """'multicast' (outputs stored through an NVLink multicast address inside the
+    kernel, then a signal barrier), 'nccl' (all-gather + re-assembly) or, for
+    'auto', multicast where the node supports it."""
+    if world == 1:
+        return "none"
+    if gather == "auto":
+        from .mirror import MirrorBuffer
+        return "multicast" if MirrorBuffer.available() else "nccl"
+    if gather not in ("multicast", "nccl"):
+        raise ValueError(f"unknown gather {gather!r}")
+    return gather
+
+
 class HeadShardedDecode:
     """One decode step of the head-sharded path on this rank. `comm` is the
-    node's communicator (alpakann_b200.comm.Comm); world 1 needs none."""
+    node's communicator (alpakann_b200.comm.Comm), used by the NCCL gather;
+    world 1 needs none. gather: 'auto' | 'multicast' | 'nccl' (choose_gather)."""
 
-    def __init__(self, shard: HeadShard, B: int, D: int, dtype=torch.float32, device="cuda", comm=None):
-        if shard.world > 1 and comm is None:
+    def __init__(self, shard: HeadShard, B: int, D: int, dtype=torch.float32, device="cuda", comm=None,
+                 gather: str = "auto"):
+        self.gather = choose_gather(gather, shard.world)
+        if self.gather == "nccl" and comm is None:
             raise ValueError("a sharded step over several ranks needs a Comm")
         self.shard, self.B, self.D, self.comm = shard, B, D, comm
+        self.gathered = None
+        if self.gather == "multicast":
+            from .mirror import MirrorBuffer
+            self.mirror = MirrorBuffer((B, 1, shard.heads, D), dtype)
+            self.out = self.mirror.tensor
+            self.out_local = self.out[:, :, shard.head_slice, :]  # this rank's heads of every copy
+            self._out_mc = self.mirror.mirror_of(self.out_local)
+            return
         self.out_local = torch.empty((B, 1, shard.local_heads, D), dtype=dtype, device=device)
         self.out = torch.empty((B, 1, shard.heads, D), dtype=dtype, device=device)
         self.gathered = gathered_buffer(shard, B, 1, D, dtype, device) if shard.world > 1 else None
@@ -112,6 +144,11 @@ class HeadShardedDecode:
         onHost.nn.ropeInPlace(queue, None, q, knew, cos, sin, RopeLayout.BTHD, position)
         if self.shard.world == 1:
             onHost.nn.attentionDecode(queue, None, q, k_cache, v_cache, self.out, scale, g, AttentionKvLayout.BHTD)
+            return self.out
+        if self.gather == "multicast":
+            onHost.nn.attentionDecodeMirror(queue, None, q, k_cache, v_cache, self.out_local, self._out_mc, scale, g,
+                                            AttentionKvLayout.BHTD)
+            self.mirror.barrier(queue)
             return self.out
         onHost.nn.attentionDecode(queue, None, q, k_cache, v_cache, self.out_local, scale, g,
                                   AttentionKvLayout.BHTD)
@@ -129,10 +166,18 @@ class HeadShardedPrefill:
     at the end. `comm` as in HeadShardedDecode."""
 
     def __init__(self, shard: HeadShard, B: int, T: int, D: int, dtype=torch.float32, device="cuda", comm=None,
-                 streams: int = 4):
-        if shard.world > 1 and comm is None:
+                 streams: int = 4, gather: str = "auto"):
+        self.gather = choose_gather(gather, shard.world)
+        if self.gather == "nccl" and comm is None:
             raise ValueError("a sharded prefill over several ranks needs a Comm")
         self.shard, self.B, self.T, self.D, self.comm = shard, B, T, D, comm
+        if self.gather == "multicast":
+            from .mirror import MirrorBuffer
+            self.mirror = MirrorBuffer((B, T, shard.heads, D), dtype)
+            self.out = self.mirror.tensor
+            self.out_local = self.out[:, :, shard.head_slice, :]
+            self._out_mc = self.mirror.mirror_of(self.out_local)
+            return
         self.out = torch.empty((B, T, shard.heads, D), dtype=dtype, device=device)
         if shard.world > 1:
             self.out_local = torch.empty((B, T, shard.local_heads, D), dtype=dtype, device=device)
@@ -150,6 +195,11 @@ class HeadShardedPrefill:
         g = self.shard.heads // self.shard.kv_heads
         if self.shard.world == 1:
             onHost.nn.attentionPrefill(queue, None, q, k, v, self.out, scale, g, layout, causal)
+            return self.out
+        if self.gather == "multicast":  # every rank's heads land in every copy inside the kernel
+            onHost.nn.attentionPrefillMirror(queue, None, q, k, v, self.out_local, self._out_mc, scale, g, layout,
+                                             causal)
+            self.mirror.barrier(queue)
             return self.out
         caller = queue.stream if not isinstance(queue.stream, int) else torch.cuda.ExternalStream(queue.stream)
         comm_q = Queue(self._comm_stream)

@@ -53,6 +53,9 @@ def parse():
     p.add_argument("--prefill-only", metavar="B,T,H,D[,f64]", default=None,
                    help="run only the fused causal prefill on this shape (--steps launches) and print its time; "
                         "the small case the prefill ncu captures use")
+    p.add_argument("--decode-only", metavar="B,Tk,H,D", default=None,
+                   help="run only the fused decode kernel on this BHTD cache shape (--steps launches, fp32) and print "
+                        "its time; the small case the decode ncu captures use")
     p.add_argument("--ops", action="store_true",
                    help="measure only the HBM-bound ops (elementwise, bias+activation, reductions, maskedSoftmax) "
                         "and the MLP layers on 1 GiB operands; one JSON line per op")
@@ -98,16 +101,20 @@ def ncu_traffic(workload):
 
 
 class Clocks:
-    """nvidia-smi sampler (200 ms) for the timed region."""
+    """nvidia-smi sampler (every 50 ms) of the GPUs this run uses, started
+    before the timed region; stop() keeps the samples taken inside it."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, gpu_ids):
         self.samples = []
+        self.gpus = gpu_ids
+        sel = ["-i", ",".join(gpu_ids)] if gpu_ids else []
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(["nvidia-smi"] + sel + [f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
@@ -121,13 +128,13 @@ class Clocks:
     def stop(self, t0, t1):
         if self.proc is None:
             return None
-        time.sleep(0.3)
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        inside = [s for ts, s in self.samples if t0 - 0.2 <= ts <= t1 + 0.2]
+        inside = [s for ts, s in self.samples if t0 <= ts <= t1]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for s in inside:
@@ -140,36 +147,75 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": len(self.gpus) if self.gpus else "all",
+                "window_s": round(t1 - t0, 3), "interval_ms": 50}
+
+
+def gpu_ids(world):
+    """nvidia-smi ids (UUIDs) of the GPUs of every rank, if nvidia-smi accepts them."""
+    import torch
+    import torch.distributed as dist
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+    ids = [uuid]
+    if world > 1:
+        ids = [None] * world
+        dist.all_gather_object(ids, uuid)
+    try:
+        r = subprocess.run(["nvidia-smi", "-i", ",".join(ids), "--query-gpu=index", "--format=csv,noheader"],
+                           capture_output=True, text=True, timeout=20)
+        if r.returncode == 0 and len(r.stdout.split()) == len(ids):
+            return ids
+    except (OSError, subprocess.TimeoutExpired):
+        pass
+    return None
 
 
 # ------------------------------------------------------------------ CPU ---
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 class CpuSample:
     """The oracle's per-op decode pipeline (RoPE on Q and the new K row,
-    attentionScores, scale, softmax, attentionApply) on `batches` x `heads`
-    of the workload, inputs prepared once."""
+    attentionScores, scale, softmax, attentionApply) for ONE sequence of the
+    batch with all of its heads, inputs prepared once. One sample step decodes
+    one token; its K/V (2 GiB for the 32768-key cache) stream from DRAM on
+    every step, as the full batch would."""
 
-    def __init__(self, w, batches, heads):
+    def __init__(self, w):
         import numpy as np
 
         import oracle
         self.oracle = oracle
         B, Tk, H, D = w["B"], w["Tk"], w["H"], w["D"]
         g = np.random.default_rng(0)
-        self.q = g.standard_normal((batches, 1, heads, D)).astype(np.float32)
-        self.kn = g.standard_normal((batches, 1, heads, D)).astype(np.float32)
-        self.k = g.standard_normal((batches, heads, Tk, D)).astype(np.float32)
-        self.v = g.standard_normal((batches, heads, Tk, D)).astype(np.float32)
+        f32 = np.float32
+        self.q = g.standard_normal((1, 1, H, D), dtype=f32)
+        self.kn = g.standard_normal((1, 1, H, D), dtype=f32)
+        # K / V: N(0,1) draws for 4 heads, repeated over the others (the timed
+        # loops do not depend on the values; every head still has its own
+        # memory, so the whole sample streams from DRAM)
+        self.k = np.empty((1, H, Tk, D), f32)
+        self.v = np.empty((1, H, Tk, D), f32)
+        base = min(H, 4)
+        kb, vb = (g.standard_normal((base, Tk, D), dtype=f32) for _ in range(2))
+        for h in range(H):
+            self.k[0, h] = kb[h % base]
+            self.v[0, h] = vb[h % base]
         ang = np.arange(Tk + 1, dtype=np.float64)[:, None] * np.power(w["theta"], -2.0 * np.arange(D // 2) / D)[None]
-        self.cos, self.sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
-        self.s = np.empty((batches, heads, 1, Tk), np.float32)
+        self.cos, self.sin = np.cos(ang).astype(f32), np.sin(ang).astype(f32)
+        self.s = np.empty((1, H, 1, Tk), f32)
         self.p = np.empty_like(self.s)
         self.o = np.empty_like(self.q)
         self.rq, self.rk = np.empty_like(self.q), np.empty_like(self.kn)
-        self.scale = np.float32(1.0 / math.sqrt(D))
+        self.scale = f32(1.0 / math.sqrt(D))
         self.Tk = Tk
-        self.frac = (batches * heads) / (B * H)
-        self.desc = f"{batches} sequence(s) x {heads} head(s) of {B}x{H} per step, scaled by {1 / self.frac:g}"
+        self.kv_mib = 2 * self.k.nbytes / 2**20
+        self.desc = (f"one step = 1 of the {B} sequences with all {H} heads ({self.kv_mib:.0f} MiB of K/V streamed "
+                     f"from DRAM), the oracle's per-element loops on {{cores}} OpenMP threads; tokens/s = sequences/s")
 
     def step(self):
         o = self.oracle
@@ -180,19 +226,22 @@ class CpuSample:
         o.softmax(self.s, self.p, 3)
         o.attention_apply(self.p, self.v, self.o, 1, 1)
 
-    def time_full_steps(self, seconds=None, steps=None):
-        """Seconds per FULL workload step, from timing the sample."""
+    def time_steps(self, seconds=None, steps=None):
+        """Seconds per sample step (one token)."""
         reps, t0 = 0, time.perf_counter()
         while (steps is not None and reps < steps) or (seconds is not None and
                                                        (reps == 0 or time.perf_counter() - t0 < seconds)):
             self.step()
             reps += 1
-        return (time.perf_counter() - t0) / reps / self.frac, reps
+        return (time.perf_counter() - t0) / reps, reps
 
 
-def cpu_sample_for(w):
-    # c2: one sequence x all heads (1/8 of a step); c5: one sequence x one head (1/1024)
-    return CpuSample(w, 1, w["H"]) if w["Tk"] <= 4096 else CpuSample(w, 1, 1)
+def decode_config(w):
+    """The `config` both arms print (identical, so the two lines compare)."""
+    return {"workload": w["desc"], "batch": w["B"], "kv_len": w["Tk"], "heads": w["H"], "head_dim": w["D"],
+            "l2": "every step streams a K/V working set larger than the last-level cache (GPU: the KV cache, "
+                  "rotated over copies when a shard is smaller than 3x L2; CPU: one sequence's K/V, 2 GiB at "
+                  "32768 keys)"}
 
 
 def run_reference(args, w):
@@ -200,19 +249,19 @@ def run_reference(args, w):
     if rank != 0:
         return
     import oracle
-    oracle.set_threads(os.cpu_count() or 1)
-    smp = cpu_sample_for(w)
+    cores = host_cores()
+    oracle.set_threads(cores)
+    smp = CpuSample(w)
     for _ in range(args.warmup):
         smp.step()
-    step, _ = smp.time_full_steps(steps=args.steps)
-    value = w["B"] / step
+    step, _ = smp.time_steps(steps=args.steps)
+    value = 1.0 / step  # one token per sample step
     line = {"impl": "reference", "metric": "decode attn tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w["desc"], "batch": w["B"], "kv_len": w["Tk"], "heads": w["H"],
-                       "head_dim": w["D"]},
+            "config": decode_config(w),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
-                             "sample": smp.desc},
+                             "sample": smp.desc.format(cores=oracle.max_threads())},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -229,7 +278,7 @@ class DecodeBench:
         import alpakann_b200 as ann
         from alpakann_b200 import _capi
         from alpakann_b200.sharded import HeadShard, HeadShardedDecode
-        self.torch, self.capi, self.w = torch, _capi, w
+        self.torch, self.capi, self.w, self.ann = torch, _capi, w, ann
         self.world = world
         B, Tk, H, D = w["B"], w["Tk"], w["H"], w["D"]
         self.shard = HeadShard(rank, world, H, H)
@@ -247,6 +296,13 @@ class DecodeBench:
         self.cos = torch.from_numpy(np.cos(ang)).to(f32).cuda()
         self.sin = torch.from_numpy(np.sin(ang)).to(f32).cuda()
         self.scale = 1.0 / math.sqrt(D)
+        # the path starts with rmsNorm of the step's hidden states [B, d_model]
+        # (eps 1e-5, weight 1 + N(0, 0.02)), replicated on every rank
+        dm = H * D
+        self.hidden = torch.randn((B, dm), generator=gen, dtype=f32, device="cuda")
+        self.norm_w = 1.0 + 0.02 * torch.randn((dm,), generator=gen, dtype=f32, device="cuda")
+        self.normed = torch.empty_like(self.hidden)
+        self.eps = 1e-5
         self.sharded = HeadShardedDecode(self.shard, B, D, f32, "cuda", comm)
         self.comm = comm
         self.stream = torch.cuda.current_stream()
@@ -254,27 +310,41 @@ class DecodeBench:
         # descriptors built once: the device-timed loop only issues C-ABI calls
         V = _capi.view
         self.vq, self.vkn, self.vcos, self.vsin = V(self.q), V(self.knew), V(self.cos), V(self.sin)
+        self.vh, self.vw, self.vn = V(self.hidden), V(self.norm_w), V(self.normed)
         self.vout = V(self.sharded.out if world == 1 else self.sharded.out_local)
         self.vkv = [(V(k), V(v)) for k, v in self.caches]
-        if world > 1:
+        self.gather = self.sharded.gather
+        if self.gather == "nccl":
             self.vsrc, self.vdst = V(self.sharded._src), V(self.sharded._dst)
-        self.launches_per_step = 2 if world == 1 else 3  # rope, decode (+ re-assembly); NCCL's own kernel not counted
+        # rmsNorm, rope, decode (+ re-assembly after NCCL, whose own kernel is not
+        # counted; or the signal barrier after the multicast stores)
+        self.launches_per_step = 3 if world == 1 else 4
         self.gather_bytes = self.sharded.out_local.numel() * 4
         # pinned host buffers of the end-to-end step
         self.hq = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
         self.hk = torch.randn((B, 1, Hl, D), dtype=f32).pin_memory()
+        self.hh = torch.randn((B, dm), dtype=f32).pin_memory()
         self.hout = torch.empty((B, 1, H, D), dtype=f32).pin_memory()
+        self.h2d_bytes = (self.hq.numel() + self.hk.numel() + self.hh.numel()) * 4
+        self.d2h_bytes = self.hout.numel() * 4
 
     def step(self, i, ev=None):
         lib, R, sh, chk = self.capi.lib, ctypes.byref, self.stream.cuda_stream, self.capi.check
+        chk(lib.ann_rms_norm_f32(sh, R(self.vh), R(self.vw), R(self.vn), self.eps))
         chk(lib.ann_rope_inplace_f32(sh, R(self.vq), R(self.vkn), R(self.vcos), R(self.vsin), 0, self.w["Tk"]))
         vk, vv = self.vkv[i % self.copies]
         if ev is not None:
             ev[0].record(self.stream)
-        chk(lib.ann_attention_decode_f32(sh, R(self.vq), R(vk), R(vv), R(self.vout), self.scale, 1, 1))
+        if self.gather == "multicast":  # every rank's heads go to every rank's copy from inside the kernel
+            chk(lib.ann_attention_decode_mirror_f32(sh, R(self.vq), R(vk), R(vv), R(self.vout),
+                                                    ctypes.c_void_p(self.sharded._out_mc), self.scale, 1, 1))
+        else:
+            chk(lib.ann_attention_decode_f32(sh, R(self.vq), R(vk), R(vv), R(self.vout), self.scale, 1, 1))
         if ev is not None:
             ev[1].record(self.stream)
-        if self.world > 1:  # this library's NCCL all-gather, then the re-assembly kernel
+        if self.gather == "multicast":
+            self.sharded.mirror.barrier(self.queue)
+        elif self.gather == "nccl":  # this library's NCCL all-gather, then the re-assembly kernel
             chk(lib.ann_comm_allgather(self.comm._h, sh, self.sharded.out_local.data_ptr(),
                                        self.sharded.gathered.data_ptr(), self.gather_bytes))
             chk(lib.ann_scale_f32(sh, R(self.vsrc), 1.0, R(self.vdst)))
@@ -284,9 +354,52 @@ class DecodeBench:
         pinned host memory and the full output read back."""
         self.q.copy_(self.hq, non_blocking=True)
         self.knew.copy_(self.hk, non_blocking=True)
+        self.hidden.copy_(self.hh, non_blocking=True)
+        self.ann.onHost.nn.rmsNorm(self.queue, None, self.hidden, self.norm_w, self.normed, self.eps)
         k, v = self.caches[i % self.copies]
         out = self.sharded.step(self.queue, self.q, self.knew, k, v, self.cos, self.sin, self.w["Tk"], self.scale)
         self.hout.copy_(out, non_blocking=True)
+
+    def check_parity(self, seqs=2):
+        """One step, then the gathered output of `seqs` sequences (all heads of
+        every rank) against an fp64 recomputation on the device of each
+        rank's own heads (rotated q, that rank's K/V cache), and the rmsNorm
+        output against an fp64 recomputation. Tolerance |a-b| <= 1e-4|b| + 1e-5.
+        Returns the worst error over ranks, as a fraction of the tolerance."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        self.e2e_step(0)
+        torch.cuda.synchronize()
+        out = self.hout.clone()
+        k, v = self.caches[0]
+        f64 = torch.float64
+        B = self.w["B"]
+        sel = [0, B - 1][:seqs]
+        q = self.q[sel].to(f64)  # [s, 1, Hl, D], rotated in place by the step
+        ref = []
+        for j, b in enumerate(sel):
+            s_ = torch.einsum("hd,htd->ht", q[j, 0], k[b].to(f64)) * self.scale
+            p_ = torch.softmax(s_, dim=-1)
+            ref.append(torch.einsum("ht,htd->hd", p_, v[b].to(f64)))
+        ref = torch.stack(ref)[:, None]  # [s, 1, Hl, D]
+        if self.world > 1:
+            parts = [torch.empty_like(ref) for _ in range(self.world)]
+            dist.all_gather(parts, ref.contiguous())
+            ref = torch.cat(parts, dim=2)
+        got = out[sel].to(f64).cuda()
+        worst = float(((got - ref).abs() / (1e-4 * ref.abs() + 1e-5)).max())
+        x = self.hh.to(f64).cuda()
+        nref = x * torch.rsqrt((x * x).mean(dim=1, keepdim=True) + self.eps) * self.norm_w.to(f64)
+        worst_n = float(((self.normed.to(f64) - nref).abs() / (1e-4 * nref.abs() + 1e-5)).max())
+        t = torch.tensor([worst, worst_n], dtype=f64, device="cuda")
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return {"ok": bool(t[0] <= 1.0 and t[1] <= 1.0), "decode_err_over_tol": float(t[0]),
+                "rmsnorm_err_over_tol": float(t[1]),
+                "sample": f"{len(sel)} of {B} sequences x all {self.w['H']} heads of the gathered output and the "
+                          f"rmsNorm output, vs fp64 recomputation on each head's own rank; "
+                          f"tolerance |a-b| <= 1e-4 |b| + 1e-5"}
 
     def release(self):
         self.caches.clear()
@@ -311,27 +424,42 @@ def max_over_ranks(values, world):
     return [float(x) for x in t]
 
 
-def measure(bench, steps, warmup, world, rank, with_clocks):
+def measure(bench, steps, warmup, world, rank, clock_ids, min_region_s=1.0, max_repeats=60):
+    """W warm-up steps, then the timed loop of EXACTLY `steps` steps, each
+    repetition bracketed by a barrier and a device synchronize on both sides,
+    repeated until the timed repetitions add up to about `min_region_s` (so
+    that the clock sampler sees the GPUs busy). Device time per repetition =
+    CUDA events on the launching stream, max over ranks; the reported time is
+    the median repetition."""
     import torch
     for i in range(warmup):
         bench.step(i)
     barrier(world)
-    clocks = Clocks() if (with_clocks and rank == 0) else None
-    if clocks:
-        time.sleep(0.5)
+    clocks = Clocks(clock_ids) if (clock_ids is not None and rank == 0) else None
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
+    reps, kernel_s = [], []
     t_wall0 = time.time()
-    start.record(bench.stream)
-    for i in range(steps):
-        bench.step(i, kev[i])
-    end.record(bench.stream)
-    barrier(world)
+    repeats = max_repeats
+    r = 0
+    while r < repeats:
+        barrier(world)
+        start.record(bench.stream)
+        for i in range(steps):
+            bench.step(i, kev[i])
+        end.record(bench.stream)
+        barrier(world)
+        el, ks = max_over_ranks([start.elapsed_time(end) / 1e3,
+                                 sum(a.elapsed_time(b) for a, b in kev) / 1e3 / steps], world)
+        reps.append(el)
+        kernel_s.append(ks)
+        if r == 0:  # every rank takes the same repeat count
+            repeats = int(max(1, min(max_repeats, math.ceil(min_region_s / max(el, 1e-6)))))
+        r += 1
     t_wall1 = time.time()
-    elapsed = start.elapsed_time(end) / 1e3
-    kernel_s = sum(a.elapsed_time(b) for a, b in kev) / 1e3 / steps
     clk = clocks.stop(t_wall0, t_wall1) if clocks else None
+    elapsed = statistics.median(reps)
+    kernel = statistics.median(kernel_s)
 
     e2e_steps = max(1, min(steps, 1000))
     for i in range(min(warmup, 5)):
@@ -343,9 +471,14 @@ def measure(bench, steps, warmup, world, rank, with_clocks):
         bench.e2e_step(i)
     e1.record(bench.stream)
     barrier(world)
-    e2e_s = e0.elapsed_time(e1) / 1e3 / e2e_steps
-    elapsed, kernel_s, e2e_s = max_over_ranks([elapsed, kernel_s, e2e_s], world)
-    return elapsed, kernel_s, e2e_s, e2e_steps, clk
+    e2e_s = max_over_ranks([e0.elapsed_time(e1) / 1e3 / e2e_steps], world)[0]
+    return elapsed, kernel, e2e_s, e2e_steps, clk, len(reps), (min(reps), max(reps))
+
+
+GATHER_DESC = {"none": "", "nccl": " + NCCL all-gather + re-assembly",
+               "multicast": " + NVLink multicast stores of every rank's heads from inside the kernel + signal barrier"}
+GATHER_STEP = {"none": "", "nccl": " -> NCCL all-gather -> re-assembly into BTHD",
+               "multicast": " (its output stores reach every rank's copy through NVSwitch multicast) -> signal barrier"}
 
 
 PREFILL = {
@@ -374,8 +507,9 @@ def measure_prefill(name, world, rank, comm, reps=10):
     queue = ann.Queue()
     sc = 1.0 / math.sqrt(D)
     sharded = HeadShardedPrefill(HeadShard(rank, world, H, H), B, T, D, dt, "cuda", comm)
-    for _ in range(2):
-        sharded.run(queue, q, k, v, sc)
+    out = sharded.run(queue, q, k, v, sc)
+    parity = prefill_parity(out, q, k, v, sc, rank, world)
+    sharded.run(queue, q, k, v, sc)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -385,10 +519,12 @@ def measure_prefill(name, world, rank, comm, reps=10):
     barrier(world)
     t = max_over_ranks([e0.elapsed_time(e1) / 1e3 / reps], world)[0]
     flops = 4 * B * H * D * T * (T + 1) / 2
-    del q, k, v, sharded
+    gather = sharded.gather
+    del q, k, v, out, sharded
     torch.cuda.empty_cache()
     res = {"workload": p["desc"], "ms": t * 1e3, "tflops": flops / t / 1e12, "tokens_per_s": B * T / t,
-           "dtype": p["dtype"], "gathered": world > 1}
+           "dtype": p["dtype"], "gathered": world > 1, "parallelism": f"head-sharded x{world}"
+           + GATHER_DESC[gather].replace("decode", "prefill"), "parity": parity}
     if p["dtype"] == "f32":
         # 3xTF32: every useful flop costs three tf32 tensor flops
         pk, kind = tf32_peak()
@@ -403,6 +539,38 @@ def measure_prefill(name, world, rank, comm, reps=10):
                    fp64_peak_kind="cuBLAS DGEMM 4096^3, measured in this run",
                    frac_of_fp64_peak=res["tflops"] / world / pk)
     return res
+
+
+def prefill_parity(out, q, k, v, scale, rank, world, rows=(0, 1, 777, -1)):
+    """The gathered prefill output at a few query rows of every batch and head
+    against an fp64 recomputation on the device by the rank that owns the head
+    (causal, top-left mask). Tolerance |a-b| <= rtol |b| + atol with the fp32
+    (1e-4, 1e-5) or fp64 (1e-11, 1e-12) pair; returns the worst error as a
+    fraction of the tolerance, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    f64 = torch.float64
+    B, T, Hl, D = q.shape
+    rtol, atol = (1e-4, 1e-5) if q.dtype == torch.float32 else (1e-11, 1e-12)
+    idx = sorted({r % T for r in rows})
+    ref = torch.empty((B, len(idx), Hl, D), dtype=f64, device="cuda")
+    for j, i in enumerate(idx):
+        qi = q[:, i].to(f64)                                   # [B, Hl, D]
+        s_ = torch.einsum("bhd,bthd->bht", qi, k[:, :i + 1].to(f64)) * scale
+        ref[:, j] = torch.einsum("bht,bthd->bhd", torch.softmax(s_, -1), v[:, :i + 1].to(f64))
+    if world > 1:
+        parts = [torch.empty_like(ref) for _ in range(world)]
+        dist.all_gather(parts, ref)
+        ref = torch.cat(parts, dim=2)
+    got = out[:, idx].to(f64)
+    worst = ((got - ref).abs() / (rtol * ref.abs() + atol)).max()
+    if world > 1:
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    w = float(worst)
+    return {"ok": w <= 1.0, "err_over_tol": w,
+            "sample": f"query rows {idx} of every batch and all heads of the gathered output vs fp64 recomputation "
+                      f"on each head's own rank; tolerance |a-b| <= {rtol:g} |b| + {atol:g}"}
 
 
 def fp64_gemm_tflops():
@@ -452,6 +620,32 @@ def prefill_only(args):
     flops = 4 * B * H * D * T * (T + 1) / 2
     print(json.dumps({"prefill": args.prefill_only, "launches": args.steps, "ms": t * 1e3,
                       "tflops": flops / t / 1e12}), flush=True)
+
+
+def decode_only(args):
+    """--decode-only B,Tk,H,D: fused decode launches on one GPU, CUDA-event timed."""
+    import torch
+
+    import alpakann_b200 as ann
+    B, Tk, H, D = (int(x) for x in args.decode_only.split(","))
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn((B, 1, H, D), generator=gen, device="cuda")
+    k, v = (torch.randn((B, H, Tk, D), generator=gen, device="cuda") for _ in range(2))
+    o = torch.empty_like(q)
+    queue = ann.Queue()
+    lay = ann.AttentionKvLayout.BHTD
+    for _ in range(args.warmup):
+        ann.onHost.nn.attentionDecode(queue, None, q, k, v, o, None, 1, lay)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ann.onHost.nn.attentionDecode(queue, None, q, k, v, o, None, 1, lay)
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
+    alg = 2 * B * H * Tk * D * 4 + 2 * B * H * D * 4
+    print(json.dumps({"decode": args.decode_only, "launches": args.steps, "us": t * 1e6, "alg_bytes": alg,
+                      "GBps": alg / t / 1e9}), flush=True)
 
 
 def ops_only(args):
@@ -693,6 +887,9 @@ def main():
     if args.prefill_only:
         prefill_only(args)
         return
+    if args.decode_only:
+        decode_only(args)
+        return
     import torch
     import torch.distributed as dist
 
@@ -707,10 +904,13 @@ def main():
         join(rank, world, "nccl", timeout_s=120, device=torch.device("cuda", local))
         comm = Comm.from_torch(timeout_s=120)
     peak, peak_kind = peaks()
+    clock_ids = gpu_ids(world)
 
-    def run(wl, steps, warmup, with_clocks):
+    def run(wl, steps, warmup, with_clocks, check=False):
         bench = DecodeBench(WORKLOADS[wl], rank, world, comm)
-        elapsed, kernel_s, e2e_s, e2e_steps, clk = measure(bench, steps, warmup, world, rank, with_clocks)
+        parity = bench.check_parity() if check else None
+        elapsed, kernel_s, e2e_s, e2e_steps, clk, nrep, spread = measure(
+            bench, steps, warmup, world, rank, clock_ids if with_clocks else None)
         ww = WORKLOADS[wl]
         B, Tk, H, D = ww["B"], ww["Tk"], ww["H"], ww["D"]
         Hl = H // world
@@ -718,18 +918,20 @@ def main():
         res = dict(value=B * steps / elapsed, ms_per_step=elapsed / steps * 1e3, kernel_us=kernel_s * 1e6,
                    achieved=alg / kernel_s / 1e9, e2e=B / e2e_s, e2e_steps=e2e_steps, clk=clk,
                    copies=bench.copies, kv_mib=bench.kv_bytes / 2**20, launches=bench.launches_per_step * steps,
-                   h2d=2 * B * Hl * D * 4 * world, d2h=B * H * D * 4 * world, alg=alg)
+                   h2d=bench.h2d_bytes, d2h=bench.d2h_bytes, alg=alg, parity=parity, repeats=nrep,
+                   rep_ms=[x / steps * 1e3 for x in spread], gather=bench.gather)
         bench.release()
         return res
 
-    main_res = run(args.workload, args.steps, args.warmup, True)
+    main_res = run(args.workload, args.steps, args.warmup, True, check=True)
     extra = {}
     if not args.no_extra:
         other = "c2" if args.workload == "c5" else "c5"
-        o = run(other, max(10, args.steps if other == "c2" else args.steps // 16), args.warmup, False)
+        o = run(other, max(10, args.steps if other == "c2" else args.steps // 16), args.warmup, False, check=True)
         extra[other] = {"workload": WORKLOADS[other]["desc"], "value": o["value"], "unit": "tokens/s",
                         "ms_per_step": o["ms_per_step"], "kernel_us": o["kernel_us"],
-                        "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"]}
+                        "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"],
+                        "parity": o["parity"]}
         for name in ("c3", "c4"):
             extra[f"{name}_prefill"] = measure_prefill(name, world, rank, comm)
 
@@ -738,20 +940,24 @@ def main():
         cpu = None
         if world == 1:
             import oracle
-            smp = cpu_sample_for(w)
+            oracle.set_threads(host_cores())
+            smp = CpuSample(w)
             smp.step()
-            cpu_step, reps = smp.time_full_steps(seconds=args.cpu_seconds)
-            cpu = {"value": w["B"] / cpu_step, "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
-                   "sample": f"{smp.desc}; {reps} reps"}
+            cpu_step, reps = smp.time_steps(seconds=args.cpu_seconds)
+            cpu = {"value": 1.0 / cpu_step, "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
+                   "sample": smp.desc.format(cores=oracle.max_threads()) + f"; {reps} steps"}
         line = {
             "metric": "decode attn tokens/s", "value": r["value"], "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w["desc"], "batch": w["B"], "kv_len": w["Tk"], "heads": w["H"],
-                       "head_dim": w["D"],
-                       "parallelism": f"head-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-                       "l2": f"inputs larger than L2: {r['copies']} KV cache cop{'y' if r['copies'] == 1 else 'ies'} "
-                             f"of {r['kv_mib']:.0f} MiB per GPU, rotated per step"},
+            "config": decode_config(w),
+            "parallelism": f"head-sharded x{world}" + GATHER_DESC[r["gather"]],
+            "step": "rmsNorm [B, d_model] -> ropeInPlace(Q, new K row) -> fused decode over this rank's KV cache"
+                    + GATHER_STEP[r["gather"]],
+            "timing": {"repeats": r["repeats"], "each": f"{args.steps} steps between barriers + synchronize",
+                       "reported": "median repetition (max over ranks)", "min_max_ms_per_step": r["rep_ms"],
+                       "kv_cache_copies": r["copies"], "kv_mib_per_gpu": r["kv_mib"]},
+            "parity": r["parity"],
             "roofline": {"bound": "hbm", "achieved": r["achieved"], "peak": peak, "unit": "GB/s",
                          "frac": r["achieved"] / peak,
                          "traffic": ncu_traffic(args.workload) if world == 1 else None,
@@ -761,7 +967,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"], "steps": r["e2e_steps"]},
-            "gpu_launches": r["launches"],
+            "gpu_launches": r["launches"] * r["repeats"],
             "clocks": r["clk"],
             "extra": extra,
         }

@@ -416,6 +416,45 @@ int ann_comm_allgather(ann_comm comm, ann_stream stream, const void* send, void*
 int ann_comm_destroy(ann_comm comm);
 int ann_comm_abort(ann_comm comm);
 
+/* ---- head sharding without a collective: multicast ("mirror") outputs -------
+ * No reference counterpart. The full output [B,T,H,D] lives in memory that
+ * every rank of the node has bound to one NVLink multicast object (NVSwitch
+ * NVLS; e.g. torch symmetric memory). Each rank computes its heads into its
+ * slice `out` of its own copy, and `out_mirror` is the multicast address of
+ * out's first element: every result store is a multimem store that the switch
+ * writes into EVERY rank's copy, inside the producing kernel, so the gather
+ * overlaps the computation tile by tile and needs neither a collective nor a
+ * re-assembly pass. The kernels fence at system scope before they retire;
+ * ann_signal_barrier, enqueued after them on every rank, then publishes
+ * all ranks' results to the rank's later work. Same shapes and semantics as
+ * ann_attention_decode_* / ann_attention_prefill_* (prefill: the tensor-core
+ * kernels only, else ANN_ENOTSUP). Only stores go through the multicast
+ * address: nothing in this library loads from multicast or peer memory.
+ *
+ * ann_signal_barrier: `signals` = this rank's array of nranks uint32 words,
+ *   zero before the first call; `peer_signals` = a DEVICE array of nranks
+ *   pointers, entry p = rank p's array as addressed from this GPU (peer
+ *   mappings; entry `rank` = signals). Stores `epoch` into word `rank` of every
+ *   rank's array (release, system scope) and waits until every word of its
+ *   own array holds it (acquire). Every rank calls it in the same order with
+ *   epochs 1, 2, 3, ...; a wait that has not completed after timeout_ns sets
+ *   ANN_DEVERR_WAIT_TIMEOUT (ann_take_device_error) and the kernel returns.
+ *   nranks <= 32. Plain stores only: no multimem, no peer loads. */
+int ann_attention_decode_mirror_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                                    const ann_view* out, void* out_mirror, float scale,
+                                    uint32_t queries_per_kv_group, int32_t kv_layout);
+int ann_attention_decode_mirror_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                                    const ann_view* out, void* out_mirror, double scale,
+                                    uint32_t queries_per_kv_group, int32_t kv_layout);
+int ann_attention_prefill_mirror_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                                     const ann_view* out, void* out_mirror, float scale,
+                                     uint32_t queries_per_kv_group, int32_t kv_layout, int32_t causal);
+int ann_attention_prefill_mirror_f64(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
+                                     const ann_view* out, void* out_mirror, double scale,
+                                     uint32_t queries_per_kv_group, int32_t kv_layout, int32_t causal);
+int ann_signal_barrier(ann_stream stream, uint32_t* signals, uint32_t* const* peer_signals, int32_t nranks,
+                       int32_t rank, uint32_t epoch, uint64_t timeout_ns);
+
 /* ---- flat model artifacts: onHost/core/binary.hpp ------------------------
  * TensorSpec (binary.hpp:33-39): one tensor of a little-endian ".bin" file of
  * the neural-bunch model format v1. `shape` (row-major, informational) may be

@@ -54,3 +54,36 @@ def test_wait_that_completes_reports_nothing(ann):
     queue = ann.Queue()
     _capi.check(_capi.lib.ann_selftest_wait(queue.handle, 1, 5_000_000))
     assert queue.take_device_error() == 0
+
+
+def test_signal_barrier_single_rank_and_absent_rank(ann):
+    """ann_signal_barrier on one GPU, no multicast, no peer memory: with one
+    rank every epoch completes at once; with a second rank that never signals
+    (its word is a flag nothing sets) the bounded wait runs out, reports
+    ANN_DEVERR_WAIT_TIMEOUT, and the context stays usable."""
+    import ctypes
+
+    import torch
+    from alpakann_b200 import _capi
+    queue = ann.Queue()
+    assert queue.take_device_error() == 0
+    sig = torch.zeros(2, dtype=torch.int32, device="cuda")
+    one = torch.tensor([sig.data_ptr()], dtype=torch.int64, device="cuda")
+    for epoch in (1, 2, 3):
+        _capi.check(_capi.lib.ann_signal_barrier(queue.handle, ctypes.c_void_p(sig.data_ptr()),
+                                                 ctypes.c_void_p(one.data_ptr()), 1, 0, epoch, 1_000_000_000))
+    assert queue.take_device_error() == 0
+    assert sig[0].item() == 3
+    sig.zero_()
+    two = torch.tensor([sig.data_ptr(), sig.data_ptr()], dtype=torch.int64, device="cuda")
+    _capi.check(_capi.lib.ann_signal_barrier(queue.handle, ctypes.c_void_p(sig.data_ptr()),
+                                             ctypes.c_void_p(two.data_ptr()), 2, 0, 1, 20_000_000))  # 20 ms
+    assert queue.take_device_error() & _capi.ANN_DEVERR_WAIT_TIMEOUT
+    assert sig.tolist() == [1, 0]
+    x = torch.randn(1000, device="cuda")
+    y = torch.empty_like(x)
+    ann.onHost.ops.scale(queue, None, x, 2.0, y)
+    assert torch.equal(y, x * 2)
+    with pytest.raises(_capi.AnnShapeError):  # epochs start at 1
+        _capi.check(_capi.lib.ann_signal_barrier(queue.handle, ctypes.c_void_p(sig.data_ptr()),
+                                                 ctypes.c_void_p(one.data_ptr()), 1, 0, 0, 1_000_000))

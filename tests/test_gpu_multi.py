@@ -3,9 +3,11 @@
 On one GPU: a 1-rank communicator gathers exactly, and a rank whose peer never
 joins ends in ANN_ENCCL at its deadline (host-side bootstrap wait; no kernel
 runs). On two GPUs: the gathered decode and prefill outputs equal the 1-GPU
-outputs bit for bit -- the same kernels run the same per-head arithmetic, and the
-decode split is pinned (ANN_DECODE_SPLITS) so that both runs sum every row in
-the same order."""
+outputs bit for bit, through the NCCL all-gather and through the multicast
+stores (alpakann_b200.mirror) -- the same kernels run the same per-head
+arithmetic, and the decode split is pinned (ANN_DECODE_SPLITS) so that both
+runs sum every row in the same order. The signal barrier's bounded wait runs
+out on one GPU when no rank signals (no multicast, no peer memory)."""
 import math
 import os
 import socket
@@ -28,7 +30,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result):
+def _worker(rank, world, port, result, gather):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), ANN_DECODE_SPLITS="2")
     torch.cuda.set_device(rank)
     import torch.distributed as dist
@@ -51,9 +53,12 @@ def _worker(rank, world, port, result):
         sc = 1.0 / math.sqrt(D)
         shard = HeadShard(rank, world, H, Hkv)
         hs, ks = shard.head_slice, shard.kv_head_slice
-        dec = HeadShardedDecode(shard, B, D, torch.float32, "cuda", comm)
-        got = dec.step(ann.Queue(), q[:, :, hs].contiguous().cuda(), knew[:, :, hs].contiguous().cuda(),
-                       k[:, ks].contiguous().cuda(), v[:, ks].contiguous().cuda(), cos, sin, Tk, sc).cpu()
+        dec = HeadShardedDecode(shard, B, D, torch.float32, "cuda", comm, gather=gather)
+        res["gather"] = dec.gather
+        got = None
+        for _ in range(2):  # twice: the second step's barrier runs on the next epoch
+            got = dec.step(ann.Queue(), q[:, :, hs].contiguous().cuda(), knew[:, :, hs].contiguous().cuda(),
+                           k[:, ks].contiguous().cuda(), v[:, ks].contiguous().cuda(), cos, sin, Tk, sc).cpu()
         one = HeadShardedDecode(HeadShard(0, 1, H, Hkv), B, D, torch.float32, "cuda")
         ref = one.step(ann.Queue(), q.cuda(), knew.cuda(), k.cuda(), v.cuda(), cos, sin, Tk, sc).cpu()
         res["decode"] = bool(torch.equal(got, ref))
@@ -63,7 +68,7 @@ def _worker(rank, world, port, result):
             q, k, v = (torch.randn(B, T, H, D, generator=gen, dtype=dt) for _ in range(3))
             shard = HeadShard(rank, world, H, H)
             hs = shard.head_slice
-            sp = HeadShardedPrefill(shard, B, T, D, dt, "cuda", comm)
+            sp = HeadShardedPrefill(shard, B, T, D, dt, "cuda", comm, gather=gather)
             sc = 1.0 / math.sqrt(D)
             got = sp.run(ann.Queue(), *(x[:, :, hs].contiguous().cuda() for x in (q, k, v)), sc).cpu()
             ref = torch.empty(B, T, H, D, dtype=dt, device="cuda")
@@ -73,6 +78,8 @@ def _worker(rank, world, port, result):
         res["device_error"] = ann.Queue().take_device_error()
         result[rank] = res
     finally:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank leaves while another may still store into its memory
         comm.close()
         dist.destroy_process_group()
 
@@ -116,10 +123,23 @@ def test_comm_rank_that_never_joins_ends_in_enccl():
     assert seconds < 60
 
 
+def _multicast_available():
+    if not _two_gpus():
+        return False
+    from alpakann_b200.mirror import MirrorBuffer
+    return MirrorBuffer.available()
+
+
 @pytest.mark.skipif(not _two_gpus(), reason="needs 2 GPUs")
-def test_two_gpu_head_sharding_equals_one_gpu():
+@pytest.mark.parametrize("gather", ["nccl", "multicast"])
+def test_two_gpu_head_sharding_equals_one_gpu(gather):
+    """Both gathers: the NCCL all-gather + re-assembly, and the multicast
+    stores from inside the kernels + signal barrier (where the node has NVLink
+    multicast)."""
+    if gather == "multicast" and not _multicast_available():
+        pytest.skip("no NVLink multicast on this node")
     mgr = mp.get_context("spawn").Manager()
     result = mgr.dict()
-    mp.start_processes(_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
-    want = {"decode": True, "prefill_f32": True, "prefill_f64": True, "device_error": 0}
+    mp.start_processes(_worker, args=(2, _free_port(), result, gather), nprocs=2, join=True, start_method="spawn")
+    want = {"decode": True, "prefill_f32": True, "prefill_f64": True, "device_error": 0, "gather": gather}
     assert dict(result) == {0: want, 1: want}
