@@ -25,7 +25,7 @@
 //   row -> one bulk copy (cp.async.bulk, shared -> global) per row segment,
 //   so the 4-byte-per-thread scatter of row-per-thread TMEM reads never
 //   reaches global memory. Work unit: (batch*head, 256-row tile, key chunk).
-// apply_pair_kernel: 32-key chunks of P are loaded coalesced into shared
+// apply_pair_kernel: 64-key chunks of P are loaded coalesced into shared
 //   memory, read back one row per thread, split into hi / lo and stored into
 //   TMEM (the A operand); V chunks (each CTA half of the head dims, raw + lo,
 //   MN-major 32-byte-atom swizzle) two buffers deep; O accumulates in TMEM.
@@ -54,6 +54,7 @@ __device__ unsigned int g_atc_error;
 constexpr int kBM = 128;                    // rows per CTA
 constexpr int kRowThreads = 256;            // warps 0..7
 constexpr int kThreads = kRowThreads + 32;  // + warp 8 (MMA issuer)
+constexpr int kScThreads = kRowThreads + 64;  // scores: + warps 8 and 9 (even / odd key tiles)
 
 __device__ __forceinline__ float tf32_lo(float x) {
     return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
@@ -84,20 +85,6 @@ __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t b
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// 16 consecutive TMEM columns of this thread's lane (32x32b shape, x16)
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, float const (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15, %16};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-        "r"(__float_as_uint(v[15]))
-        : "memory");
-}
 
 // ============================================================================
 // attentionScores
@@ -141,7 +128,7 @@ struct ScArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
+__global__ void __launch_bounds__(kScThreads, 1) scores_pair_kernel(ScArgs a) {
     using C = ScCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -173,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
         for (int i = 0; i < 2; ++i) mbar_init(kready + 8 * i, C::ROW_ARRIVALS);
         for (int i = 0; i < 2; ++i) mbar_init(sfree + 8 * i, C::ROW_ARRIVALS);
         for (int i = 0; i < 2; ++i) mbar_init(sfull + 8 * i, 1);
-        mbar_init(drain, 1);
+        mbar_init(drain, 2);  // one final commit from each issuer
         fence_mbar_init();
         *abort = 0;
     }
@@ -186,9 +173,13 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
     tc::fence_after_sync();
     uint32_t const tmem = *slot;
 
-    if (warp == 8) {
+    if (warp >= 8) {
         // ============================ MMA issue (CTA 0) ============================
+        // Two issuers: warp 8 the even key tiles (K buffer 0, S buffer 0), warp 9
+        // the odd ones (buffer 1); each waits only on its own buffer's barriers,
+        // and one thread alone cannot issue as fast as the tensor pipe runs.
         if (lane == 0 && rank == 0) {
+            int const par = warp - 8;
             uint64_t const k_desc = tc::smem_desc(sbase + C::OFF_K, 16, 1024, tc::kSwizzle128B);
             auto at = [](uint64_t desc, uint32_t off) { return desc + static_cast<uint64_t>(off >> 4); };
             auto commit = [](uint32_t b_local) {
@@ -198,8 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
             auto wait = [&](uint32_t b_local, uint32_t parity) {
                 return mbar_wait_or_abort<true>(b_local, parity, abort);
             };
-            bool ok = n_t <= 0 || wait(qready, 0);
-            for (int t = 0; t < n_t && ok; ++t) {
+            bool ok = n_t <= par || wait(qready, 0);
+            for (int t = par; t < n_t && ok; t += 2) {
                 ok = wait(kready + 8 * (t & 1), (t >> 1) & 1) && (t < 2 || wait(sfree + 8 * (t & 1), ((t - 2) >> 1) & 1));
                 if (!ok) break;
                 tc::fence_after_sync();
@@ -327,11 +318,11 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
 // ============================================================================
 template <int D>
 struct ApCfg {
-    static constexpr int KC = 32;                // keys per chunk (MMA K = 4 x 8)
+    static constexpr int KC = 64;                // keys per chunk (MMA K = 8 x 8)
     static constexpr int VCOLS = D / 2;          // head dims of a V chunk held by this CTA
     static constexpr int TILE_V = KC * VCOLS * 4;  // bytes of V hi (or lo) per buffer
     static constexpr int BLK_V = KC * 128;       // one 32-float column block of V
-    static constexpr int TILE_P = kBM * KC * 4;  // raw P chunk, 128 rows x 128 bytes
+    static constexpr int TILE_P = kBM * KC * 4;  // raw P chunk, 128 rows x 256 bytes
     static constexpr int OFF_V = 0;              // buffer i: hi at 2*i*TILE_V, lo at + TILE_V
     static constexpr int OFF_P = 4 * TILE_V;     // buffer i at OFF_P + i*TILE_P
     static constexpr int OFF_BAR = OFF_P + 2 * TILE_P;
@@ -342,7 +333,7 @@ struct ApCfg {
     // >= 120 KB: one CTA per SM, so that its TMEM allocation never waits
     static constexpr int SMEM = USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024;
     static constexpr uint32_t O_COL = 0, P_HI = D, P_LO = D + 2 * KC;  // buffer b at + KC b
-    static constexpr uint32_t TMEM_COLS = 256;
+    static constexpr uint32_t TMEM_COLS = 512;
     static_assert(P_LO + 2 * KC <= TMEM_COLS, "TMEM budget");
     static constexpr uint32_t IDESC = tc::idesc_tf32(2 * kBM, D, true);
     static constexpr uint32_t ROW_ARRIVALS = 2 * kRowThreads;
@@ -436,11 +427,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
         int const r = tid & (kBM - 1), h = tid >> 7;
         uint32_t const lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
         int64_t const qi = q0 + r;
-        // P chunk: 128 rows x 32 keys, element e = i * 256 + tid is row e / 8,
-        // float4 e % 8 (coalesced: a warp reads four whole 128-byte row pieces)
-        constexpr int PERP = kBM * (C::KC / 4) / kRowThreads;  // 4
+        // P chunk: 128 rows x 64 keys, element e = i * 256 + tid is row e / 16,
+        // float4 e % 16 (coalesced: a warp reads two whole 256-byte row pieces)
+        constexpr int NC4 = C::KC / 4;                          // float4 per P row piece
+        constexpr int PERP = kBM * NC4 / kRowThreads;           // 8
         constexpr int NV4V = C::VCOLS / 4;
-        constexpr int PERV = C::KC * NV4V / kRowThreads;  // 1 (D 64) or 2 (D 128)
+        constexpr int PERV = C::KC * NV4V / kRowThreads;  // 2 (D 64) or 4 (D 128)
         static_assert(PERV >= 1, "V chunk per thread");
         float const* pbase = a.p + b * a.p_b + hq * a.p_h;
         float const* vbase = a.v + b * a.v_b + kvh * a.v_h + rank * C::VCOLS;
@@ -449,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
             int64_t const key0 = (c_begin + c) * C::KC;
 #pragma unroll
             for (int i = 0; i < PERP; ++i) {
-                int const e = i * kRowThreads + tid, row = e >> 3, c4 = e & 7;
+                int const e = i * kRowThreads + tid, row = e / NC4, c4 = e % NC4;
                 int64_t const qrow = q0 + row, key = key0 + c4 * 4;
                 rp[i] = (qrow < a.Tq && key < a.Tk)
                             ? __ldg(reinterpret_cast<float4 const*>(pbase + qrow * a.p_t + key))
@@ -467,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
             unsigned char* pb = smem + C::OFF_P + buf * C::TILE_P;
 #pragma unroll
             for (int i = 0; i < PERP; ++i) {
-                int const e = i * kRowThreads + tid, row = e >> 3, c4 = e & 7;
-                *reinterpret_cast<float4*>(pb + row * 128 + ((c4 ^ (row & 7)) << 4)) = rp[i];
+                int const e = i * kRowThreads + tid, row = e / NC4, c4 = e % NC4;
+                *reinterpret_cast<float4*>(pb + row * (C::KC * 4) + ((c4 ^ (row & 7)) << 4)) = rp[i];
             }
             unsigned char* hi = smem + C::OFF_V + buf * 2 * C::TILE_V;
 #pragma unroll
@@ -497,20 +489,20 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
             stage(buf);
             if (c + 1 < n_c) load(c + 1);
             row_sync();  // the whole P chunk is in shared memory
-            {  // this thread's 16 keys of row r: hi -> TMEM P_HI, lo -> TMEM P_LO
-                unsigned char const* prow = smem + C::OFF_P + buf * C::TILE_P + r * 128;
-                float hi[16], lo[16];
+            {  // this thread's 32 keys of row r: hi -> TMEM P_HI, lo -> TMEM P_LO
+                unsigned char const* prow = smem + C::OFF_P + buf * C::TILE_P + r * (C::KC * 4);
+                float hi[32], lo[32];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    int const c4 = 4 * h + j;
+                for (int j = 0; j < 8; ++j) {
+                    int const c4 = 8 * h + j;
                     float4 const x = *reinterpret_cast<float4 const*>(prow + ((c4 ^ (r & 7)) << 4));
                     float4 const y = tf32_lo(x);
                     hi[4 * j] = x.x, hi[4 * j + 1] = x.y, hi[4 * j + 2] = x.z, hi[4 * j + 3] = x.w;
                     lo[4 * j] = y.x, lo[4 * j + 1] = y.y, lo[4 * j + 2] = y.z, lo[4 * j + 3] = y.w;
                 }
-                uint32_t const col = C::KC * static_cast<uint32_t>(buf) + 16 * h;
-                tmem_st16(tmem + lane_off + C::P_HI + col, hi);
-                tmem_st16(tmem + lane_off + C::P_LO + col, lo);
+                uint32_t const col = C::KC * static_cast<uint32_t>(buf) + 32 * h;
+                tc::tmem_st32(tmem + lane_off + C::P_HI + col, hi);
+                tc::tmem_st32(tmem + lane_off + C::P_LO + col, lo);
             }
             tc::tmem_st_wait();
             tc::fence_before_sync();
@@ -554,7 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
 }
 
 template <typename K>
-int cluster_launch(K kernel, int smem, int64_t ctas, ann_stream stream, const char* what, auto const& args) {
+int cluster_launch(K kernel, int threads, int smem, int64_t ctas, ann_stream stream, const char* what,
+                   auto const& args) {
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute cl{};
     cl.id = cudaLaunchAttributeClusterDimension;
@@ -562,7 +555,7 @@ int cluster_launch(K kernel, int smem, int64_t ctas, ann_stream stream, const ch
     cl.val.clusterDim.y = 1;
     cl.val.clusterDim.z = 1;
     cfg.gridDim = dim3(static_cast<unsigned>(ctas));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = as_stream(stream);
     cfg.attrs = &cl;
@@ -602,7 +595,8 @@ int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
     a.chunks = static_cast<int>(ceil_div(a.k_tiles, best));
     int64_t const ctas = 2 * bhs * a.q_tiles * a.chunks;
     if (ctas > INT32_MAX) return fail(ANN_ENOTSUP, "attentionScores: grid too large.");
-    return cluster_launch(scores_pair_kernel<D>, C::SMEM, ctas, stream, "attentionScores (tensor cores)", a);
+    return cluster_launch(scores_pair_kernel<D>, kScThreads, C::SMEM, ctas, stream, "attentionScores (tensor cores)",
+                          a);
 }
 
 template <int D>
@@ -623,7 +617,7 @@ int launch_apply(ann_stream stream, ApArgs& a, int64_t bhs, bool can_split, void
     }
     int64_t const ctas = 2 * units * a.splits;
     if (ctas > INT32_MAX) return fail(ANN_ENOTSUP, "attentionApply: grid too large.");
-    return cluster_launch(apply_pair_kernel<D>, C::SMEM, ctas, stream, "attentionApply (tensor cores)", a);
+    return cluster_launch(apply_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionApply (tensor cores)", a);
 }
 
 bool rows16(const Dims& d, int unit_axis) {  // unit stride on `unit_axis`, 16-byte aligned rows

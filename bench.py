@@ -745,15 +745,17 @@ def ops_only(args):
                           "frac_of_hbm_peak": round(nbytes / t / 1e9 / peak, 3), "peak_GBps": peak,
                           "peak_kind": kind, "bytes_per_launch": nbytes}), flush=True)
     # the drop-in attentionScores / attentionApply (scores materialised, as the
-    # reference does): one c3-like slice, B 1, T 4096, 8 heads of 128, fp32,
-    # against the nominal FP32 SIMT peak (148 SMs x 128 lanes x 2 x 1965 MHz);
-    # a fixed shape (512 MiB of scores) whatever --ops-elems is
+    # reference does): one c3-like slice, B 1, T 4096, 8 heads of 128, fp32 on
+    # the tensor cores (3xTF32: three tf32 MMAs per useful product), against the
+    # 3xTF32 ceiling = measured tf32 rate / 3; a fixed shape (512 MiB of
+    # scores) whatever --ops-elems is
     Tq, Hs, Dh = 4096, 8, 128
     q4 = torch.randn((1, Tq, Hs, Dh), device=dev)
     k4 = torch.randn((1, Tq, Hs, Dh), device=dev)
     s4 = torch.empty((1, Hs, Tq, Tq), device=dev)
     o4 = torch.empty((1, Tq, Hs, Dh), device=dev)
-    simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    tf32, tf32_kind = tf32_peak()
+    ceiling = tf32 / 3
     flops = 2 * Hs * Tq * Tq * Dh
     for name, fn in ((f"attentionScores Q,K [1,{Tq},{Hs},{Dh}] -> S [1,{Hs},{Tq},{Tq}]",
                       lambda: nn.attentionScores(None, None, q4, k4, s4)),
@@ -761,7 +763,8 @@ def ops_only(args):
                       lambda: nn.attentionApply(None, None, s4, k4, o4))):
         t = timed(fn, reps=5, warm=2)
         print(json.dumps({"op": name, "dtype": "f32", "ms": round(t * 1e3, 3), "TFLOPs": round(flops / t / 1e12, 2),
-                          "frac_of_fp32_simt_nominal": round(flops / t / 1e12 / simt_peak, 3)}), flush=True)
+                          "frac_of_3xtf32_ceiling": round(flops / t / 1e12 / ceiling, 3),
+                          "ceiling_tflops": round(ceiling, 1), "ceiling_kind": tf32_kind + ", / 3"}), flush=True)
     del q4, k4, s4, o4
     # the same two ops in fp64 at the c4 prefill shape (B 2, T 1024, 16 heads
     # of 64), against the DGEMM rate cuBLAS reaches on this GPU

@@ -69,6 +69,24 @@ def assert_close(actual, expected, dtype, what=""):
                              f"(rtol {rtol}, atol {atol}, {int((err > bound).sum())} bad of {err.size})")
 
 
+def assert_dot_close(actual, expected, absdot, K, dtype, what=""):
+    """assert_close for contractions (sums of K products): on top of the
+    tolerance, each output may differ by the dot-product rounding bound
+    4 eps sqrt(K) sum|a b| (sum|a b| from the oracle on |a| and |b|), since sums
+    that cancel to near 0 round differently in any two summation orders (the
+    tensor-core kernels add in a different order from the reference's
+    sequential loop)."""
+    rtol, atol = tol_for(dtype)
+    actual = np.asarray(actual, dtype=np.float64)
+    expected = np.asarray(expected, dtype=np.float64)
+    err = np.abs(actual - expected)
+    bound = rtol * np.abs(expected) + atol + 4 * np.finfo(dtype).eps * np.sqrt(K) * np.asarray(absdot, np.float64)
+    if not (err <= bound).all():
+        i = np.unravel_index(np.argmax(err - bound), err.shape)
+        raise AssertionError(f"{what}: max violation at {i}: {actual[i]!r} vs {expected[i]!r} "
+                             f"({int((err > bound).sum())} bad of {err.size})")
+
+
 def rng(seed):
     return np.random.default_rng(seed)
 

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.helpers import assert_close, normal, rng, rope_tables
+from tests.helpers import assert_close, assert_dot_close, normal, rng, rope_tables
 
 pytestmark = pytest.mark.gpu
 
@@ -95,7 +95,8 @@ def test_prefill_block_small(ann, T):
     rs = np.empty((B, H, Tt, Tt), T)
     oracle.attention_scores(rq, rk, rs)
     hs = host(s)
-    assert_close(hs, rs, T, "scores")
+    absdot = oracle.attention_scores(np.abs(rq), np.abs(rk), np.empty_like(rs))
+    assert_dot_close(hs, rs, absdot, D, T, "scores")
 
     scale = T(1.0 / math.sqrt(D))
     ops.scale(q, None, s, scale, s)
@@ -114,8 +115,10 @@ def test_prefill_block_small(ann, T):
     o = empty((B, Tt, H, D), T)
     nn.attentionApply(q, None, p, V4, o)
     ro = np.empty((B, Tt, H, D), T)
-    oracle.attention_apply(hp, host(V4), ro)
-    assert_close(host(o), ro, T, "attentionApply")
+    hv = host(V4)
+    oracle.attention_apply(hp, hv, ro)
+    absdot = oracle.attention_apply(np.abs(hp), np.abs(hv), np.empty_like(ro))
+    assert_dot_close(host(o), ro, absdot, Tt, T, "attentionApply")
 
 
 # -------------------------------------------------------------------- c2 ---
@@ -158,9 +161,11 @@ def test_decode_c2_per_op_and_fused(ann):
     ops.scale(queue, None, s, scale, s)
     nn.softmax(queue, None, s, p, 3)
     nn.attentionApply(queue, None, p, dv, o, 1, ann.AttentionKvLayout.BHTD)
-    assert_close(host(s), rs, T, "scores*scale")
+    abs_s = oracle.attention_scores(np.abs(rq), np.abs(k), np.empty_like(rs), 1, 1) * scale
+    abs_o = oracle.attention_apply(np.abs(rp), np.abs(v), np.empty_like(ro), 1, 1)
+    assert_dot_close(host(s), rs, abs_s, D, T, "scores*scale")
     assert_close(host(p), rp, T, "softmax")
-    assert_close(host(o), ro, T, "per-op out")
+    assert_dot_close(host(o), ro, abs_o, Tk, T, "per-op out")
 
     of = empty((B, 1, H, D), T)
     nn.attentionDecode(queue, None, dq, dk, dv, of, scale, 1, ann.AttentionKvLayout.BHTD)
