@@ -19,6 +19,8 @@
 // in its S registers -- with b0 = V[8j + 2t (+1)][8n + g].
 // The online softmax (exact rescale every tile) reduces a row over the 4
 // threads of a quad with two shuffles.
+#include <cooperative_groups.h>
+
 #include <cstdlib>
 #include <mutex>
 
@@ -76,6 +78,7 @@ struct F64Args {
     int q_tiles;
     int64_t bhs;         // batch * query heads
     int64_t head_chunk;  // (batch, head) pairs per dispatch chunk
+    int splits;          // CTAs (one cluster) sharing the key range of one query tile: 1, 2 or 4
 };
 
 __device__ __forceinline__ void dmma(double (&c)[4], double a0, double a1, double b0) {
@@ -91,6 +94,68 @@ __device__ __forceinline__ double quad_max(double x) {
 __device__ __forceinline__ double quad_sum(double x) {
     x += __shfl_xor_sync(0xffffffffu, x, 1);
     return x + __shfl_xor_sync(0xffffffffu, x, 2);
+}
+
+// Merge of the key-range splits of one query tile (a cluster of a.splits CTAs):
+// each CTA leaves its unnormalised O, row max and row sum in its own shared
+// memory (the K/V stages, drained by now), then CTA s combines rows
+// [64 s / S, 64 (s + 1) / S) of all partials through distributed shared memory
+// with the log-sum-exp rule O = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M),
+// M = max_s m_s, and stores them. The second cluster barrier keeps every CTA's
+// shared memory alive until its peers have read it.
+template <int D>
+__device__ void merge_splits(F64Args const& a, unsigned char* smem, double const (&o)[D / 8][4],
+                             double const (&m_run)[2], double const (&l_run)[2], int q_rows, int64_t b, int64_t hq,
+                             int64_t q0) {
+    namespace cg = cooperative_groups;
+    constexpr int NO = D / 8;
+    constexpr int LDP = D + 1;  // partial O row pitch in doubles
+    int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int const g = lane >> 2, t = lane & 3;
+    int const r0 = 16 * warp + g;
+    // [kBM][LDP] O, then m[kBM], l[kBM], over the Q tile and the K/V stages (all
+    // free now; they hold more than this for every tile size)
+    double* part = reinterpret_cast<double*>(smem);
+    // smallest layout (16-key tiles): Q (kBM rows) + four 16-row K/V stages of D + 2 doubles
+    static_assert((kBM * (D + 1) + 2 * kBM) * 8 <= (kBM + 4 * 16) * (D + 2) * 8, "merge buffer fits");
+    double* pm = part + kBM * LDP;
+    double* pl = pm + kBM;
+    __syncthreads();  // every warp is done with the K/V stages
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        int const r = r0 + 8 * h;
+#pragma unroll
+        for (int n = 0; n < NO; ++n) {
+            part[r * LDP + 8 * n + 2 * t] = o[n][2 * h];
+            part[r * LDP + 8 * n + 2 * t + 1] = o[n][2 * h + 1];
+        }
+        if (t == 0) {
+            pm[r] = m_run[h];
+            pl[r] = l_run[h];
+        }
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    int const S = a.splits, s = static_cast<int>(cluster.block_rank());
+    int const row_lo = kBM * s / S, row_hi = kBM * (s + 1) / S;
+    for (int e = tid; e < (row_hi - row_lo) * D; e += kThreads) {
+        int const r = row_lo + e / D, c = e % D;
+        if (r >= q_rows) continue;
+        double M = Lowest<double>::value;
+        for (int p = 0; p < S; ++p) M = fmax(M, cluster.map_shared_rank(pm, p)[r]);
+        double L = 0.0, acc = 0.0;
+        for (int p = 0; p < S; ++p) {
+            double const w = exp(cluster.map_shared_rank(pm, p)[r] - M);
+            L += w * cluster.map_shared_rank(pl, p)[r];
+            acc += w * cluster.map_shared_rank(part, p)[r * LDP + c];
+        }
+        double const val = L > 0.0 ? acc / L : 0.0;
+        int64_t const off = b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + c * a.o_d;
+        if (a.mirror) mc::store(a.mirror + off, val);
+        else a.out[off] = val;
+    }
+    if (a.mirror) __threadfence_system();
+    cluster.sync();
 }
 
 template <int D, int BN>
@@ -109,8 +174,11 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
     int const g = lane >> 2, t = lane & 3;
     // 1-D grid in chunks of a.head_chunk (batch, head) pairs (head_chunk_for):
     // inside a chunk the query tiles go from the last (most keys) down, so the
-    // heaviest CTAs start first, while the K/V of one chunk stay in L2
-    int64_t const lin = blockIdx.x, per_chunk = a.head_chunk * a.q_tiles;
+    // heaviest CTAs start first, while the K/V of one chunk stay in L2. With
+    // a.splits > 1 a cluster of that many CTAs shares one query tile, CTA s
+    // taking the s-th contiguous share of its key tiles.
+    int const split = static_cast<int>(blockIdx.x % a.splits);
+    int64_t const lin = blockIdx.x / a.splits, per_chunk = a.head_chunk * a.q_tiles;
     int64_t const chunk = lin / per_chunk, in_chunk = lin % per_chunk;
     int64_t const chunk_bh = a.bhs - chunk * a.head_chunk < a.head_chunk ? a.bhs - chunk * a.head_chunk : a.head_chunk;
     int const qt = a.q_tiles - 1 - static_cast<int>(in_chunk / chunk_bh);
@@ -119,15 +187,18 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
     int64_t const q0 = static_cast<int64_t>(qt) * kBM;
     int const q_rows = static_cast<int>(q0 + kBM <= a.Tq ? kBM : a.Tq - q0);
     int64_t const k_end = a.causal ? (a.Tk < q0 + kBM ? a.Tk : q0 + kBM) : a.Tk;
-    int const n_kt = static_cast<int>((k_end + kBN - 1) / kBN);
+    int const n_all = static_cast<int>((k_end + kBN - 1) / kBN);  // key tiles of this query tile
+    int const kt0 = static_cast<int>(static_cast<int64_t>(n_all) * split / a.splits);  // this CTA's share
+    int const n_kt = static_cast<int>(static_cast<int64_t>(n_all) * (split + 1) / a.splits) - kt0;
+    bool const has_last = kt0 + n_kt == n_all;  // holds the (possibly ragged) last key tile
 
     double const* qbase = a.q + b * a.q_b + q0 * a.q_t + hq * a.q_h;
     double const* kbase = a.k + b * a.k_b + kvh * a.k_h;
     double const* vbase = a.v + b * a.v_b + kvh * a.v_h;
 
-    auto issue_kv = [&](int kt) {  // warp 0: K and V rows of key tile kt into stage kt & 1
+    auto issue_kv = [&](int kt) {  // warp 0: K and V rows of this CTA's key tile kt into stage kt & 1
         int const s = kt & 1;
-        int64_t const key0 = static_cast<int64_t>(kt) * kBN;
+        int64_t const key0 = static_cast<int64_t>(kt0 + kt) * kBN;
         int const rows = static_cast<int>(key0 + kBN <= a.Tk ? kBN : a.Tk - key0);
         uint32_t const bar = bar0 + 8 * (1 + s);
         if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * rows * C::ROWB));
@@ -155,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
     // be finite (their P is 0, and 0 * NaN is not); K rows there are masked by
     // select. The last tile's stage is zeroed once it is free for that tile.
     for (int i = tid; i < (kBM - q_rows) * C::LD; i += kThreads) Qs[q_rows * C::LD + i] = 0.0;
-    int const v_tail = n_kt > 0 ? static_cast<int>(static_cast<int64_t>(n_kt) * kBN - a.Tk) : 0;
+    int const v_tail = n_kt > 0 && has_last ? static_cast<int>(static_cast<int64_t>(n_all) * kBN - a.Tk) : 0;
     auto zero_v_tail = [&]() {  // all threads; rows [kBN - v_tail, kBN) of the last tile's stage
         double* vt = Vs + ((n_kt - 1) & 1) * C::TILE + (kBN - v_tail) * C::LD;
         for (int i = tid; i < v_tail * C::LD; i += kThreads) vt[i] = 0.0;
@@ -181,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         }
         double const* Kt = Ks + s * C::TILE;
         double const* Vt = Vs + s * C::TILE;
-        int64_t const key0 = static_cast<int64_t>(kt) * kBN;
+        int64_t const key0 = static_cast<int64_t>(kt0 + kt) * kBN;
 
         // ---- S = Q K^T: 16 rows x 32 keys per warp
         double sacc[NJ][4];
@@ -249,6 +320,38 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
             for (int kt = abort_kt; kt < (n_kt < abort_kt + 2 ? n_kt : abort_kt + 2); ++kt)  // drain (bounded)
                 mbar_wait_bounded(bar0 + 8 * (1 + (kt & 1)), (kt >> 1) & 1);
         }
+        if (a.splits > 1) {  // the other CTAs of the cluster still meet at both barriers
+            __syncthreads();
+            cooperative_groups::this_cluster().sync();
+            cooperative_groups::this_cluster().sync();
+        }
+        return;
+    }
+    if (a.splits > 1) {
+        merge_splits<D>(a, smem, o, m_run, l_run, q_rows, b, hq, q0);
+        return;
+    }
+    if (a.mirror != nullptr && a.o_pairs) {
+        // Multicast output: whole rows a warp instruction (one NVLink packet per
+        // 512 contiguous bytes, not 64 bytes from each of 8 rows), staged in the
+        // Q tile, which no MMA reads any more.
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            double const inv = l_run[h] > 0.0 ? 1.0 / l_run[h] : 0.0;
+#pragma unroll
+            for (int n = 0; n < NO; ++n)
+                *reinterpret_cast<double2*>(Qs + (r0 + 8 * h) * C::LD + 8 * n + 2 * t) =
+                    make_double2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+        }
+        __syncthreads();
+        constexpr int PAIRS = D / 2;  // double2 per row
+        for (int e = tid; e < q_rows * PAIRS; e += kThreads) {
+            int const r = e / PAIRS, c2 = e % PAIRS;
+            double2 const val = *reinterpret_cast<double2 const*>(Qs + r * C::LD + 2 * c2);
+            mc::store(a.mirror + b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + 2 * c2, val);
+        }
+        __threadfence_system();  // performed at system scope before the CTA retires
         return;
     }
     int64_t const obase_off = b * a.o_b + q0 * a.o_t + hq * a.o_h;
@@ -297,13 +400,50 @@ int launch_f64_bn(ann_stream stream, F64Args& a, double scale, int64_t batch_hea
         return fail(ANN_ECUDA, "attention prefill (fp64 MMA) setup: %s", cudaGetErrorString(attr));
     a.bhs = batch_heads;
     a.head_chunk = head_chunk_for(batch_heads, a.q_tiles, 2 * a.Tk * D * 8, C::MIN_CTAS);
-    dim3 grid(static_cast<unsigned>(a.q_tiles * batch_heads));
-    prefill_f64_kernel<D, BN><<<grid, kThreads, C::SMEM, as_stream(stream)>>>(a, scale);
-    return check_launch("attention prefill (fp64 MMA)");
+    int64_t const ctas = static_cast<int64_t>(a.q_tiles) * batch_heads * a.splits;
+    if (a.splits == 1) {
+        prefill_f64_kernel<D, BN><<<dim3(static_cast<unsigned>(ctas)), kThreads, C::SMEM, as_stream(stream)>>>(a,
+                                                                                                             scale);
+        return check_launch("attention prefill (fp64 MMA)");
+    }
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute cl{};
+    cl.id = cudaLaunchAttributeClusterDimension;
+    cl.val.clusterDim.x = static_cast<unsigned>(a.splits);
+    cl.val.clusterDim.y = 1;
+    cl.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = as_stream(stream);
+    cfg.attrs = &cl;
+    cfg.numAttrs = 1;
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, prefill_f64_kernel<D, BN>, a, scale);
+    if (e != cudaSuccess) return fail(ANN_ECUDA, "attention prefill (fp64 MMA, key splits): %s", cudaGetErrorString(e));
+    return check_launch("attention prefill (fp64 MMA, key splits)");
+}
+
+// Key-range splits per query tile: 1 while the grid already fills the GPU,
+// else the smallest of 2 / 4 that gives about two CTAs per SM (a head-sharded
+// rank's few heads leave most SMs idle, and the last query tiles hold every
+// key: without a split they alone set the time). ANN_PREFILL_F64_SPLITS pins it.
+int f64_splits(int64_t tiles, int max_key_tiles) {
+    if (const char* env = std::getenv("ANN_PREFILL_F64_SPLITS")) {
+        int const sp = std::atoi(env);
+        if (sp == 1 || sp == 2 || sp == 4) return sp;
+    }
+    int64_t const want = 2 * static_cast<int64_t>(sm_count());
+    int sp = 1;
+    while (sp < 4 && tiles * sp < want && max_key_tiles >= 4 * sp) sp *= 2;
+    return sp;
 }
 
 template <int D>
 int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads) {
+    int64_t const tiles = static_cast<int64_t>(a.q_tiles) * batch_heads;
+    a.splits = f64_splits(tiles, static_cast<int>(ceil_div(a.causal ? a.Tq : a.Tk, 32)));
+    if (tiles * a.splits > INT32_MAX) a.splits = 1;
+    if (a.splits > 1) return launch_f64_bn<D, 32>(stream, a, scale, batch_heads);
     if constexpr (D <= 64) {
         // 16-key tiles once the grid fills at least four waves of 3-CTA slots
         if (static_cast<int64_t>(a.q_tiles) * batch_heads >= int64_t{4} * 3 * sm_count())

@@ -114,6 +114,19 @@ __device__ __forceinline__ float exp2_approx(float x) {
 __device__ __forceinline__ void row_sync() {  // the 256 row threads (warps 0..7) of this CTA
     asm volatile("bar.sync 1, %0;" ::"n"(kRowThreads) : "memory");
 }
+// row_sync that also ORs `v` over the 256 row threads: every one gets the same answer
+__device__ __forceinline__ bool row_sync_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "n"(kRowThreads)
+        : "memory");
+    return r != 0;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, float scale) {
@@ -443,8 +456,46 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
         // buffer; every row thread reaches this barrier exactly once
         float* lx = reinterpret_cast<float*>(smem + C::OFF_PLO);
         if (ok) lx[tid] = l_part;
-        row_sync();
-        if (ok) {
+        bool const all_ok = !row_sync_any(!ok);  // the same for every row thread
+        if (a.mirror != nullptr && a.o_vec) {
+            // Multicast output: each store is one NVLink packet to the switch, so the
+            // rows are written whole by a warp (512 contiguous bytes an instruction),
+            // not 16 bytes from each of 32 rows. O goes through a padded staging
+            // tile over the K / V buffers, which no MMA reads any more.
+            constexpr int PITCH = D * 4 + 16;
+            unsigned char* stage = smem + C::OFF_K;
+            static_assert(kBM * PITCH <= 4 * (C::TILE_K + C::TILE_V), "staging fits the K / V buffers");
+            if (all_ok) {
+                tc::fence_after_sync();
+                float const l_sum = lx[r] + lx[r + kBM];
+                float const inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    int const col = h * HD + 32 * c;
+                    float ov[32];
+                    tc::tmem_ld32(tmem + lane_off + C::O_COL + col, ov);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(stage + r * PITCH + (col + j) * 4) =
+                            make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                }
+            }
+            row_sync();
+            if (all_ok) {
+                constexpr int TPR = D / 4;     // threads per row, a float4 each
+                constexpr int RPW = 32 / TPR;  // rows per warp instruction
+                int const sub = lane / TPR, c4 = lane % TPR;
+                for (int rr = warp * RPW + sub; rr < kBM; rr += 8 * RPW) {
+                    int64_t const qr = q0 + rr;
+                    if (qr >= a.Tq) continue;
+                    float4 const val = *reinterpret_cast<float4 const*>(stage + rr * PITCH + c4 * 16);
+                    mc::store(a.mirror + b * a.o_b + qr * a.o_t + hq * a.o_h + c4 * 4, val);
+                }
+                // performed at system scope before the CTA retires (the barrier
+                // that follows the kernel publishes them)
+                __threadfence_system();
+            }
+        } else if (all_ok) {
             tc::fence_after_sync();
             float const l_sum = lx[r] + lx[r + kBM];
             float const inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
@@ -459,12 +510,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                 if (qi < a.Tq) {
                     if (a.o_vec) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 const val =
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(orow + col + j) =
                                 make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
-                            if (mrow) mc::store(mrow + col + j, val);
-                            else *reinterpret_cast<float4*>(orow + col + j) = val;
-                        }
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
@@ -474,8 +522,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                     }
                 }
             }
-            // the multicast stores are performed at system scope before this
-            // CTA retires (the barrier that follows the kernel publishes them)
             if (mrow) __threadfence_system();
         }
     }

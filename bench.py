@@ -267,6 +267,33 @@ def run_reference(args, w):
 
 
 # ------------------------------------------------------------------ GPU ---
+class DecodeE2E(ctypes.Structure):
+    """struct DecodeE2E of tests/cpp/decode_e2e.cpp (the step through the C++ drop-in header)."""
+    _fields_ = [("B", ctypes.c_int32), ("Hl", ctypes.c_int32), ("H", ctypes.c_int32), ("Tk", ctypes.c_int32),
+                ("D", ctypes.c_int32), ("dm", ctypes.c_int32), ("eps", ctypes.c_float), ("scale", ctypes.c_float),
+                ("position", ctypes.c_uint32),
+                ("h_q", ctypes.c_void_p), ("h_knew", ctypes.c_void_p), ("h_hidden", ctypes.c_void_p),
+                ("h_out", ctypes.c_void_p), ("q", ctypes.c_void_p), ("knew", ctypes.c_void_p),
+                ("hidden", ctypes.c_void_p), ("normed", ctypes.c_void_p), ("norm_w", ctypes.c_void_p),
+                ("cos_t", ctypes.c_void_p), ("sin_t", ctypes.c_void_p), ("k_caches", ctypes.c_void_p),
+                ("v_caches", ctypes.c_void_p), ("n_caches", ctypes.c_int32), ("out", ctypes.c_void_p),
+                ("head0", ctypes.c_int32), ("out_mirror", ctypes.c_void_p), ("signals", ctypes.c_void_p),
+                ("peer_signals", ctypes.c_void_p), ("nranks", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("epoch", ctypes.c_uint32), ("timeout_ns", ctypes.c_uint64)]
+
+
+def e2e_library():
+    """tests/cpp/_build/libdecode_e2e.so (built by tests/cpp/build.py), or None."""
+    path = os.path.join(ROOT, "tests", "cpp", "_build", "libdecode_e2e.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    lib.decode_e2e_run.argtypes = [ctypes.POINTER(DecodeE2E), ctypes.c_int, ctypes.c_void_p,
+                                   ctypes.POINTER(ctypes.c_float)]
+    lib.decode_e2e_error.restype = ctypes.c_char_p
+    return lib
+
+
 class DecodeBench:
     """Inputs and the two step flavours (device-resident and end-to-end) of
     the head-sharded decode workload on this rank."""
@@ -348,6 +375,48 @@ class DecodeBench:
             chk(lib.ann_comm_allgather(self.comm._h, sh, self.sharded.out_local.data_ptr(),
                                        self.sharded.gathered.data_ptr(), self.gather_bytes))
             chk(lib.ann_scale_f32(sh, R(self.vsrc), 1.0, R(self.vdst)))
+
+    def cpp_e2e_setup(self):
+        """The DecodeE2E record for the C++ step (None where it does not apply:
+        no library, or the NCCL gather, which the C++ step does not run)."""
+        lib = e2e_library()
+        if lib is None or self.gather == "nccl":
+            return None
+        w, sh = self.w, self.sharded
+        st = DecodeE2E()
+        st.B, st.Hl, st.H, st.Tk, st.D, st.dm = w["B"], self.shard.local_heads, w["H"], w["Tk"], w["D"], w["H"] * w["D"]
+        st.eps, st.scale, st.position = self.eps, self.scale, w["Tk"]
+        st.h_q, st.h_knew, st.h_hidden, st.h_out = (t.data_ptr() for t in (self.hq, self.hk, self.hh, self.hout))
+        st.q, st.knew, st.hidden, st.normed = (t.data_ptr() for t in (self.q, self.knew, self.hidden, self.normed))
+        st.norm_w, st.cos_t, st.sin_t = self.norm_w.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr()
+        self._kp = (ctypes.c_void_p * self.copies)(*[k.data_ptr() for k, _ in self.caches])
+        self._vp = (ctypes.c_void_p * self.copies)(*[v.data_ptr() for _, v in self.caches])
+        st.k_caches, st.v_caches = ctypes.cast(self._kp, ctypes.c_void_p), ctypes.cast(self._vp, ctypes.c_void_p)
+        st.n_caches = self.copies
+        st.out = sh.out.data_ptr()
+        st.head0 = self.shard.head_slice.start if self.world > 1 else 0
+        st.nranks, st.rank = self.world, self.shard.rank
+        if self.gather == "multicast":
+            m = sh.mirror
+            st.out_mirror, st.signals, st.peer_signals = sh._out_mc, m._sig.data_ptr(), m._peer_sig.data_ptr()
+            st.timeout_ns = m.timeout_ns
+        self._e2e_lib, self._e2e = lib, st
+        return st
+
+    def cpp_e2e(self, steps):
+        """`steps` decode steps through the C++ drop-in header with host buffers;
+        returns the device seconds between events around them."""
+        st = self._e2e
+        if self.gather == "multicast":
+            st.epoch = self.sharded.mirror._epoch
+        ms = ctypes.c_float(0)
+        rc = self._e2e_lib.decode_e2e_run(ctypes.byref(st), steps, ctypes.c_void_p(self.stream.cuda_stream),
+                                          ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError("C++ decode step: " + self._e2e_lib.decode_e2e_error().decode())
+        if self.gather == "multicast":
+            self.sharded.mirror._epoch = st.epoch
+        return ms.value / 1e3
 
     def e2e_step(self, i):
         """Through the public Python API, with the step's inputs copied from
@@ -461,18 +530,30 @@ def measure(bench, steps, warmup, world, rank, clock_ids, min_region_s=1.0, max_
     elapsed = statistics.median(reps)
     kernel = statistics.median(kernel_s)
 
+    # end to end: through the C++ drop-in header (alpaka::nn::onHost) with host
+    # buffers where its step applies, else through the Python mirror of the API
     e2e_steps = max(1, min(steps, 1000))
-    for i in range(min(warmup, 5)):
-        bench.e2e_step(i)
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(bench.stream)
-    for i in range(e2e_steps):
-        bench.e2e_step(i)
-    e1.record(bench.stream)
-    barrier(world)
-    e2e_s = max_over_ranks([e0.elapsed_time(e1) / 1e3 / e2e_steps], world)[0]
-    return elapsed, kernel, e2e_s, e2e_steps, clk, len(reps), (min(reps), max(reps))
+    cpp = bench.cpp_e2e_setup() is not None
+    if cpp:
+        bench.cpp_e2e(min(warmup, 5) or 1)
+        barrier(world)
+        e2e_s = bench.cpp_e2e(e2e_steps) / e2e_steps
+        barrier(world)
+    else:
+        for i in range(min(warmup, 5)):
+            bench.e2e_step(i)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(bench.stream)
+        for i in range(e2e_steps):
+            bench.e2e_step(i)
+        e1.record(bench.stream)
+        barrier(world)
+        e2e_s = e0.elapsed_time(e1) / 1e3 / e2e_steps
+    e2e_s = max_over_ranks([e2e_s], world)[0]
+    api = ("C++ alpaka::nn::onHost header (tests/cpp/decode_e2e.cpp)" if cpp else
+           "Python mirror of alpaka::nn::onHost (alpakann_b200.onHost)")
+    return elapsed, kernel, e2e_s, e2e_steps, clk, len(reps), (min(reps), max(reps)), api
 
 
 GATHER_DESC = {"none": "", "nccl": " + NCCL all-gather + re-assembly",
@@ -912,7 +993,7 @@ def main():
     def run(wl, steps, warmup, with_clocks, check=False):
         bench = DecodeBench(WORKLOADS[wl], rank, world, comm)
         parity = bench.check_parity() if check else None
-        elapsed, kernel_s, e2e_s, e2e_steps, clk, nrep, spread = measure(
+        elapsed, kernel_s, e2e_s, e2e_steps, clk, nrep, spread, api = measure(
             bench, steps, warmup, world, rank, clock_ids if with_clocks else None)
         ww = WORKLOADS[wl]
         B, Tk, H, D = ww["B"], ww["Tk"], ww["H"], ww["D"]
@@ -922,7 +1003,7 @@ def main():
                    achieved=alg / kernel_s / 1e9, e2e=B / e2e_s, e2e_steps=e2e_steps, clk=clk,
                    copies=bench.copies, kv_mib=bench.kv_bytes / 2**20, launches=bench.launches_per_step * steps,
                    h2d=bench.h2d_bytes, d2h=bench.d2h_bytes, alg=alg, parity=parity, repeats=nrep,
-                   rep_ms=[x / steps * 1e3 for x in spread], gather=bench.gather)
+                   rep_ms=[x / steps * 1e3 for x in spread], gather=bench.gather, api=api)
         bench.release()
         return res
 
@@ -969,7 +1050,7 @@ def main():
                          "frac_of_8TBs_nominal": r["achieved"] / 8000.0},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
-                    "d2h_bytes_per_step": r["d2h"], "steps": r["e2e_steps"]},
+                    "d2h_bytes_per_step": r["d2h"], "steps": r["e2e_steps"], "api": r["api"]},
             "gpu_launches": r["launches"] * r["repeats"],
             "clocks": r["clk"],
             "extra": extra,

@@ -808,9 +808,53 @@ void attentionPrefill(auto& queue, auto /*exec*/, auto const& Q, auto const& K, 
                                            static_cast<int32_t>(kvLayout), causal ? 1 : 0));
 }
 
+// attentionDecode / attentionPrefill whose result stores go through `outMirror`,
+// the NVLink multicast address of out's first element, into every rank's copy
+// of the output (include/ann_b200.h, multicast outputs); enqueue
+// b200::signalBarrier after them on every rank.
+template <typename T_Type>
+void attentionDecodeMirror(auto& queue, auto /*exec*/, auto const& Q, auto const& K, auto const& V, auto& out,
+                           void* outMirror, T_Type scale, uint32_t queriesPerKvGroup = 1u,
+                           alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BHTD) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto q = d::to_ann(Q), k = d::to_ann(K), v = d::to_ann(V), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_decode_mirror_f32(d::stream_of(queue), &q, &k, &v, &o, outMirror, scale,
+                                                 queriesPerKvGroup, static_cast<int32_t>(kvLayout)));
+    else
+        d::check(ann_attention_decode_mirror_f64(d::stream_of(queue), &q, &k, &v, &o, outMirror, scale,
+                                                 queriesPerKvGroup, static_cast<int32_t>(kvLayout)));
+}
+
+template <typename T_Type>
+void attentionPrefillMirror(auto& queue, auto /*exec*/, auto const& Q, auto const& K, auto const& V, auto& out,
+                            void* outMirror, T_Type scale, uint32_t queriesPerKvGroup = 1u,
+                            alpaka::nn::AttentionKvLayout kvLayout = alpaka::nn::AttentionKvLayout::BTHD,
+                            bool causal = true) {
+    namespace d = alpaka::nn::b200::detail;
+    d::require_float<T_Type>();
+    auto q = d::to_ann(Q), k = d::to_ann(K), v = d::to_ann(V), o = d::to_ann(out);
+    if constexpr (d::is_f32<T_Type>)
+        d::check(ann_attention_prefill_mirror_f32(d::stream_of(queue), &q, &k, &v, &o, outMirror, scale,
+                                                  queriesPerKvGroup, static_cast<int32_t>(kvLayout), causal ? 1 : 0));
+    else
+        d::check(ann_attention_prefill_mirror_f64(d::stream_of(queue), &q, &k, &v, &o, outMirror, scale,
+                                                  queriesPerKvGroup, static_cast<int32_t>(kvLayout), causal ? 1 : 0));
+}
+
 }  // namespace alpaka::nn::onHost::nn
 
 namespace alpaka::nn::b200 {
+
+// Cross-rank barrier over peer-addressable signal words (ann_signal_barrier):
+// epochs 1, 2, 3, ... in the same order on every rank; a wait that runs out
+// sets ANN_DEVERR_WAIT_TIMEOUT (ann_take_device_error).
+template <typename Q>
+void signalBarrier(Q& queue, uint32_t* signals, uint32_t* const* peerSignals, int nranks, int rank, uint32_t epoch,
+                   uint64_t timeoutNs = 5000000000ull) {
+    detail::check(ann_signal_barrier(detail::stream_of(queue), signals, peerSignals, nranks, rank, epoch, timeoutNs));
+}
 
 // One rank of the node's NCCL communicator (ann_comm_*), on the current CUDA
 // device. Rank 0 creates the rendezvous id with uniqueId() and hands its bytes

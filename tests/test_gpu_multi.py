@@ -5,8 +5,9 @@ joins ends in ANN_ENCCL at its deadline (host-side bootstrap wait; no kernel
 runs). On two GPUs: the gathered decode and prefill outputs equal the 1-GPU
 outputs bit for bit, through the NCCL all-gather and through the multicast
 stores (alpakann_b200.mirror) -- the same kernels run the same per-head
-arithmetic, and the decode split is pinned (ANN_DECODE_SPLITS) so that both
-runs sum every row in the same order. The signal barrier's bounded wait runs
+arithmetic, and the decode split and the fp64 prefill's key split are pinned
+(ANN_DECODE_SPLITS, ANN_PREFILL_F64_SPLITS) so that both runs sum every row in
+the same order. The signal barrier's bounded wait runs
 out on one GPU when no rank signals (no multicast, no peer memory)."""
 import math
 import os
@@ -31,7 +32,8 @@ def _free_port():
 
 
 def _worker(rank, world, port, result, gather):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), ANN_DECODE_SPLITS="2")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), ANN_DECODE_SPLITS="2",
+                      ANN_PREFILL_F64_SPLITS="2")
     torch.cuda.set_device(rank)
     import torch.distributed as dist
 

@@ -149,3 +149,27 @@ def test_prefill_fp64_long_grid_sampled(ann):
 def test_prefill_c3_fp32_sampled(ann):
     """c3: batch 4, seq 4096, 32 heads x 128, fp32, causal."""
     _sampled(ann, np.float32, 4, 4096, 32, 128, 3)
+
+
+@pytest.mark.parametrize("splits", ["1", "2", "4"])
+@pytest.mark.parametrize("shape,causal", [((1, 333, 2, 64), True), ((2, 160, 3, 128), True),
+                                          ((1, 100, 2, 64), False), ((1, 40, 2, 64), True)])
+def test_prefill_f64_key_splits(ann, monkeypatch, kernel, splits, shape, causal):
+    """fp64 on the FP64 tensor cores with the key range of every query tile split
+    over a cluster of 1, 2 or 4 CTAs (merged through distributed shared memory
+    with the log-sum-exp rule): ragged query and key tiles, splits with no keys
+    (40 rows: two 32-key tiles over four CTAs), causal and not, against the
+    oracle. The split count a head-sharded rank picks on its own is one of these."""
+    if kernel != "tensor":
+        pytest.skip("the split is a property of the fp64 tensor-core kernel")
+    monkeypatch.setenv("ANN_PREFILL_F64_SPLITS", splits)
+    T = np.float64
+    B, Tt, H, D = shape
+    g = rng(Tt * 7 + D + int(splits))
+    q, k, v = (normal(g, (B, Tt, H, D), T) for _ in range(3))
+    if not causal:
+        k, v = (normal(g, (B, Tt + 37, H, D), T) for _ in range(2))
+    scale = 1.0 / math.sqrt(D)
+    want = oracle_pipeline(q, k, v, scale, 1, 0, causal)
+    got = run(ann, q, k, v, scale, 1, 0, causal)
+    assert_close(got, want, T, f"fp64 prefill, {splits} key splits")
