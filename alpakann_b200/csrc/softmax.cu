@@ -19,6 +19,8 @@
 // tested with one compare per element.
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "reduce.cuh"
 #include "tma.cuh"
@@ -651,6 +653,163 @@ bool bulk_launched(SoftmaxArgs const& a, cudaStream_t s) {
     return true;
 }
 
+// Long aligned rows (over 64 KB of input + mask) split over a cluster of
+// kSplit CTAs: CTA s brings the s-th quarter of the row into its shared
+// memory by one bulk copy, the row's max and sum are combined across the
+// cluster through distributed shared memory, and each CTA normalises and
+// writes its quarter. A quarter-row per CTA lets several CTAs (rows) per SM be
+// in flight, where softmax_bulk holds one whole row per SM (rows of 32768
+// fp32: one 128 KiB copy at a time, the SM idle while it lands). Waits are
+// bounded; a CTA whose copy does not land sets ANN_DEVERR_WAIT_TIMEOUT and
+// keeps joining the cluster barriers (its peers still meet it there) without
+// issuing more copies.
+constexpr int kSplit = 4;
+constexpr int64_t kSplitMinBytes = int64_t{64} << 10, kSplitPartBytes = int64_t{56} << 10;
+
+template <typename T, bool MASK>
+__global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
+    namespace cg = cooperative_groups;
+    using P = typename Vec16<T>::type;
+    constexpr int NV = Vec16<T>::n;
+    extern __shared__ __align__(128) unsigned char part_smem[];
+    __shared__ __align__(8) uint64_t full;
+    __shared__ T scratch[8];
+    __shared__ T xch[2];  // this CTA's max and sum, read by the peers
+    cg::cluster_group cluster = cg::this_cluster();
+    int const tid = threadIdx.x, s = static_cast<int>(cluster.block_rank());
+    int64_t const part = a.len / kSplit, pieces = part / NV, e_begin = s * part;
+    uint32_t const part_bytes = static_cast<uint32_t>(part) * sizeof(T);
+    int64_t const n_clusters = gridDim.x / kSplit, cid = blockIdx.x / kSplit;
+    int64_t const iters = ceil_div(a.rows - cid, n_clusters);
+    uint32_t const bar = smem_u32(&full), dst = smem_u32(part_smem);
+    T const* in = static_cast<T const*>(a.in);
+    T const* mk = static_cast<T const*>(a.mask);
+    T* out = static_cast<T*>(a.out);
+    T* buf = reinterpret_cast<T*>(part_smem);
+    T const* mbuf = buf + part;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    bool dead = false;  // a copy did not land: no more copies, but every barrier is still joined
+    for (int64_t it = 0; it < iters; ++it) {
+        int64_t const row = cid + it * n_clusters;
+        int64_t oi, oo, om = 0, lo, hi;
+        row_offsets(a, row, oi, oo, om);
+        kept_range(a, row, lo, hi);
+        if (tid == 0 && !dead) {
+            mbar_arrive_expect_tx(bar, part_bytes * (MASK ? 2u : 1u));
+            bulk_copy_g2s(dst, in + oi + e_begin, part_bytes, bar);
+            if constexpr (MASK) bulk_copy_g2s(dst + part_bytes, mk + om + e_begin, part_bytes, bar);
+        }
+        bool const ok = dead || mbar_wait_bounded(bar, static_cast<uint32_t>(it & 1));
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicOr(&g_softmax_error, ANN_DEVERR_WAIT_TIMEOUT);
+                mbar_wait_bounded(bar, static_cast<uint32_t>(it & 1));  // the copy in flight (bounded)
+            }
+            dead = true;
+        }
+        T m = Lowest<T>::value;
+        if (!dead) {
+            for (int64_t p = tid; p < pieces; p += 256) {
+                int64_t const e0 = p * NV;
+                P x = *reinterpret_cast<P const*>(buf + e0);
+                T* xe = reinterpret_cast<T*>(&x);
+                if constexpr (MASK) {
+                    P const y = *reinterpret_cast<P const*>(mbuf + e0);
+                    T const* ye = reinterpret_cast<T const*>(&y);
+#pragma unroll
+                    for (int k = 0; k < NV; ++k) xe[k] = add_rn(xe[k], ye[k]);
+                }
+#pragma unroll
+                for (int k = 0; k < NV; ++k) {
+                    int64_t const e = e_begin + e0 + k;
+                    if (e < lo || e >= hi) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
+                    m = fmax(m, xe[k]);
+                }
+                *reinterpret_cast<P*>(buf + e0) = x;
+            }
+        }
+        m = block_max<8>(m, scratch);
+        if (tid == 0) xch[0] = m;
+        cluster.sync();
+        T M = Lowest<T>::value;
+        for (int r = 0; r < kSplit; ++r) M = fmax(M, cluster.map_shared_rank(xch, r)[0]);
+        T sum{};
+        if (!dead) {
+            for (int64_t p = tid; p < pieces; p += 256) {
+                int64_t const e0 = p * NV;
+                P x = *reinterpret_cast<P const*>(buf + e0);
+                T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+                for (int k = 0; k < NV; ++k) {
+                    xe[k] = exp_t(xe[k] - M);
+                    sum += xe[k];
+                }
+                *reinterpret_cast<P*>(buf + e0) = x;
+            }
+        }
+        sum = block_sum<8>(sum, scratch);
+        if (tid == 0) xch[1] = sum;
+        cluster.sync();
+        T L{};
+        for (int r = 0; r < kSplit; ++r) L += cluster.map_shared_rank(xch, r)[1];
+        // one division per row; unkept slots tested only when the sum < 1 (see softmax_regs)
+        T const inv = T(1) / L;
+        bool const exact = !(L >= T(1));
+        if (!dead) {
+            for (int64_t p = tid; p < pieces; p += 256) {
+                int64_t const e0 = p * NV;
+                P x = *reinterpret_cast<P const*>(buf + e0);
+                T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+                for (int k = 0; k < NV; ++k) {
+                    int64_t const e = e_begin + e0 + k;
+                    xe[k] = exact && (e < lo || e >= hi) ? T(0) : xe[k] * inv;
+                }
+                *reinterpret_cast<P*>(out + oo + e_begin + e0) = x;
+            }
+        }
+        cluster.sync();  // the peers have read xch, and this CTA is done with its buffer
+    }
+}
+
+// Launches softmax_cluster on a grid of resident clusters; false when it does not apply.
+template <typename T, bool MASK>
+bool cluster_launched(SoftmaxArgs const& a, cudaStream_t s) {
+    int64_t const bytes = a.len * static_cast<int64_t>(sizeof(T)) * (MASK ? 2 : 1);
+    constexpr int NV = Vec16<T>::n;
+    if (bytes <= kSplitMinBytes || bytes > kSplit * kSplitPartBytes || a.len % (kSplit * NV) != 0) return false;
+    int const smem = static_cast<int>(bytes / kSplit);
+    auto kernel = softmax_cluster<T, MASK>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute cl{};
+    cl.id = cudaLaunchAttributeClusterDimension;
+    cl.val.clusterDim.x = kSplit;
+    cl.val.clusterDim.y = 1;
+    cl.val.clusterDim.z = 1;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = s;
+    cfg.attrs = &cl;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(kSplit);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    int64_t const n = a.rows < clusters ? a.rows : clusters;
+    cfg.gridDim = dim3(static_cast<unsigned>(n * kSplit));
+    return cudaLaunchKernelEx(&cfg, kernel, a) == cudaSuccess;
+}
+
 // MASK: maskedSoftmax (onAcc/internal/nn/softmax.hpp:76-116), the row is
 // input + mask and nothing is skipped.
 template <typename T, int GROUP, bool MASK>
@@ -805,7 +964,9 @@ int softmax(ann_stream stream, const ann_view* in_v, const ann_view* out_v, uint
     auto launch = [&](auto mask_tag) {
         constexpr bool M = decltype(mask_tag)::value;
         constexpr int CV = 8 / NV;  // 16-byte pieces per lane
-        if (vec && a.len > 8192 && bulk_launched<T, M>(a, s)) {
+        if (vec && a.len > 8192 && cluster_launched<T, M>(a, s)) {
+            // quarter rows by bulk copy on clusters of four CTAs (softmax_cluster)
+        } else if (vec && a.len > 8192 && bulk_launched<T, M>(a, s)) {
             // whole rows by bulk copy (softmax_bulk)
         } else if (smem_row) {
             size_t const bytes = static_cast<size_t>(row_bytes);

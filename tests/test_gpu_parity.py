@@ -252,6 +252,32 @@ def test_softmax_row_lengths(ann, T, L):
     assert_close(host(out), ref, T, "softmax")
 
 
+@pytest.mark.parametrize("T,L,rows", [(np.float32, 32768, 700), (np.float64, 16384, 5), (np.float32, 20000, 3)])
+@pytest.mark.parametrize("kind", ["softmax", "causal", "masked"])
+def test_softmax_long_rows_on_clusters(ann, T, L, rows, kind):
+    """Rows of 64 to 224 KB: a quarter of each row per CTA of a four-CTA
+    cluster, the row max and sum combined through distributed shared memory.
+    700 rows of 32768 are more rows than resident clusters (each cluster walks
+    several); causal rows keep a prefix (query axis 1 against the key axis);
+    maskedSoftmax doubles the bytes a row."""
+    g = rng(L + rows)
+    x = normal(g, (rows, 1, L), T) * T(4)
+    ref = np.empty_like(x)
+    out = empty(x.shape, T)
+    nn = ann.onHost.nn
+    if kind == "softmax":
+        oracle.softmax(x, ref, 2)
+        nn.softmax(ann.Queue(), None, dev(x), out, 2)
+    elif kind == "causal":  # query index = row (axis 0), key = axis 2: keeps [0, row]
+        oracle.causal_softmax(x, ref, 2, 0, 2)
+        nn.causalSoftmax(ann.Queue(), None, dev(x), out, 2, 0, 2)
+    else:
+        m = normal(g, x.shape, T)
+        oracle.masked_softmax(x, m, ref, 2)
+        nn.maskedSoftmax(ann.Queue(), None, dev(x), dev(m), out, 2)
+    assert_close(host(out), ref, T, kind)
+
+
 # ----------------------------------------------------- rms / embedding ---
 @pytest.mark.parametrize("T", [np.float32, np.float64])
 @pytest.mark.parametrize("shape", [(3, 5), (4, 256), (2, 3, 1024), (5, 4096), (3, 8192), (2, 1027)])
