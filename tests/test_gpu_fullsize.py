@@ -64,3 +64,77 @@ def test_decode_full_size(ann, cfg):
     assert queue.take_device_error() == 0
     del k, v
     torch.cuda.empty_cache()
+
+
+def _fp64_attention(q, k, v, scale, causal, kv_bhtd):
+    """Every output row of q [B,Tq,H,D] against k / v ([B,H,Tk,D] when kv_bhtd,
+    else [B,Tk,H,D]) recomputed in fp64 on the device, one (batch, head) at a
+    time: scores, scale, (top-left causal) softmax, apply."""
+    import torch
+    B, Tq, H, D = q.shape
+    out = torch.empty(q.shape, dtype=torch.float64, device=q.device)
+    for b in range(B):
+        for h in range(H):
+            qh = q[b, :, h].double()
+            kh = (k[b, h] if kv_bhtd else k[b, :, h]).double()
+            vh = (v[b, h] if kv_bhtd else v[b, :, h]).double()
+            s = (qh @ kh.T) * scale
+            if causal:
+                s.masked_fill_(torch.ones_like(s, dtype=torch.bool).triu(1), float("-inf"))
+            out[b, :, h] = torch.softmax(s, dim=-1) @ vh
+    return out
+
+
+def _assert_full(got, ref, T, what):
+    import torch
+    rtol, atol = (1e-4, 1e-5) if T == np.float32 else (1e-11, 1e-12)
+    err = (got.double() - ref).abs()
+    bound = rtol * ref.abs() + atol
+    worst = float((err / bound).max())
+    assert worst <= 1.0, f"{what}: worst error {worst:.3f} of the tolerance, {int((err > bound).sum())} bad"
+    assert bool(torch.isfinite(got).all())
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(B=4, T=4096, H=32, D=128, T_=np.float32, name="c3"),
+    dict(B=2, T=1024, H=16, D=64, T_=np.float64, name="c4"),
+], ids=["c3", "c4"])
+def test_prefill_full_output_vs_fp64(ann, cfg):
+    """The WHOLE c3 (fp32) / c4 (fp64) prefill output, every tile edge and
+    every split merge, against an fp64 recomputation on the device."""
+    import torch
+    B, Tt, H, D, T = cfg["B"], cfg["T"], cfg["H"], cfg["D"], cfg["T_"]
+    dt = torch.float32 if T == np.float32 else torch.float64
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    q, k, v = (torch.randn((B, Tt, H, D), generator=gen, dtype=dt, device="cuda") for _ in range(3))
+    out = torch.full_like(q, float("nan"))
+    scale = 1.0 / math.sqrt(D)
+    queue = ann.Queue()
+    ann.onHost.nn.attentionPrefill(queue, None, q, k, v, out, scale, 1, ann.AttentionKvLayout.BTHD, True)
+    torch.cuda.synchronize()
+    assert queue.take_device_error() == 0
+    _assert_full(out, _fp64_attention(q, k, v, scale, True, False), T, cfg["name"])
+
+
+def test_decode_c5_full_output_vs_fp64(ann):
+    """The WHOLE c5 decode output (batch 16, cache 32768, 64 heads x 128, fp32,
+    32 GiB of K+V) against an fp64 recomputation on the device."""
+    import torch
+    B, Tk, H, D = 16, 32768, 64, 128
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    k = torch.randn((B, H, Tk, D), generator=gen, device="cuda")
+    v = torch.randn((B, H, Tk, D), generator=gen, device="cuda")
+    q = torch.randn((B, 1, H, D), generator=gen, device="cuda")
+    out = torch.full_like(q, float("nan"))
+    scale = 1.0 / math.sqrt(D)
+    queue = ann.Queue()
+    ann.onHost.nn.attentionDecode(queue, None, q, k, v, out, scale, 1, ann.AttentionKvLayout.BHTD)
+    torch.cuda.synchronize()
+    assert queue.take_device_error() == 0
+    ref = torch.empty((B, 1, H, D), dtype=torch.float64, device="cuda")
+    for b in range(B):  # one sequence at a time: its K / V in fp64 is 2 x 2 GiB
+        s = torch.einsum("hd,htd->ht", q[b, 0].double(), k[b].double()) * scale
+        ref[b, 0] = torch.einsum("ht,htd->hd", torch.softmax(s, -1), v[b].double())
+    _assert_full(out, ref, np.float32, "c5")
+    del k, v
+    torch.cuda.empty_cache()
