@@ -140,8 +140,10 @@ __global__ void __launch_bounds__(kThreads) mlp_tile(GemmArgs a) {
 }
 
 // Row pitch (elements) of a row-major view with unit column stride, or -1.
+// An empty view has no elements to address: any pitch will do.
 int64_t row_pitch(const Dims& d) {
     if (d.rank != 2) return -1;
+    if (d.ext[0] == 0 || d.ext[1] == 0) return d.ext[1];
     if (d.ext[1] > 1 && d.str[1] != 1) return -1;
     if (d.ext[0] <= 1) return d.ext[1];
     return d.str[0] >= d.ext[1] ? d.str[0] : -1;

@@ -1,12 +1,10 @@
-// tcgen05.cuh -- sm_100a tensor-core (tcgen05 / TMEM) and tensor-TMA helpers, inline PTX.
+// tcgen05.cuh -- sm_100a tensor-core (tcgen05 / TMEM) helpers, inline PTX.
 //
 // cta_group::1 forms for single-SM kernels and cta_group::2 forms for kernels
-// on SM pairs (a 2-CTA cluster sharing each MMA). No TMA load here or anywhere
-// in the library uses cluster multicast; the only `.multicast::cluster` is
-// tcgen05.commit's mbarrier signal to both CTAs of a pair.
+// on SM pairs (a 2-CTA cluster sharing each MMA). No copy into shared memory
+// anywhere in the library is multicast to the CTAs of a cluster; the pair
+// kernels signal both CTAs' mbarriers with two tcgen05.commit instructions.
 #pragma once
-
-#include <cuda.h>
 
 #include <cstdint>
 
@@ -207,16 +205,6 @@ __device__ __forceinline__ float to_tf32(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
-}
-
-// ---- tensor TMA --------------------------------------------------------------
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, CUtensorMap const* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-        "[%6];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
-        : "memory");
 }
 
 }  // namespace ann::tc

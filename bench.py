@@ -622,6 +622,70 @@ def measure_prefill(name, world, rank, comm, reps=10):
     return res
 
 
+def measure_prefill_block(world, rank, comm, reps=5):
+    """The c3 block as the path runs it (test/unit/nn/attention.cpp:856-974
+    composes it): hidden states [B*T, d_model] -> rmsNorm (eps 1e-6, weight
+    1 + N(0, 0.02)) -> qkvProjection (cuBLAS fp32 GEMMs, weights
+    N(0, 1/sqrt(d_model)); column-parallel: this rank's heads' columns) ->
+    ropeInPlace(Q, K) (theta 1e4) -> fused causal prefill of this rank's heads
+    -> gather into every rank's BTHD output. CUDA events around each stage
+    (max over ranks of the means); the attention TFLOP/s of the line's
+    c3_prefill counts the attention stage alone."""
+    import numpy as np
+    import torch
+
+    import alpakann_b200 as ann
+    from alpakann_b200.sharded import HeadShard, HeadShardedPrefill
+    B, T, H, D = 4, 4096, 32, 128
+    dm, Hl, N = H * D, H // world, 4 * 4096
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    x = torch.randn((N, dm), generator=gen, device="cuda")
+    w = 1.0 + 0.02 * torch.randn((dm,), generator=gen, device="cuda")
+    Ws = [torch.randn((dm, Hl * D), generator=gen, device="cuda") / math.sqrt(dm) for _ in range(3)]
+    y = torch.empty_like(x)
+    Q, K, V = (torch.empty((N, Hl * D), device="cuda") for _ in range(3))
+    ang = np.arange(T, dtype=np.float64)[:, None] * np.power(1e4, -2.0 * np.arange(D // 2) / D)[None]
+    cos, sin = torch.from_numpy(np.cos(ang)).float().cuda(), torch.from_numpy(np.sin(ang)).float().cuda()
+    sharded = HeadShardedPrefill(HeadShard(rank, world, H, H), B, T, D, torch.float32, "cuda", comm)
+    queue = ann.Queue()
+    nn = ann.onHost.nn
+    q4, k4, v4 = (t.view(B, T, Hl, D) for t in (Q, K, V))
+    stages = ["rmsNorm", "qkvProjection", "ropeInPlace", "attention + gather"]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
+    acc = [0.0] * len(stages)
+
+    def block(timed):
+        if timed:
+            ev[0].record()
+        nn.rmsNorm(queue, None, x, w, y, 1e-6)
+        if timed:
+            ev[1].record()
+        nn.qkvProjection(queue, y, Ws[0], Ws[1], Ws[2], Q, K, V)
+        if timed:
+            ev[2].record()
+        nn.ropeInPlace(queue, None, q4, k4, cos, sin)
+        if timed:
+            ev[3].record()
+        sharded.run(queue, q4, k4, v4, 1.0 / math.sqrt(D))
+        if timed:
+            ev[4].record()
+
+    block(False)
+    barrier(world)
+    for _ in range(reps):
+        block(True)
+        torch.cuda.synchronize()
+        for i in range(len(stages)):
+            acc[i] += ev[i].elapsed_time(ev[i + 1]) / reps
+    acc = max_over_ranks(acc, world)
+    del x, y, Q, K, V, Ws, sharded
+    torch.cuda.empty_cache()
+    return {"workload": "prefill block: hidden [16384, 4096] -> rmsNorm -> qkvProjection -> ropeInPlace -> causal "
+                        "attention [4, 4096, 32 x 128], fp32", "ms": sum(acc),
+            "stages_ms": {n: round(t, 4) for n, t in zip(stages, acc)},
+            "tokens_per_s": N / (sum(acc) / 1e3), "qkv": "cuBLAS fp32 GEMMs, column-parallel over the ranks"}
+
+
 def prefill_parity(out, q, k, v, scale, rank, world, rows=(0, 1, 777, -1)):
     """The gathered prefill output at a few query rows of every batch and head
     against an fp64 recomputation on the device by the rank that owns the head
@@ -1018,6 +1082,7 @@ def main():
                         "parity": o["parity"]}
         for name in ("c3", "c4"):
             extra[f"{name}_prefill"] = measure_prefill(name, world, rank, comm)
+        extra["c3_block"] = measure_prefill_block(world, rank, comm)
 
     if rank == 0:
         r = main_res
