@@ -443,6 +443,12 @@ int launch_f64(ann_stream stream, F64Args& a, double scale, int64_t batch_heads)
     int64_t const tiles = static_cast<int64_t>(a.q_tiles) * batch_heads;
     a.splits = f64_splits(tiles, static_cast<int>(ceil_div(a.causal ? a.Tq : a.Tk, 32)));
     if (tiles * a.splits > INT32_MAX) a.splits = 1;
+    if constexpr (D <= 64) {  // ANN_PREFILL_F64_TILE=16 / 32 pins the key tile
+        if (const char* env = std::getenv("ANN_PREFILL_F64_TILE")) {
+            if (std::atoi(env) == 16) return launch_f64_bn<D, 16>(stream, a, scale, batch_heads);
+            if (std::atoi(env) == 32) return launch_f64_bn<D, 32>(stream, a, scale, batch_heads);
+        }
+    }
     if (a.splits > 1) return launch_f64_bn<D, 32>(stream, a, scale, batch_heads);
     if constexpr (D <= 64) {
         // 16-key tiles once the grid fills at least four waves of 3-CTA slots
