@@ -674,7 +674,7 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
     extern __shared__ __align__(128) unsigned char part_smem[];
     __shared__ __align__(8) uint64_t full;
     __shared__ T scratch[8];
-    __shared__ T xch[2];  // this CTA's max and sum, read by the peers
+    __shared__ T xch[2][2];  // this CTA's max and sum, read by the peers; two rows' worth (by parity)
     cg::cluster_group cluster = cg::this_cluster();
     int const tid = threadIdx.x, s = static_cast<int>(cluster.block_rank());
     int64_t const part = a.len / kSplit, pieces = part / NV, e_begin = s * part;
@@ -732,11 +732,12 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
                 *reinterpret_cast<P*>(buf + e0) = x;
             }
         }
+        T* x = xch[it & 1];
         m = block_max<8>(m, scratch);
-        if (tid == 0) xch[0] = m;
+        if (tid == 0) x[0] = m;
         cluster.sync();
         T M = Lowest<T>::value;
-        for (int r = 0; r < kSplit; ++r) M = fmax(M, cluster.map_shared_rank(xch, r)[0]);
+        for (int r = 0; r < kSplit; ++r) M = fmax(M, cluster.map_shared_rank(x, r)[0]);
         T sum{};
         if (!dead) {
             for (int64_t p = tid; p < pieces; p += 256) {
@@ -752,10 +753,10 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
             }
         }
         sum = block_sum<8>(sum, scratch);
-        if (tid == 0) xch[1] = sum;
+        if (tid == 0) x[1] = sum;
         cluster.sync();
         T L{};
-        for (int r = 0; r < kSplit; ++r) L += cluster.map_shared_rank(xch, r)[1];
+        for (int r = 0; r < kSplit; ++r) L += cluster.map_shared_rank(x, r)[1];
         // one division per row; unkept slots tested only when the sum < 1 (see softmax_regs)
         T const inv = T(1) / L;
         bool const exact = !(L >= T(1));
@@ -772,8 +773,14 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
                 *reinterpret_cast<P*>(out + oo + e_begin + e0) = x;
             }
         }
-        cluster.sync();  // the peers have read xch, and this CTA is done with its buffer
+        // This CTA is done with its buffer before the next copy lands in it. No
+        // cluster barrier here: the peers read this row's exchange slot before
+        // they reach the next row's first cluster barrier, and the next row
+        // writes the other slot (a cluster barrier right after the output
+        // stores would wait for all of them to drain).
+        __syncthreads();
     }
+    cluster.sync();  // the peers' last reads of this CTA's exchange slots are done before it exits
 }
 
 // Launches softmax_cluster on a grid of resident clusters; false when it does not apply.
