@@ -281,7 +281,11 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
                     if (live) tmax = fmax(tmax, x);
                 }
             double const m_new = fmax(m_run[h], quad_max(tmax));
-            double const alpha = exp(m_run[h] - m_new);
+            // rescale only when the row max grew (the same in the 4 threads of a
+            // quad): otherwise alpha = exp(0) = 1 and every product by it is exact,
+            // so skipping them changes no bit
+            bool const grow = m_new != m_run[h];
+            double const alpha = grow ? exp(m_run[h] - m_new) : 1.0;
             double psum = 0.0;
 #pragma unroll
             for (int j = 0; j < NJ; ++j)
@@ -291,12 +295,14 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
                     sacc[j][2 * h + e] = p;
                     psum += p;
                 }
-            l_run[h] = l_run[h] * alpha + quad_sum(psum);
+            l_run[h] = (grow ? l_run[h] * alpha : l_run[h]) + quad_sum(psum);
             m_run[h] = m_new;
+            if (grow) {
 #pragma unroll
-            for (int n = 0; n < NO; ++n) {
-                o[n][2 * h] *= alpha;
-                o[n][2 * h + 1] *= alpha;
+                for (int n = 0; n < NO; ++n) {
+                    o[n][2 * h] *= alpha;
+                    o[n][2 * h + 1] *= alpha;
+                }
             }
         }
 
