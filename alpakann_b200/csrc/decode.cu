@@ -327,7 +327,6 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
             if (mout) mc::store(mout + d * a.o_d, val);
             else out[d * a.o_d] = val;
         }
-        if (mout) __threadfence_system();  // performed at system scope before the CTA retires
         return;
     }
     for (int d = tid; d < D; d += kThreads) {
@@ -361,7 +360,6 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecodeArgs a, T scale)
         if (mout) mc::store(mout + (lo + tid) * a.o_d, val);
         else out[(lo + tid) * a.o_d] = val;
     }
-    if (mout) __threadfence_system();  // performed at system scope before the CTA retires
     cluster.sync();  // peers' shared memory must outlive the reads above
 }
 

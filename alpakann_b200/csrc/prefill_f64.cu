@@ -154,7 +154,6 @@ __device__ void merge_splits(F64Args const& a, unsigned char* smem, double const
         if (a.mirror) mc::store(a.mirror + off, val);
         else a.out[off] = val;
     }
-    if (a.mirror) __threadfence_system();
     cluster.sync();
 }
 
@@ -337,10 +336,11 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         merge_splits<D>(a, smem, o, m_run, l_run, q_rows, b, hq, q0);
         return;
     }
-    if (a.mirror != nullptr && a.o_pairs) {
-        // Multicast output: whole rows a warp instruction (one NVLink packet per
-        // 512 contiguous bytes, not 64 bytes from each of 8 rows), staged in the
-        // Q tile, which no MMA reads any more.
+    if (a.o_pairs) {
+        // Whole rows a warp instruction (512 contiguous bytes, one packet stream
+        // to the switch for a multicast output; not 64 bytes from each of 8
+        // rows), staged in the Q tile, which no MMA reads any more. No
+        // system-scope fence: the signal barrier after the kernel fences.
         __syncthreads();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -355,9 +355,10 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         for (int e = tid; e < q_rows * PAIRS; e += kThreads) {
             int const r = e / PAIRS, c2 = e % PAIRS;
             double2 const val = *reinterpret_cast<double2 const*>(Qs + r * C::LD + 2 * c2);
-            mc::store(a.mirror + b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + 2 * c2, val);
+            int64_t const off = b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + 2 * c2;
+            if (a.mirror != nullptr) mc::store(a.mirror + off, val);
+            else *reinterpret_cast<double2*>(a.out + off) = val;
         }
-        __threadfence_system();  // performed at system scope before the CTA retires
         return;
     }
     int64_t const obase_off = b * a.o_b + q0 * a.o_t + hq * a.o_h;
@@ -388,9 +389,6 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
             }
         }
     }
-    // the multicast stores are performed at system scope before the CTA
-    // retires (the barrier that follows the kernel publishes them)
-    if (a.mirror) __threadfence_system();
 }
 
 template <int D, int BN>
@@ -430,15 +428,17 @@ int launch_f64_bn(ann_stream stream, F64Args& a, double scale, int64_t batch_hea
 }
 
 // Key-range splits per query tile: 1 while the grid already fills the GPU,
-// else the smallest of 2 / 4 that gives about two CTAs per SM (a head-sharded
+// else 2 or 4, doubling while the CTAs are fewer than the SMs (a head-sharded
 // rank's few heads leave most SMs idle, and the last query tiles hold every
-// key: without a split they alone set the time). ANN_PREFILL_F64_SPLITS pins it.
+// key: without a split they alone set the time). Measured on c4 shards: 128
+// tiles (2 GPUs) 0.163 ms with 2 splits, 0.202 with 4, 0.228 with none; 512
+// tiles (1 GPU) fastest with none. ANN_PREFILL_F64_SPLITS pins it.
 int f64_splits(int64_t tiles, int max_key_tiles) {
     if (const char* env = std::getenv("ANN_PREFILL_F64_SPLITS")) {
         int const sp = std::atoi(env);
         if (sp == 1 || sp == 2 || sp == 4) return sp;
     }
-    int64_t const want = 2 * static_cast<int64_t>(sm_count());
+    int64_t const want = static_cast<int64_t>(sm_count());
     int sp = 1;
     while (sp < 4 && tiles * sp < want && max_key_tiles >= 4 * sp) sp *= 2;
     return sp;

@@ -457,11 +457,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
         float* lx = reinterpret_cast<float*>(smem + C::OFF_PLO);
         if (ok) lx[tid] = l_part;
         bool const all_ok = !row_sync_any(!ok);  // the same for every row thread
-        if (a.mirror != nullptr && a.o_vec) {
-            // Multicast output: each store is one NVLink packet to the switch, so the
-            // rows are written whole by a warp (512 contiguous bytes an instruction),
-            // not 16 bytes from each of 32 rows. O goes through a padded staging
-            // tile over the K / V buffers, which no MMA reads any more.
+        if (a.o_vec) {
+            // O rows are written whole by a warp (512 contiguous bytes an
+            // instruction), not 16 bytes from each of 32 rows: one packet stream to
+            // the switch for a multicast output, full lines for a local one. O goes
+            // through a padded staging tile over the K / V buffers, which no MMA
+            // reads any more. (No system-scope fence before the CTA retires: the
+            // signal barrier that follows the kernel in stream order fences, and its
+            // release covers every store of this kernel. A fence in each CTA cost
+            // 0.17 ms of 1.51 on the 2-GPU c3 run.)
             constexpr int PITCH = D * 4 + 16;
             unsigned char* stage = smem + C::OFF_K;
             static_assert(kBM * PITCH <= 4 * (C::TILE_K + C::TILE_V), "staging fits the K / V buffers");
@@ -489,11 +493,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                     int64_t const qr = q0 + rr;
                     if (qr >= a.Tq) continue;
                     float4 const val = *reinterpret_cast<float4 const*>(stage + rr * PITCH + c4 * 16);
-                    mc::store(a.mirror + b * a.o_b + qr * a.o_t + hq * a.o_h + c4 * 4, val);
+                    int64_t const off = b * a.o_b + qr * a.o_t + hq * a.o_h + c4 * 4;
+                    if (a.mirror != nullptr) mc::store(a.mirror + off, val);
+                    else *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = val;
                 }
-                // performed at system scope before the CTA retires (the barrier
-                // that follows the kernel publishes them)
-                __threadfence_system();
             }
         } else if (all_ok) {
             tc::fence_after_sync();
@@ -522,7 +525,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                     }
                 }
             }
-            if (mrow) __threadfence_system();
         }
     }
 
