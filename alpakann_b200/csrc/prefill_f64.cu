@@ -336,11 +336,12 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         merge_splits<D>(a, smem, o, m_run, l_run, q_rows, b, hq, q0);
         return;
     }
-    if (a.o_pairs) {
-        // Whole rows a warp instruction (512 contiguous bytes, one packet stream
-        // to the switch for a multicast output; not 64 bytes from each of 8
-        // rows), staged in the Q tile, which no MMA reads any more. No
-        // system-scope fence: the signal barrier after the kernel fences.
+    if (a.mirror != nullptr && a.o_pairs) {
+        // Multicast output: whole rows a warp instruction (512 contiguous bytes,
+        // one packet stream to the switch; not 64 bytes from each of 8 rows),
+        // staged in the Q tile, which no MMA reads any more. No system-scope
+        // fence: the signal barrier after the kernel fences. (Local outputs keep
+        // the direct stores below: staging them measured no faster on c4.)
         __syncthreads();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -355,9 +356,7 @@ __global__ void __launch_bounds__(kThreads, FCfg<D, BN>::MIN_CTAS) prefill_f64_k
         for (int e = tid; e < q_rows * PAIRS; e += kThreads) {
             int const r = e / PAIRS, c2 = e % PAIRS;
             double2 const val = *reinterpret_cast<double2 const*>(Qs + r * C::LD + 2 * c2);
-            int64_t const off = b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + 2 * c2;
-            if (a.mirror != nullptr) mc::store(a.mirror + off, val);
-            else *reinterpret_cast<double2*>(a.out + off) = val;
+            mc::store(a.mirror + b * a.o_b + (q0 + r) * a.o_t + hq * a.o_h + 2 * c2, val);
         }
         return;
     }
