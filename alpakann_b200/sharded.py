@@ -97,6 +97,25 @@ def reassembly_views(gathered: torch.Tensor, out: torch.Tensor):
     return gathered.permute(1, 2, 0, 3, 4), out.view(B, T, G, Hl, D)
 
 
+def _mirror_or_none(shape, dtype, gather_requested: str):
+    """A MirrorBuffer for 'multicast' / 'auto'; for 'auto' every rank agrees on the
+    outcome (one all-reduce), and a failure anywhere means the NCCL gather on every
+    rank. None when the NCCL gather is to be used."""
+    import torch.distributed as dist
+
+    from .mirror import MirrorBuffer
+    if gather_requested == "multicast":
+        return MirrorBuffer(shape, dtype)
+    buf, ok = None, 1
+    try:
+        buf = MirrorBuffer(shape, dtype)
+    except Exception:  # no multicast object on this node after all
+        ok = 0
+    flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return buf if int(flag) == 1 else None
+
+
 def choose_gather(gather: str, world: int) -> str:
     """'multicast' (outputs stored through an NVLink multicast address inside the
     kernel, then a signal barrier), 'nccl' (all-gather + re-assembly) or, for
@@ -124,8 +143,12 @@ class HeadShardedDecode:
         self.shard, self.B, self.D, self.comm = shard, B, D, comm
         self.gathered = None
         if self.gather == "multicast":
-            from .mirror import MirrorBuffer
-            self.mirror = MirrorBuffer((B, 1, shard.heads, D), dtype)
+            self.mirror = _mirror_or_none((B, 1, shard.heads, D), dtype, gather)
+            if self.mirror is None:
+                if comm is None:
+                    raise ValueError("no multicast on this node, and the NCCL gather needs a Comm")
+                self.gather = "nccl"
+        if self.gather == "multicast":
             self.out = self.mirror.tensor
             self.out_local = self.out[:, :, shard.head_slice, :]  # this rank's heads of every copy
             self._out_mc = self.mirror.mirror_of(self.out_local)
@@ -172,8 +195,12 @@ class HeadShardedPrefill:
             raise ValueError("a sharded prefill over several ranks needs a Comm")
         self.shard, self.B, self.T, self.D, self.comm = shard, B, T, D, comm
         if self.gather == "multicast":
-            from .mirror import MirrorBuffer
-            self.mirror = MirrorBuffer((B, T, shard.heads, D), dtype)
+            self.mirror = _mirror_or_none((B, T, shard.heads, D), dtype, gather)
+            if self.mirror is None:
+                if comm is None:
+                    raise ValueError("no multicast on this node, and the NCCL gather needs a Comm")
+                self.gather = "nccl"
+        if self.gather == "multicast":
             self.out = self.mirror.tensor
             self.out_local = self.out[:, :, shard.head_slice, :]
             self._out_mc = self.mirror.mirror_of(self.out_local)
