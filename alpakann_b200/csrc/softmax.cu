@@ -711,10 +711,16 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
             }
             dead = true;
         }
+        // the kept range [lo, hi) within this CTA's part, in 32-bit; a part kept
+        // whole (every non-causal row) takes the loops without per-element tests
+        int const plo = static_cast<int>(lo - e_begin < 0 ? 0 : (lo - e_begin > part ? part : lo - e_begin));
+        int const phi = static_cast<int>(hi - e_begin < 0 ? 0 : (hi - e_begin > part ? part : hi - e_begin));
+        bool const whole = plo == 0 && phi == static_cast<int>(part);
+        int const np = static_cast<int>(pieces);
         T m = Lowest<T>::value;
         if (!dead) {
-            for (int64_t p = tid; p < pieces; p += 256) {
-                int64_t const e0 = p * NV;
+            for (int p = tid; p < np; p += 256) {
+                int const e0 = p * NV;
                 P x = *reinterpret_cast<P const*>(buf + e0);
                 T* xe = reinterpret_cast<T*>(&x);
                 if constexpr (MASK) {
@@ -723,13 +729,18 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
 #pragma unroll
                     for (int k = 0; k < NV; ++k) xe[k] = add_rn(xe[k], ye[k]);
                 }
+                if (whole) {
 #pragma unroll
-                for (int k = 0; k < NV; ++k) {
-                    int64_t const e = e_begin + e0 + k;
-                    if (e < lo || e >= hi) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
-                    m = fmax(m, xe[k]);
+                    for (int k = 0; k < NV; ++k) m = fmax(m, xe[k]);
+                    if constexpr (MASK) *reinterpret_cast<P*>(buf + e0) = x;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NV; ++k) {
+                        if (e0 + k < plo || e0 + k >= phi) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
+                        m = fmax(m, xe[k]);
+                    }
+                    *reinterpret_cast<P*>(buf + e0) = x;
                 }
-                *reinterpret_cast<P*>(buf + e0) = x;
             }
         }
         T* x = xch[it & 1];
@@ -740,8 +751,8 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
         for (int r = 0; r < kSplit; ++r) M = fmax(M, cluster.map_shared_rank(x, r)[0]);
         T sum{};
         if (!dead) {
-            for (int64_t p = tid; p < pieces; p += 256) {
-                int64_t const e0 = p * NV;
+            for (int p = tid; p < np; p += 256) {
+                int const e0 = p * NV;
                 P x = *reinterpret_cast<P const*>(buf + e0);
                 T* xe = reinterpret_cast<T*>(&x);
 #pragma unroll
@@ -761,16 +772,20 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
         T const inv = T(1) / L;
         bool const exact = !(L >= T(1));
         if (!dead) {
-            for (int64_t p = tid; p < pieces; p += 256) {
-                int64_t const e0 = p * NV;
+            bool const plain = whole || !exact;
+            T* orow = out + oo + e_begin;
+            for (int p = tid; p < np; p += 256) {
+                int const e0 = p * NV;
                 P x = *reinterpret_cast<P const*>(buf + e0);
                 T* xe = reinterpret_cast<T*>(&x);
+                if (plain) {
 #pragma unroll
-                for (int k = 0; k < NV; ++k) {
-                    int64_t const e = e_begin + e0 + k;
-                    xe[k] = exact && (e < lo || e >= hi) ? T(0) : xe[k] * inv;
+                    for (int k = 0; k < NV; ++k) xe[k] = xe[k] * inv;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NV; ++k) xe[k] = (e0 + k < plo || e0 + k >= phi) ? T(0) : xe[k] * inv;
                 }
-                *reinterpret_cast<P*>(out + oo + e_begin + e0) = x;
+                *reinterpret_cast<P*>(orow + e0) = x;
             }
         }
         // This CTA is done with its buffer before the next copy lands in it. No
