@@ -427,17 +427,18 @@ int launch_f64_bn(ann_stream stream, F64Args& a, double scale, int64_t batch_hea
 }
 
 // Key-range splits per query tile: 1 while the grid already fills the GPU,
-// else 2 or 4, doubling while the CTAs are fewer than the SMs (a head-sharded
-// rank's few heads leave most SMs idle, and the last query tiles hold every
-// key: without a split they alone set the time). Measured on c4 shards: 128
-// tiles (2 GPUs) 0.163 ms with 2 splits, 0.202 with 4, 0.228 with none; 512
-// tiles (1 GPU) fastest with none. ANN_PREFILL_F64_SPLITS pins it.
+// else 2 or 4, doubling while the CTAs are fewer than two an SM (a
+// head-sharded rank's few heads leave most SMs idle, and the last query tiles
+// hold every key: without a split they alone set the time). Measured on c4
+// (64-row tiles): 256 tiles (the 2-GPU shard) 0.163 ms with 2 splits, 0.202
+// with 4, 0.228 with none; 512 tiles (1 GPU) fastest with none (0.236 ms, 0.300
+// with 2). ANN_PREFILL_F64_SPLITS pins it.
 int f64_splits(int64_t tiles, int max_key_tiles) {
     if (const char* env = std::getenv("ANN_PREFILL_F64_SPLITS")) {
         int const sp = std::atoi(env);
         if (sp == 1 || sp == 2 || sp == 4) return sp;
     }
-    int64_t const want = static_cast<int64_t>(sm_count());
+    int64_t const want = 2 * static_cast<int64_t>(sm_count());
     int sp = 1;
     while (sp < 4 && tiles * sp < want && max_key_tiles >= 4 * sp) sp *= 2;
     return sp;
