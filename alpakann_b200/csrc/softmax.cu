@@ -654,30 +654,38 @@ bool bulk_launched(SoftmaxArgs const& a, cudaStream_t s) {
 }
 
 // Long aligned rows (over 64 KB of input + mask) split over a cluster of
-// kSplit CTAs: CTA s brings the s-th quarter of the row into its shared
-// memory by one bulk copy, the row's max and sum are combined across the
-// cluster through distributed shared memory, and each CTA normalises and
-// writes its quarter. A quarter-row per CTA lets several CTAs (rows) per SM be
-// in flight, where softmax_bulk holds one whole row per SM (rows of 32768
-// fp32: one 128 KiB copy at a time, the SM idle while it lands). Waits are
-// bounded; a CTA whose copy does not land sets ANN_DEVERR_WAIT_TIMEOUT and
-// keeps joining the cluster barriers (its peers still meet it there) without
-// issuing more copies.
-constexpr int kSplit = 4;
+// kSplit CTAs. CTA s brings the s-th part of the row into its shared memory by
+// one bulk copy and reads it into registers (at most kSplitVecs 16-byte pieces
+// a thread), and at once issues the copy of its part of the next row into the
+// same buffer: a copy is in flight while the row is reduced, exponentiated and
+// written, and the buffer stays one stage (several clusters an SM). Max and
+// sum: the CTA reduces its part (shuffles, then one warp over the per-warp
+// values), and one lane per peer sends the CTA's value into that peer's
+// exchange slot with st.async, completing on the peer's mbarrier; every CTA
+// combines the kSplit values in rank order, so all hold the same max and sum.
+// No cluster-wide barrier inside the row loop: its release would wait for
+// this CTA's output stores of the previous row to drain. Waits are bounded; a
+// CTA whose copy does not land sets ANN_DEVERR_WAIT_TIMEOUT and keeps sending
+// its (empty) values without issuing more copies; an exchange that does not
+// complete sets the same bit and the CTA stops waiting on exchanges.
+constexpr int kSplit = 4, kSplitVecs = 8;
 constexpr int64_t kSplitMinBytes = int64_t{64} << 10, kSplitPartBytes = int64_t{56} << 10;
 
-template <typename T, bool MASK>
-__global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
+template <typename T, bool MASK, int THREADS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) softmax_cluster(SoftmaxArgs a) {
     namespace cg = cooperative_groups;
     using P = typename Vec16<T>::type;
-    constexpr int NV = Vec16<T>::n;
+    constexpr int NV = Vec16<T>::n, WARPS = THREADS / 32;
+    static_assert(WARPS <= 32 && kSplit <= 32, "one warp combines the warps' values and sends to the peers");
     extern __shared__ __align__(128) unsigned char part_smem[];
     __shared__ __align__(8) uint64_t full;
-    __shared__ T scratch[8];
-    __shared__ T xch[2][2];  // this CTA's max and sum, read by the peers; two rows' worth (by parity)
-    cg::cluster_group cluster = cg::this_cluster();
-    int const tid = threadIdx.x, s = static_cast<int>(cluster.block_rank());
-    int64_t const part = a.len / kSplit, pieces = part / NV, e_begin = s * part;
+    __shared__ __align__(8) uint64_t xbar[2][2];  // [row parity][max, sum]: the peers' values have arrived
+    __shared__ T xv[2][2][kSplit];                // [row parity][max, sum][source CTA]
+    __shared__ T red[2][WARPS];                   // per-warp max / sum of this CTA
+    int const tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int const s = static_cast<int>(cluster_ctarank());
+    int64_t const part = a.len / kSplit, e_begin = s * part;
+    int const np = static_cast<int>(part / NV);  // pieces of this CTA's part, <= kSplitVecs * THREADS
     uint32_t const part_bytes = static_cast<uint32_t>(part) * sizeof(T);
     int64_t const n_clusters = gridDim.x / kSplit, cid = blockIdx.x / kSplit;
     int64_t const iters = ceil_div(a.rows - cid, n_clusters);
@@ -685,27 +693,58 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
     T const* in = static_cast<T const*>(a.in);
     T const* mk = static_cast<T const*>(a.mask);
     T* out = static_cast<T*>(a.out);
-    T* buf = reinterpret_cast<T*>(part_smem);
+    T const* buf = reinterpret_cast<T const*>(part_smem);
     T const* mbuf = buf + part;
+    auto issue = [&](int64_t it) {  // thread 0: this CTA's part of row cid + it * n_clusters
+        int64_t oi, oo, om = 0;
+        row_offsets(a, cid + it * n_clusters, oi, oo, om);
+        mbar_arrive_expect_tx(bar, part_bytes * (MASK ? 2u : 1u));
+        bulk_copy_g2s(dst, in + oi + e_begin, part_bytes, bar);
+        if constexpr (MASK) bulk_copy_g2s(dst + part_bytes, mk + om + e_begin, part_bytes, bar);
+    };
     if (tid == 0) {
         mbar_init(bar, 1);
+        for (int p = 0; p < 2; ++p)
+            for (int k = 0; k < 2; ++k) mbar_init(smem_u32(&xbar[p][k]), 1);
         fence_mbar_init();
+        if (iters > 0) issue(0);
     }
     __syncthreads();
-    bool dead = false;  // a copy did not land: no more copies, but every barrier is still joined
+    cg::this_cluster().sync();  // every peer's exchange barriers exist before the first value is sent to them
+    bool dead = false;          // a copy did not land: no more copies, but every exchange is still joined
+    bool lost = false;          // an exchange did not complete: no more waits on exchanges
+    // The row's max (K = 0) or sum (K = 1) over the cluster, from this thread's
+    // partial v; `at_barrier` runs in thread 0 once every thread has arrived.
+    auto exchange = [&](T v, int K, int64_t it, auto&& at_barrier) -> T {
+        v = K == 0 ? warp_max(v) : warp_sum(v);
+        if (lane == 0) red[K][warp] = v;
+        __syncthreads();
+        if (tid == 0) at_barrier();
+        int const par = static_cast<int>(it & 1);
+        uint32_t const xb = smem_u32(&xbar[par][K]);
+        if (warp == 0) {
+            T c = lane < WARPS ? red[K][lane] : (K == 0 ? Lowest<T>::value : T(0));
+            c = K == 0 ? warp_max(c) : warp_sum(c);
+            if (lane == 0) mbar_arrive_expect_tx(xb, kSplit * sizeof(T));
+            if (lane < kSplit) st_async_cluster(map_cluster(smem_u32(&xv[par][K][s]), lane), c, map_cluster(xb, lane));
+        }
+        if (!lost && !mbar_wait_bounded<true>(xb, static_cast<uint32_t>((it >> 1) & 1))) {
+            if (tid == 0) atomicOr(&g_softmax_error, ANN_DEVERR_WAIT_TIMEOUT);
+            lost = true;
+        }
+        T r = xv[par][K][0];
+#pragma unroll
+        for (int q = 1; q < kSplit; ++q) r = K == 0 ? fmax(r, xv[par][K][q]) : r + xv[par][K][q];
+        return r;
+    };
     for (int64_t it = 0; it < iters; ++it) {
         int64_t const row = cid + it * n_clusters;
         int64_t oi, oo, om = 0, lo, hi;
         row_offsets(a, row, oi, oo, om);
         kept_range(a, row, lo, hi);
-        if (tid == 0 && !dead) {
-            mbar_arrive_expect_tx(bar, part_bytes * (MASK ? 2u : 1u));
-            bulk_copy_g2s(dst, in + oi + e_begin, part_bytes, bar);
-            if constexpr (MASK) bulk_copy_g2s(dst + part_bytes, mk + om + e_begin, part_bytes, bar);
-        }
         bool const ok = dead || mbar_wait_bounded(bar, static_cast<uint32_t>(it & 1));
         if (__syncthreads_or(!ok)) {
-            if (tid == 0) {
+            if (tid == 0 && !dead) {
                 atomicOr(&g_softmax_error, ANN_DEVERR_WAIT_TIMEOUT);
                 mbar_wait_bounded(bar, static_cast<uint32_t>(it & 1));  // the copy in flight (bounded)
             }
@@ -716,13 +755,16 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
         int const plo = static_cast<int>(lo - e_begin < 0 ? 0 : (lo - e_begin > part ? part : lo - e_begin));
         int const phi = static_cast<int>(hi - e_begin < 0 ? 0 : (hi - e_begin > part ? part : hi - e_begin));
         bool const whole = plo == 0 && phi == static_cast<int>(part);
-        int const np = static_cast<int>(pieces);
+        P v[kSplitVecs];
         T m = Lowest<T>::value;
         if (!dead) {
-            for (int p = tid; p < np; p += 256) {
+#pragma unroll
+            for (int j = 0; j < kSplitVecs; ++j) {
+                int const p = tid + j * THREADS;
+                if (p >= np) break;
                 int const e0 = p * NV;
-                P x = *reinterpret_cast<P const*>(buf + e0);
-                T* xe = reinterpret_cast<T*>(&x);
+                v[j] = *reinterpret_cast<P const*>(buf + e0);
+                T* xe = reinterpret_cast<T*>(&v[j]);
                 if constexpr (MASK) {
                     P const y = *reinterpret_cast<P const*>(mbuf + e0);
                     T const* ye = reinterpret_cast<T const*>(&y);
@@ -732,52 +774,46 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
                 if (whole) {
 #pragma unroll
                     for (int k = 0; k < NV; ++k) m = fmax(m, xe[k]);
-                    if constexpr (MASK) *reinterpret_cast<P*>(buf + e0) = x;
                 } else {
 #pragma unroll
                     for (int k = 0; k < NV; ++k) {
                         if (e0 + k < plo || e0 + k >= phi) xe[k] = neg_inf(T{});  // exp of it is exactly 0 below
                         m = fmax(m, xe[k]);
                     }
-                    *reinterpret_cast<P*>(buf + e0) = x;
                 }
             }
         }
-        T* x = xch[it & 1];
-        m = block_max<8>(m, scratch);
-        if (tid == 0) x[0] = m;
-        cluster.sync();
-        T M = Lowest<T>::value;
-        for (int r = 0; r < kSplit; ++r) M = fmax(M, cluster.map_shared_rank(x, r)[0]);
+        // every thread holds its pieces once it reaches the exchange's CTA
+        // barrier: the buffer takes the next row's part from there on
+        T const M = exchange(m, 0, it, [&] {
+            if (!dead && it + 1 < iters) issue(it + 1);
+        });
         T sum{};
         if (!dead) {
-            for (int p = tid; p < np; p += 256) {
-                int const e0 = p * NV;
-                P x = *reinterpret_cast<P const*>(buf + e0);
-                T* xe = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int j = 0; j < kSplitVecs; ++j) {
+                if (tid + j * THREADS >= np) break;
+                T* xe = reinterpret_cast<T*>(&v[j]);
 #pragma unroll
                 for (int k = 0; k < NV; ++k) {
                     xe[k] = exp_t(xe[k] - M);
                     sum += xe[k];
                 }
-                *reinterpret_cast<P*>(buf + e0) = x;
             }
         }
-        sum = block_sum<8>(sum, scratch);
-        if (tid == 0) x[1] = sum;
-        cluster.sync();
-        T L{};
-        for (int r = 0; r < kSplit; ++r) L += cluster.map_shared_rank(x, r)[1];
+        T const L = exchange(sum, 1, it, [] {});
         // one division per row; unkept slots tested only when the sum < 1 (see softmax_regs)
         T const inv = T(1) / L;
         bool const exact = !(L >= T(1));
         if (!dead) {
             bool const plain = whole || !exact;
             T* orow = out + oo + e_begin;
-            for (int p = tid; p < np; p += 256) {
+#pragma unroll
+            for (int j = 0; j < kSplitVecs; ++j) {
+                int const p = tid + j * THREADS;
+                if (p >= np) break;
                 int const e0 = p * NV;
-                P x = *reinterpret_cast<P const*>(buf + e0);
-                T* xe = reinterpret_cast<T*>(&x);
+                T* xe = reinterpret_cast<T*>(&v[j]);
                 if (plain) {
 #pragma unroll
                     for (int k = 0; k < NV; ++k) xe[k] = xe[k] * inv;
@@ -785,27 +821,22 @@ __global__ void __launch_bounds__(256) softmax_cluster(SoftmaxArgs a) {
 #pragma unroll
                     for (int k = 0; k < NV; ++k) xe[k] = (e0 + k < plo || e0 + k >= phi) ? T(0) : xe[k] * inv;
                 }
-                *reinterpret_cast<P*>(orow + e0) = x;
+                *reinterpret_cast<P*>(orow + e0) = v[j];
             }
         }
-        // This CTA is done with its buffer before the next copy lands in it. No
-        // cluster barrier here: the peers read this row's exchange slot before
-        // they reach the next row's first cluster barrier, and the next row
-        // writes the other slot (a cluster barrier right after the output
-        // stores would wait for all of them to drain).
-        __syncthreads();
     }
-    cluster.sync();  // the peers' last reads of this CTA's exchange slots are done before it exits
+    cg::this_cluster().sync();  // no CTA leaves while a peer's value may still be on its way to it
 }
 
-// Launches softmax_cluster on a grid of resident clusters; false when it does not apply.
-template <typename T, bool MASK>
-bool cluster_launched(SoftmaxArgs const& a, cudaStream_t s) {
-    int64_t const bytes = a.len * static_cast<int64_t>(sizeof(T)) * (MASK ? 2 : 1);
-    constexpr int NV = Vec16<T>::n;
-    if (bytes <= kSplitMinBytes || bytes > kSplit * kSplitPartBytes || a.len % (kSplit * NV) != 0) return false;
-    int const smem = static_cast<int>(bytes / kSplit);
-    auto kernel = softmax_cluster<T, MASK>;
+// Launches softmax_cluster<T, MASK, THREADS, MINB> on a grid of resident
+// clusters. MINB caps the registers: fp32 rows of 32768 on B200 (back-to-back
+// launches) took 90.6 us with three CTAs of 80 registers an SM = 0.90 of the
+// measured copy rate; two CTAs of 128 registers, or four of 64 with spills,
+// were slower (single launches: 115 and 132 us against 104). Two copy stages
+// a CTA (93.3 us) and clusters of eight CTAs (92.7) did not pay either.
+template <typename T, bool MASK, int THREADS, int MINB>
+bool cluster_launch(SoftmaxArgs const& a, int smem, cudaStream_t s) {
+    auto kernel = softmax_cluster<T, MASK, THREADS, MINB>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
         cudaGetLastError();
         return false;
@@ -816,7 +847,7 @@ bool cluster_launched(SoftmaxArgs const& a, cudaStream_t s) {
     cl.val.clusterDim.x = kSplit;
     cl.val.clusterDim.y = 1;
     cl.val.clusterDim.z = 1;
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = s;
     cfg.attrs = &cl;
@@ -830,6 +861,22 @@ bool cluster_launched(SoftmaxArgs const& a, cudaStream_t s) {
     int64_t const n = a.rows < clusters ? a.rows : clusters;
     cfg.gridDim = dim3(static_cast<unsigned>(n * kSplit));
     return cudaLaunchKernelEx(&cfg, kernel, a) == cudaSuccess;
+}
+
+// softmax_cluster where it applies: 256 threads a CTA while a part fits their
+// registers (kSplitVecs pieces a thread: rows up to 32768 fp32 / 16384 fp64),
+// 512 beyond; false when it does not apply.
+template <typename T, bool MASK>
+bool cluster_launched(SoftmaxArgs const& a, cudaStream_t s) {
+    int64_t const bytes = a.len * static_cast<int64_t>(sizeof(T)) * (MASK ? 2 : 1);
+    constexpr int NV = Vec16<T>::n;
+    if (bytes <= kSplitMinBytes || bytes > kSplit * kSplitPartBytes || a.len % (kSplit * NV) != 0) return false;
+    int const smem = static_cast<int>(bytes / kSplit);
+    int64_t const pieces = a.len / kSplit / NV;
+    constexpr bool f32 = sizeof(T) == 4;  // fp64 exp needs more registers: one CTA fewer an SM
+    if (pieces <= int64_t{kSplitVecs} * 256) return cluster_launch<T, MASK, 256, f32 ? 3 : 2>(a, smem, s);
+    if (pieces <= int64_t{kSplitVecs} * 512) return cluster_launch<T, MASK, 512, f32 ? 2 : 1>(a, smem, s);
+    return false;
 }
 
 // MASK: maskedSoftmax (onAcc/internal/nn/softmax.hpp:76-116), the row is

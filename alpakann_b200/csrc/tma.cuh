@@ -52,6 +52,20 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Asynchronous store of 4 / 8 bytes into shared memory of a CTA of the cluster
+// (shared::cluster addresses), completing as transaction bytes on that CTA's
+// mbarrier `bar_cluster`: a value reaches a peer without any barrier over the
+// whole cluster.
+__device__ __forceinline__ void st_async_cluster(uint32_t addr_cluster, float v, uint32_t bar_cluster) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr_cluster),
+                 "r"(__float_as_uint(v)), "r"(bar_cluster)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_cluster(uint32_t addr_cluster, double v, uint32_t bar_cluster) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(addr_cluster),
+                 "l"(__double_as_longlong(v)), "r"(bar_cluster)
+                 : "memory");
+}
 // try_wait with acquire semantics at cluster scope: for barriers that threads of
 // another CTA of the cluster arrive on.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
@@ -86,13 +100,16 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 // Waits for the phase with the given parity to complete. Returns false if it
 // has not completed after `limit_ns` (the caller reports an error and stops).
+// CLUSTER: acquire at cluster scope (arrivals or st.async from other CTAs).
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
-    if (mbar_try_wait(bar, parity)) return true;
+    auto probe = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+    if (probe()) return true;
     uint64_t const t0 = global_timer_ns();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+            if (probe()) return true;
         if (global_timer_ns() - t0 > limit_ns) return false;
     }
 }
