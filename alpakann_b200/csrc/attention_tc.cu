@@ -25,13 +25,18 @@
 //   row -> one bulk copy (cp.async.bulk, shared -> global) per row segment,
 //   so the 4-byte-per-thread scatter of row-per-thread TMEM reads never
 //   reaches global memory. Work unit: (batch*head, 256-row tile, key chunk).
-// apply_pair_kernel: 64-key chunks of P are loaded coalesced into shared
-//   memory, read back one row per thread, split into hi / lo and stored into
-//   TMEM (the A operand); V chunks (each CTA half of the head dims, raw + lo,
-//   MN-major 32-byte-atom swizzle) two buffers deep; O accumulates in TMEM.
+// apply_pair_kernel: a copy warp brings 64-key chunks of P into a 4-deep
+//   ring of shared-memory stages (one bulk copy per 256-byte row piece, rows
+//   padded by 16 bytes), so P, the large operand, is always several chunks in
+//   flight without passing through registers; each row thread reads its row
+//   back, splits it into hi / lo and stores both into TMEM (the A operand); V
+//   chunks (each CTA half of the head dims, raw + lo, MN-major 32-byte-atom
+//   swizzle) two buffers deep; O accumulates in TMEM.
 //   With few tiles the key range is split in two and both halves add into a
 //   zeroed output (red.global.add: 0 + a + b in either order is a + b, so the
 //   result does not depend on which half finishes first).
+#include <cuda.h>
+
 #include <cstdlib>
 #include <mutex>
 
@@ -61,10 +66,8 @@ __device__ __forceinline__ float tf32_lo(float x) {
 __device__ __forceinline__ float4 tf32_lo(float4 x) {
     return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
 }
-__device__ __forceinline__ void row_sync() {  // the 256 row threads of this CTA
-    asm volatile("bar.sync 1, %0;" ::"n"(kRowThreads) : "memory");
-}
-// row_sync that also ORs `v` over the 256 row threads: every one gets the same answer
+// A barrier of the 256 row threads of this CTA that also ORs `v` over them:
+// every one gets the same answer
 __device__ __forceinline__ bool row_sync_any(bool v) {
     uint32_t r;
     asm volatile(
@@ -317,26 +320,30 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
 // ============================================================================
 template <int D>
 struct ApCfg {
-    static constexpr int KC = 64;                // keys per chunk (MMA K = 8 x 8)
-    static constexpr int VCOLS = D / 2;          // head dims of a V chunk held by this CTA
+    static constexpr int KC = 64;                  // keys per chunk (MMA K = 8 x 8)
+    static constexpr int VCOLS = D / 2;            // head dims of a V chunk held by this CTA
     static constexpr int TILE_V = KC * VCOLS * 4;  // bytes of V hi (or lo) per buffer
-    static constexpr int BLK_V = KC * 128;       // one 32-float column block of V
-    static constexpr int TILE_P = kBM * KC * 4;  // raw P chunk, 128 rows x 256 bytes
-    static constexpr int OFF_V = 0;              // buffer i: hi at 2*i*TILE_V, lo at + TILE_V
-    static constexpr int OFF_P = 4 * TILE_V;     // buffer i at OFF_P + i*TILE_P
-    static constexpr int OFF_BAR = OFF_P + 2 * TILE_P;
-    // barriers: pready[2] pvdone[2] drain
-    static constexpr int NBAR = 5;
+    static constexpr int BLK_V = KC * 128;         // one 32-float column block of V
+    static constexpr int BOX_P = kBM * 128;        // one TMA box of P: 128 rows x 32 keys, 128-byte swizzle
+    static constexpr int STAGE_P = 2 * BOX_P;      // one P chunk: keys [0, 32) and [32, 64)
+    static constexpr int NST = 4;                  // P stages
+    static constexpr int OFF_V = 0;                // buffer i: hi at 2*i*TILE_V, lo at + TILE_V
+    static constexpr int OFF_P = 4 * TILE_V;       // stage i at OFF_P + i*STAGE_P
+    static constexpr int OFF_BAR = OFF_P + NST * STAGE_P;
+    // barriers: pready[2] pvdone[2] drain pfull[NST] pfree[NST]
+    static constexpr int NBAR = 5 + 2 * NST;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;
     static constexpr int USED = OFF_SLOT + 16;
     // >= 120 KB: one CTA per SM, so that its TMEM allocation never waits
     static constexpr int SMEM = USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static constexpr uint32_t O_COL = 0, P_HI = D, P_LO = D + 2 * KC;  // buffer b at + KC b
     static constexpr uint32_t TMEM_COLS = 512;
     static_assert(P_LO + 2 * KC <= TMEM_COLS, "TMEM budget");
     static constexpr uint32_t IDESC = tc::idesc_tf32(2 * kBM, D, true);
     static constexpr uint32_t ROW_ARRIVALS = 2 * kRowThreads;
 };
+constexpr int kApThreads = kRowThreads + 64;  // + warp 8 (MMA issuer) and warp 9 (P copies)
 
 struct ApArgs {
     const float* p;
@@ -353,7 +360,7 @@ struct ApArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
+__global__ void __launch_bounds__(kApThreads, 1) apply_pair_kernel(ApArgs a, const __grid_constant__ CUtensorMap pmap) {
     using C = ApCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -361,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
     unsigned char* smem = smem_raw + pad;
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
-    uint32_t const pready = bar, pvdone = bar + 16, drain = bar + 32;
+    uint32_t const pready = bar, pvdone = bar + 16, drain = bar + 32, pfull = bar + 40, pfree = pfull + 8 * C::NST;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
@@ -384,6 +391,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
         for (int i = 0; i < 2; ++i) mbar_init(pready + 8 * i, C::ROW_ARRIVALS);
         for (int i = 0; i < 2; ++i) mbar_init(pvdone + 8 * i, 1);
         mbar_init(drain, 1);
+        for (int i = 0; i < C::NST; ++i) mbar_init(pfull + 8 * i, 1);
+        for (int i = 0; i < C::NST; ++i) mbar_init(pfree + 8 * i, kRowThreads);
         fence_mbar_init();
         *abort = 0;
     }
@@ -422,30 +431,41 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
             commit(drain);
             if (!mbar_wait_bounded(drain, 0)) *abort = 1;
         }
+    } else if (warp == 9) {
+        // P of this CTA's 128 query rows, chunk by chunk, into an NST-deep ring
+        // of stages: two TMA boxes a chunk (128 rows x 32 keys each, 128-byte
+        // swizzle: 16-byte piece j of row r at r * 128 + ((j ^ (r % 8)) << 4)).
+        // Rows past Tq and keys past Tk arrive as zeros.
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < n_c; ++c) {
+                int const st = c % C::NST;
+                if (c >= C::NST && !mbar_wait_or_abort(pfree + 8 * st, ((c - C::NST) / C::NST) & 1, abort)) break;
+                int const key0 = static_cast<int>((c_begin + c) * C::KC);
+                uint32_t const full_bar = pfull + 8 * st, dst = sbase + C::OFF_P + st * C::STAGE_P;
+                mbar_arrive_expect_tx(full_bar, C::STAGE_P);
+                tma_load_4d(dst, &pmap, key0, static_cast<int>(q0), static_cast<int>(hq), static_cast<int>(b),
+                            full_bar);
+                tma_load_4d(dst + C::BOX_P, &pmap, key0 + 32, static_cast<int>(q0), static_cast<int>(hq),
+                            static_cast<int>(b), full_bar);
+                issued = c + 1;
+            }
+            // every copy has landed before the CTA can exit (the row threads
+            // have waited for all of them, unless they stopped early); bounded
+            for (int c = issued - C::NST < 0 ? 0 : issued - C::NST; c < issued; ++c)
+                mbar_wait_bounded(pfull + 8 * (c % C::NST), static_cast<uint32_t>((c / C::NST) & 1));
+        }
     } else {
         int const r = tid & (kBM - 1), h = tid >> 7;
         uint32_t const lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
         int64_t const qi = q0 + r;
-        // P chunk: 128 rows x 64 keys, element e = i * 256 + tid is row e / 16,
-        // float4 e % 16 (coalesced: a warp reads two whole 256-byte row pieces)
-        constexpr int NC4 = C::KC / 4;                          // float4 per P row piece
-        constexpr int PERP = kBM * NC4 / kRowThreads;           // 8
         constexpr int NV4V = C::VCOLS / 4;
         constexpr int PERV = C::KC * NV4V / kRowThreads;  // 2 (D 64) or 4 (D 128)
         static_assert(PERV >= 1, "V chunk per thread");
-        float const* pbase = a.p + b * a.p_b + hq * a.p_h;
         float const* vbase = a.v + b * a.v_b + kvh * a.v_h + rank * C::VCOLS;
-        float4 rp[PERP], rv[PERV];
-        auto load = [&](int c) {
+        float4 rv[PERV];
+        auto load_v = [&](int c) {
             int64_t const key0 = (c_begin + c) * C::KC;
-#pragma unroll
-            for (int i = 0; i < PERP; ++i) {
-                int const e = i * kRowThreads + tid, row = e / NC4, c4 = e % NC4;
-                int64_t const qrow = q0 + row, key = key0 + c4 * 4;
-                rp[i] = (qrow < a.Tq && key < a.Tk)
-                            ? __ldg(reinterpret_cast<float4 const*>(pbase + qrow * a.p_t + key))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
 #pragma unroll
             for (int i = 0; i < PERV; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4V, c4 = e % NV4V;
@@ -454,13 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
                                    : make_float4(0.f, 0.f, 0.f, 0.f);  // V rows past Tk must be finite
             }
         };
-        auto stage = [&](int buf) {  // raw P (row-swizzled) and V hi / lo (MN-major) into shared memory
-            unsigned char* pb = smem + C::OFF_P + buf * C::TILE_P;
-#pragma unroll
-            for (int i = 0; i < PERP; ++i) {
-                int const e = i * kRowThreads + tid, row = e / NC4, c4 = e % NC4;
-                *reinterpret_cast<float4*>(pb + row * (C::KC * 4) + ((c4 ^ (row & 7)) << 4)) = rp[i];
-            }
+        auto stage_v = [&](int buf) {  // V hi / lo (MN-major, 32-byte chunks XOR row % 4)
             unsigned char* hi = smem + C::OFF_V + buf * 2 * C::TILE_V;
 #pragma unroll
             for (int i = 0; i < PERV; ++i) {
@@ -472,33 +486,33 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
             }
             tc::fence_proxy_async_smem();
         };
-        if (n_c > 0) load(0);
+        if (n_c > 0) load_v(0);
         bool ok = true;
         for (int c = 0; c < n_c; ++c) {
-            int const buf = c & 1;
-            // buffer `buf` (P in TMEM and shared memory, V) was last read by PV(c-2);
-            // the decision to stop is taken by all row threads together, since
-            // they meet at the barriers below
-            bool const late = c >= 2 && !mbar_wait_or_abort(pvdone + 8 * buf, ((c - 2) >> 1) & 1, abort);
-            if (row_sync_any(late || *abort != 0)) {
+            int const buf = c & 1, st = c % C::NST;
+            // TMEM P buffer and V buffer `buf` were last read by PV(c-2); P chunk c
+            // has landed. The decision to stop is taken by all row threads
+            // together, since they meet at the barriers below.
+            bool fail = c >= 2 && !mbar_wait_or_abort(pvdone + 8 * buf, ((c - 2) >> 1) & 1, abort);
+            if (!fail) fail = !mbar_wait_or_abort(pfull + 8 * st, static_cast<uint32_t>((c / C::NST) & 1), abort);
+            if (row_sync_any(fail || *abort != 0)) {
                 ok = false;
                 break;
             }
             tc::fence_after_sync();
-            stage(buf);
-            if (c + 1 < n_c) load(c + 1);
-            row_sync();  // the whole P chunk is in shared memory
-            {  // this thread's 32 keys of row r: hi -> TMEM P_HI, lo -> TMEM P_LO
-                unsigned char const* prow = smem + C::OFF_P + buf * C::TILE_P + r * (C::KC * 4);
+            stage_v(buf);
+            if (c + 1 < n_c) load_v(c + 1);
+            {  // this thread's 32 keys of row r (box h): hi -> TMEM P_HI, lo -> TMEM P_LO
+                unsigned char const* prow = smem + C::OFF_P + st * C::STAGE_P + h * C::BOX_P + r * 128;
                 float hi[32], lo[32];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    int const c4 = 8 * h + j;
-                    float4 const x = *reinterpret_cast<float4 const*>(prow + ((c4 ^ (r & 7)) << 4));
+                    float4 const x = *reinterpret_cast<float4 const*>(prow + ((j ^ (r & 7)) << 4));
                     float4 const y = tf32_lo(x);
                     hi[4 * j] = x.x, hi[4 * j + 1] = x.y, hi[4 * j + 2] = x.z, hi[4 * j + 3] = x.w;
                     lo[4 * j] = y.x, lo[4 * j + 1] = y.y, lo[4 * j + 2] = y.z, lo[4 * j + 3] = y.w;
                 }
+                mbar_arrive(pfree + 8 * st);  // the stage may take chunk c + NST
                 uint32_t const col = C::KC * static_cast<uint32_t>(buf) + 32 * h;
                 tc::tmem_st32(tmem + lane_off + C::P_HI + col, hi);
                 tc::tmem_st32(tmem + lane_off + C::P_LO + col, lo);
@@ -544,9 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_pair_kernel(ApArgs a) {
     }
 }
 
-template <typename K>
+template <typename K, typename... A>
 int cluster_launch(K kernel, int threads, int smem, int64_t ctas, ann_stream stream, const char* what,
-                   auto const& args) {
+                   A const&... args) {
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute cl{};
     cl.id = cudaLaunchAttributeClusterDimension;
@@ -559,7 +573,7 @@ int cluster_launch(K kernel, int threads, int smem, int64_t ctas, ann_stream str
     cfg.stream = as_stream(stream);
     cfg.attrs = &cl;
     cfg.numAttrs = 1;
-    cudaError_t const e = cudaLaunchKernelEx(&cfg, kernel, args);
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, kernel, args...);
     if (e != cudaSuccess) return fail(ANN_ECUDA, "%s: %s", what, cudaGetErrorString(e));
     return check_launch(what);
 }
@@ -597,9 +611,51 @@ int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
     return cluster_launch(scores_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionScores (tensor cores)", a);
 }
 
+// cuTensorMapEncodeTiled from the driver (through the runtime's entry-point
+// query, so the library does not link libcuda), or null.
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Tensor map of P [B, Hq, Tq, Tk] (keys innermost), boxes of 128 rows x 32
+// keys with the 128-byte swizzle, zeros outside.
+int probs_map(ApArgs const& a, int64_t B, CUtensorMap* map) {
+    EncodeTiled const enc = encode_tiled();
+    if (enc == nullptr) return fail(ANN_ECUDA, "attentionApply: cuTensorMapEncodeTiled is not available.");
+    cuuint64_t const dims[4] = {static_cast<cuuint64_t>(a.Tk), static_cast<cuuint64_t>(a.Tq),
+                                static_cast<cuuint64_t>(a.Hq), static_cast<cuuint64_t>(B)};
+    // the stride of a dimension of extent 1 is never used: give it a legal value
+    int64_t const st_t = a.p_t, st_h = a.Hq == 1 ? st_t * a.Tq : a.p_h, st_b = B == 1 ? st_h * a.Hq : a.p_b;
+    cuuint64_t const strides[3] = {static_cast<cuuint64_t>(st_t) * 4, static_cast<cuuint64_t>(st_h) * 4,
+                                   static_cast<cuuint64_t>(st_b) * 4};
+    cuuint32_t const box[4] = {32, static_cast<cuuint32_t>(kBM), 1, 1};
+    cuuint32_t const unit[4] = {1, 1, 1, 1};
+    CUresult const r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(a.p), dims, strides, box, unit,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ANN_ECUDA, "attentionApply: cuTensorMapEncodeTiled failed (%d).", int(r));
+    return ANN_OK;
+}
+
 template <int D>
 int launch_apply(ann_stream stream, ApArgs& a, int64_t bhs, bool can_split, void* out_zero, size_t out_bytes) {
     using C = ApCfg<D>;
+    CUtensorMap pmap{};
+    ANN_TRY(probs_map(a, bhs / a.Hq, &pmap));
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
@@ -615,7 +671,8 @@ int launch_apply(ann_stream stream, ApArgs& a, int64_t bhs, bool can_split, void
     }
     int64_t const ctas = 2 * units * a.splits;
     if (ctas > INT32_MAX) return fail(ANN_ENOTSUP, "attentionApply: grid too large.");
-    return cluster_launch(apply_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionApply (tensor cores)", a);
+    return cluster_launch(apply_pair_kernel<D>, kApThreads, C::SMEM, ctas, stream, "attentionApply (tensor cores)", a,
+                          pmap);
 }
 
 bool rows16(const Dims& d, int unit_axis) {  // unit stride on `unit_axis`, 16-byte aligned rows
@@ -673,6 +730,11 @@ int apply_tc_f32(ann_stream stream, const Dims& p, const Dims& v, const Dims& o,
     int64_t const B = o.ext[0], Tq = o.ext[1], Hq = o.ext[2], D = o.ext[3], Tk = p.ext[3];
     if ((D != 64 && D != 128) || Tk % 4 != 0 || Tq < 1 || Tk < 1) return ANN_OK;
     if (!rows16(p, 3) || !rows16(v, 3) || !rows16(o, 3)) return ANN_OK;
+    // TMA coordinates are 32-bit; tensor-map strides below 2^40 bytes
+    if (Tk + 64 > INT32_MAX || Tq > INT32_MAX || Hq > INT32_MAX || B > INT32_MAX) return ANN_OK;
+    for (int i = 0; i < 3; ++i)
+        if ((p.str[i] <= 0 && p.ext[i] > 1) || p.str[i] >= (int64_t{1} << 36)) return ANN_OK;
+    if (p.str[2] * Tq >= (int64_t{1} << 36) || p.str[2] * Tq * Hq >= (int64_t{1} << 36)) return ANN_OK;
     ApArgs a{};
     a.p = static_cast<const float*>(p.data);
     a.v = static_cast<const float*>(v.data);

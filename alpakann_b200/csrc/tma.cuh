@@ -1,7 +1,8 @@
-// tma.cuh -- mbarrier and 1-D bulk-copy (TMA) helpers for sm_100a, inline PTX.
+// tma.cuh -- mbarrier, 1-D bulk-copy and tiled tensor-copy (TMA) helpers for
+// sm_100a, inline PTX.
 //
-// Only the non-multicast CTA-local forms are used: a bulk copy from global
-// memory of THIS GPU into the issuing CTA's own shared memory.
+// Only CTA-local forms are used: a copy from global memory of THIS GPU into
+// the issuing CTA's own shared memory, never to several CTAs at once.
 #pragma once
 
 #include <cstdint>
@@ -141,6 +142,20 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
+}
+
+// Tiled tensor copy (TMA) of one box of a 4-D tensor map, global -> this
+// CTA's own shared memory, completion as transaction bytes on `bar` (the full
+// box, elements outside the tensor read as zero). `map` is the address of a
+// __grid_constant__ CUtensorMap kernel parameter; the innermost coordinate c0
+// times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
 }
 
 }  // namespace ann

@@ -110,6 +110,25 @@ def test_apply_tensor_cores(ann, case):
     assert queue.take_device_error() == 0
 
 
+def test_apply_strided_probs(ann):
+    """P as a view with padded rows (row pitch Tk + 12 floats, NaN in the pad):
+    each row's bulk copy starts at its own pitch and takes Tk keys only."""
+    import torch
+    B, Tq, Tk, Hq, D = 2, 200, 324, 2, 64
+    g = rng(11)
+    p = normal(g, (B, Hq, Tq, Tk), np.float32)
+    v = normal(g, (B, Tk, Hq, D), np.float32)
+    want = oracle.attention_apply(p, v, np.empty((B, Tq, Hq, D), np.float32), 1, 0)
+    absdot = oracle.attention_apply(np.abs(p), np.abs(v), np.empty_like(want), 1, 0)
+    big = torch.full((B, Hq, Tq, Tk + 12), float("nan"), device="cuda")
+    big[..., :Tk] = dev(p)
+    o = torch.full((B, Tq, Hq, D), float("nan"), device="cuda")
+    queue = ann.Queue()
+    ann.onHost.nn.attentionApply(queue, None, big[..., :Tk], dev(v), o)
+    check(host(o), want, absdot, Tk)
+    assert queue.take_device_error() == 0
+
+
 def test_apply_split_is_deterministic(ann):
     """The two halves of the key range add into the output in either order:
     repeated calls give identical bits."""
