@@ -21,10 +21,10 @@
 // scores_pair_kernel: Q (hi and lo) in TMEM as the A operand for the CTA's
 //   whole life; 128-key K tiles (each CTA 64 keys, raw + lo, K-major 128-byte
 //   swizzle) two buffers deep; S accumulators double-buffered in TMEM. The
-//   epilogue moves S rows TMEM -> registers -> a padded shared-memory staging
-//   row -> one bulk copy (cp.async.bulk, shared -> global) per row segment,
-//   so the 4-byte-per-thread scatter of row-per-thread TMEM reads never
-//   reaches global memory. Work unit: (batch*head, 256-row tile, key chunk).
+//   epilogue moves S rows TMEM -> registers -> two 32-row x 32-key staging
+//   boxes per warp (128-byte swizzle) -> one TMA tensor store per box, issued
+//   by the warp itself, which clips rows past Tq and keys past Tk. Work unit:
+//   (batch*head, 256-row tile, key chunk).
 // apply_pair_kernel: a copy warp brings 64-key chunks of P into a 4-deep
 //   ring of shared-memory stages (one bulk copy per 256-byte row piece, rows
 //   padded by 16 bytes), so P, the large operand, is always several chunks in
@@ -80,10 +80,6 @@ __device__ __forceinline__ bool row_sync_any(bool v) {
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
-                 : "memory");
-}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -97,10 +93,10 @@ struct ScCfg {
     static constexpr int KROWS = NT / 2;            // keys of a tile held by this CTA
     static constexpr int TILE_K = KROWS * D * 4;    // bytes of K hi (or lo) per buffer
     static constexpr int BLK_K = KROWS * 128;       // one 32-float column block of K
-    static constexpr int PITCH = NT * 4 + 16;       // staging row pitch (16-byte pad: no bank conflicts)
+    static constexpr int BOX_S = 32 * 128;          // one TMA box of S: 32 rows x 32 keys, 128-byte swizzle
     static constexpr int OFF_K = 0;                 // buffer i: hi at 2*i*TILE_K, lo at + TILE_K
-    static constexpr int OFF_ST = 4 * TILE_K;       // S staging, kBM rows
-    static constexpr int OFF_BAR = OFF_ST + kBM * PITCH;
+    static constexpr int OFF_ST = 4 * TILE_K;       // S staging: two boxes per row warp
+    static constexpr int OFF_BAR = OFF_ST + 16 * BOX_S;
     // barriers: qready kready[2] sfree[2] sfull[2] drain
     static constexpr int NBAR = 8;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
@@ -130,7 +126,7 @@ struct ScArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, const __grid_constant__ CUtensorMap smap) {
     using C = ScCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -269,15 +265,18 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
             signal(kready + 8 * t);
         }
         if (n_t > 2) load_k(2);
-        unsigned char* st_row = smem + C::OFF_ST + r * C::PITCH + h * (C::NT / 2) * 4;
-        uint32_t const st_row_s = sbase + C::OFF_ST + r * C::PITCH + h * (C::NT / 2) * 4;
-        float* srow = a.s + b * a.s_b + hq * a.s_h + qi * a.s_t;
-        bool ok = true;
-        for (int t = 0; t < n_t && ok; ++t) {
+        // S leaves through two staging boxes per warp (its 32 rows x the 64
+        // keys of this half: 32 keys a box) and one TMA store per box, issued
+        // by the warp's lane 0 once the warp has staged them; the store clips
+        // rows past Tq and keys past Tk.
+        unsigned char* st_row = smem + C::OFF_ST + 2 * warp * C::BOX_S + lane * 128;
+        uint32_t const st_warp = sbase + C::OFF_ST + 2 * warp * C::BOX_S;
+        int64_t const row0 = q0 + 32 * (warp & 3);  // the warp's first row
+        for (int t = 0; t < n_t; ++t) {
             uint32_t const sb = static_cast<uint32_t>(t & 1);
-            ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * sb, (t >> 1) & 1, abort));
-            if (!ok) break;  // S(t) done: K buffer t % 2 is free
-            tc::fence_after_sync();
+            bool const ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * sb, (t >> 1) & 1, abort));
+            if (!ok) break;  // warp-uniform: the TMEM loads below are warp-collective
+            tc::fence_after_sync();  // S(t) done: K buffer t % 2 is free
             if (t + 2 < n_t) {
                 store_k(t & 1);  // K(t+2)
                 signal(kready + 8 * (t & 1));
@@ -288,19 +287,25 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a) {
             tc::tmem_ld32x2(s_col, s_col + 32, sv);
             tc::fence_before_sync();
             signal(sfree + 8 * sb);
-            bulk_wait_read();  // this thread's previous row segment has left the staging row
+            if (lane == 0) bulk_wait_read();  // the warp's previous stores have read its boxes
+            __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 64; j += 4)
-                *reinterpret_cast<float4*>(st_row + 4 * j) = make_float4(sv[j], sv[j + 1], sv[j + 2], sv[j + 3]);
+            for (int j = 0; j < 16; ++j)  // piece j of the 64 keys: box j / 8, piece j % 8
+                *reinterpret_cast<float4*>(st_row + (j >> 3) * C::BOX_S + (((j & 7) ^ (lane & 7)) << 4)) =
+                    make_float4(sv[4 * j], sv[4 * j + 1], sv[4 * j + 2], sv[4 * j + 3]);
             tc::fence_proxy_async_smem();
-            int64_t const col0 = static_cast<int64_t>(t_begin + t) * C::NT + 64 * h;
-            int64_t const n_cols = a.Tk - col0 < 64 ? a.Tk - col0 : 64;
-            if (qi < a.Tq && n_cols > 0) {
-                bulk_store(srow + col0, st_row_s, static_cast<uint32_t>(n_cols * 4));
+            __syncwarp();
+            if (lane == 0) {
+                int64_t const key0 = static_cast<int64_t>(t_begin + t) * C::NT + 64 * h;
+#pragma unroll
+                for (int x = 0; x < 2; ++x)
+                    if (key0 + 32 * x < a.Tk && row0 < a.Tq)  // boxes wholly outside are not issued
+                        tma_store_4d(&smap, static_cast<int>(key0 + 32 * x), static_cast<int>(row0),
+                                     static_cast<int>(hq), static_cast<int>(b), st_warp + x * C::BOX_S);
                 bulk_commit();
             }
         }
-        bulk_wait_all();
+        if (lane == 0) bulk_wait_all();
     }
 
     // CTA 1 also sees the issuer's final commit land on its own barrier, so that
@@ -583,6 +588,60 @@ bool tc_disabled() {
     return env != nullptr && env[0] == '1';
 }
 
+// cuTensorMapEncodeTiled from the driver (through the runtime's entry-point
+// query, so the library does not link libcuda), or null.
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// A rank-4 view [B, H, T, K] (K innermost, unit stride) that a tensor map can
+// describe with 32-bit coordinates: every stride positive where its extent is
+// above 1, and every byte offset below 2^38.
+bool tma_view(const Dims& d) {
+    for (int i = 0; i < 4; ++i)
+        if (d.ext[i] + 64 > INT32_MAX) return false;
+    for (int i = 0; i < 3; ++i)
+        if ((d.str[i] <= 0 && d.ext[i] > 1) || d.str[i] >= (int64_t{1} << 36)) return false;
+    return d.str[2] * d.ext[2] * d.ext[1] < (int64_t{1} << 36);
+}
+
+// Tensor map of an fp32 [B, H, T, K] view with the given extents (those the
+// kernel covers; elements past them read as zero / are not written), boxes of
+// box_rows rows x 32 keys with the 128-byte swizzle: 16-byte piece j of box
+// row r at r * 128 + ((j ^ (r % 8)) << 4) in shared memory.
+int map_bhtk(const float* base, int64_t B, int64_t H, int64_t T, int64_t K, int64_t s_b, int64_t s_h, int64_t s_t,
+             uint32_t box_rows, CUtensorMap* map, const char* what) {
+    EncodeTiled const enc = encode_tiled();
+    if (enc == nullptr) return fail(ANN_ECUDA, "%s: cuTensorMapEncodeTiled is not available.", what);
+    // the stride of a dimension of extent 1 is never used: give it a legal value
+    int64_t const st_h = H == 1 ? s_t * T : s_h, st_b = B == 1 ? st_h * H : s_b;
+    cuuint64_t const dims[4] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(B)};
+    cuuint64_t const strides[3] = {static_cast<cuuint64_t>(s_t) * 4, static_cast<cuuint64_t>(st_h) * 4,
+                                   static_cast<cuuint64_t>(st_b) * 4};
+    cuuint32_t const box[4] = {32, box_rows, 1, 1};
+    cuuint32_t const unit[4] = {1, 1, 1, 1};
+    CUresult const r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, unit,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ANN_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d).", what, int(r));
+    return ANN_OK;
+}
+
 template <int D>
 int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
     using C = ScCfg<D>;
@@ -608,54 +667,17 @@ int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
     a.chunks = static_cast<int>(ceil_div(a.k_tiles, best));
     int64_t const ctas = 2 * bhs * a.q_tiles * a.chunks;
     if (ctas > INT32_MAX) return fail(ANN_ENOTSUP, "attentionScores: grid too large.");
-    return cluster_launch(scores_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionScores (tensor cores)", a);
-}
-
-// cuTensorMapEncodeTiled from the driver (through the runtime's entry-point
-// query, so the library does not link libcuda), or null.
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiled encode_tiled() {
-    static std::once_flag once;
-    static EncodeTiled fn = nullptr;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(f);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
-// Tensor map of P [B, Hq, Tq, Tk] (keys innermost), boxes of 128 rows x 32
-// keys with the 128-byte swizzle, zeros outside.
-int probs_map(ApArgs const& a, int64_t B, CUtensorMap* map) {
-    EncodeTiled const enc = encode_tiled();
-    if (enc == nullptr) return fail(ANN_ECUDA, "attentionApply: cuTensorMapEncodeTiled is not available.");
-    cuuint64_t const dims[4] = {static_cast<cuuint64_t>(a.Tk), static_cast<cuuint64_t>(a.Tq),
-                                static_cast<cuuint64_t>(a.Hq), static_cast<cuuint64_t>(B)};
-    // the stride of a dimension of extent 1 is never used: give it a legal value
-    int64_t const st_t = a.p_t, st_h = a.Hq == 1 ? st_t * a.Tq : a.p_h, st_b = B == 1 ? st_h * a.Hq : a.p_b;
-    cuuint64_t const strides[3] = {static_cast<cuuint64_t>(st_t) * 4, static_cast<cuuint64_t>(st_h) * 4,
-                                   static_cast<cuuint64_t>(st_b) * 4};
-    cuuint32_t const box[4] = {32, static_cast<cuuint32_t>(kBM), 1, 1};
-    cuuint32_t const unit[4] = {1, 1, 1, 1};
-    CUresult const r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(a.p), dims, strides, box, unit,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(ANN_ECUDA, "attentionApply: cuTensorMapEncodeTiled failed (%d).", int(r));
-    return ANN_OK;
+    CUtensorMap smap{};
+    ANN_TRY(map_bhtk(a.s, bhs / a.Hq, a.Hq, a.Tq, a.Tk, a.s_b, a.s_h, a.s_t, 32, &smap, "attentionScores"));
+    return cluster_launch(scores_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionScores (tensor cores)", a,
+                          smap);
 }
 
 template <int D>
 int launch_apply(ann_stream stream, ApArgs& a, int64_t bhs, bool can_split, void* out_zero, size_t out_bytes) {
     using C = ApCfg<D>;
     CUtensorMap pmap{};
-    ANN_TRY(probs_map(a, bhs / a.Hq, &pmap));
+    ANN_TRY(map_bhtk(a.p, bhs / a.Hq, a.Hq, a.Tq, a.Tk, a.p_b, a.p_h, a.p_t, kBM, &pmap, "attentionApply"));
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
@@ -694,7 +716,7 @@ int scores_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& s
     int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
     int64_t const B = s.ext[0], Hq = s.ext[1], Tq = s.ext[2], Tk = s.ext[3], D = q.ext[3];
     if ((D != 64 && D != 128) || Tk % 4 != 0 || Tq < 1 || Tk < 1) return ANN_OK;
-    if (!rows16(q, 3) || !rows16(k, 3) || !rows16(s, 3)) return ANN_OK;
+    if (!rows16(q, 3) || !rows16(k, 3) || !rows16(s, 3) || !tma_view(s)) return ANN_OK;
     ScArgs a{};
     a.q = static_cast<const float*>(q.data);
     a.k = static_cast<const float*>(k.data);
@@ -730,11 +752,7 @@ int apply_tc_f32(ann_stream stream, const Dims& p, const Dims& v, const Dims& o,
     int64_t const B = o.ext[0], Tq = o.ext[1], Hq = o.ext[2], D = o.ext[3], Tk = p.ext[3];
     if ((D != 64 && D != 128) || Tk % 4 != 0 || Tq < 1 || Tk < 1) return ANN_OK;
     if (!rows16(p, 3) || !rows16(v, 3) || !rows16(o, 3)) return ANN_OK;
-    // TMA coordinates are 32-bit; tensor-map strides below 2^40 bytes
-    if (Tk + 64 > INT32_MAX || Tq > INT32_MAX || Hq > INT32_MAX || B > INT32_MAX) return ANN_OK;
-    for (int i = 0; i < 3; ++i)
-        if ((p.str[i] <= 0 && p.ext[i] > 1) || p.str[i] >= (int64_t{1} << 36)) return ANN_OK;
-    if (p.str[2] * Tq >= (int64_t{1} << 36) || p.str[2] * Tq * Hq >= (int64_t{1} << 36)) return ANN_OK;
+    if (!tma_view(p)) return ANN_OK;
     ApArgs a{};
     a.p = static_cast<const float*>(p.data);
     a.v = static_cast<const float*>(v.data);

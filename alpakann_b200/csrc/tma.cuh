@@ -158,4 +158,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c
         : "memory");
 }
 
+// Tiled tensor copy (TMA) of one box from this CTA's shared memory into a
+// 4-D tensor map (elements outside the tensor are not written), in the
+// thread's bulk async-group. Coordinates must not be negative; c0 times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_4d(const void* map, int c0, int c1, int c2, int c3, uint32_t src) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+        : "memory");
+}
+
 }  // namespace ann
