@@ -573,7 +573,7 @@ PREFILL = {
 }
 
 
-def measure_prefill(name, world, rank, comm, clock_ids=None, reps=10, sustained_s=1.0, max_repeats=100):
+def measure_prefill(name, world, rank, comm, clock_ids=None, reps=10, sustained_s=1.0, max_repeats=1000):
     """Fused causal prefill of this rank's heads (heads sharded over ranks) and,
     for N > 1, the gather of the outputs into every rank's BTHD output, timed
     with CUDA events; TFLOP/s counts QK^T + PV over the causal half including
