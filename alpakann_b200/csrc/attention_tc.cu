@@ -35,14 +35,13 @@
 //   With few tiles the key range is split in two and both halves add into a
 //   zeroed output (red.global.add: 0 + a + b in either order is a + b, so the
 //   result does not depend on which half finishes first).
-#include <cuda.h>
-
 #include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
+#include "tmap.cuh"
 
 namespace ann {
 
@@ -588,58 +587,15 @@ bool tc_disabled() {
     return env != nullptr && env[0] == '1';
 }
 
-// cuTensorMapEncodeTiled from the driver (through the runtime's entry-point
-// query, so the library does not link libcuda), or null.
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiled encode_tiled() {
-    static std::once_flag once;
-    static EncodeTiled fn = nullptr;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(f);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
-// A rank-4 view [B, H, T, K] (K innermost, unit stride) that a tensor map can
-// describe with 32-bit coordinates: every stride positive where its extent is
-// above 1, and every byte offset below 2^38.
-bool tma_view(const Dims& d) {
-    for (int i = 0; i < 4; ++i)
-        if (d.ext[i] + 64 > INT32_MAX) return false;
-    for (int i = 0; i < 3; ++i)
-        if ((d.str[i] <= 0 && d.ext[i] > 1) || d.str[i] >= (int64_t{1} << 36)) return false;
-    return d.str[2] * d.ext[2] * d.ext[1] < (int64_t{1} << 36);
-}
-
-// Tensor map of an fp32 [B, H, T, K] view with the given extents (those the
-// kernel covers; elements past them read as zero / are not written), boxes of
-// box_rows rows x 32 keys with the 128-byte swizzle: 16-byte piece j of box
-// row r at r * 128 + ((j ^ (r % 8)) << 4) in shared memory.
+// Tensor map of an fp32 [B, H, T, K] view (K innermost) with the given
+// extents, boxes of box_rows rows x 32 keys (tmap.cuh).
 int map_bhtk(const float* base, int64_t B, int64_t H, int64_t T, int64_t K, int64_t s_b, int64_t s_h, int64_t s_t,
              uint32_t box_rows, CUtensorMap* map, const char* what) {
-    EncodeTiled const enc = encode_tiled();
-    if (enc == nullptr) return fail(ANN_ECUDA, "%s: cuTensorMapEncodeTiled is not available.", what);
-    // the stride of a dimension of extent 1 is never used: give it a legal value
-    int64_t const st_h = H == 1 ? s_t * T : s_h, st_b = B == 1 ? st_h * H : s_b;
-    cuuint64_t const dims[4] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(H),
-                                static_cast<cuuint64_t>(B)};
-    cuuint64_t const strides[3] = {static_cast<cuuint64_t>(s_t) * 4, static_cast<cuuint64_t>(st_h) * 4,
-                                   static_cast<cuuint64_t>(st_b) * 4};
-    cuuint32_t const box[4] = {32, box_rows, 1, 1};
-    cuuint32_t const unit[4] = {1, 1, 1, 1};
-    CUresult const r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, unit,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(ANN_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d).", what, int(r));
-    return ANN_OK;
+    return map_f32_4d(map, base, {K, T, H, B}, {s_t, s_h, s_b}, 32, box_rows, what);
+}
+
+bool tma_view(const Dims& d) {  // a [B, H, T, K] view with unit-stride K
+    return tma_view_ok({d.ext[3], d.ext[2], d.ext[1], d.ext[0]}, {d.str[2], d.str[1], d.str[0]});
 }
 
 template <int D>

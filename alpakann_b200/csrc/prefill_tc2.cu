@@ -17,6 +17,10 @@
 // and O += P_hi V_hi + P_hi V_lo + P_lo V_hi.
 //   TMEM  [Q_hi | O | S0 (64) | S1 (64) | P_hi (64)]            (D = 128: 448 columns)
 //   smem  K hi/lo x 2 | V hi/lo x 2 (half tiles) | P_lo | Q_lo  (D = 128: 224 KB)
+// Raw K and V tiles arrive by TMA tensor loads straight into the K_hi / V_hi
+// buffers (a box is one column block of the K-major 128-byte-swizzled K layout
+// or of the MN-major 32-byte-atom V layout); the row threads add the lo parts
+// beside them. Q passes through the row threads' registers (Q_hi goes to TMEM).
 // Row threads signal the barriers CTA 0's issuers wait on through the cluster
 // window; the issuers commit each group of MMAs to both CTAs' barriers. Every
 // wait is bounded; on a timeout both CTAs stop, the issuers drain their MMAs,
@@ -29,6 +33,7 @@
 #include "reduce.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
+#include "tmap.cuh"
 
 namespace ann {
 
@@ -61,8 +66,8 @@ struct PairCfg {
     static constexpr int OFF_PLO = OFF_V + 4 * TILE_V;
     static constexpr int OFF_QLO = OFF_PLO + 2 * PLO_BLK;
     static constexpr int OFF_BAR = OFF_QLO + (D / 32) * QLO_BLK;
-    // barriers: qready kready[2] vready[2] sfull[2] sfree[2] pfull pvdone drain_s drain_pv
-    static constexpr int NBAR = 13;
+    // barriers: qready kready[2] vready[2] sfull[2] sfree[2] pfull pvdone drain_s drain_pv kfull[2] vfull[2]
+    static constexpr int NBAR = 17;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
     static constexpr int USED = OFF_SLOT + 16;
     // + 1 KB to align the base to the 1 KB swizzle atom; >= 120 KB so that a
@@ -129,7 +134,9 @@ __device__ __forceinline__ bool row_sync_any(bool v) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, float scale) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, float scale,
+                                                                   const __grid_constant__ CUtensorMap kmap,
+                                                                   const __grid_constant__ CUtensorMap vmap) {
     using C = PairCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -138,7 +145,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
     uint32_t const qready = bar, kready = bar + 8, vready = bar + 24, sfull = bar + 40, sfree = bar + 56,
-                   pfull = bar + 72, pvdone = bar + 80, drain_s = bar + 88, drain_pv = bar + 96;
+                   pfull = bar + 72, pvdone = bar + 80, drain_s = bar + 88, drain_pv = bar + 96, kfull = bar + 104,
+                   vfull = bar + 120;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
@@ -173,6 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
         mbar_init(pvdone, 1);
         mbar_init(drain_s, 1);
         mbar_init(drain_pv, 1);
+        for (int i = 0; i < 2; ++i) mbar_init(kfull + 8 * i, 1);
+        for (int i = 0; i < 2; ++i) mbar_init(vfull + 8 * i, 1);
         fence_mbar_init();
         *abort = 0;
     }
@@ -266,53 +276,62 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
         constexpr int NV4K = D / 4, NV4V = C::VCOLS / 4;
         constexpr int PERK = C::KROWS * NV4K / kRowThreads;  // float4 per thread per tile
         constexpr int PERV = kBN * NV4V / kRowThreads;
-        float const* kbase = a.k + b * a.k_b + kvh * a.k_h;
-        float const* vbase = a.v + b * a.v_b + kvh * a.v_h + rank * C::VCOLS;
-        float4 rk[PERK], rv[PERV];
-        auto load_k = [&](int t) {
+        // Raw K and V tiles arrive by TMA (thread 0 issues). K: D / 32 boxes of 32
+        // keys x 32 dims, each one 32-dim column block of the K-major 128-byte
+        // swizzled layout; V: this CTA's D / 64 boxes of 64 keys x 32 dims, each
+        // one column block of the MN-major layout with 32-byte atoms. The raw
+        // values land where the MMA reads K_hi / V_hi, keys past Tk read as zero
+        // (V rows past Tk must be finite); the row threads then add lo.
+        int k_issued = 0, k_done = 0;  // K tiles issued / converted (thread 0 drains the rest)
+        int v_issued = 0, v_done = 0;  // V tiles likewise
+        auto issue_k = [&](int t) {    // thread 0: K(t) into buffer t % 2, once that buffer is free
+            uint32_t const full_bar = kfull + 8 * (t & 1), dst = sbase + C::OFF_K + (t & 1) * 2 * C::TILE_K;
+            mbar_arrive_expect_tx(full_bar, C::TILE_K);
 #pragma unroll
-            for (int i = 0; i < PERK; ++i) {
-                int const e = i * kRowThreads + tid, row = e / NV4K, c4 = e % NV4K;
-                int64_t const key = static_cast<int64_t>(t) * kBN + rank * C::KROWS + row;
-                rk[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(kbase + key * a.k_t) + c4)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            for (int cb = 0; cb < D / 32; ++cb)
+                tma_load_4d(dst + cb * C::BLK_K, &kmap, 32 * cb, t * kBN + rank * C::KROWS, static_cast<int>(kvh),
+                            static_cast<int>(b), full_bar);
+            k_issued = t + 1;
         };
-        auto load_v = [&](int t) {
-#pragma unroll
-            for (int i = 0; i < PERV; ++i) {
-                int const e = i * kRowThreads + tid, row = e / NV4V, c4 = e % NV4V;
-                int64_t const key = static_cast<int64_t>(t) * kBN + row;
-                rv[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(vbase + key * a.v_t) + c4)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);  // V rows past Tk must be finite
-            }
-        };
-        auto store_k = [&](int buf) {  // K-major, 16-byte chunks XOR (row % 8)
-            unsigned char* hi = smem + C::OFF_K + buf * 2 * C::TILE_K;
+        auto convert_k = [&](int t) {  // K(t) has landed: lo = x - trunc13(x) beside it
+            if (!mbar_wait_or_abort(kfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1), abort)) return false;
+            unsigned char* hi = smem + C::OFF_K + (t & 1) * 2 * C::TILE_K;
 #pragma unroll
             for (int i = 0; i < PERK; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4K, c4 = e % NV4K;
                 int const off = (c4 >> 3) * C::BLK_K + row * 128 + (((c4 & 7) ^ (row & 7)) << 4);
-                *reinterpret_cast<float4*>(hi + off) = rk[i];
-                *reinterpret_cast<float4*>(hi + C::TILE_K + off) = tf32_lo(rk[i]);
+                *reinterpret_cast<float4*>(hi + C::TILE_K + off) = tf32_lo(*reinterpret_cast<float4 const*>(hi + off));
             }
             tc::fence_proxy_async_smem();  // visible to the tensor core
+            k_done = t + 1;
+            return true;
         };
-        auto store_v = [&](int buf) {  // MN-major, 32-byte chunks XOR (row % 4)
-            unsigned char* hi = smem + C::OFF_V + buf * 2 * C::TILE_V;
+        auto issue_v = [&](int t) {  // thread 0: V(t) into buffer t % 2, once PV(t-2) is done with it
+            uint32_t const full_bar = vfull + 8 * (t & 1), dst = sbase + C::OFF_V + (t & 1) * 2 * C::TILE_V;
+            mbar_arrive_expect_tx(full_bar, C::TILE_V);
+#pragma unroll
+            for (int cb = 0; cb < C::VCOLS / 32; ++cb)
+                tma_load_4d(dst + cb * C::BLK_V, &vmap, rank * C::VCOLS + 32 * cb, t * kBN, static_cast<int>(kvh),
+                            static_cast<int>(b), full_bar);
+            v_issued = t + 1;
+        };
+        auto convert_v = [&](int t) {  // V(t) has landed: lo beside it (MN-major, 32-byte chunks XOR row % 4)
+            if (!mbar_wait_or_abort(vfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1), abort)) return false;
+            unsigned char* hi = smem + C::OFF_V + (t & 1) * 2 * C::TILE_V;
 #pragma unroll
             for (int i = 0; i < PERV; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4V, c4 = e % NV4V;
                 int const off =
                     (c4 >> 3) * C::BLK_V + row * 128 + ((((c4 & 7) >> 1) ^ (row & 3)) << 5) + ((c4 & 1) << 4);
-                *reinterpret_cast<float4*>(hi + off) = rv[i];
-                *reinterpret_cast<float4*>(hi + C::TILE_V + off) = tf32_lo(rv[i]);
+                *reinterpret_cast<float4*>(hi + C::TILE_V + off) = tf32_lo(*reinterpret_cast<float4 const*>(hi + off));
             }
             tc::fence_proxy_async_smem();
+            v_done = t + 1;
+            return true;
         };
-        if (n_kt > 0) {
-            load_k(0);
-            load_v(0);
+        if (tid == 0) {
+            for (int t = 0; t < (n_kt < 2 ? n_kt : 2); ++t) issue_k(t);
+            if (n_kt > 0) issue_v(0);
         }
         {  // Q row half: hi (raw) -> TMEM, lo -> shared memory (K-major, 128-byte swizzle)
             float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h + h * HD;
@@ -335,24 +354,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
             tc::fence_before_sync();
             signal(qready);
         }
-        // K runs two tiles ahead: K(0), K(1) now; K(t+2) into buffer t % 2 as soon
-        // as S(t) has landed. V runs one tile ahead: V(0) now, V(t+1) into buffer
-        // (t+1) % 2 once PV(t-1) is done with it, so that PV(t) waits only for P(t).
-        for (int t = 0; t < (n_kt < 2 ? n_kt : 2); ++t) {
-            if (t == 1) load_k(1);
-            store_k(t);
-            signal(kready + 8 * t);
+        // K runs two tiles ahead: K(0), K(1) now; K(t+2) is copied into buffer
+        // t % 2 as soon as S(t) has landed and gets its lo part at the end of
+        // tile t (S(t+2) is not due before S(t+1) and PV(t) have run). V runs one
+        // tile ahead: V(0) now; V(t+1) is copied into buffer (t+1) % 2 once PV(t-1)
+        // is done with it and gets its lo part in tile t+1 after the softmax,
+        // before P(t+1) is published, so that PV(t+1) waits only for P(t+1).
+        bool ok = true;
+        for (int t = 0; t < (n_kt < 2 ? n_kt : 2) && ok; ++t) {
+            ok = __all_sync(0xffffffffu, convert_k(t));
+            if (ok) signal(kready + 8 * t);
         }
-        if (n_kt > 2) load_k(2);
-        if (n_kt > 0) {
-            store_v(0);
-            signal(vready);
-            if (n_kt > 1) load_v(1);
+        if (ok && n_kt > 0) {
+            ok = __all_sync(0xffffffffu, convert_v(0));
+            if (ok) signal(vready);
         }
         unsigned char* plo_row = smem + C::OFF_PLO + h * C::PLO_BLK + r * 128;
         float const c2 = scale * kLog2e;  // scores are taken in log2 units: s * scale * log2(e)
         float m_used = Lowest<float>::value, l_part = 0.f;
-        bool ok = true;
         // Decisions after a wait are made warp-uniform (__all_sync): tcgen05.ld/st
         // are warp-collective, so a warp must never split on an abort.
         for (int t = 0; t < n_kt && ok; ++t) {
@@ -365,11 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
             tc::tmem_ld32x2(s_col + 32 * h, s_col + 32 * (1 - h), sv);
             tc::fence_before_sync();
             signal(sfree + 8 * sb);  // S(t+2) may overwrite this buffer
-            if (t + 2 < n_kt) {
-                store_k(t & 1);  // K(t+2)
-                signal(kready + 8 * (t & 1));
-                if (t + 3 < n_kt) load_k(t + 3);
-            }
+            if (tid == 0 && t + 2 < n_kt && *abort == 0) issue_k(t + 2);  // K buffer t % 2 is free
             // live keys: kj < Tk and (not causal or kj <= qi), a prefix of the tile;
             // masking is by selects, not branches, so that the exps overlap
             int64_t const key0 = static_cast<int64_t>(t) * kBN;
@@ -418,6 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
                 }
             }
             l_part += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+            if (t > 0) {  // V(t), copied during tile t-1: its lo part
+                ok = __all_sync(0xffffffffu, convert_v(t));
+                if (!ok) break;
+                signal(vready + 8 * (t & 1));
+            }
             // PV(t-1) has finished with V, P_hi, P_lo and O
             ok = t == 0 || mbar_wait_or_abort(pvdone, (t - 1) & 1, abort);
             ok = __all_sync(0xffffffffu, ok);
@@ -444,11 +464,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
             tc::fence_proxy_async_smem();
             tc::fence_before_sync();
             signal(pfull);
-            if (t + 1 < n_kt) {  // V(t+1): its buffer was last read by PV(t-1), done
-                store_v((t + 1) & 1);
-                signal(vready + 8 * ((t + 1) & 1));
-                if (t + 2 < n_kt) load_v(t + 2);
+            // V(t+1): its buffer was last read by PV(t-1), done
+            if (tid == 0 && t + 1 < n_kt && *abort == 0) issue_v(t + 1);
+            if (t + 2 < n_kt) {  // K(t+2), copied at the top of this tile: its lo part
+                ok = __all_sync(0xffffffffu, convert_k(t + 2));
+                if (!ok) break;
+                signal(kready + 8 * (t & 1));
             }
+        }
+        if (tid == 0) {  // no K / V copy may still be landing when the CTA leaves (bounded)
+            for (int t = k_done; t < k_issued; ++t)
+                mbar_wait_bounded(kfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1));
+            for (int t = v_done; t < v_issued; ++t)
+                mbar_wait_bounded(vfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1));
         }
         if (ok && n_kt > 0) ok = mbar_wait_or_abort(pvdone, (n_kt - 1) & 1, abort);
         ok = __all_sync(0xffffffffu, ok);
@@ -552,6 +580,17 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
     });
     if (attr != cudaSuccess) return ANN_OK;  // not handled: the single-SM kernel runs
     int const tok = layout == ANN_LAYOUT_BTHD ? 1 : 2, head = layout == ANN_LAYOUT_BTHD ? 2 : 1;
+    // K [B, Tk, Hkv, D] or [B, Hkv, Tk, D] as a tensor map over (d, key, head, batch)
+    int64_t const kdims[4] = {k.ext[3], k.ext[tok], k.ext[head], k.ext[0]};
+    int64_t const kstr[3] = {k.str[tok], k.str[head], k.str[0]};
+    if (!tma_view_ok(kdims, kstr)) return ANN_OK;  // not handled: the single-SM kernel runs
+    int64_t const vdims[4] = {v.ext[3], v.ext[tok], v.ext[head], v.ext[0]};
+    int64_t const vstr[3] = {v.str[tok], v.str[head], v.str[0]};
+    if (!tma_view_ok(vdims, vstr)) return ANN_OK;
+    CUtensorMap kmap{}, vmap{};
+    ANN_TRY(map_f32_4d(&kmap, k.data, kdims, kstr, 32, C::KROWS, "attention prefill (SM pairs)"));
+    ANN_TRY(map_f32_4d(&vmap, v.data, vdims, vstr, 32, kBN, "attention prefill (SM pairs)",
+                       CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
     PairArgs a{};
     a.out = o.data;
     a.mirror = static_cast<float*>(mirror);
@@ -602,7 +641,7 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
         return ANN_OK;  // not handled
     }
     handled = true;
-    cudaError_t const e = cudaLaunchKernelEx(&cfg, prefill_pair_kernel<D>, a, scale);
+    cudaError_t const e = cudaLaunchKernelEx(&cfg, prefill_pair_kernel<D>, a, scale, kmap, vmap);
     if (e != cudaSuccess) return fail(ANN_ECUDA, "attention prefill (SM pairs): %s", cudaGetErrorString(e));
     return check_launch("attention prefill (SM pairs)");
 }
