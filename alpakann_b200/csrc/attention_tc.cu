@@ -19,8 +19,8 @@
 // free TMEM and report ANN_DEVERR_WAIT_TIMEOUT.
 //
 // scores_pair_kernel: Q (hi and lo) in TMEM as the A operand for the CTA's
-//   whole life; 128-key K tiles (each CTA 64 keys, raw + lo, K-major 128-byte
-//   swizzle) two buffers deep; S accumulators double-buffered in TMEM. The
+//   whole life; 128-key K tiles (each CTA 64 keys, raw by TMA tensor loads +
+//   lo added by the row threads, K-major 128-byte swizzle) two buffers deep; S accumulators double-buffered in TMEM. The
 //   epilogue moves S rows TMEM -> registers -> two 32-row x 32-key staging
 //   boxes per warp (128-byte swizzle) -> one TMA tensor store per box, issued
 //   by the warp itself, which clips rows past Tq and keys past Tk. Work unit:
@@ -96,8 +96,8 @@ struct ScCfg {
     static constexpr int OFF_K = 0;                 // buffer i: hi at 2*i*TILE_K, lo at + TILE_K
     static constexpr int OFF_ST = 4 * TILE_K;       // S staging: two boxes per row warp
     static constexpr int OFF_BAR = OFF_ST + 16 * BOX_S;
-    // barriers: qready kready[2] sfree[2] sfull[2] drain
-    static constexpr int NBAR = 8;
+    // barriers: qready kready[2] sfree[2] sfull[2] drain kfull[2]
+    static constexpr int NBAR = 10;
     static constexpr int OFF_SLOT = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
     static constexpr int USED = OFF_SLOT + 16;
     static constexpr int SMEM = USED + 1024;  // + 1 KB to align the base to the swizzle atom
@@ -125,7 +125,8 @@ struct ScArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, const __grid_constant__ CUtensorMap smap) {
+__global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, const __grid_constant__ CUtensorMap smap,
+                                                                  const __grid_constant__ CUtensorMap kmap) {
     using C = ScCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     uint32_t const raw_base = smem_u32(smem_raw);
@@ -133,7 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
     unsigned char* smem = smem_raw + pad;
     uint32_t const sbase = raw_base + pad;
     uint32_t const bar = sbase + C::OFF_BAR;
-    uint32_t const qready = bar, kready = bar + 8, sfree = bar + 24, sfull = bar + 40, drain = bar + 56;
+    uint32_t const qready = bar, kready = bar + 8, sfree = bar + 24, sfull = bar + 40, drain = bar + 56,
+                   kfull = bar + 64;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::OFF_SLOT + 4);
 
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
         for (int i = 0; i < 2; ++i) mbar_init(sfree + 8 * i, C::ROW_ARRIVALS);
         for (int i = 0; i < 2; ++i) mbar_init(sfull + 8 * i, 1);
         mbar_init(drain, 1);
+        for (int i = 0; i < 2; ++i) mbar_init(kfull + 8 * i, 1);
         fence_mbar_init();
         *abort = 0;
     }
@@ -213,29 +216,35 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
         int64_t const qi = q0 + r;
         constexpr int NV4 = D / 4;                                // float4 per K row
         constexpr int PERK = C::KROWS * NV4 / kRowThreads;        // float4 per thread per tile
-        float const* kbase = a.k + b * a.k_b + kvh * a.k_h;
-        float4 rk[PERK];
-        auto load_k = [&](int t) {  // keys [NT t + KROWS rank, + KROWS) of the tile
+        // Raw K tiles (keys [NT t + KROWS rank, + KROWS) of tile t) arrive by TMA,
+        // D / 32 boxes of KROWS keys x 32 dims, each one column block of the
+        // K-major 128-byte-swizzled K_hi layout (keys past Tk read as zero);
+        // the row threads add lo beside them.
+        int k_issued = 0, k_done = 0;  // K tiles issued / converted (thread 0 drains the rest)
+        auto issue_k = [&](int t) {    // thread 0: K(t) into buffer t % 2, once S(t-2) has read it
+            uint32_t const full_bar = kfull + 8 * (t & 1), dst = sbase + C::OFF_K + (t & 1) * 2 * C::TILE_K;
+            mbar_arrive_expect_tx(full_bar, C::TILE_K);
 #pragma unroll
-            for (int i = 0; i < PERK; ++i) {
-                int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
-                int64_t const key = static_cast<int64_t>(t_begin + t) * C::NT + rank * C::KROWS + row;
-                rk[i] = key < a.Tk ? __ldg(reinterpret_cast<float4 const*>(kbase + key * a.k_t) + c4)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            for (int cb = 0; cb < D / 32; ++cb)
+                tma_load_4d(dst + cb * C::BLK_K, &kmap, 32 * cb, (t_begin + t) * C::NT + rank * C::KROWS,
+                            static_cast<int>(kvh), static_cast<int>(b), full_bar);
+            k_issued = t + 1;
         };
-        auto store_k = [&](int buf) {  // K-major, 16-byte chunks XOR (row % 8)
-            unsigned char* hi = smem + C::OFF_K + buf * 2 * C::TILE_K;
+        auto convert_k = [&](int t) {  // K(t) has landed: lo = x - trunc13(x) beside it
+            if (!mbar_wait_or_abort(kfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1), abort)) return false;
+            unsigned char* hi = smem + C::OFF_K + (t & 1) * 2 * C::TILE_K;
 #pragma unroll
             for (int i = 0; i < PERK; ++i) {
                 int const e = i * kRowThreads + tid, row = e / NV4, c4 = e % NV4;
                 int const off = (c4 >> 3) * C::BLK_K + row * 128 + (((c4 & 7) ^ (row & 7)) << 4);
-                *reinterpret_cast<float4*>(hi + off) = rk[i];
-                *reinterpret_cast<float4*>(hi + C::TILE_K + off) = tf32_lo(rk[i]);
+                *reinterpret_cast<float4*>(hi + C::TILE_K + off) = tf32_lo(*reinterpret_cast<float4 const*>(hi + off));
             }
             tc::fence_proxy_async_smem();
+            k_done = t + 1;
+            return true;
         };
-        if (n_t > 0) load_k(0);
+        if (tid == 0)
+            for (int t = 0; t < (n_t < 2 ? n_t : 2); ++t) issue_k(t);
         {  // Q row half -> TMEM: hi (raw) at Q_HI, lo at Q_LO
             constexpr int HD = D / 2;
             float const* qrow = a.q + b * a.q_b + qi * a.q_t + hq * a.q_h + h * HD;
@@ -258,12 +267,11 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
             tc::fence_before_sync();
             signal(qready);
         }
-        for (int t = 0; t < (n_t < 2 ? n_t : 2); ++t) {
-            if (t == 1) load_k(1);
-            store_k(t);
-            signal(kready + 8 * t);
+        bool ok = true;
+        for (int t = 0; t < (n_t < 2 ? n_t : 2) && ok; ++t) {
+            ok = __all_sync(0xffffffffu, convert_k(t));
+            if (ok) signal(kready + 8 * t);
         }
-        if (n_t > 2) load_k(2);
         // S leaves through two staging boxes per warp (its 32 rows x the 64
         // keys of this half: 32 keys a box) and one TMA store per box, issued
         // by the warp's lane 0 once the warp has staged them; the store clips
@@ -271,16 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
         unsigned char* st_row = smem + C::OFF_ST + 2 * warp * C::BOX_S + lane * 128;
         uint32_t const st_warp = sbase + C::OFF_ST + 2 * warp * C::BOX_S;
         int64_t const row0 = q0 + 32 * (warp & 3);  // the warp's first row
-        for (int t = 0; t < n_t; ++t) {
+        for (int t = 0; t < n_t && ok; ++t) {
             uint32_t const sb = static_cast<uint32_t>(t & 1);
-            bool const ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * sb, (t >> 1) & 1, abort));
+            ok = __all_sync(0xffffffffu, mbar_wait_or_abort(sfull + 8 * sb, (t >> 1) & 1, abort));
             if (!ok) break;  // warp-uniform: the TMEM loads below are warp-collective
             tc::fence_after_sync();  // S(t) done: K buffer t % 2 is free
-            if (t + 2 < n_t) {
-                store_k(t & 1);  // K(t+2)
-                signal(kready + 8 * (t & 1));
-                if (t + 3 < n_t) load_k(t + 3);
-            }
+            if (tid == 0 && t + 2 < n_t && *abort == 0) issue_k(t + 2);
             float sv[64];  // this thread's half of row r: keys [64 h, 64 h + 64) of the tile
             uint32_t const s_col = tmem + lane_off + C::S_COL + C::NT * sb + 64 * h;
             tc::tmem_ld32x2(s_col, s_col + 32, sv);
@@ -303,8 +307,16 @@ __global__ void __launch_bounds__(kThreads, 1) scores_pair_kernel(ScArgs a, cons
                                      static_cast<int>(hq), static_cast<int>(b), st_warp + x * C::BOX_S);
                 bulk_commit();
             }
+            if (t + 2 < n_t) {  // K(t+2), copied at the top of this tile: its lo part
+                ok = __all_sync(0xffffffffu, convert_k(t + 2));
+                if (!ok) break;
+                signal(kready + 8 * (t & 1));
+            }
         }
         if (lane == 0) bulk_wait_all();
+        if (tid == 0)  // no K copy may still be landing when the CTA leaves (bounded)
+            for (int t = k_done; t < k_issued; ++t)
+                mbar_wait_bounded(kfull + 8 * (t & 1), static_cast<uint32_t>((t >> 1) & 1));
     }
 
     // CTA 1 also sees the issuer's final commit land on its own barrier, so that
@@ -599,7 +611,7 @@ bool tma_view(const Dims& d) {  // a [B, H, T, K] view with unit-stride K
 }
 
 template <int D>
-int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
+int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs, int64_t const (&kdims)[4], int64_t const (&kstr)[3]) {
     using C = ScCfg<D>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
@@ -623,10 +635,11 @@ int launch_scores(ann_stream stream, ScArgs& a, int64_t bhs) {
     a.chunks = static_cast<int>(ceil_div(a.k_tiles, best));
     int64_t const ctas = 2 * bhs * a.q_tiles * a.chunks;
     if (ctas > INT32_MAX) return fail(ANN_ENOTSUP, "attentionScores: grid too large.");
-    CUtensorMap smap{};
+    CUtensorMap smap{}, kmap{};
     ANN_TRY(map_bhtk(a.s, bhs / a.Hq, a.Hq, a.Tq, a.Tk, a.s_b, a.s_h, a.s_t, 32, &smap, "attentionScores"));
+    ANN_TRY(map_f32_4d(&kmap, a.k, kdims, kstr, 32, C::KROWS, "attentionScores"));
     return cluster_launch(scores_pair_kernel<D>, kThreads, C::SMEM, ctas, stream, "attentionScores (tensor cores)", a,
-                          smap);
+                          smap, kmap);
 }
 
 template <int D>
@@ -673,6 +686,9 @@ int scores_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& s
     int64_t const B = s.ext[0], Hq = s.ext[1], Tq = s.ext[2], Tk = s.ext[3], D = q.ext[3];
     if ((D != 64 && D != 128) || Tk % 4 != 0 || Tq < 1 || Tk < 1) return ANN_OK;
     if (!rows16(q, 3) || !rows16(k, 3) || !rows16(s, 3) || !tma_view(s)) return ANN_OK;
+    int64_t const kdims[4] = {k.ext[3], k.ext[tok], k.ext[head], k.ext[0]};  // K as (d, key, head, batch)
+    int64_t const kstr[3] = {k.str[tok], k.str[head], k.str[0]};
+    if (!tma_view_ok(kdims, kstr)) return ANN_OK;
     ScArgs a{};
     a.q = static_cast<const float*>(q.data);
     a.k = static_cast<const float*>(k.data);
@@ -695,7 +711,8 @@ int scores_tc_f32(ann_stream stream, const Dims& q, const Dims& k, const Dims& s
     a.q_tiles = static_cast<int>(q_tiles);
     a.k_tiles = static_cast<int>(k_tiles);
     handled = true;
-    return D == 64 ? launch_scores<64>(stream, a, B * Hq) : launch_scores<128>(stream, a, B * Hq);
+    return D == 64 ? launch_scores<64>(stream, a, B * Hq, kdims, kstr)
+                   : launch_scores<128>(stream, a, B * Hq, kdims, kstr);
 }
 
 // fp32 attentionApply on the tensor cores (D 64 / 128, unit-stride 16-byte
