@@ -110,6 +110,25 @@ def test_apply_tensor_cores(ann, case):
     assert queue.take_device_error() == 0
 
 
+def test_scores_over_cache_view(ann):
+    """K as a view into a larger BHTD cache (heads 1..2 of 3, the first Tk of
+    Tcap positions): the K tiles come through a TMA tensor map with the cache's
+    strides."""
+    import torch
+    B, Tq, Tk, Tcap, Hq, D = 2, 270, 300, 333, 2, 128
+    g = rng(13)
+    q = normal(g, (B, Tq, Hq, D), np.float32)
+    kc = normal(g, (B, 3, Tcap, D), np.float32)
+    k = np.ascontiguousarray(kc[:, 1:3, :Tk])
+    want = oracle.attention_scores(q, k, np.empty((B, Hq, Tq, Tk), np.float32), 1, 1)
+    absdot = oracle.attention_scores(np.abs(q), np.abs(k), np.empty_like(want), 1, 1)
+    s = torch.full((B, Hq, Tq, Tk), float("nan"), device="cuda")
+    queue = ann.Queue()
+    ann.onHost.nn.attentionScores(queue, None, dev(q), dev(kc)[:, 1:3, :Tk], s, 1, 1)
+    check(host(s), want, absdot, D)
+    assert queue.take_device_error() == 0
+
+
 def test_apply_strided_probs(ann):
     """P as a view with padded rows (row pitch Tk + 12 floats, NaN in the pad):
     each row's bulk copy starts at its own pitch and takes Tk keys only."""

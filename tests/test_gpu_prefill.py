@@ -111,6 +111,28 @@ def test_prefill_gqa_layouts(ann, T, layout):
     assert_close(run(ann, q, k, v, 0.125, 4, layout, True), ref, T, "prefill gqa")
 
 
+@pytest.mark.parametrize("T", [np.float32, np.float64])
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_kv_cache_views(ann, T, D):
+    """K / V as views into a larger BHTD cache: heads 1..2 of 4, the first Tk of
+    Tcap positions (the layout of a KV cache with spare capacity). The fp32 path
+    reads them through TMA tensor maps with these strides."""
+    import torch
+    g = rng(77 + D)
+    B, Tq, Tk, Tcap, Hq = 2, 150, 150, 203, 2
+    q = normal(g, (B, Tq, Hq, D), T)
+    kc, vc = normal(g, (B, 4, Tcap, D), T), normal(g, (B, 4, Tcap, D), T)
+    k, v = kc[:, 1:3, :Tk], vc[:, 1:3, :Tk]
+    sc = 1.0 / math.sqrt(D)
+    ref = oracle_pipeline(q, np.ascontiguousarray(k), np.ascontiguousarray(v), sc, 1, 1, True)
+    o = empty(q.shape, T)
+    queue = ann.Queue()
+    kd, vd = dev(kc), dev(vc)
+    ann.onHost.nn.attentionPrefill(queue, None, dev(q), kd[:, 1:3, :Tk], vd[:, 1:3, :Tk], o, sc, 1, 1, True)
+    assert_close(host(o), ref, T, "prefill over cache views")
+    assert queue.take_device_error() == 0
+
+
 def _sampled(ann, T, B, Tt, H, D, seed, nrows=24):
     import torch
     dt = torch.float32 if T == np.float32 else torch.float64
