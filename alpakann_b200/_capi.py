@@ -61,6 +61,8 @@ SIGNATURES = {
                                         ctypes.c_int),
     "ann_signal_barrier": ([_S, ctypes.c_void_p, ctypes.c_void_p, _i32, _i32, _u32, ctypes.c_uint64],
                            ctypes.c_int),
+    "ann_signal_barrier_dev": ([_S, ctypes.c_void_p, ctypes.c_void_p, _i32, _i32, ctypes.c_void_p, ctypes.c_uint64],
+                               ctypes.c_int),
     "ann_sha256_file": ([ctypes.c_char_p, ctypes.c_char_p], ctypes.c_int),
     "ann_sha256_bytes": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p], ctypes.c_int),
     "ann_load_binary_tensor": ([_S, ctypes.c_char_p, ctypes.POINTER(AnnTensorSpec), ctypes.c_size_t,

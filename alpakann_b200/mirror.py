@@ -6,7 +6,8 @@ every rank has bound to ONE NVLink multicast object, here torch symmetric
 memory (plumbing only: it allocates, maps the peers' copies and creates the
 multicast object). Each rank's decode / prefill kernel stores its head slice
 through the multicast address, so the switch writes it into every rank's
-copy while the kernel runs; one signal barrier (ann_signal_barrier) after the
+copy while the kernel runs; one signal barrier (ann_signal_barrier_dev, its
+epoch kept in device memory so that a CUDA graph can replay it) after the
 kernel tells every rank that all slices have landed.
 
 MirrorBuffer.available() says whether this node can do it (NVSwitch
@@ -50,7 +51,7 @@ class MirrorBuffer:
         off = self._sig.data_ptr() - int(self._hs.buffer_ptrs[self.rank])
         ptrs = [int(p) + off for p in self._hs.buffer_ptrs]
         self._peer_sig = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
-        self._epoch = 0
+        self._epoch_word = torch.zeros((1,), dtype=torch.int32, device="cuda")  # this rank's last epoch
         self.timeout_ns = int(timeout_s * 1e9)
         torch.cuda.synchronize()
         dist.barrier(group)  # every rank's signals are zero before anyone signals
@@ -73,13 +74,19 @@ class MirrorBuffer:
             raise ValueError("view is not inside this buffer")
         return self._mc + off
 
+    @property
+    def epoch_word(self) -> int:
+        """Device address of this rank's epoch word (every barrier on these
+        signals, from Python or the C++ header, advances it on the device)."""
+        return self._epoch_word.data_ptr()
+
     def barrier(self, queue):
         """Enqueue the barrier on `queue` (every rank, same order): afterwards every
-        rank's copy holds all ranks' stores made through the multicast address."""
-        self._epoch = (self._epoch + 1) & 0xFFFFFFFF or 1
-        check(lib.ann_signal_barrier(queue.handle, ctypes.c_void_p(self._sig.data_ptr()),
-                                     ctypes.c_void_p(self._peer_sig.data_ptr()), self.world, self.rank, self._epoch,
-                                     self.timeout_ns))
+        rank's copy holds all ranks' stores made through the multicast address.
+        Capturable in a CUDA graph: the epoch advances on the device."""
+        check(lib.ann_signal_barrier_dev(queue.handle, ctypes.c_void_p(self._sig.data_ptr()),
+                                         ctypes.c_void_p(self._peer_sig.data_ptr()), self.world, self.rank,
+                                         ctypes.c_void_p(self.epoch_word), self.timeout_ns))
 
 
 __all__ = ["MirrorBuffer"]

@@ -282,7 +282,7 @@ class DecodeE2E(ctypes.Structure):
                 ("v_caches", ctypes.c_void_p), ("n_caches", ctypes.c_int32), ("out", ctypes.c_void_p),
                 ("head0", ctypes.c_int32), ("out_mirror", ctypes.c_void_p), ("signals", ctypes.c_void_p),
                 ("peer_signals", ctypes.c_void_p), ("nranks", ctypes.c_int32), ("rank", ctypes.c_int32),
-                ("epoch", ctypes.c_uint32), ("timeout_ns", ctypes.c_uint64)]
+                ("epoch_word", ctypes.c_void_p), ("timeout_ns", ctypes.c_uint64)]
 
 
 def e2e_library():
@@ -379,6 +379,45 @@ class DecodeBench:
                                        self.sharded.gathered.data_ptr(), self.gather_bytes))
             chk(lib.ann_scale_f32(sh, R(self.vsrc), 1.0, R(self.vdst)))
 
+    def graph_ms(self, replays, world):
+        """The device-resident step captured once in a CUDA graph (one step per
+        cache copy; rmsNorm, RoPE, decode and, across ranks, the multicast
+        stores and the device-epoch signal barrier) and replayed `replays`
+        times between events on the capturing stream: device ms per step, max
+        over ranks. None for the NCCL gather (not captured)."""
+        torch = self.torch
+        if self.gather == "nccl":
+            return None
+        s = torch.cuda.Stream()
+        s.wait_stream(self.stream)
+        saved = self.stream, self.queue
+        self.stream, self.queue = s, self.ann.Queue(s)
+        try:
+            for i in range(self.copies):  # uncaptured warm-up on the capturing stream
+                self.step(i)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(self.copies):
+                    self.step(i)
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    g.replay()
+                s.synchronize()
+                barrier(world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for _ in range(replays):
+                    g.replay()
+                e1.record(s)
+                e1.synchronize()
+            barrier(world)
+            t = max_over_ranks([e0.elapsed_time(e1) / (replays * self.copies)], world)[0]
+            del g
+        finally:
+            self.stream, self.queue = saved
+        return t
+
     def cpp_e2e_setup(self):
         """The DecodeE2E record for the C++ step (None where it does not apply:
         no library, or the NCCL gather, which the C++ step does not run)."""
@@ -402,7 +441,7 @@ class DecodeBench:
         if self.gather == "multicast":
             m = sh.mirror
             st.out_mirror, st.signals, st.peer_signals = sh._out_mc, m._sig.data_ptr(), m._peer_sig.data_ptr()
-            st.timeout_ns = m.timeout_ns
+            st.epoch_word, st.timeout_ns = m.epoch_word, m.timeout_ns
         self._e2e_lib, self._e2e = lib, st
         return st
 
@@ -410,15 +449,11 @@ class DecodeBench:
         """`steps` decode steps through the C++ drop-in header with host buffers;
         returns the device seconds between events around them."""
         st = self._e2e
-        if self.gather == "multicast":
-            st.epoch = self.sharded.mirror._epoch
         ms = ctypes.c_float(0)
         rc = self._e2e_lib.decode_e2e_run(ctypes.byref(st), steps, ctypes.c_void_p(self.stream.cuda_stream),
                                           ctypes.byref(ms))
         if rc != 0:
             raise RuntimeError("C++ decode step: " + self._e2e_lib.decode_e2e_error().decode())
-        if self.gather == "multicast":
-            self.sharded.mirror._epoch = st.epoch
         return ms.value / 1e3
 
     def e2e_step(self, i):
@@ -1093,11 +1128,14 @@ def main():
         B, Tk, H, D = ww["B"], ww["Tk"], ww["H"], ww["D"]
         Hl = H // world
         alg = 2 * B * Hl * Tk * D * 4 + 2 * B * Hl * D * 4  # per launch per GPU: K+V read, Q read, O write
+        g_ms = bench.graph_ms(max(10, min(steps, 200)), world)
+        graph = None if g_ms is None else {"ms_per_step": g_ms, "value": B / (g_ms / 1e3), "unit": "tokens/s",
+                                           "how": "the step captured once in a CUDA graph and replayed"}
         res = dict(value=B * steps / elapsed, ms_per_step=elapsed / steps * 1e3, kernel_us=kernel_s * 1e6,
                    achieved=alg / kernel_s / 1e9, e2e=B / e2e_s, e2e_steps=e2e_steps, clk=clk,
                    copies=bench.copies, kv_mib=bench.kv_bytes / 2**20, launches=bench.launches_per_step * steps,
                    h2d=bench.h2d_bytes, d2h=bench.d2h_bytes, alg=alg, parity=parity, repeats=nrep,
-                   rep_ms=[x / steps * 1e3 for x in spread], gather=bench.gather, api=api)
+                   rep_ms=[x / steps * 1e3 for x in spread], gather=bench.gather, api=api, graph=graph)
         bench.release()
         return res
 
@@ -1109,7 +1147,7 @@ def main():
         extra[other] = {"workload": WORKLOADS[other]["desc"], "value": o["value"], "unit": "tokens/s",
                         "ms_per_step": o["ms_per_step"], "kernel_us": o["kernel_us"],
                         "achieved_gbs": o["achieved"], "frac": o["achieved"] / peak, "e2e": o["e2e"],
-                        "parity": o["parity"]}
+                        "parity": o["parity"], "graph": o["graph"]}
         for name in ("c3", "c4"):
             extra[f"{name}_prefill"] = measure_prefill(name, world, rank, comm, clock_ids)
         extra["c3_block"] = measure_prefill_block(world, rank, comm)
@@ -1147,6 +1185,7 @@ def main():
             "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"], "steps": r["e2e_steps"], "api": r["api"]},
             "gpu_launches": r["launches"] * r["repeats"],
+            "graph": r["graph"],
             "clocks": r["clk"],
             "extra": extra,
         }

@@ -856,6 +856,16 @@ void signalBarrier(Q& queue, uint32_t* signals, uint32_t* const* peerSignals, in
     detail::check(ann_signal_barrier(detail::stream_of(queue), signals, peerSignals, nranks, rank, epoch, timeoutNs));
 }
 
+// The same barrier with its epoch in device memory (ann_signal_barrier_dev):
+// `epochWord` (zero before the first call) advances on the device, so the call
+// can be captured in a CUDA graph and replayed.
+template <typename Q>
+void signalBarrierDev(Q& queue, uint32_t* signals, uint32_t* const* peerSignals, int nranks, int rank,
+                      uint32_t* epochWord, uint64_t timeoutNs = 5000000000ull) {
+    detail::check(
+        ann_signal_barrier_dev(detail::stream_of(queue), signals, peerSignals, nranks, rank, epochWord, timeoutNs));
+}
+
 // One rank of the node's NCCL communicator (ann_comm_*), on the current CUDA
 // device. Rank 0 creates the rendezvous id with uniqueId() and hands its bytes
 // to the other ranks out of band; a rank whose peers do not all join within

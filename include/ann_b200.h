@@ -424,9 +424,10 @@ int ann_comm_abort(ann_comm comm);
  * out's first element: every result store is a multimem store that the switch
  * writes into EVERY rank's copy, inside the producing kernel, so the gather
  * overlaps the computation tile by tile and needs neither a collective nor a
- * re-assembly pass. The kernels fence at system scope before they retire;
- * ann_signal_barrier, enqueued after them on every rank, then publishes
- * all ranks' results to the rank's later work. Same shapes and semantics as
+ * re-assembly pass. ann_signal_barrier, enqueued after them on every rank,
+ * publishes all ranks' results to the rank's later work: it fences at system
+ * scope before its release stores, which covers every store the producing
+ * kernel made before it in stream order (the kernels themselves do not fence). Same shapes and semantics as
  * ann_attention_decode_* / ann_attention_prefill_* (prefill: the tensor-core
  * kernels only, else ANN_ENOTSUP). Only stores go through the multicast
  * address: nothing in this library loads from multicast or peer memory.
@@ -439,7 +440,12 @@ int ann_comm_abort(ann_comm comm);
  *   own array holds it (acquire). Every rank calls it in the same order with
  *   epochs 1, 2, 3, ...; a wait that has not completed after timeout_ns sets
  *   ANN_DEVERR_WAIT_TIMEOUT (ann_take_device_error) and the kernel returns.
- *   nranks <= 32. Plain stores only: no multimem, no peer loads. */
+ *   nranks <= 32. Plain stores only: no multimem, no peer loads.
+ * ann_signal_barrier_dev: the same barrier with the epoch kept in this rank's
+ *   device memory: `epoch_word` (one uint32, zero before the first call) is
+ *   read, its successor (skipping 0) used as the epoch and written back by the
+ *   kernel, so the call can be captured in a CUDA graph and replayed. Use one
+ *   of the two forms per signal array. */
 int ann_attention_decode_mirror_f32(ann_stream stream, const ann_view* q, const ann_view* k, const ann_view* v,
                                     const ann_view* out, void* out_mirror, float scale,
                                     uint32_t queries_per_kv_group, int32_t kv_layout);
@@ -454,6 +460,8 @@ int ann_attention_prefill_mirror_f64(ann_stream stream, const ann_view* q, const
                                      uint32_t queries_per_kv_group, int32_t kv_layout, int32_t causal);
 int ann_signal_barrier(ann_stream stream, uint32_t* signals, uint32_t* const* peer_signals, int32_t nranks,
                        int32_t rank, uint32_t epoch, uint64_t timeout_ns);
+int ann_signal_barrier_dev(ann_stream stream, uint32_t* signals, uint32_t* const* peer_signals, int32_t nranks,
+                           int32_t rank, uint32_t* epoch_word, uint64_t timeout_ns);
 
 /* ---- flat model artifacts: onHost/core/binary.hpp ------------------------
  * TensorSpec (binary.hpp:33-39): one tensor of a little-endian ".bin" file of

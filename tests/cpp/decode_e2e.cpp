@@ -50,7 +50,7 @@ struct DecodeE2E {
     uint32_t* signals;
     uint32_t* const* peer_signals;
     int32_t nranks, rank;
-    uint32_t epoch;  // in: last epoch used; out: last epoch after the steps
+    uint32_t* epoch_word;  // this rank's barrier epoch, in device memory
     uint64_t timeout_ns;
 };
 
@@ -96,8 +96,8 @@ int decode_e2e_run(DecodeE2E* a, int steps, cudaStream_t stream, float* ms) {
             } else {
                 nn::attentionDecodeMirror<float>(queue, 0, vq, vk, vv, vout, a->out_mirror, a->scale, 1u,
                                                  alpaka::nn::AttentionKvLayout::BHTD);
-                a->epoch = a->epoch + 1u == 0u ? 1u : a->epoch + 1u;
-                b2::signalBarrier(queue, a->signals, a->peer_signals, a->nranks, a->rank, a->epoch, a->timeout_ns);
+                b2::signalBarrierDev(queue, a->signals, a->peer_signals, a->nranks, a->rank, a->epoch_word,
+                                     a->timeout_ns);
             }
             cudaMemcpyAsync(a->h_out, a->out, ob, cudaMemcpyDeviceToHost, stream);
         }

@@ -87,3 +87,53 @@ def test_signal_barrier_single_rank_and_absent_rank(ann):
     with pytest.raises(_capi.AnnShapeError):  # epochs start at 1
         _capi.check(_capi.lib.ann_signal_barrier(queue.handle, ctypes.c_void_p(sig.data_ptr()),
                                                  ctypes.c_void_p(one.data_ptr()), 1, 0, 0, 1_000_000))
+
+
+def test_signal_barrier_dev_epochs_and_graph_replay(ann):
+    """ann_signal_barrier_dev keeps the epoch in device memory: it advances with
+    every call, also when the call is captured in a CUDA graph and replayed;
+    with a second rank that never signals the bounded wait runs out as for
+    ann_signal_barrier (no multicast, no peer memory)."""
+    import ctypes
+
+    import torch
+    from alpakann_b200 import _capi
+    lib = _capi.lib
+    s = torch.cuda.Stream()
+    queue = ann.Queue(s)
+    assert queue.take_device_error() == 0
+    sig = torch.zeros(2, dtype=torch.int32, device="cuda")
+    word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    one = torch.tensor([sig.data_ptr()], dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+
+    def barrier(peers, nranks, timeout_ns=1_000_000_000):
+        _capi.check(lib.ann_signal_barrier_dev(queue.handle, ctypes.c_void_p(sig.data_ptr()),
+                                               ctypes.c_void_p(peers.data_ptr()), nranks, 0,
+                                               ctypes.c_void_p(word.data_ptr()), timeout_ns))
+
+    for _ in range(2):
+        barrier(one, 1)
+    s.synchronize()
+    assert word.item() == 2 and sig[0].item() == 2
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        barrier(one, 1)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            g.replay()
+    s.synchronize()
+    assert word.item() == 5 and sig[0].item() == 5  # captured once, three new epochs
+    assert queue.take_device_error() == 0
+    del g
+    sig.zero_()
+    word.zero_()
+    two = torch.tensor([sig.data_ptr(), sig.data_ptr()], dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    barrier(two, 2, 20_000_000)  # 20 ms
+    assert queue.take_device_error() & _capi.ANN_DEVERR_WAIT_TIMEOUT
+    assert sig.tolist() == [1, 0] and word.item() == 1
+    with pytest.raises(_capi.AnnShapeError):  # an epoch word is required
+        _capi.check(lib.ann_signal_barrier_dev(queue.handle, ctypes.c_void_p(sig.data_ptr()),
+                                               ctypes.c_void_p(one.data_ptr()), 1, 0, None, 1_000_000))
+
