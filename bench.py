@@ -684,6 +684,20 @@ def measure_prefill(name, world, rank, comm, clock_ids=None, reps=10, sustained_
         res.update(kernel=f"prefill_f64_kernel<{D}> (FP64 tensor cores, mma.sync m16n8k4)", fp64_peak_tflops=pk,
                    fp64_peak_kind="cuBLAS DGEMM 4096^3, measured in this run",
                    frac_of_fp64_peak=res["tflops"] / world / pk, sustained=sustained)
+    if world > 1:
+        # fused compute + collective: the target time of a rank is the slower of
+        # its useful flops at the compute ceiling and the bytes of the output that
+        # must reach it over NVLink (every other rank's heads) at the measured
+        # peer-copy rate of this pool, 770 GB/s per direction
+        elem = 4 if p["dtype"] == "f32" else 8
+        ingress = (world - 1) / world * B * T * H * D * elem
+        ceiling = pk / 3 if p["dtype"] == "f32" else pk
+        t_compute = flops / world / (ceiling * 1e12)
+        t_link = ingress / 770e9
+        target = max(t_compute, t_link)
+        res["fused_roofline"] = {"target_ms": target * 1e3, "bound": "nvlink" if t_link >= t_compute else "compute",
+                                 "compute_ms": t_compute * 1e3, "nvlink_ms": t_link * 1e3,
+                                 "nvlink_bytes_per_gpu": ingress, "link_gbs": 770.0, "frac": target / t}
     return res
 
 
