@@ -99,6 +99,7 @@ struct PairArgs {
     int q_tiles;         // 256-row tiles
     int64_t bhs;         // batch * query heads
     int64_t head_chunk;  // (batch, head) pairs per dispatch chunk
+    int alternate;       // query tiles in the order heaviest, lightest, 2nd heaviest, ... (see launch_pair)
 };
 
 // lo part of the 3xTF32 split (see prefill_tc.cu): x - trunc13(x), exact in fp32.
@@ -155,11 +156,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(PairArgs a, f
     // 1-D grid of pairs in chunks of a.head_chunk (batch, head) pairs
     // (head_chunk_for): inside a chunk the query tiles go from the last (most
     // keys) down, so the heaviest pairs start first, while the K/V of one chunk
-    // stay in L2
+    // stay in L2; or, with a.alternate, heaviest, lightest, second heaviest,
+    // second lightest, ..., so that tiles finish (and their outputs leave)
+    // from the start of the kernel on
     int64_t const lin = blockIdx.x / 2, per_chunk = a.head_chunk * a.q_tiles;
     int64_t const chunk = lin / per_chunk, in_chunk = lin % per_chunk;
     int64_t const chunk_bh = a.bhs - chunk * a.head_chunk < a.head_chunk ? a.bhs - chunk * a.head_chunk : a.head_chunk;
-    int const qt = a.q_tiles - 1 - static_cast<int>(in_chunk / chunk_bh);
+    int const order = static_cast<int>(in_chunk / chunk_bh);  // this tile's place in the dispatch order
+    int const qt = a.alternate ? ((order & 1) ? order / 2 : a.q_tiles - 1 - order / 2) : a.q_tiles - 1 - order;
     int64_t const bh = chunk * a.head_chunk + in_chunk % chunk_bh;
     int64_t const hq = bh % a.Hq, b = bh / a.Hq, kvh = hq / a.g;
     int64_t const tile_q0 = static_cast<int64_t>(qt) * 2 * kBM;
@@ -623,6 +627,15 @@ int launch_pair(ann_stream stream, const Dims& q, const Dims& k, const Dims& v, 
     a.bhs = bhs;
     // a chunk is counted in CTAs: two per 256-row tile
     a.head_chunk = head_chunk_for(bhs, 2 * tiles, 2 * a.Tk * q.ext[3] * 4, 1);
+    // ANN_PREFILL_ALTERNATE=1: query tiles alternate heavy and light. Meant for
+    // a multicast output with few waves of pairs (c3 head-sharded over 8 GPUs:
+    // 3.5 waves), where every tile's output must also cross NVLink into the
+    // other ranks: with the heaviest tiles first nothing finishes during the
+    // first wave, so the link idles and later the stores back up into the SMs.
+    // A greedy-dispatch model with the link's rate puts it at 1.22 instead of
+    // 1.49 x the compute time at 8 GPUs (worse at 2 GPUs); not measured on 8
+    // GPUs yet, so not the default.
+    if (const char* env = std::getenv("ANN_PREFILL_ALTERNATE")) a.alternate = env[0] == '1';
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute cl{};
     cl.id = cudaLaunchAttributeClusterDimension;

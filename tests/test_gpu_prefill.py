@@ -133,6 +133,24 @@ def test_prefill_kv_cache_views(ann, T, D):
     assert queue.take_device_error() == 0
 
 
+@pytest.mark.parametrize("shape", [(2, 1000, 3, 128), (1, 300, 2, 64)])
+def test_prefill_alternating_tile_order_same_bits(ann, monkeypatch, shape):
+    """ANN_PREFILL_ALTERNATE=1: the fp32 pair kernel takes its query tiles in
+    the order heaviest, lightest, second heaviest, ... (the order it uses for
+    multicast outputs with few waves of work); every tile is computed exactly
+    as before, so the output is bit-identical to the default order."""
+    B, Tt, H, D = shape
+    g = rng(Tt + D)
+    q, k, v = (normal(g, (B, Tt, H, D), np.float32) for _ in range(3))
+    sc = 1.0 / math.sqrt(D)
+    monkeypatch.setenv("ANN_PREFILL_ALTERNATE", "0")
+    base = run(ann, q, k, v, sc, 1, 0, True)
+    monkeypatch.setenv("ANN_PREFILL_ALTERNATE", "1")
+    alt = run(ann, q, k, v, sc, 1, 0, True)
+    assert np.array_equal(base, alt)
+    assert_close(alt, oracle_pipeline(q, k, v, sc, 1, 0, True), np.float32, "prefill, alternating order")
+
+
 def _sampled(ann, T, B, Tt, H, D, seed, nrows=24):
     import torch
     dt = torch.float32 if T == np.float32 else torch.float64
